@@ -1,0 +1,135 @@
+// api_kernels.cpp — C-ABI entry points for single convolution primitives on device buffers.
+// Each call plans, launches and synchronises one operation (used by the kernel-level tests and
+// by callers that want one layer at a time); the training step uses persistent plans instead.
+#include <cstdio>
+#include <vector>
+
+#include "../../include/wuburvc_b200.h"
+#include "conv_plan.h"
+#include "small_kernels.cuh"
+
+using namespace wb;
+
+namespace {
+
+struct Scratch {
+  int* err = nullptr;
+  float* part = nullptr;
+  int* tabs = nullptr;
+  ~Scratch() {
+    if (err) cudaFree(err);
+    if (part) cudaFree(part);
+    if (tabs) cudaFree(tabs);
+  }
+};
+
+int finish(cudaStream_t st, int* derr) {
+  cudaError_t e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) {
+    fprintf(stderr, "wuburvc_b200: CUDA error %s\n", cudaGetErrorString(e));
+    return WUBU_B200_ERR_CUDA;
+  }
+  int h = 0;
+  cudaMemcpy(&h, derr, sizeof(int), cudaMemcpyDeviceToHost);
+  if (h) {
+    fprintf(stderr, "wuburvc_b200: kernel reported error %d (wait timeout)\n", h);
+    return WUBU_B200_ERR_TIMEOUT;
+  }
+  return WUBU_B200_OK;
+}
+
+Epi plain_epi(const float* bias, float* out) {
+  Epi e{};
+  e.bias = bias;
+  e.out_f32 = out;
+  e.scale = 1.f;
+  e.slope = 0.1f;
+  return e;
+}
+
+int run_wgrad(WgradLaunch& L, Scratch& s, int layout, int c_out, int k, float* dw, cudaStream_t st) {
+  std::vector<int> tab(L.row_tap);
+  tab.insert(tab.end(), L.row_oc.begin(), L.row_oc.end());
+  if (cudaMalloc(&s.tabs, tab.size() * sizeof(int)) != cudaSuccess) return WUBU_B200_ERR_CUDA;
+  cudaMemcpy(s.tabs, tab.data(), tab.size() * sizeof(int), cudaMemcpyHostToDevice);
+  if (L.run(st) != cudaSuccess) return WUBU_B200_ERR_CUDA;
+  const int rows = L.p.n_mtiles * 128;
+  wgrad_reduce(s.part, L.splits, rows, L.p.n_total, s.tabs, s.tabs + rows, layout, c_out, k, dw, 0, st);
+  return finish(st, s.err);
+}
+
+}  // namespace
+
+extern "C" {
+
+int wubu_b200_conv1d(const void* x_hi, const void* x_lo, const void* w_hi, const void* w_lo, const float* bias,
+                     float* out, int B, int C_in, int T, int C_out, int k, int dil, int pad, int split,
+                     void* stream) {
+  cudaStream_t st = (cudaStream_t)stream;
+  Scratch s;
+  if (cudaMalloc(&s.err, sizeof(int)) != cudaSuccess) return WUBU_B200_ERR_CUDA;
+  cudaMemsetAsync(s.err, 0, sizeof(int), st);
+  ConvGeom g{B, T, T + 2 * pad - dil * (k - 1), C_in, C_out, k, dil, pad};
+  ConvLaunch L;
+  if (!plan_conv(L, g, x_hi, x_lo, w_hi, w_lo, split, plain_epi(bias, out), s.err)) return WUBU_B200_ERR_SHAPE;
+  if (L.run(st) != cudaSuccess) return WUBU_B200_ERR_CUDA;
+  return finish(st, s.err);
+}
+
+int wubu_b200_conv1d_wgrad(const void* dy, const void* x, float* dw, int B, int C_in, int T, int C_out, int k,
+                           int dil, int pad, void* stream) {
+  cudaStream_t st = (cudaStream_t)stream;
+  Scratch s;
+  if (cudaMalloc(&s.err, sizeof(int)) != cudaSuccess) return WUBU_B200_ERR_CUDA;
+  cudaMemsetAsync(s.err, 0, sizeof(int), st);
+  ConvGeom g{B, T, T + 2 * pad - dil * (k - 1), C_in, C_out, k, dil, pad};
+  WgradLaunch L;
+  if (!plan_wgrad(L, g, dy, x, nullptr, ~size_t(0), 296, s.err)) return WUBU_B200_ERR_SHAPE;
+  if (cudaMalloc(&s.part, wgrad_part_floats(L) * sizeof(float)) != cudaSuccess) return WUBU_B200_ERR_CUDA;
+  L.p.part = s.part;
+  return run_wgrad(L, s, 0, C_out, k, dw, st);
+}
+
+int wubu_b200_convT(const void* x_hi, const void* x_lo, const void* wp_hi, const void* wp_lo, const float* bias,
+                    float* out, int B, int C_in, int T_in, int C_out, int k, int stride, int pad, int split,
+                    void* stream) {
+  cudaStream_t st = (cudaStream_t)stream;
+  Scratch s;
+  if (cudaMalloc(&s.err, sizeof(int)) != cudaSuccess) return WUBU_B200_ERR_CUDA;
+  cudaMemsetAsync(s.err, 0, sizeof(int), st);
+  ConvLaunch L;
+  if (!plan_convT(L, B, T_in, C_in, C_out, k, stride, pad, x_hi, x_lo, wp_hi, wp_lo, split, plain_epi(bias, out),
+                  s.err))
+    return WUBU_B200_ERR_SHAPE;
+  if (L.run(st) != cudaSuccess) return WUBU_B200_ERR_CUDA;
+  return finish(st, s.err);
+}
+
+int wubu_b200_convT_dgrad(const void* dy, const void* wd, float* dx, int B, int C_in, int T_in, int C_out, int k,
+                          int stride, int pad, void* stream) {
+  cudaStream_t st = (cudaStream_t)stream;
+  Scratch s;
+  if (cudaMalloc(&s.err, sizeof(int)) != cudaSuccess) return WUBU_B200_ERR_CUDA;
+  cudaMemsetAsync(s.err, 0, sizeof(int), st);
+  ConvLaunch L;
+  if (!plan_convT_dgrad(L, B, T_in, C_in, C_out, k, stride, pad, dy, wd, plain_epi(nullptr, dx), s.err))
+    return WUBU_B200_ERR_SHAPE;
+  if (L.run(st) != cudaSuccess) return WUBU_B200_ERR_CUDA;
+  return finish(st, s.err);
+}
+
+int wubu_b200_convT_wgrad(const void* x, const void* dy, float* dw, int B, int C_in, int T_in, int C_out, int k,
+                          int stride, int pad, void* stream) {
+  cudaStream_t st = (cudaStream_t)stream;
+  Scratch s;
+  if (cudaMalloc(&s.err, sizeof(int)) != cudaSuccess) return WUBU_B200_ERR_CUDA;
+  cudaMemsetAsync(s.err, 0, sizeof(int), st);
+  WgradLaunch L;
+  if (!plan_convT_wgrad(L, B, T_in, C_in, C_out, k, stride, pad, x, dy, nullptr, ~size_t(0), 296, s.err))
+    return WUBU_B200_ERR_SHAPE;
+  if (cudaMalloc(&s.part, wgrad_part_floats(L) * sizeof(float)) != cudaSuccess) return WUBU_B200_ERR_CUDA;
+  L.p.part = s.part;
+  return run_wgrad(L, s, 1, C_out, k, dw, st);
+}
+
+}  // extern "C"

@@ -1,0 +1,323 @@
+// conv_plan.cpp — TMA descriptors and launch parameters for the tcgen05 convolution kernels.
+#include "conv_plan.h"
+
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+namespace wb {
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+int pow2_cols(int n) {
+  int c = 32;
+  while (c < n) c <<= 1;
+  return c;
+}
+
+constexpr size_t kSmemBudget = 220 * 1024;
+
+}  // namespace
+
+bool make_map_bf16_3d(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
+                      uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t b0, uint32_t b1, uint32_t b2) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
+  cuuint32_t box[3] = {b0, b1, b2};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUtensorMapSwizzle sw = (b0 * 2 == 128) ? CU_TENSOR_MAP_SWIZZLE_128B
+                          : (b0 * 2 == 64) ? CU_TENSOR_MAP_SWIZZLE_64B
+                                           : CU_TENSOR_MAP_SWIZZLE_32B;
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    fprintf(stderr, "wuburvc_b200: cuTensorMapEncodeTiled failed (%d) dims %llu %llu %llu box %u %u %u\n", (int)r,
+            (unsigned long long)d0, (unsigned long long)d1, (unsigned long long)d2, b0, b1, b2);
+    return false;
+  }
+  return true;
+}
+
+// choose K chunk / stages for the forward-type kernel
+static void pick_fwd_tiling(int c_in, int n_tile, int split, int& kc, int& stages, size_t& smem) {
+  kc = (c_in % 64 == 0) ? 64 : 32;
+  for (;;) {
+    const int nA = split ? 2 : 1;
+    const size_t stage = (size_t)nA * (128 * kc * 2 + (size_t)n_tile * kc * 2);
+    stages = (int)std::min<size_t>(8, (kSmemBudget - 1024 - 256) / stage);
+    if (stages >= 3 || kc == 32) {
+      smem = stages * stage + 1024 /*align*/ + 256 /*barriers*/;
+      return;
+    }
+    kc = 32;
+  }
+}
+
+static bool finish_fwd(ConvLaunch& L, int B, int c_in, int n_total, int split, int nphase, int* err) {
+  TcConvParams& p = L.p;
+  int n_tile = std::min(n_total, 256);
+  while (n_total % n_tile) n_tile -= 16;
+  if (n_tile < 16 || n_tile % 16 || n_total % 32) return false;
+  if (c_in % 32) return false;
+  pick_fwd_tiling(c_in, n_tile, split, L.kc, p.stages, L.smem);
+  p.n_tile = n_tile;
+  p.n_total = n_total;
+  p.n_chunks = c_in / L.kc;
+  p.split = split;
+  p.tmem_cols = pow2_cols(n_tile);
+  p.tiles_per_item = (p.m_rows + 127) / 128;
+  p.err = err;
+  L.grid = dim3(B * p.tiles_per_item, n_total / n_tile, nphase);
+  return true;
+}
+
+bool plan_conv(ConvLaunch& L, const ConvGeom& g, const void* x_hi, const void* x_lo, const void* w_hi,
+               const void* w_lo, int split, const Epi& epi, int* err) {
+  memset(&L.p, 0, sizeof(L.p));
+  memset(&L.maps, 0, sizeof(L.maps));
+  TcConvParams& p = L.p;
+  if (g.k > kMaxTapList) return false;
+  p.m_rows = g.T_out;
+  p.t_out = g.T_out;
+  p.out_stride = 1;
+  p.out_off[0] = 0;
+  p.tap_start[0] = 0;
+  p.tap_start[1] = g.k;
+  for (int t = 0; t < g.k; ++t) {
+    p.tap_map[t] = 0;
+    p.tap_shift[t] = (short)(-g.pad + g.dil * t);
+    p.tap_w[t] = (short)t;
+  }
+  p.lo_base = 1;
+  p.epi = epi;
+  int n_tile = std::min(g.C_out, 256);
+  while (g.C_out % n_tile) n_tile -= 16;
+  int kc, stages;
+  size_t smem;
+  pick_fwd_tiling(g.C_in, n_tile, split, kc, stages, smem);
+  const uint64_t rs = (uint64_t)g.C_in * 2, is = rs * g.T_in;
+  if (!make_map_bf16_3d(&L.maps.a[0], x_hi, g.C_in, g.T_in, g.B, rs, is, kc, 128, 1)) return false;
+  if (split && !make_map_bf16_3d(&L.maps.a[1], x_lo, g.C_in, g.T_in, g.B, rs, is, kc, 128, 1)) return false;
+  const uint64_t wr = (uint64_t)g.C_in * 2, wt = wr * g.C_out;
+  if (!make_map_bf16_3d(&L.maps.w_hi, w_hi, g.C_in, g.C_out, g.k, wr, wt, kc, n_tile, 1)) return false;
+  if (split && !make_map_bf16_3d(&L.maps.w_lo, w_lo, g.C_in, g.C_out, g.k, wr, wt, kc, n_tile, 1)) return false;
+  return finish_fwd(L, g.B, g.C_in, g.C_out, split, 1, err);
+}
+
+bool plan_convT(ConvLaunch& L, int B, int T_in, int C_in, int C_out, int k, int s, int pad, const void* x_hi,
+                const void* x_lo, const void* wp_hi, const void* wp_lo, int split, const Epi& epi, int* err) {
+  memset(&L.p, 0, sizeof(L.p));
+  memset(&L.maps, 0, sizeof(L.maps));
+  TcConvParams& p = L.p;
+  if (s > kMaxPhases || k > kMaxTapList || pad >= s) return false;
+  p.m_rows = T_in + 1;
+  p.t_out = T_in * s;
+  p.out_stride = s;
+  int n = 0;
+  for (int r = 0; r < s; ++r) {
+    p.out_off[r] = r - pad;
+    p.tap_start[r] = n;
+    for (int m = 0; r + s * m < k; ++m) {
+      p.tap_map[n] = 0;
+      p.tap_shift[n] = (short)(-m);
+      p.tap_w[n] = (short)n;  // packed phase-tap order
+      ++n;
+    }
+  }
+  p.tap_start[s] = n;
+  p.lo_base = 1;
+  p.epi = epi;
+  int n_tile = std::min(C_out, 256);
+  int kc, stages;
+  size_t smem;
+  pick_fwd_tiling(C_in, n_tile, split, kc, stages, smem);
+  const uint64_t rs = (uint64_t)C_in * 2, is = rs * T_in;
+  if (!make_map_bf16_3d(&L.maps.a[0], x_hi, C_in, T_in, B, rs, is, kc, 128, 1)) return false;
+  if (split && !make_map_bf16_3d(&L.maps.a[1], x_lo, C_in, T_in, B, rs, is, kc, 128, 1)) return false;
+  const uint64_t wr = (uint64_t)C_in * 2, wt = wr * C_out;
+  if (!make_map_bf16_3d(&L.maps.w_hi, wp_hi, C_in, C_out, k, wr, wt, kc, n_tile, 1)) return false;
+  if (split && !make_map_bf16_3d(&L.maps.w_lo, wp_lo, C_in, C_out, k, wr, wt, kc, n_tile, 1)) return false;
+  return finish_fwd(L, B, C_in, C_out, split, s, err);
+}
+
+static int floordiv(int a, int b) { return (a >= 0) ? a / b : -((-a + b - 1) / b); }
+
+bool plan_convT_dgrad(ConvLaunch& L, int B, int T_in, int C_in, int C_out, int k, int s, int pad, const void* dy,
+                      const void* wd, const Epi& epi, int* err) {
+  memset(&L.p, 0, sizeof(L.p));
+  memset(&L.maps, 0, sizeof(L.maps));
+  TcConvParams& p = L.p;
+  if (s > kMaxMaps || k > kMaxTapList) return false;
+  const int T_out = T_in * s;
+  p.m_rows = T_in;
+  p.t_out = T_in;
+  p.out_stride = 1;
+  p.out_off[0] = 0;
+  p.tap_start[0] = 0;
+  p.tap_start[1] = k;
+  for (int t = 0; t < k; ++t) {
+    const int d = t - pad;
+    const int r = ((d % s) + s) % s;
+    p.tap_map[t] = (signed char)r;
+    p.tap_shift[t] = (short)floordiv(d, s);
+    p.tap_w[t] = (short)t;
+  }
+  p.lo_base = 0;
+  p.epi = epi;
+  int n_tile = std::min(C_in, 256);
+  int kc, stages;
+  size_t smem;
+  pick_fwd_tiling(C_out, n_tile, 0, kc, stages, smem);
+  for (int r = 0; r < s; ++r) {
+    const uint64_t rows = (uint64_t)(T_out - r + s - 1) / s;
+    const char* base = static_cast<const char*>(dy) + (size_t)r * C_out * 2;
+    if (!make_map_bf16_3d(&L.maps.a[r], base, C_out, rows, B, (uint64_t)s * C_out * 2, (uint64_t)T_out * C_out * 2,
+                          kc, 128, 1))
+      return false;
+  }
+  const uint64_t wr = (uint64_t)C_out * 2, wt = wr * C_in;
+  if (!make_map_bf16_3d(&L.maps.w_hi, wd, C_out, C_in, k, wr, wt, kc, n_tile, 1)) return false;
+  return finish_fwd(L, B, C_out, C_in, 0, 1, err);
+}
+
+// ------------------------------------------------------------------------------------------------
+// weight gradients
+// ------------------------------------------------------------------------------------------------
+static bool finish_wgrad(WgradLaunch& L, int B, int T_rows, int C_in, int C_out, int n_atoms_total,
+                         const int* a_map, const int* a_shift, const int* a_oc0, const int* a_tap, float* part,
+                         size_t cap, int target_ctas, int* err) {
+  TcWgParams& p = L.p;
+  p.atom_m = std::min(C_out, 64);
+  if (C_out % p.atom_m || (p.atom_m != 32 && p.atom_m != 64)) return false;
+  p.m_atoms = 128 / p.atom_m;
+  p.n_mtiles = (n_atoms_total + p.m_atoms - 1) / p.m_atoms;
+  if (p.n_mtiles > 64) return false;
+  for (int mt = 0; mt < p.n_mtiles; ++mt)
+    for (int j = 0; j < 4; ++j) {
+      const int a = mt * p.m_atoms + j;
+      const bool use = j < p.m_atoms && a < n_atoms_total;
+      p.atom_map[mt][j] = use ? (signed char)a_map[a] : 0;
+      p.atom_shift[mt][j] = use ? (short)a_shift[a] : 0;
+      p.atom_oc0[mt][j] = use ? (short)a_oc0[a] : 0;
+      p.atom_tap[mt][j] = use ? (short)a_tap[a] : -1;
+    }
+  int n_tile = std::min(C_in, 256);
+  while (C_in % n_tile) n_tile -= 16;
+  if (n_tile % 32 && n_tile != 16) return false;
+  p.n_in = n_tile;
+  p.n_total = C_in;
+  const int atom_n = std::min(n_tile, 64);
+  if (n_tile % atom_n || (atom_n != 32 && atom_n != 64)) return false;
+  p.n_atoms = n_tile / atom_n;
+  p.c_out = C_out;
+  p.t_rows = T_rows;
+  p.kblocks_per_item = (T_rows + 63) / 64;
+  p.total_kblocks = B * p.kblocks_per_item;
+  const int n_ntiles = C_in / n_tile;
+  const int base = p.n_mtiles * n_ntiles;
+  int splits = std::max(1, std::min(p.total_kblocks, (target_ctas + base - 1) / base));
+  p.kb_per_split = (p.total_kblocks + splits - 1) / splits;
+  splits = (p.total_kblocks + p.kb_per_split - 1) / p.kb_per_split;
+  const size_t stage = 128 * 64 * 2 + (size_t)n_tile * 64 * 2;
+  p.stages = (int)std::min<size_t>(6, (kSmemBudget - 1024 - 256) / stage);
+  L.smem = p.stages * stage + 1024 + 256;
+  p.tmem_cols = pow2_cols(n_tile);
+  p.err = err;
+  p.part = part;
+  L.splits = splits;
+  L.grid = dim3(p.n_mtiles, splits, n_ntiles);
+  if ((size_t)splits * p.n_mtiles * 128 * C_in > cap) return false;
+  L.row_tap.assign((size_t)p.n_mtiles * 128, -1);
+  L.row_oc.assign((size_t)p.n_mtiles * 128, 0);
+  for (int mt = 0; mt < p.n_mtiles; ++mt)
+    for (int m = 0; m < 128; ++m) {
+      const int j = m / p.atom_m;
+      L.row_tap[mt * 128 + m] = p.atom_tap[mt][j];
+      L.row_oc[mt * 128 + m] = p.atom_oc0[mt][j] + m % p.atom_m;
+    }
+  return true;
+}
+
+size_t wgrad_part_floats(const WgradLaunch& L) {
+  return (size_t)L.splits * L.p.n_mtiles * 128 * L.p.n_total;
+}
+
+bool plan_wgrad(WgradLaunch& L, const ConvGeom& g, const void* dy, const void* x, float* part, size_t cap,
+                int target_ctas, int* err) {
+  memset(&L.p, 0, sizeof(L.p));
+  memset(&L.maps, 0, sizeof(L.maps));
+  const int atom_m = std::min(g.C_out, 64);
+  const int oc_chunks = g.C_out / atom_m;
+  std::vector<int> am, ash, aoc, atap;
+  for (int t = 0; t < g.k; ++t)
+    for (int c = 0; c < oc_chunks; ++c) {
+      am.push_back(0);
+      ash.push_back(g.pad - g.dil * t);
+      aoc.push_back(c * atom_m);
+      atap.push_back(t);
+    }
+  if (!make_map_bf16_3d(&L.maps.d[0], dy, g.C_out, g.T_out, g.B, (uint64_t)g.C_out * 2,
+                        (uint64_t)g.C_out * 2 * g.T_out, atom_m, 64, 1))
+    return false;
+  const int n_tile = std::min(g.C_in, 256);
+  const int atom_n = std::min(n_tile, 64);
+  if (!make_map_bf16_3d(&L.maps.x, x, g.C_in, g.T_in, g.B, (uint64_t)g.C_in * 2, (uint64_t)g.C_in * 2 * g.T_in,
+                        atom_n, 64, 1))
+    return false;
+  return finish_wgrad(L, g.B, g.T_in, g.C_in, g.C_out, (int)am.size(), am.data(), ash.data(), aoc.data(),
+                      atap.data(), part, cap, target_ctas, err);
+}
+
+bool plan_convT_wgrad(WgradLaunch& L, int B, int T_in, int C_in, int C_out, int k, int s, int pad, const void* x,
+                      const void* dy, float* part, size_t cap, int target_ctas, int* err) {
+  memset(&L.p, 0, sizeof(L.p));
+  memset(&L.maps, 0, sizeof(L.maps));
+  if (s > kMaxMaps) return false;
+  const int T_out = T_in * s;
+  const int atom_m = std::min(C_out, 64);
+  const int oc_chunks = C_out / atom_m;
+  for (int r = 0; r < s; ++r) {
+    const uint64_t rows = (uint64_t)(T_out - r + s - 1) / s;
+    const char* base = static_cast<const char*>(dy) + (size_t)r * C_out * 2;
+    if (!make_map_bf16_3d(&L.maps.d[r], base, C_out, rows, B, (uint64_t)s * C_out * 2, (uint64_t)T_out * C_out * 2,
+                          atom_m, 64, 1))
+      return false;
+  }
+  std::vector<int> am, ash, aoc, atap;
+  for (int t = 0; t < k; ++t)
+    for (int c = 0; c < oc_chunks; ++c) {
+      const int d = t - pad;
+      const int r = ((d % s) + s) % s;
+      am.push_back(r);
+      ash.push_back(floordiv(d, s));
+      aoc.push_back(c * atom_m);
+      atap.push_back(t);
+    }
+  const int n_tile = std::min(C_in, 256);
+  const int atom_n = std::min(n_tile, 64);
+  if (!make_map_bf16_3d(&L.maps.x, x, C_in, T_in, B, (uint64_t)C_in * 2, (uint64_t)C_in * 2 * T_in, atom_n, 64, 1))
+    return false;
+  return finish_wgrad(L, B, T_in, C_in, C_out, (int)am.size(), am.data(), ash.data(), aoc.data(), atap.data(), part,
+                      cap, target_ctas, err);
+}
+
+}  // namespace wb

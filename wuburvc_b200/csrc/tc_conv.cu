@@ -1,0 +1,404 @@
+// tc_conv.cu — tcgen05/TMEM implicit-GEMM kernels (sm_100a).  See tc_conv.cuh.
+#include "tc_conv.cuh"
+
+namespace wb {
+
+// ---------------------------------------------------------------------------------------------
+// Epilogue helpers
+// ---------------------------------------------------------------------------------------------
+
+// Warp transpose-reduction: on return v[0] of lane l holds sum over lanes of the input v[l].
+WB_DEV float warp_colsum32(float* v, int lane) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    const bool upper = (lane & off) != 0;
+#pragma unroll
+    for (int i = 0; i < off; ++i) {
+      float send = upper ? v[i] : v[i + off];
+      float keep = upper ? v[i + off] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+    }
+  }
+  return v[0];
+}
+
+WB_DEV void load_bf16x32(const bf16* p, float* out) {
+  const uint4* q = reinterpret_cast<const uint4*>(p);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint4 u = q[i];
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 f = __bfloat1622float2(h[j]);
+      out[i * 8 + j * 2] = f.x;
+      out[i * 8 + j * 2 + 1] = f.y;
+    }
+  }
+}
+
+WB_DEV void store_bf16x32(bf16* p, const bf16* v) {
+  uint4* q = reinterpret_cast<uint4*>(p);
+  const uint4* s = reinterpret_cast<const uint4*>(v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) q[i] = s[i];
+}
+
+WB_DEV void load_f32x32(const float* p, float* out) {
+  const float4* q = reinterpret_cast<const float4*>(p);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float4 f = q[i];
+    out[i * 4] = f.x; out[i * 4 + 1] = f.y; out[i * 4 + 2] = f.z; out[i * 4 + 3] = f.w;
+  }
+}
+
+WB_DEV void store_f32x32(float* p, const float* v) {
+  float4* q = reinterpret_cast<float4*>(p);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) q[i] = make_float4(v[i * 4], v[i * 4 + 1], v[i * 4 + 2], v[i * 4 + 3]);
+}
+
+// Sums `v` (one row per thread, 32 columns) over the 128 rows of the CTA's four epilogue warps
+// and writes the 32 column sums to dst[0..31] (thread 0..31 of warp 0 store).
+WB_DEV void cta_colsum32(float* v, float* red /*smem [4][32]*/, int warp, int lane, float* dst,
+                         int epi_bar_threads) {
+  float s = warp_colsum32(v, lane);
+  red[warp * 32 + lane] = s;
+  asm volatile("bar.sync 1, %0;" ::"r"(epi_bar_threads));
+  if (warp == 0) dst[lane] = red[lane] + red[32 + lane] + red[64 + lane] + red[96 + lane];
+  asm volatile("bar.sync 1, %0;" ::"r"(epi_bar_threads));
+}
+
+// ---------------------------------------------------------------------------------------------
+// tc_conv kernel
+// ---------------------------------------------------------------------------------------------
+template <int KC>
+__global__ void __launch_bounds__(192, 1)
+    tc_conv_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcConvParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ float red[128];
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int phase = blockIdx.z;
+  const int tile = blockIdx.x;
+  const int item = tile / p.tiles_per_item;
+  const int q0 = (tile % p.tiles_per_item) * 128;
+  const int N = p.n_tile;
+  const int n0 = blockIdx.y * N;
+  const int tap0 = p.tap_start[phase];
+  const int ntaps = p.tap_start[phase + 1] - tap0;
+  const int ksteps = ntaps * p.n_chunks;
+  const int S = p.stages;
+  const int nA = p.split ? 2 : 1;
+  constexpr uint32_t a_bytes = 128u * KC * 2u;
+  const uint32_t w_bytes = (uint32_t)N * KC * 2u;
+  const uint32_t stage_bytes = nA * (a_bytes + w_bytes);
+
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * stage_bytes);
+  uint64_t* empty = full + S;
+  uint64_t* accf = empty + S;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accf + 1);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    mbar_init(accf, 1);
+    fence_barrier_init();
+  }
+  if (warp == 5) tmem_alloc(tmem_slot, (uint32_t)p.tmem_cols);
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      for (int ks = 0; ks < ksteps; ++ks) {
+        const int s = ks % S;
+        if (ks >= S && !mbar_wait(&empty[s], ((ks / S) & 1) ^ 1, p.err, ERR_WAIT_EMPTY)) break;
+        const int t = ks / p.n_chunks, c = ks - t * p.n_chunks;
+        const int ti = tap0 + t;
+        const int mi = p.tap_map[ti];
+        const int row = q0 + p.tap_shift[ti];
+        uint8_t* st = smem + (size_t)s * stage_bytes;
+        mbar_arrive_expect_tx(&full[s], stage_bytes);
+        tma_load_3d(st, &maps.a[mi], &full[s], c * KC, row, item);
+        if (p.split) tma_load_3d(st + a_bytes, &maps.a[p.lo_base + mi], &full[s], c * KC, row, item);
+        uint8_t* wd = st + nA * a_bytes;
+        tma_load_3d(wd, &maps.w_hi, &full[s], c * KC, n0, p.tap_w[ti]);
+        if (p.split) tma_load_3d(wd + w_bytes, &maps.w_lo, &full[s], c * KC, n0, p.tap_w[ti]);
+      }
+    }
+  } else if (warp == 5) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc_bf16(128, N, 0, 0);
+      constexpr uint32_t layout = (KC == 64) ? 2u : 4u;        // 128B / 64B swizzle
+      constexpr uint32_t sbo = (KC == 64) ? 1024u : 512u;       // 8 rows x row bytes
+      const uint32_t sbase = smem_u32(smem);
+      bool ok = true;
+      for (int ks = 0; ks < ksteps && ok; ++ks) {
+        const int s = ks % S;
+        if (!mbar_wait(&full[s], (ks / S) & 1, p.err, ERR_WAIT_FULL)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t a_hi = sbase + (uint32_t)s * stage_bytes;
+        const uint32_t a_lo = a_hi + a_bytes;
+        const uint32_t w_hi = a_hi + nA * a_bytes;
+        const uint32_t w_lo = w_hi + w_bytes;
+#pragma unroll
+        for (int k = 0; k < KC / 16; ++k) {
+          const uint32_t koff = (uint32_t)k * 32u;
+          const uint64_t dah = make_sdesc(a_hi + koff, 16, sbo, layout);
+          const uint64_t dwh = make_sdesc(w_hi + koff, 16, sbo, layout);
+          umma_f16(tmem, dah, dwh, idesc, (ks | k) != 0);
+          if (p.split) {
+            const uint64_t dal = make_sdesc(a_lo + koff, 16, sbo, layout);
+            const uint64_t dwl = make_sdesc(w_lo + koff, 16, sbo, layout);
+            umma_f16(tmem, dal, dwh, idesc, 1);
+            umma_f16(tmem, dah, dwl, idesc, 1);
+          }
+        }
+        umma_commit(&empty[s]);
+      }
+      if (ok) umma_commit(accf);
+    }
+  } else {
+    // ---------------- epilogue (warps 0..3 <-> TMEM lanes 0..127) ----------------
+    const bool ok = mbar_wait(accf, 0, p.err, ERR_WAIT_ACC);
+    tc_fence_after();
+    const Epi& e = p.epi;
+    const int q = q0 + warp * 32 + lane;
+    const int orow = q * p.out_stride + p.out_off[phase];
+    const bool valid = ok && q < p.m_rows && orow >= 0 && orow < p.t_out;
+    const size_t row_off = ((size_t)item * p.t_out + (valid ? orow : 0)) * p.n_total + n0;
+    const size_t part_row = (size_t)(blockIdx.z * gridDim.x + blockIdx.x) * p.n_total + n0;
+    for (int c0 = 0; c0 < N; c0 += 32) {
+      float v[32];
+      tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
+      if (!ok) continue;
+      const size_t off = row_off + c0;
+      if (e.mask_src) {
+        float x[32];
+        if (valid) load_bf16x32(e.mask_src + off, x);
+        else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) x[i] = 0.f;
+        }
+        if (e.act_kind == 1) {
+          float ga[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float a = e.mask_alpha[n0 + c0 + i];
+            float sn, cs;
+            sincosf(a * x[i], &sn, &cs);
+            const float s2 = 2.f * sn * cs;                       // sin(2 a x)
+            ga[i] = valid ? v[i] * (x[i] * s2 / a - sn * sn / (a * a)) : 0.f;
+            v[i] *= 1.f + s2;
+          }
+          if (e.alpha_part) {
+            float tmp[32];
+            cta_colsum32(ga, red, warp, lane, tmp, 128);
+            if (warp == 0) e.alpha_part[part_row + c0 + lane] = tmp[lane];
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] *= (x[i] > 0.f) ? 1.f : e.slope;
+        }
+      }
+      if (e.bias) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] += e.bias[n0 + c0 + i];
+      }
+      if (e.rowadd) {
+        const float* ra = e.rowadd + (size_t)item * p.n_total + n0 + c0;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] += ra[i];
+      }
+      if (e.res && valid) {
+        float r[32];
+        load_f32x32(e.res + off, r);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] += r[i];
+      }
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] *= e.scale;
+      if (e.colsum) {
+        float cv[32], tmp[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) cv[i] = valid ? v[i] : 0.f;
+        cta_colsum32(cv, red, warp, lane, tmp, 128);
+        if (warp == 0) e.colsum[part_row + c0 + lane] = tmp[lane];
+      }
+      if (!valid) continue;
+      if (e.accumulate) {
+        float r[32];
+        load_f32x32(e.out_f32 + off, r);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] += r[i];
+      }
+      if (e.out_f32) store_f32x32(e.out_f32 + off, v);
+      if (e.out_bf16) {
+        __align__(16) bf16 b[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) b[i] = __float2bfloat16_rn(v[i]);
+        store_bf16x32(e.out_bf16 + off, b);
+      }
+      if (e.pre_hi) {
+        __align__(16) bf16 b[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) b[i] = __float2bfloat16_rn(v[i]);
+        store_bf16x32(e.pre_hi + off, b);
+      }
+      if (e.act_hi) {
+        __align__(16) bf16 h[32];
+        __align__(16) bf16 l[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float a = (e.act_kind == 1) ? snake(v[i], e.act_alpha[n0 + c0 + i]) : lrelu(v[i], e.slope);
+          split_bf16(a, h[i], l[i]);
+        }
+        store_bf16x32(e.act_hi + off, h);
+        if (e.act_lo) store_bf16x32(e.act_lo + off, l);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, (uint32_t)p.tmem_cols);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// tc_wgrad kernel: partial dW tiles over a K (time) range
+// ---------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(192, 1)
+    tc_wgrad_kernel(const __grid_constant__ TcWgMaps maps, const __grid_constant__ TcWgParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int mt = blockIdx.x;
+  const int split = blockIdx.y;
+  const int nbase = blockIdx.z * p.n_in;
+  const int kb0 = split * p.kb_per_split;
+  const int kb1 = min(p.total_kblocks, kb0 + p.kb_per_split);
+  const int ksteps = max(0, kb1 - kb0);
+  const int S = p.stages;
+  const uint32_t atom_a_bytes = 64u * (uint32_t)p.atom_m * 2u;
+  const uint32_t a_bytes = 128u * 64u * 2u;
+  const int atom_n = p.n_in / p.n_atoms;
+  const uint32_t atom_b_bytes = 64u * (uint32_t)atom_n * 2u;
+  const uint32_t b_bytes = (uint32_t)p.n_in * 64u * 2u;
+  const uint32_t stage_bytes = a_bytes + b_bytes;
+
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * stage_bytes);
+  uint64_t* empty = full + S;
+  uint64_t* accf = empty + S;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accf + 1);
+
+  int n_used = 0;
+  uint32_t load_bytes = b_bytes;
+  for (int j = 0; j < p.m_atoms; ++j)
+    if (p.atom_tap[mt][j] >= 0) { ++n_used; load_bytes += atom_a_bytes; }
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    mbar_init(accf, 1);
+    fence_barrier_init();
+  }
+  if (warp == 5) tmem_alloc(tmem_slot, (uint32_t)p.tmem_cols);
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      for (int ks = 0; ks < ksteps; ++ks) {
+        const int s = ks % S;
+        if (ks >= S && !mbar_wait(&empty[s], ((ks / S) & 1) ^ 1, p.err, ERR_WAIT_EMPTY)) break;
+        const int kb = kb0 + ks;
+        const int item = kb / p.kblocks_per_item;
+        const int t0 = (kb - item * p.kblocks_per_item) * 64;
+        uint8_t* st = smem + (size_t)s * stage_bytes;
+        mbar_arrive_expect_tx(&full[s], load_bytes);
+        for (int j = 0; j < p.m_atoms; ++j) {
+          if (p.atom_tap[mt][j] < 0) continue;
+          tma_load_3d(st + j * atom_a_bytes, &maps.d[p.atom_map[mt][j]], &full[s], p.atom_oc0[mt][j],
+                      t0 + p.atom_shift[mt][j], item);
+        }
+        for (int j = 0; j < p.n_atoms; ++j)
+          tma_load_3d(st + a_bytes + j * atom_b_bytes, &maps.x, &full[s], nbase + j * atom_n, t0, item);
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc_bf16(128, p.n_in, 1, 1);
+      const uint32_t la = (p.atom_m == 64) ? 2u : 4u, sboa = (uint32_t)p.atom_m * 16u;
+      const uint32_t lb = (atom_n == 64) ? 2u : 4u, sbob = (uint32_t)atom_n * 16u;
+      const uint32_t sbase = smem_u32(smem);
+      bool ok = true;
+      for (int ks = 0; ks < ksteps; ++ks) {
+        const int s = ks % S;
+        if (!mbar_wait(&full[s], (ks / S) & 1, p.err, ERR_WAIT_FULL)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t ab = sbase + (uint32_t)s * stage_bytes;
+        const uint32_t bb = ab + a_bytes;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {  // 64 time rows = 4 x K16
+          const uint64_t da = make_sdesc(ab + (uint32_t)k * 2u * sboa, atom_a_bytes, sboa, la);
+          const uint64_t db = make_sdesc(bb + (uint32_t)k * 2u * sbob, atom_b_bytes, sbob, lb);
+          umma_f16(tmem, da, db, idesc, (ks | k) != 0);
+        }
+        umma_commit(&empty[s]);
+      }
+      if (ok) umma_commit(accf);
+    }
+  } else {
+    bool ok = ksteps > 0 ? mbar_wait(accf, 0, p.err, ERR_WAIT_ACC) : true;
+    tc_fence_after();
+    const int m = warp * 32 + lane;
+    float* dst = p.part + ((size_t)split * p.n_mtiles * 128 + (size_t)mt * 128 + m) * p.n_total + nbase;
+    for (int c0 = 0; c0 < p.n_in; c0 += 32) {
+      float v[32];
+      if (ksteps > 0) tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
+      else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = 0.f;
+      }
+      if (!ok) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = 0.f;
+      }
+      store_f32x32(dst + c0, v);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, (uint32_t)p.tmem_cols);
+  }
+}
+
+// explicit instantiations / launch wrappers (host)
+cudaError_t launch_tc_conv(const TcMaps& maps, const TcConvParams& p, int kc, dim3 grid, size_t smem,
+                           cudaStream_t st) {
+  if (kc == 64) {
+    cudaFuncSetAttribute(tc_conv_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    tc_conv_kernel<64><<<grid, 192, smem, st>>>(maps, p);
+  } else {
+    cudaFuncSetAttribute(tc_conv_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    tc_conv_kernel<32><<<grid, 192, smem, st>>>(maps, p);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_tc_wgrad(const TcWgMaps& maps, const TcWgParams& p, dim3 grid, size_t smem, cudaStream_t st) {
+  cudaFuncSetAttribute(tc_wgrad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  tc_wgrad_kernel<<<grid, 192, smem, st>>>(maps, p);
+  return cudaGetLastError();
+}
+
+}  // namespace wb

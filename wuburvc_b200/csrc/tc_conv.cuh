@@ -1,0 +1,106 @@
+// tc_conv.cuh — tcgen05/TMEM implicit-GEMM kernels for the generator's convolutions.
+//
+// Two kernels cover every dense contraction of the training step:
+//
+//  * tc_conv  : out[b, q*stride+off, n] = epilogue( sum_taps sum_c A_tap[b, q+shift, c] * W[tap, n, c] )
+//               A is a channels-last activation tensor [B][T][C] read through TMA with a per-tap row
+//               shift (padding and dilation come from TMA out-of-bounds zero fill).  It serves the
+//               Conv1d forward, the Conv1d input-gradient (flipped taps, transposed weights), the
+//               polyphase ConvTranspose1d forward (one phase per blockIdx.z) and the ConvTranspose1d
+//               input-gradient (one strided A view per tap residue).  In split mode the A and W
+//               operands are bf16 hi/lo pairs and three MMAs (hi*hi + lo*hi + hi*lo) give an
+//               fp32-accurate product.
+//  * tc_wgrad : dW[tap, o, i] = sum_{b,t} dOut[b, t - shift_tap, o] * A[b, t, i], split over time
+//               (K) across CTAs with deterministic fp32 partials.  Both operands are MN-major in
+//               shared memory; several taps are packed into one 128-row M tile when C_out < 128.
+#pragma once
+#include "common.cuh"
+
+namespace wb {
+
+constexpr int kMaxMaps = 14;
+constexpr int kMaxTapList = 48;
+constexpr int kMaxPhases = 12;
+
+// ---------------------------------------------------------------------------------------------
+// forward-type kernel (conv fwd / dgrad / convT polyphase)
+// ---------------------------------------------------------------------------------------------
+struct Epi {
+  const float* bias;        // [n_total]
+  const float* rowadd;      // [B][n_total], broadcast over time (cond(g))
+  const bf16* mask_src;     // [B][T][n_total]: activated value (lrelu) or pre-activation (snake)
+  const float* mask_alpha;  // [n_total] snake alpha for the mask
+  float* alpha_part;        // [tiles][n_total] snake d(alpha) partial sums
+  const float* res;         // [B][T][n_total] fp32 residual added after the mask
+  float* out_f32;           // [B][T][n_total]
+  bf16* out_bf16;           // [B][T][n_total]
+  bf16* act_hi;             // [B][T][n_total] activation of the result, bf16 hi part
+  bf16* act_lo;             //                                       ... lo part
+  const float* act_alpha;   // [n_total] snake alpha of the activation
+  bf16* pre_hi;             // [B][T][n_total] bf16 copy of the result (snake pre-activation)
+  float* colsum;            // [tiles][n_total] column-sum partials (bias gradients)
+  float scale;
+  float slope;              // lrelu slope (activation and mask)
+  int accumulate;           // out_f32 += result
+  int act_kind;             // 0 lrelu, 1 snake
+};
+
+struct TcMaps {
+  CUtensorMap a[kMaxMaps];  // A operand maps; lo maps at a[lo_base + i]
+  CUtensorMap w_hi;
+  CUtensorMap w_lo;
+};
+
+struct TcConvParams {
+  int m_rows;          // q rows per item
+  int tiles_per_item;  // ceil(m_rows / 128)
+  int n_tile;          // GEMM N per CTA (multiple of 16, <= 256)
+  int n_total;         // channel pitch of every [B][T][C] output
+  int n_chunks;        // C_in / KC
+  int split;           // bf16x3 forward
+  int lo_base;
+  int stages;
+  int tmem_cols;
+  int t_out;           // output rows per item
+  int out_stride;      // output row = q * out_stride + out_off[phase]
+  int out_off[kMaxPhases];
+  int tap_start[kMaxPhases + 1];
+  signed char tap_map[kMaxTapList];
+  short tap_shift[kMaxTapList];
+  short tap_w[kMaxTapList];
+  Epi epi;
+  int* err;
+};
+
+// ---------------------------------------------------------------------------------------------
+// weight-gradient kernel
+// ---------------------------------------------------------------------------------------------
+struct TcWgMaps {
+  CUtensorMap d[kMaxMaps];  // dOut views (one per tap residue for ConvTranspose)
+  CUtensorMap x;            // activation operand [B][T][C_in]
+};
+
+struct TcWgParams {
+  int t_rows;          // time rows of the activation operand per item
+  int kblocks_per_item;
+  int total_kblocks;   // items * kblocks_per_item
+  int kb_per_split;
+  int n_in;            // GEMM N per CTA (input channels of one N tile), multiple of 16, <= 256
+  int n_total;         // total input channels (partial row pitch); N tile = blockIdx.z
+  int n_atoms;         // N atoms of the activation tile (n_in / atom_n)
+  int c_out;           // channels of dOut
+  int m_atoms;         // 128 / atom_m
+  int atom_m;          // 32 or 64 (dOut channels per atom)
+  int stages;
+  int tmem_cols;
+  // per M tile: atoms (tap, oc0) packed along M
+  int n_mtiles;
+  signed char atom_map[64][4];   // [mtile][atom] -> dOut map index
+  short atom_shift[64][4];       // row shift of the dOut view
+  short atom_oc0[64][4];         // first output channel of the atom
+  short atom_tap[64][4];         // tap index (for the partial layout); -1 = unused atom
+  float* part;                   // [split][n_mtiles*128][n_total] fp32 partials
+  int* err;
+};
+
+}  // namespace wb
