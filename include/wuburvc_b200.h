@@ -71,6 +71,97 @@ int wubu_b200_convT_dgrad(const void* dy, const void* wd, float* dx, int B, int 
 int wubu_b200_convT_wgrad(const void* x, const void* dy, float* dw, int B, int C_in, int T_in,
                           int C_out, int k, int stride, int pad, void* stream);
 
+/* ---------------------------------------------------------------------------------------
+ * 2. generator training step
+ * ------------------------------------------------------------------------------------- */
+
+/* Generator topology.  Mirrors the reference model config (WuBuRVCModel upsample_rates /
+ * upsample_kernel_sizes / resblock_k / resblock_dil, src/wubu_rvc_parity.h:206-217) and the
+ * upstream GeneratorNSF constructor (knowledge/rvc_original/infer/module/models.py:403-475). */
+typedef struct WubuB200GenConfig {
+  int sample_rate;            /* 40000 / 32000 / 48000 */
+  int n_ups;                  /* must be 4 */
+  int upsample_rates[4];      /* e.g. 10,10,2,2 */
+  int upsample_kernels[4];    /* e.g. 16,16,4,4 */
+  int initial_channel;        /* 512 */
+  int in_channels;            /* 192 (z channels) */
+  int gin_channels;           /* 256 speaker-embedding channels, 0 = no cond(g) */
+  int n_kernels;              /* 3 resblock stacks per stage */
+  int resblock_kernels[3];    /* 3, 7, 11 */
+  int n_dilations;            /* 3 conv pairs per stack */
+  int resblock_dilations[3][3];
+  int harmonic_num;           /* 8 -> 9 source harmonics */
+  float sine_amp;             /* 0.1 */
+  float noise_std;            /* 0.003 */
+  int activation;             /* 0 = LeakyReLU, 1 = Snake(alpha per channel) */
+  float lrelu_slope;          /* 0.1 */
+  float final_slope;          /* slope of the activation before conv_post (0.1 in the reference) */
+  int weight_norm;            /* 1: ups / resblock weights trained as (g, v) */
+  int nsf;                    /* 1: harmonic source + noise convs */
+} WubuB200GenConfig;
+
+typedef struct WubuB200TrainOptions {
+  int batch;                  /* items per step on this GPU */
+  int frames;                 /* frames per item */
+  int device;                 /* CUDA device ordinal */
+  float lr, beta1, beta2, eps, weight_decay;  /* AdamW, src/wubu_train.c:57-73 */
+  unsigned long long seed;    /* source-noise generator seed */
+} WubuB200TrainOptions;
+
+typedef struct WubuB200Gen WubuB200Gen; /* opaque */
+
+/* Parameter table (host only, needs no GPU).  The flat fp32 buffer holds every trainable
+ * tensor at a 64-float aligned offset; names follow the reference registry
+ * (src/wubu_train.c:131-210: dec.conv_pre.weight, dec.ups.L.*, dec.resblocks.R.convsX.P.*,
+ * dec.conv_post.weight) plus the GeneratorNSF extras (dec.cond.*, dec.noise_convs.L.*,
+ * dec.m_source.l_linear.*, weight_g/weight_v pairs, Snake alphas). */
+int wubu_b200_gen_param_count(const WubuB200GenConfig* cfg);
+long long wubu_b200_gen_param_total(const WubuB200GenConfig* cfg);
+int wubu_b200_gen_param_info(const WubuB200GenConfig* cfg, int index, char* name, int name_cap, int* shape3,
+                             long long* offset, long long* numel);
+/* Deterministic init: conv weights / v ~ N(0, 0.01), g = ||v|| per dim-0 row, biases 0,
+ * Snake alpha 1, l_linear weight U(-1/3, 1/3). */
+int wubu_b200_gen_init_params(const WubuB200GenConfig* cfg, unsigned long long seed, float* host_flat);
+
+/* Model lifecycle: allocates every device buffer and builds every launch plan once. */
+WubuB200Gen* wubu_b200_gen_create(const WubuB200GenConfig* cfg, const WubuB200TrainOptions* opt);
+void wubu_b200_gen_destroy(WubuB200Gen* gen);
+int wubu_b200_gen_set_params(WubuB200Gen* gen, const float* host_flat);
+int wubu_b200_gen_get_params(WubuB200Gen* gen, float* host_flat);
+int wubu_b200_gen_get_grads(WubuB200Gen* gen, float* host_flat);
+int wubu_b200_gen_samples(const WubuB200Gen* gen); /* output samples per item */
+
+/* Step inputs, host pointers (copied in), all fp32:
+ *   z    [B][in_channels][F]     latent (reference layout: channels x frames)
+ *   f0   [B][F]                  Hz, 0 = unvoiced (may be NULL when nsf == 0)
+ *   g    [B][gin_channels]       speaker embedding (may be NULL when gin == 0)
+ *   noise[B][T][harmonic_num+1]  standard-normal source noise, or NULL -> device generator
+ *                                (counter-based, keyed by opt.seed and noise_stream)
+ *   dldy [B][T]                  upstream gradient dL/d(audio)                            */
+#define WUBU_B200_INPUTS_RESIDENT 1 /* use the inputs already on the device (last upload) */
+int wubu_b200_gen_upload(WubuB200Gen* gen, const float* z, const float* f0, const float* g, const float* noise,
+                         const float* dldy);
+int wubu_b200_gen_forward(WubuB200Gen* gen, unsigned long long noise_stream, float* audio_out);
+int wubu_b200_gen_backward(WubuB200Gen* gen);
+int wubu_b200_gen_adamw(WubuB200Gen* gen);
+/* One full step (upload unless RESIDENT, forward, backward, gradient all-reduce when a
+ * communicator is attached, AdamW).  audio_out (host, may be NULL) receives the forward output.
+ * The step is captured once into a CUDA graph and replayed. */
+int wubu_b200_gen_train_step(WubuB200Gen* gen, const float* z, const float* f0, const float* g, const float* noise,
+                             const float* dldy, float* audio_out, unsigned long long noise_stream, int flags);
+/* Enqueue one resident-input step without synchronising (for device-side timing). */
+int wubu_b200_gen_train_step_async(WubuB200Gen* gen, unsigned long long noise_stream);
+/* The model's CUDA stream (cudaStream_t) for timing with events. */
+void* wubu_b200_gen_stream(WubuB200Gen* gen);
+/* Host synchronisation + device error word check. */
+int wubu_b200_gen_sync(WubuB200Gen* gen);
+
+/* Data parallelism: one process per GPU.  Rank 0 creates the 128-byte NCCL unique id and the
+ * caller ships it to the other ranks; every rank then attaches it.  Gradients are summed
+ * over ranks in buckets on a communication stream while the backward runs, then scaled 1/world. */
+int wubu_b200_nccl_unique_id(void* out128);
+int wubu_b200_gen_attach_comm(WubuB200Gen* gen, int rank, int world, const void* id128);
+
 #ifdef __cplusplus
 }
 #endif

@@ -85,6 +85,86 @@ def counter_rand_ini(seed: int, stream: int, dim: int) -> np.ndarray:
     return r
 
 
+def _name_stream(name: str) -> int:
+    import zlib
+    return zlib.crc32(name.encode()) + 7
+
+
+def param_names(cfg):
+    """Named parameter shapes of the generator in the reference layout."""
+    out = {}
+    C0 = cfg["upsample_initial_channel"]
+    rates, kers = cfg["upsample_rates"], cfg["upsample_kernels"]
+    snake = cfg["activation"] == "snake"
+    wnorm = cfg["weight_norm"]
+    out["dec.conv_pre.weight"] = (C0, cfg["in_channels"], 7)
+    out["dec.conv_pre.bias"] = (C0,)
+    if cfg["gin_channels"]:
+        out["dec.cond.weight"] = (C0, cfg["gin_channels"], 1)
+        out["dec.cond.bias"] = (C0,)
+    if cfg["nsf"]:
+        out["dec.m_source.l_linear.weight"] = (1, cfg["harmonic_num"] + 1)
+        out["dec.m_source.l_linear.bias"] = (1,)
+    nk = len(cfg["resblock_kernels"])
+    for L in range(len(rates)):
+        cin, c = C0 >> L, C0 >> (L + 1)
+        if wnorm:
+            out[f"dec.ups.{L}.weight_g"] = (cin, 1, 1)
+            out[f"dec.ups.{L}.weight_v"] = (cin, c, kers[L])
+        else:
+            out[f"dec.ups.{L}.weight"] = (cin, c, kers[L])
+        out[f"dec.ups.{L}.bias"] = (c,)
+        if snake:
+            out[f"dec.ups_act.{L}.alpha"] = (cin,)
+        if cfg["nsf"]:
+            k, s, p = noise_conv_geom(cfg, L)
+            out[f"dec.noise_convs.{L}.weight"] = (c, 1, k)
+            out[f"dec.noise_convs.{L}.bias"] = (c,)
+        for j, kk in enumerate(cfg["resblock_kernels"]):
+            R = L * nk + j
+            for ct in (1, 2):
+                for pi in range(len(cfg["resblock_dilations"][j])):
+                    base = f"dec.resblocks.{R}.convs{ct}.{pi}"
+                    if wnorm:
+                        out[base + ".weight_g"] = (c, 1, 1)
+                    out[base + ".weight_v"] = (c, c, kk)
+                    out[base + ".bias"] = (c,)
+                    if snake:
+                        out[f"dec.resblocks.{R}.alpha{ct}.{pi}"] = (c,)
+    if snake:
+        out["dec.post_act.alpha"] = (C0 >> len(rates),)
+    out["dec.conv_post.weight"] = (1, C0 >> len(rates), 7)
+    return out
+
+
+def init_params_ref(cfg, seed: int, w_std: float = 0.01, bias_std: float = 0.0):
+    """Deterministic named parameters (reference layout): conv weights / v ~ N(0, w_std) from
+    the counter generator (stream keyed by the tensor name), g = ||v|| per dim-0 row,
+    biases N(0, bias_std), Snake alpha 1, l_linear weight U(-1/3, 1/3)."""
+    P = {}
+    shapes = param_names(cfg)
+    for name, shp in shapes.items():
+        n = int(np.prod(shp))
+        st = _name_stream(name)
+        if name.endswith(".alpha"):
+            P[name] = np.ones(shp, np.float32)
+        elif name.endswith("l_linear.weight"):
+            u1, _ = counter_uniform_pair(seed, st, np.arange(n, dtype=np.uint64))
+            P[name] = ((2 * u1 - 1) / 3).reshape(shp).astype(np.float32)
+        elif name.endswith(".bias"):
+            P[name] = (bias_std * counter_normal(seed, st, n)).reshape(shp).astype(np.float32)
+        elif name.endswith(".weight_g"):
+            continue
+        else:
+            P[name] = (w_std * counter_normal(seed, st, n)).reshape(shp).astype(np.float32)
+    for name in shapes:
+        if name.endswith(".weight_g"):
+            v = P[name[:-1] + "v"]
+            P[name] = np.linalg.norm(v.reshape(v.shape[0], -1).astype(np.float64), axis=1).reshape(
+                shapes[name]).astype(np.float32)
+    return P
+
+
 # --------------------------------------------------------------------------
 # building blocks
 # --------------------------------------------------------------------------

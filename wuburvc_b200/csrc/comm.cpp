@@ -1,0 +1,183 @@
+// comm.cpp — data-parallel gradient all-reduce over NCCL (loaded at run time).
+//
+// One process per GPU.  The flat gradient buffer is ordered by backward completion, so each
+// stage of the backward finishes a contiguous range; that range is all-reduced on a separate
+// communication stream as soon as the stage's last kernel is done, overlapping the remaining
+// backward.  AdamW waits for the last bucket and applies the 1/world scaling.
+#include <dlfcn.h>
+
+#include <cstdio>
+#include <cstring>
+#include <vector>
+
+#include "gen_model.h"
+
+namespace wb {
+
+namespace {
+
+// Minimal NCCL ABI (stable since NCCL 2.x).
+typedef struct ncclComm* ncclComm_t;
+typedef struct {
+  char internal[128];
+} ncclUniqueId;
+typedef enum { ncclSuccess = 0 } ncclResult_t;
+enum { ncclFloat32 = 7 };
+enum { ncclSum = 0 };
+
+struct NcclApi {
+  void* h = nullptr;
+  int (*GetUniqueId)(ncclUniqueId*) = nullptr;
+  int (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  int (*AllReduce)(const void*, void*, size_t, int, int, ncclComm_t, cudaStream_t) = nullptr;
+  int (*CommDestroy)(ncclComm_t) = nullptr;
+  int (*CommAbort)(ncclComm_t) = nullptr;
+  const char* (*GetErrorString)(int) = nullptr;
+  bool ok = false;
+};
+
+NcclApi& nccl() {
+  static NcclApi api;
+  static bool tried = false;
+  if (tried) return api;
+  tried = true;
+  const char* names[] = {"libnccl.so.2", "libnccl.so"};
+  for (const char* n : names) {
+    api.h = dlopen(n, RTLD_NOW | RTLD_GLOBAL);
+    if (api.h) break;
+  }
+  if (!api.h) {
+    fprintf(stderr, "wuburvc_b200: libnccl.so.2 not found (%s)\n", dlerror());
+    return api;
+  }
+  api.GetUniqueId = (int (*)(ncclUniqueId*))dlsym(api.h, "ncclGetUniqueId");
+  api.CommInitRank = (int (*)(ncclComm_t*, int, ncclUniqueId, int))dlsym(api.h, "ncclCommInitRank");
+  api.AllReduce = (int (*)(const void*, void*, size_t, int, int, ncclComm_t, cudaStream_t))dlsym(api.h, "ncclAllReduce");
+  api.CommDestroy = (int (*)(ncclComm_t))dlsym(api.h, "ncclCommDestroy");
+  api.CommAbort = (int (*)(ncclComm_t))dlsym(api.h, "ncclCommAbort");
+  api.GetErrorString = (const char* (*)(int))dlsym(api.h, "ncclGetErrorString");
+  api.ok = api.GetUniqueId && api.CommInitRank && api.AllReduce && api.CommDestroy;
+  return api;
+}
+
+}  // namespace
+
+struct Comm {
+  ncclComm_t comm = nullptr;
+  int rank = 0, world = 1;
+  cudaStream_t cs = nullptr;
+  cudaEvent_t done = nullptr;
+  std::vector<cudaEvent_t> ready;           // one per bucket, recorded on the main stream
+  std::vector<std::pair<long long, long long>> buckets;  // [off, end) in floats
+};
+
+// Bucket boundaries: end of conv_post + stage 3, stage 2, stage 1, stage 0, and the rest.
+static std::vector<std::pair<long long, long long>> make_buckets(const Gen& m) {
+  std::vector<long long> ends;
+  for (int L = 3; L >= 0; --L) {
+    const std::string key = "dec.ups." + std::to_string(L) + ".bias";
+    long long end = 0;
+    for (const auto& e : m.table.e)
+      if (e.name == key || e.name == "dec.ups_act." + std::to_string(L) + ".alpha") end = std::max(end, e.off + e.n);
+    ends.push_back((end + 63) / 64 * 64);
+  }
+  ends.push_back(m.table.total);
+  std::vector<std::pair<long long, long long>> b;
+  long long prev = 0;
+  for (long long e : ends) {
+    if (e > prev) b.push_back({prev, e});
+    prev = std::max(prev, e);
+  }
+  return b;
+}
+
+int comm_bucket_count(Gen& m) { return m.comm ? (int)m.comm->buckets.size() : 0; }
+
+// Called on the main stream after bucket `b`'s gradients are final: the comm stream waits for
+// them and all-reduces them in place.
+int comm_bucket_ready(Gen& m, int b) {
+  Comm* c = m.comm;
+  if (!c || c->world <= 1) return 0;
+  NcclApi& api = nccl();
+  if (cudaEventRecord(c->ready[b], m.stream) != cudaSuccess) return WUBU_B200_ERR_CUDA;
+  if (cudaStreamWaitEvent(c->cs, c->ready[b], 0) != cudaSuccess) return WUBU_B200_ERR_CUDA;
+  const auto& r = c->buckets[b];
+  const int rc = api.AllReduce(m.grads + r.first, m.grads + r.first, (size_t)(r.second - r.first), ncclFloat32,
+                               ncclSum, c->comm, c->cs);
+  if (rc != ncclSuccess) {
+    fprintf(stderr, "wuburvc_b200: ncclAllReduce failed: %s\n", api.GetErrorString ? api.GetErrorString(rc) : "?");
+    return WUBU_B200_ERR_COMM;
+  }
+  return 0;
+}
+
+// Main stream waits for every bucket (before AdamW).
+int comm_join(Gen& m) {
+  Comm* c = m.comm;
+  if (!c || c->world <= 1) return 0;
+  if (cudaEventRecord(c->done, c->cs) != cudaSuccess) return WUBU_B200_ERR_CUDA;
+  if (cudaStreamWaitEvent(m.stream, c->done, 0) != cudaSuccess) return WUBU_B200_ERR_CUDA;
+  return 0;
+}
+
+int comm_world(Gen& m) { return m.comm ? m.comm->world : 1; }
+
+int comm_allreduce_grads(Gen& m) {
+  for (int b = 0; b < comm_bucket_count(m); ++b) {
+    const int rc = comm_bucket_ready(m, b);
+    if (rc) return rc;
+  }
+  return comm_join(m);
+}
+
+void comm_destroy(Gen& m) {
+  if (!m.comm) return;
+  Comm* c = m.comm;
+  NcclApi& api = nccl();
+  if (c->cs) cudaStreamSynchronize(c->cs);
+  if (c->comm && api.CommDestroy) api.CommDestroy(c->comm);
+  for (auto e : c->ready) cudaEventDestroy(e);
+  if (c->done) cudaEventDestroy(c->done);
+  if (c->cs) cudaStreamDestroy(c->cs);
+  delete m.comm;
+  m.comm = nullptr;
+}
+
+int comm_attach(Gen& m, int rank, int world, const void* id128) {
+  if (world < 1 || rank < 0 || rank >= world || !id128) return WUBU_B200_ERR_ARG;
+  comm_destroy(m);
+  Comm* c = new Comm();
+  c->rank = rank;
+  c->world = world;
+  c->buckets = make_buckets(m);
+  if (world > 1) {
+    NcclApi& api = nccl();
+    if (!api.ok) return WUBU_B200_ERR_COMM;
+    ncclUniqueId id;
+    memcpy(&id, id128, sizeof(id));
+    cudaSetDevice(m.opt.device);
+    const int rc = api.CommInitRank(&c->comm, world, id, rank);
+    if (rc != ncclSuccess) {
+      fprintf(stderr, "wuburvc_b200: ncclCommInitRank failed: %s\n", api.GetErrorString ? api.GetErrorString(rc) : "?");
+      return WUBU_B200_ERR_COMM;
+    }
+  }
+  if (cudaStreamCreateWithFlags(&c->cs, cudaStreamNonBlocking) != cudaSuccess) return WUBU_B200_ERR_CUDA;
+  c->ready.resize(c->buckets.size());
+  for (auto& e : c->ready)
+    if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) return WUBU_B200_ERR_CUDA;
+  if (cudaEventCreateWithFlags(&c->done, cudaEventDisableTiming) != cudaSuccess) return WUBU_B200_ERR_CUDA;
+  m.comm = c;
+  return 0;
+}
+
+int comm_unique_id(void* out128) {
+  NcclApi& api = nccl();
+  if (!api.ok) return WUBU_B200_ERR_COMM;
+  ncclUniqueId id;
+  if (api.GetUniqueId(&id) != ncclSuccess) return WUBU_B200_ERR_COMM;
+  memcpy(out128, &id, sizeof(id));
+  return 0;
+}
+
+}  // namespace wb

@@ -9,6 +9,7 @@
 
 namespace wb {
 
+void tc_kernels_init();  // raises the kernels' shared-memory limit (call before graph capture)
 cudaError_t launch_tc_conv(const TcMaps& maps, const TcConvParams& p, int kc, dim3 grid, size_t smem,
                            cudaStream_t st);
 cudaError_t launch_tc_wgrad(const TcWgMaps& maps, const TcWgParams& p, dim3 grid, size_t smem,

@@ -1,0 +1,259 @@
+// gen_api.cpp — C ABI of the generator training context.
+#include <cstdio>
+#include <cstring>
+#include <vector>
+
+#include "gen_model.h"
+
+namespace wb {
+bool gen_setup(Gen& m);
+bool gen_forward(Gen& m);
+bool gen_backward(Gen& m);
+bool gen_adamw(Gen& m, float grad_scale, int bump_noise);
+void gen_free(Gen& m);
+int comm_attach(Gen& m, int rank, int world, const void* id128);
+int comm_unique_id(void* out128);
+int comm_world(Gen& m);
+}  // namespace wb
+
+using namespace wb;
+
+struct WubuB200Gen {
+  Gen m;
+};
+
+namespace {
+
+int check_err(Gen& m) {
+  cudaError_t e = cudaStreamSynchronize(m.stream);
+  if (e != cudaSuccess) {
+    fprintf(stderr, "wuburvc_b200: CUDA error: %s\n", cudaGetErrorString(e));
+    return WUBU_B200_ERR_CUDA;
+  }
+  int h = 0;
+  if (cudaMemcpy(&h, m.err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return WUBU_B200_ERR_CUDA;
+  if (h) {
+    fprintf(stderr, "wuburvc_b200: a kernel's bounded wait expired (code %d)\n", h);
+    cudaMemset(m.err, 0, sizeof(int));
+    return WUBU_B200_ERR_TIMEOUT;
+  }
+  return WUBU_B200_OK;
+}
+
+int set_noise_stream(Gen& m, unsigned long long s) {
+  // pageable source: staged before return, ordered on the model stream
+  return cudaMemcpyAsync(&m.state->noise_stream, &s, sizeof(s), cudaMemcpyHostToDevice, m.stream) == cudaSuccess
+             ? 0
+             : WUBU_B200_ERR_CUDA;
+}
+
+// forward + backward (+ bucketed all-reduce) + AdamW, enqueued on the model stream
+bool enqueue_step(Gen& m) {
+  if (!gen_forward(m) || !gen_backward(m)) return false;
+  return gen_adamw(m, 1.f / (float)comm_world(m), 1);
+}
+
+int run_step_graph(Gen& m) {
+  if (!m.graph) {
+    cudaGraph_t g = nullptr;
+    if (cudaStreamBeginCapture(m.stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) return WUBU_B200_ERR_CUDA;
+    const bool ok = enqueue_step(m);
+    const cudaError_t e = cudaStreamEndCapture(m.stream, &g);
+    if (!ok || e != cudaSuccess) {
+      if (g) cudaGraphDestroy(g);
+      fprintf(stderr, "wuburvc_b200: step capture failed (%s)\n", cudaGetErrorString(e));
+      return WUBU_B200_ERR_CUDA;
+    }
+    const cudaError_t ie = cudaGraphInstantiate(&m.graph, g, 0);
+    cudaGraphDestroy(g);
+    if (ie != cudaSuccess) {
+      m.graph = nullptr;
+      fprintf(stderr, "wuburvc_b200: graph instantiate failed (%s)\n", cudaGetErrorString(ie));
+      return WUBU_B200_ERR_CUDA;
+    }
+  }
+  return cudaGraphLaunch(m.graph, m.stream) == cudaSuccess ? 0 : WUBU_B200_ERR_CUDA;
+}
+
+int upload(Gen& m, const float* z, const float* f0, const float* g, const float* noise, const float* dldy) {
+  const WubuB200GenConfig& c = m.cfg;
+  cudaStream_t st = m.stream;
+  auto cp = [&](void* d, const void* h, size_t bytes) {
+    return cudaMemcpyAsync(d, h, bytes, cudaMemcpyHostToDevice, st) == cudaSuccess;
+  };
+  if (!z || !dldy) return WUBU_B200_ERR_ARG;
+  if (!cp(m.z, z, sizeof(float) * m.B * c.in_channels * m.F)) return WUBU_B200_ERR_CUDA;
+  if (!cp(m.dldy, dldy, sizeof(float) * m.B * m.T)) return WUBU_B200_ERR_CUDA;
+  if (c.gin_channels) {
+    if (!g) return WUBU_B200_ERR_ARG;
+    if (!cp(m.g, g, sizeof(float) * m.B * c.gin_channels)) return WUBU_B200_ERR_CUDA;
+  }
+  if (c.nsf) {
+    if (!f0) return WUBU_B200_ERR_ARG;
+    if (!cp(m.f0, f0, sizeof(float) * m.B * m.F)) return WUBU_B200_ERR_CUDA;
+    const bool had = m.has_noise_input;
+    m.has_noise_input = noise != nullptr;
+    if (noise && !cp(m.noise, noise, sizeof(float) * m.B * m.T * m.dim)) return WUBU_B200_ERR_CUDA;
+    if (had != m.has_noise_input && m.graph) {  // the captured step baked the other noise source
+      cudaGraphExecDestroy(m.graph);
+      m.graph = nullptr;
+    }
+  }
+  return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+WubuB200Gen* wubu_b200_gen_create(const WubuB200GenConfig* cfg, const WubuB200TrainOptions* opt) {
+  if (!cfg || !opt || !config_valid(*cfg) || opt->batch < 1 || opt->frames < 1) return nullptr;
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || opt->device < 0 || opt->device >= ndev) {
+    fprintf(stderr, "wuburvc_b200: no CUDA device %d\n", opt ? opt->device : -1);
+    return nullptr;
+  }
+  auto* h = new WubuB200Gen();
+  h->m.cfg = *cfg;
+  h->m.opt = *opt;
+  tc_kernels_init();
+  if (!gen_setup(h->m)) {
+    gen_free(h->m);
+    delete h;
+    return nullptr;
+  }
+  std::vector<float> p((size_t)h->m.table.total);
+  init_params(h->m.cfg, h->m.table, 0, p.data());
+  cudaMemcpy(h->m.params, p.data(), p.size() * sizeof(float), cudaMemcpyHostToDevice);
+  return h;
+}
+
+void wubu_b200_gen_destroy(WubuB200Gen* gen) {
+  if (!gen) return;
+  cudaSetDevice(gen->m.opt.device);
+  gen_free(gen->m);
+  delete gen;
+}
+
+int wubu_b200_gen_samples(const WubuB200Gen* gen) { return gen ? gen->m.T : WUBU_B200_ERR_ARG; }
+
+void* wubu_b200_gen_stream(WubuB200Gen* gen) { return gen ? (void*)gen->m.stream : nullptr; }
+
+int wubu_b200_gen_set_params(WubuB200Gen* gen, const float* host_flat) {
+  if (!gen || !host_flat) return WUBU_B200_ERR_ARG;
+  Gen& m = gen->m;
+  cudaSetDevice(m.opt.device);
+  const size_t bytes = sizeof(float) * (size_t)m.table.total;
+  if (cudaMemcpyAsync(m.params, host_flat, bytes, cudaMemcpyHostToDevice, m.stream) != cudaSuccess)
+    return WUBU_B200_ERR_CUDA;
+  // a new parameter set restarts the optimiser
+  cudaMemsetAsync(m.adam_m, 0, bytes, m.stream);
+  cudaMemsetAsync(m.adam_v, 0, bytes, m.stream);
+  cudaMemsetAsync(m.state, 0, sizeof(StepState), m.stream);
+  return check_err(m);
+}
+
+int wubu_b200_gen_get_params(WubuB200Gen* gen, float* host_flat) {
+  if (!gen || !host_flat) return WUBU_B200_ERR_ARG;
+  Gen& m = gen->m;
+  cudaSetDevice(m.opt.device);
+  if (cudaMemcpyAsync(host_flat, m.params, sizeof(float) * (size_t)m.table.total, cudaMemcpyDeviceToHost, m.stream) !=
+      cudaSuccess)
+    return WUBU_B200_ERR_CUDA;
+  return check_err(m);
+}
+
+int wubu_b200_gen_get_grads(WubuB200Gen* gen, float* host_flat) {
+  if (!gen || !host_flat) return WUBU_B200_ERR_ARG;
+  Gen& m = gen->m;
+  cudaSetDevice(m.opt.device);
+  if (cudaMemcpyAsync(host_flat, m.grads, sizeof(float) * (size_t)m.table.total, cudaMemcpyDeviceToHost, m.stream) !=
+      cudaSuccess)
+    return WUBU_B200_ERR_CUDA;
+  return check_err(m);
+}
+
+int wubu_b200_gen_upload(WubuB200Gen* gen, const float* z, const float* f0, const float* g, const float* noise,
+                         const float* dldy) {
+  if (!gen) return WUBU_B200_ERR_ARG;
+  cudaSetDevice(gen->m.opt.device);
+  const int rc = upload(gen->m, z, f0, g, noise, dldy);
+  return rc ? rc : check_err(gen->m);
+}
+
+int wubu_b200_gen_forward(WubuB200Gen* gen, unsigned long long noise_stream, float* audio_out) {
+  if (!gen) return WUBU_B200_ERR_ARG;
+  Gen& m = gen->m;
+  cudaSetDevice(m.opt.device);
+  if (set_noise_stream(m, noise_stream)) return WUBU_B200_ERR_CUDA;
+  if (!gen_forward(m)) return WUBU_B200_ERR_CUDA;
+  if (audio_out && cudaMemcpyAsync(audio_out, m.audio, sizeof(float) * m.B * m.T, cudaMemcpyDeviceToHost, m.stream) !=
+                       cudaSuccess)
+    return WUBU_B200_ERR_CUDA;
+  return check_err(m);
+}
+
+int wubu_b200_gen_backward(WubuB200Gen* gen) {
+  if (!gen) return WUBU_B200_ERR_ARG;
+  cudaSetDevice(gen->m.opt.device);
+  if (!gen_backward(gen->m)) return WUBU_B200_ERR_CUDA;
+  return check_err(gen->m);
+}
+
+int wubu_b200_gen_adamw(WubuB200Gen* gen) {
+  if (!gen) return WUBU_B200_ERR_ARG;
+  cudaSetDevice(gen->m.opt.device);
+  if (!gen_adamw(gen->m, 1.f / (float)comm_world(gen->m), 0)) return WUBU_B200_ERR_CUDA;
+  return check_err(gen->m);
+}
+
+int wubu_b200_gen_train_step(WubuB200Gen* gen, const float* z, const float* f0, const float* g, const float* noise,
+                             const float* dldy, float* audio_out, unsigned long long noise_stream, int flags) {
+  if (!gen) return WUBU_B200_ERR_ARG;
+  Gen& m = gen->m;
+  cudaSetDevice(m.opt.device);
+  if (!(flags & WUBU_B200_INPUTS_RESIDENT)) {
+    const int rc = upload(m, z, f0, g, noise, dldy);
+    if (rc) return rc;
+  }
+  if (set_noise_stream(m, noise_stream)) return WUBU_B200_ERR_CUDA;
+  const int rc = run_step_graph(m);
+  if (rc) return rc;
+  if (audio_out && cudaMemcpyAsync(audio_out, m.audio, sizeof(float) * m.B * m.T, cudaMemcpyDeviceToHost, m.stream) !=
+                       cudaSuccess)
+    return WUBU_B200_ERR_CUDA;
+  return check_err(m);
+}
+
+int wubu_b200_gen_train_step_async(WubuB200Gen* gen, unsigned long long noise_stream) {
+  if (!gen) return WUBU_B200_ERR_ARG;
+  Gen& m = gen->m;
+  cudaSetDevice(m.opt.device);
+  if (set_noise_stream(m, noise_stream)) return WUBU_B200_ERR_CUDA;
+  return run_step_graph(m);
+}
+
+int wubu_b200_gen_sync(WubuB200Gen* gen) {
+  if (!gen) return WUBU_B200_ERR_ARG;
+  cudaSetDevice(gen->m.opt.device);
+  return check_err(gen->m);
+}
+
+int wubu_b200_nccl_unique_id(void* out128) {
+  if (!out128) return WUBU_B200_ERR_ARG;
+  return comm_unique_id(out128);
+}
+
+int wubu_b200_gen_attach_comm(WubuB200Gen* gen, int rank, int world, const void* id128) {
+  if (!gen) return WUBU_B200_ERR_ARG;
+  Gen& m = gen->m;
+  cudaSetDevice(m.opt.device);
+  cudaStreamSynchronize(m.stream);
+  if (m.graph) {  // the captured step did not contain the all-reduce
+    cudaGraphExecDestroy(m.graph);
+    m.graph = nullptr;
+  }
+  return comm_attach(m, rank, world, id128);
+}
+
+}  // extern "C"

@@ -1,0 +1,518 @@
+// gen_kernels.cu — bandwidth-bound kernels of the generator training step.
+#include "gen_kernels.cuh"
+
+namespace wb {
+
+namespace {
+
+__device__ __forceinline__ float block_sum(float v, float* sh) {
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) sh[w] = v;
+  __syncthreads();
+  float t = 0.f;
+  if (threadIdx.x < 32) {
+    t = (l < (int)(blockDim.x >> 5)) ? sh[l] : 0.f;
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (l == 0) sh[0] = t;
+  }
+  __syncthreads();
+  return sh[0];
+}
+
+// ---- counter-based normal generator (splitmix64 finaliser) ----
+__device__ __forceinline__ unsigned long long mix64(unsigned long long x) {
+  x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+  x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+  return x ^ (x >> 31);
+}
+__device__ __forceinline__ void counter_u2(unsigned long long seed, unsigned long long stream, unsigned long long idx,
+                                           float& u1, float& u2) {
+  const unsigned long long key = mix64(seed * 0x9E3779B97F4A7C15ull + stream * 0xD1B54A32D192ED03ull);
+  const unsigned long long h = mix64(key ^ (idx * 0x9E3779B97F4A7C15ull));
+  u1 = (float)((h >> 40) + 1ull) * (1.0f / 16777216.0f);
+  u2 = (float)(((h >> 8) & 0xFFFFFFull) + 1ull) * (1.0f / 16777216.0f);
+}
+__device__ __forceinline__ float counter_normal(unsigned long long seed, unsigned long long stream,
+                                                unsigned long long idx) {
+  float u1, u2;
+  counter_u2(seed, stream, idx, u1, u2);
+  return sqrtf(-2.f * logf(u1)) * cospif(2.f * u2);
+}
+
+__device__ __forceinline__ float act_fwd(float x, int kind, float slope, float alpha) {
+  return kind == 1 ? snake(x, alpha) : lrelu(x, slope);
+}
+
+}  // namespace
+
+// =============================================================================================
+// weights
+// =============================================================================================
+__global__ void prep_weight_kernel(const float* __restrict__ v, const float* __restrict__ g, int rows, int cols, int k,
+                                   int is_convT, int stride, bf16* __restrict__ fwd_hi, bf16* __restrict__ fwd_lo,
+                                   bf16* __restrict__ dg, float* __restrict__ norm) {
+  __shared__ float sh[32];
+  const int r = blockIdx.x;
+  const int per = cols * k;
+  const float* vr = v + (size_t)r * per;
+  float scale = 1.f;
+  if (g) {
+    float s = 0.f;
+    for (int i = threadIdx.x; i < per; i += blockDim.x) s += vr[i] * vr[i];
+    s = block_sum(s, sh);
+    const float n = sqrtf(s);
+    scale = g[r] / n;
+    if (threadIdx.x == 0 && norm) norm[r] = n;
+  }
+  // phase-order position of each tap (ConvTranspose)
+  for (int i = threadIdx.x; i < per; i += blockDim.x) {
+    const int c = i / k, t = i - c * k;
+    const float w = vr[i] * scale;
+    bf16 hi, lo;
+    split_bf16(w, hi, lo);
+    if (!is_convT) {
+      // r = out channel, c = in channel
+      const size_t f = ((size_t)t * rows + r) * cols + c;
+      fwd_hi[f] = hi;
+      fwd_lo[f] = lo;
+      dg[((size_t)(k - 1 - t) * cols + c) * rows + r] = hi;
+    } else {
+      // r = in channel, c = out channel
+      const int ph = t % stride, m = t / stride;
+      int n = 0;
+      for (int q = 0; q < ph; ++q) n += (k - q + stride - 1) / stride;
+      n += m;
+      const size_t f = ((size_t)n * cols + c) * rows + r;
+      fwd_hi[f] = hi;
+      fwd_lo[f] = lo;
+      dg[((size_t)t * rows + r) * cols + c] = hi;
+    }
+  }
+}
+
+void prep_weight(const float* v, const float* g, int rows, int cols, int k, int is_convT, int stride, bf16* fwd_hi,
+                 bf16* fwd_lo, bf16* dg, float* norm, cudaStream_t st) {
+  prep_weight_kernel<<<rows, 256, 0, st>>>(v, g, rows, cols, k, is_convT, stride, fwd_hi, fwd_lo, dg, norm);
+}
+
+__global__ void wn_backward_kernel(const float* __restrict__ dW, const float* __restrict__ v,
+                                   const float* __restrict__ g, const float* __restrict__ norm, int per,
+                                   float* __restrict__ dv, float* __restrict__ dgo) {
+  __shared__ float sh[32];
+  const int r = blockIdx.x;
+  const float* d = dW + (size_t)r * per;
+  const float* vr = v + (size_t)r * per;
+  float s = 0.f;
+  for (int i = threadIdx.x; i < per; i += blockDim.x) s += d[i] * vr[i];
+  s = block_sum(s, sh);
+  const float n = norm[r];
+  const float dgr = s / n;
+  if (threadIdx.x == 0) dgo[r] = dgr;
+  const float a = g[r] / n, b = dgr / n;
+  for (int i = threadIdx.x; i < per; i += blockDim.x) dv[(size_t)r * per + i] = a * (d[i] - b * vr[i]);
+}
+
+void wn_backward(const float* dW, const float* v, const float* g, const float* norm, int rows, int per_row, float* dv,
+                 float* dg, cudaStream_t st) {
+  wn_backward_kernel<<<rows, 256, 0, st>>>(dW, v, g, norm, per_row, dv, dg);
+}
+
+// Step state lives on the device so a captured step graph advances it by itself.
+__global__ void step_bump_kernel(StepState* s, int bump_noise) {
+  s->adam_t += 1;
+  if (bump_noise) s->noise_stream += 1;
+}
+
+void step_bump(StepState* s, int bump_noise, cudaStream_t st) { step_bump_kernel<<<1, 1, 0, st>>>(s, bump_noise); }
+
+__global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
+                             float* __restrict__ v, long long n, float lr, float b1, float b2, float eps, float wd,
+                             const StepState* __restrict__ state, float grad_scale) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long n4 = n >> 2;
+  // bias corrections of src/wubu_train.c:97-103 (clamped, and applied twice like the reference)
+  const float t = (float)state->adam_t;
+  float bias1 = 1.0f - powf(b1, t);
+  float bias2 = 1.0f - powf(b2, t);
+  bias1 = fmaxf(bias1, 1e-12f);
+  bias2 = fmaxf(bias2, 1e-12f);
+  const float lr_eff = lr * sqrtf(bias2) / bias1;
+  if (i < n4) {
+    float4 pp = reinterpret_cast<float4*>(p)[i];
+    const float4 gg = reinterpret_cast<const float4*>(g)[i];
+    float4 mm = reinterpret_cast<float4*>(m)[i];
+    float4 vv = reinterpret_cast<float4*>(v)[i];
+    float* P4 = &pp.x; const float* G4 = &gg.x; float* M4 = &mm.x; float* V4 = &vv.x;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float gr = G4[j] * grad_scale;
+      const float mn = b1 * M4[j] + (1.f - b1) * gr;
+      const float vn = b2 * V4[j] + (1.f - b2) * gr * gr;
+      M4[j] = mn;
+      V4[j] = vn;
+      const float den = sqrtf(vn / bias2) + eps;
+      P4[j] -= lr_eff * (mn / bias1) / den + lr * wd * P4[j];
+    }
+    reinterpret_cast<float4*>(p)[i] = pp;
+    reinterpret_cast<float4*>(m)[i] = mm;
+    reinterpret_cast<float4*>(v)[i] = vv;
+  }
+}
+
+void adamw(float* p, const float* g, float* m, float* v, long long n, float lr, float b1, float b2, float eps, float wd,
+           const StepState* state, float grad_scale, cudaStream_t st) {
+  // n is a multiple of 4 (flat buffer segments are 64-float aligned)
+  const long long n4 = n >> 2;
+  adamw_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(p, g, m, v, n, lr, b1, b2, eps, wd, state, grad_scale);
+}
+
+// =============================================================================================
+// inputs / cond
+// =============================================================================================
+__global__ void pack_z_kernel(const float* __restrict__ z, int B, int C, int F, bf16* __restrict__ hi,
+                              bf16* __restrict__ lo) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)B * C * F) return;
+  const int c = (int)(i % C);
+  const long long bf = i / C;
+  const int f = (int)(bf % F), b = (int)(bf / F);
+  const float x = z[((size_t)b * C + c) * F + f];
+  split_bf16(x, hi[i], lo[i]);
+}
+
+void pack_z(const float* z, int B, int C, int F, bf16* hi, bf16* lo, cudaStream_t st) {
+  const long long n = (long long)B * C * F;
+  pack_z_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(z, B, C, F, hi, lo);
+}
+
+__global__ void cond_forward_kernel(const float* __restrict__ W, const float* __restrict__ bias,
+                                    const float* __restrict__ g, int B, int C, int gin, float* __restrict__ rowadd) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= B * C) return;
+  const int b = i / C, c = i % C;
+  float s = bias ? bias[c] : 0.f;
+  for (int j = 0; j < gin; ++j) s += W[(size_t)c * gin + j] * g[(size_t)b * gin + j];
+  rowadd[i] = s;
+}
+
+void cond_forward(const float* W, const float* bias, const float* g, int B, int C, int gin, float* rowadd,
+                  cudaStream_t st) {
+  cond_forward_kernel<<<(B * C + 255) / 256, 256, 0, st>>>(W, bias, g, B, C, gin, rowadd);
+}
+
+__global__ void cond_backward_kernel(const float* __restrict__ part, int tpi, int B, int C, const float* __restrict__ g,
+                                     int gin, float* __restrict__ dW, float* __restrict__ db) {
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= C * (gin + 1)) return;
+  const int c = idx / (gin + 1), j = idx % (gin + 1);
+  float acc = 0.f;
+  for (int b = 0; b < B; ++b) {
+    float s = 0.f;
+    for (int t = 0; t < tpi; ++t) s += part[((size_t)b * tpi + t) * C + c];
+    acc += (j < gin) ? s * g[(size_t)b * gin + j] : s;
+  }
+  if (j < gin) dW[(size_t)c * gin + j] = acc;
+  else db[c] = acc;
+}
+
+void cond_backward(const float* tile_part, int tiles_per_item, int B, int C, const float* g, int gin, float* dW,
+                   float* db, cudaStream_t st) {
+  const int n = C * (gin + 1);
+  cond_backward_kernel<<<(n + 255) / 256, 256, 0, st>>>(tile_part, tiles_per_item, B, C, g, gin, dW, db);
+}
+
+// =============================================================================================
+// harmonic source (SineGen + l_linear + tanh)
+// =============================================================================================
+__global__ void nsf_phase_kernel(const float* __restrict__ f0, int B, int F, int upp, float sr, double* acc) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  double a = 0.0;
+  for (int f = 0; f < F; ++f) {
+    acc[(size_t)b * F + f] = a;  // carry into frame f = fmod(sum of rad2 over frames < f, 1)
+    const double rad = (double)f0[(size_t)b * F + f] / (double)sr * (double)upp;
+    const double r2 = fmod(rad + 0.5, 1.0) - 0.5;
+    a = fmod(a + r2, 1.0);
+  }
+}
+
+__global__ void nsf_sample_kernel(NsfArgs a) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long T = (long long)a.F * a.upp;
+  if (i >= (long long)a.B * T) return;
+  const int b = (int)(i / T);
+  const int t = (int)(i - (long long)b * T);
+  const int f = t / a.upp, u = t - f * a.upp;
+  const float f0 = a.f0[(size_t)b * a.F + f];
+  const double ph0 = (double)f0 / (double)a.sr * (double)(u + 1) + a.acc[(size_t)b * a.F + f];
+  const float uv = f0 > 0.f ? 1.f : 0.f;
+  const float namp = uv * a.noise_std + (1.f - uv) * a.sine_amp / 3.f;
+  const unsigned long long nstream = *a.stream;
+  float lin = a.lin_b[0];
+  for (int h = 0; h < a.dim; ++h) {
+    float ri = 0.f;
+    if (h > 0) {
+      float u1, u2;
+      counter_u2(a.seed, nstream ^ 0x5A5Aull, (unsigned long long)h, u1, u2);
+      ri = u1 - 1.0f / 16777216.0f;
+    }
+    double x = ph0 * (double)(h + 1) + (double)ri;
+    x -= floor(x);
+    const float s = sinpif(2.f * (float)x) * a.sine_amp;
+    const unsigned long long idx = (unsigned long long)i * a.dim + h;
+    const float n = a.noise ? a.noise[idx] : counter_normal(a.seed, nstream, idx);
+    const float sw = s * uv + namp * n;
+    a.sw[idx] = sw;
+    lin += a.lin_w[h] * sw;
+  }
+  a.har[i] = tanhf(lin);
+}
+
+void nsf_forward(const NsfArgs& a, cudaStream_t st) {
+  nsf_phase_kernel<<<(a.B + 63) / 64, 64, 0, st>>>(a.f0, a.B, a.F, a.upp, a.sr, a.acc);
+  const long long n = (long long)a.B * a.F * a.upp;
+  nsf_sample_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(a);
+}
+
+__global__ void nsf_backward_kernel(const float* __restrict__ d_har, const float* __restrict__ har,
+                                    const float* __restrict__ sw, long long n, int dim, int nparts,
+                                    float* __restrict__ part) {
+  __shared__ float sh[32];
+  const long long per = (n + nparts - 1) / nparts;
+  const long long i0 = (long long)blockIdx.x * per, i1 = min(n, i0 + per);
+  float acc[10];
+  for (int h = 0; h <= dim && h < 10; ++h) acc[h] = 0.f;
+  for (long long i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+    const float y = har[i];
+    const float d = d_har[i] * (1.f - y * y);
+    for (int h = 0; h < dim && h < 9; ++h) acc[h] += d * sw[i * dim + h];
+    acc[9] += d;
+  }
+  for (int h = 0; h < dim && h < 9; ++h) {
+    const float s = block_sum(acc[h], sh);
+    if (threadIdx.x == 0) part[(size_t)blockIdx.x * (dim + 1) + h] = s;
+  }
+  const float s = block_sum(acc[9], sh);
+  if (threadIdx.x == 0) part[(size_t)blockIdx.x * (dim + 1) + dim] = s;
+}
+
+__global__ void rows_reduce_kernel(const float* __restrict__ part, int nparts, int n, float* __restrict__ out,
+                                   int accumulate) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float s = 0.f;
+  for (int p = 0; p < nparts; ++p) s += part[(size_t)p * n + i];
+  out[i] = accumulate ? out[i] + s : s;
+}
+
+void rows_reduce(const float* part, int nparts, int n, float* out, int accumulate, cudaStream_t st) {
+  rows_reduce_kernel<<<(n + 127) / 128, 128, 0, st>>>(part, nparts, n, out, accumulate);
+}
+
+__global__ void split_lin_kernel(const float* __restrict__ red, int dim, float* __restrict__ dw, float* __restrict__ db) {
+  const int h = threadIdx.x;
+  if (h < dim) dw[h] = red[h];
+  if (h == 0) db[0] = red[dim];
+}
+
+void nsf_backward(const float* d_har, const float* har, const float* sw, int n, int dim, float* part, int nparts,
+                  float* dlin_w, float* dlin_b, cudaStream_t st) {
+  nsf_backward_kernel<<<nparts, 256, 0, st>>>(d_har, har, sw, n, dim, nparts, part);
+  // reduce in place into the tail of `part`
+  float* red = part + (size_t)nparts * (dim + 1);
+  rows_reduce(part, nparts, dim + 1, red, 0, st);
+  split_lin_kernel<<<1, 32, 0, st>>>(red, dim, dlin_w, dlin_b);
+}
+
+// =============================================================================================
+// noise conv (+ activation of the stage input)
+// =============================================================================================
+__global__ void noise_add_act_kernel(NoiseActArgs a) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long n = (long long)a.B * a.T * a.C;
+  if (i >= n) return;
+  const int c = (int)(i % a.C);
+  const long long row = i / a.C;
+  const int b = (int)(row / a.T), j = (int)(row % a.T);
+  float x = a.x[i];
+  if (a.har) {
+    float s = a.bias[c];
+    const float* h = a.har + (size_t)b * a.T_full;
+    const float* w = a.w + (size_t)c * a.k;
+    const int t0 = j * a.stride - a.pad;
+    for (int tap = 0; tap < a.k; ++tap) {
+      const int t = t0 + tap;
+      if (t >= 0 && t < a.T_full) s += w[tap] * h[t];
+    }
+    x += s;
+    a.x[i] = x;
+  }
+  if (a.pre) a.pre[i] = __float2bfloat16_rn(x);
+  for (int q = 0; q < a.n_act; ++q) {
+    const float al = a.alpha[q] ? a.alpha[q][c] : 1.f;
+    const float y = act_fwd(x, a.act_kind, a.slope, al);
+    bf16 hi, lo;
+    split_bf16(y, hi, lo);
+    a.act_hi[q][i] = hi;
+    a.act_lo[q][i] = lo;
+  }
+}
+
+void noise_add_act(const NoiseActArgs& a, cudaStream_t st) {
+  const long long n = (long long)a.B * a.T * a.C;
+  noise_add_act_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(a);
+}
+
+__global__ void noise_dhar_kernel(const float* __restrict__ dx, const float* __restrict__ w, int B, int T, int C, int k,
+                                  int stride, int pad, int T_full, float* __restrict__ d_har, int accumulate) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)B * T_full) return;
+  const int b = (int)(i / T_full), t = (int)(i % T_full);
+  // rows j with 0 <= t + pad - j*stride < k
+  int jhi = (t + pad) / stride;
+  int jlo = t + pad - k + 1;
+  jlo = jlo <= 0 ? 0 : (jlo + stride - 1) / stride;
+  if (jhi > T - 1) jhi = T - 1;
+  float s = 0.f;
+  for (int j = jlo; j <= jhi; ++j) {
+    const int tap = t + pad - j * stride;
+    const float* r = dx + ((size_t)b * T + j) * C;
+    for (int c = 0; c < C; ++c) s += r[c] * w[(size_t)c * k + tap];
+  }
+  d_har[i] = accumulate ? d_har[i] + s : s;
+}
+
+__global__ void noise_wgrad_kernel(const float* __restrict__ dx, const float* __restrict__ har, int B, int T, int C,
+                                   int k, int stride, int pad, int T_full, int rows_per_part, float* __restrict__ part) {
+  const long long r0 = (long long)blockIdx.x * rows_per_part;
+  const long long nrows = (long long)B * T;
+  const int nout = C * k;
+  for (int o = threadIdx.x; o < nout; o += blockDim.x) {
+    const int c = o / k, tap = o % k;
+    float s = 0.f;
+    for (long long r = r0; r < r0 + rows_per_part && r < nrows; ++r) {
+      const int b = (int)(r / T), j = (int)(r % T);
+      const int t = j * stride - pad + tap;
+      if (t >= 0 && t < T_full) s += dx[r * C + c] * har[(size_t)b * T_full + t];
+    }
+    part[(size_t)blockIdx.x * nout + o] = s;
+  }
+}
+
+int noise_backward_parts(int B, int T, int rows_per_part) {
+  return (int)(((long long)B * T + rows_per_part - 1) / rows_per_part);
+}
+
+void noise_backward(const float* dx, const float* har, const float* w, int B, int T, int C, int k, int stride, int pad,
+                    int T_full, float* d_har, int accumulate_dhar, float* wpart, int rows_per_part, cudaStream_t st) {
+  const long long n = (long long)B * T_full;
+  noise_dhar_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(dx, w, B, T, C, k, stride, pad, T_full, d_har,
+                                                                  accumulate_dhar);
+  const int parts = noise_backward_parts(B, T, rows_per_part);
+  noise_wgrad_kernel<<<parts, 256, 0, st>>>(dx, har, B, T, C, k, stride, pad, T_full, rows_per_part, wpart);
+}
+
+void noise_wgrad_reduce(const float* wpart, int nparts, int C, int k, float* dW, cudaStream_t st) {
+  rows_reduce(wpart, nparts, C * k, dW, 0, st);
+}
+
+// =============================================================================================
+// conv_post (C -> 1, k taps, pad k/2) + tanh
+// =============================================================================================
+__global__ void post_forward_kernel(const bf16* __restrict__ hi, const bf16* __restrict__ lo,
+                                    const float* __restrict__ W, int B, int T, int C, int k, float* __restrict__ audio) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)B * T) return;
+  const int b = (int)(i / T), t = (int)(i % T);
+  const int pad = k / 2;
+  float s = 0.f;
+  for (int tap = 0; tap < k; ++tap) {
+    const int r = t - pad + tap;
+    if (r < 0 || r >= T) continue;
+    const size_t base = ((size_t)b * T + r) * C;
+    for (int c = 0; c < C; ++c)
+      s += (__bfloat162float(hi[base + c]) + __bfloat162float(lo[base + c])) * W[(size_t)c * k + tap];
+  }
+  audio[i] = tanhf(s);
+}
+
+void post_forward(const bf16* a_hi, const bf16* a_lo, const float* W, int B, int T, int C, int k, float* audio,
+                  cudaStream_t st) {
+  const long long n = (long long)B * T;
+  post_forward_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(a_hi, a_lo, W, B, T, C, k, audio);
+}
+
+constexpr int kPostRows = 64;
+
+int post_backward_blocks(int B, int T) { return (int)(((long long)B * T + kPostRows - 1) / kPostRows); }
+
+__global__ void __launch_bounds__(256) post_backward_kernel(PostBwdArgs a) {
+  // lane = channel (C == 32), 8 warps x 8 rows each
+  __shared__ float red[8][32 * 9];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int c = lane;
+  const int k = a.k, pad = k / 2;
+  const long long nrows = (long long)a.B * a.T;
+  float cs = 0.f, as = 0.f, dw[16];
+  for (int q = 0; q < k; ++q) dw[q] = 0.f;
+  for (int rr = warp; rr < kPostRows; rr += 8) {
+    const long long row = (long long)blockIdx.x * kPostRows + rr;
+    if (row >= nrows) break;
+    const int b = (int)(row / a.T), t = (int)(row % a.T);
+    float dpre[16];
+    for (int q = 0; q < k; ++q) {
+      const int tt = t + pad - q;  // d_pre at t + pad - tap feeds input row t through tap q
+      float d = 0.f;
+      if (tt >= 0 && tt < a.T) {
+        const float y = a.audio[(size_t)b * a.T + tt];
+        d = a.dy[(size_t)b * a.T + tt] * (1.f - y * y);
+      }
+      dpre[q] = d;
+    }
+    float da = 0.f;
+    for (int q = 0; q < k; ++q) da += dpre[q] * a.W[(size_t)c * k + q];
+    const size_t off = (size_t)row * a.C + c;
+    const float xin = __bfloat162float(a.a_hi[off]) + __bfloat162float(a.a_lo[off]);
+    for (int q = 0; q < k; ++q) dw[q] += xin * dpre[q];
+    const float x = __bfloat162float(a.mask_src[off]);
+    float deriv;
+    if (a.act_kind == 1) {
+      const float al = a.alpha[c];
+      float sn, csn;
+      sincosf(al * x, &sn, &csn);
+      const float s2 = 2.f * sn * csn;
+      as += da * (x * s2 / al - sn * sn / (al * al));
+      deriv = 1.f + s2;
+    } else {
+      deriv = x > 0.f ? 1.f : a.slope;
+    }
+    const float ds = da * deriv * a.scale;
+    a.d_stage[off] = ds;
+    a.d_stage_bf[off] = __float2bfloat16_rn(ds);
+    cs += ds;
+  }
+  red[warp][c] = cs;
+  red[warp][32 + c] = as;
+  for (int q = 0; q < k; ++q) red[warp][64 + q * 32 + c] = dw[q];
+  __syncthreads();
+  const int nval = 64 + k * 32;
+  for (int o = threadIdx.x; o < nval; o += blockDim.x) {
+    float s = 0.f;
+    for (int w = 0; w < 8; ++w) s += red[w][o];
+    if (o < 32) a.colsum_part[(size_t)blockIdx.x * a.C + o] = s;
+    else if (o < 64) {
+      if (a.alpha_part) a.alpha_part[(size_t)blockIdx.x * a.C + (o - 32)] = s;
+    } else {
+      const int q = (o - 64) / 32, cc = (o - 64) % 32;
+      a.w_part[(size_t)blockIdx.x * (a.C * k) + (size_t)cc * k + q] = s;
+    }
+  }
+}
+
+void post_backward(const PostBwdArgs& a, cudaStream_t st) {
+  post_backward_kernel<<<post_backward_blocks(a.B, a.T), 256, 0, st>>>(a);
+}
+
+}  // namespace wb

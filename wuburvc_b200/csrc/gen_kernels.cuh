@@ -1,0 +1,114 @@
+// gen_kernels.cuh — bandwidth-bound kernels of the generator training step (declarations).
+#pragma once
+#include "common.cuh"
+
+namespace wb {
+
+// ---- weights -------------------------------------------------------------------------------
+// Effective weight W (= g*v/||v|| under weight norm, else the raw parameter) -> bf16 GEMM layouts.
+//   conv  (param [C_out][C_in][k]):  fwd [k][C_out][C_in] hi/lo,  dgrad [k][C_in][C_out] (taps flipped)
+//   convT (param [C_in][C_out][k]):  fwd [k][C_out][C_in] hi/lo in phase order, dgrad [k][C_in][C_out]
+// `norm` receives ||v|| per dim-0 row under weight norm.
+void prep_weight(const float* v, const float* g, int rows, int cols, int k, int is_convT, int stride,
+                 bf16* fwd_hi, bf16* fwd_lo, bf16* dg, float* norm, cudaStream_t st);
+
+// weight-norm backward: dg[r] = <dW[r], v[r]>/n[r];  dv[r] = g[r]/n[r] * (dW[r] - dg[r]/n[r] * v[r])
+void wn_backward(const float* dW, const float* v, const float* g, const float* norm, int rows, int per_row,
+                 float* dv, float* dg, cudaStream_t st);
+
+// Per-context step state kept on the device (a captured step graph advances it itself).
+struct StepState {
+  unsigned long long noise_stream;  // source-noise stream of the current step
+  int adam_t;                       // AdamW step count
+  int pad;
+};
+void step_bump(StepState* s, int bump_noise, cudaStream_t st);
+
+// AdamW over a flat buffer, restating the reference update (bias correction applied twice).
+// Gradients are multiplied by grad_scale first (1/world under data parallelism).
+void adamw(float* p, const float* g, float* m, float* v, long long n, float lr, float b1, float b2, float eps,
+           float wd, const StepState* state, float grad_scale, cudaStream_t st);
+
+// ---- inputs --------------------------------------------------------------------------------
+// z [B][C][F] f32 -> [B][F][C] bf16 hi/lo
+void pack_z(const float* z, int B, int C, int F, bf16* hi, bf16* lo, cudaStream_t st);
+
+// cond(g): rowadd[b][c] = bias[c] + sum_i W[c][i] g[b][i]
+void cond_forward(const float* W, const float* bias, const float* g, int B, int C, int gin, float* rowadd,
+                  cudaStream_t st);
+// per-item column sums of d_pre (from colsum tile partials) -> dW_cond, db_cond
+void cond_backward(const float* tile_part, int tiles_per_item, int B, int C, const float* g, int gin, float* dW,
+                   float* db, cudaStream_t st);
+
+// ---- harmonic source ------------------------------------------------------------------------
+struct NsfArgs {
+  const float* f0;       // [B][F] Hz
+  const float* noise;    // [B][T][dim] standard normals, or null -> counter generator
+  const float* lin_w;    // [dim]
+  const float* lin_b;    // [1]
+  float* har;            // [B][T] tanh(l_linear(source))
+  float* sw;             // [B][T][dim] source before l_linear (kept for the backward)
+  double* acc;           // [B][F] scratch: phase carried into each frame
+  int B, F, upp, dim;
+  float sr, sine_amp, noise_std;
+  unsigned long long seed;
+  const unsigned long long* stream;  // device word: noise stream of this step
+};
+void nsf_forward(const NsfArgs& a, cudaStream_t st);
+// l_linear gradients from d_har [B][T] (deterministic block partials + reduce)
+void nsf_backward(const float* d_har, const float* har, const float* sw, int n, int dim, float* part, int nparts,
+                  float* dlin_w, float* dlin_b, cudaStream_t st);
+
+// ---- noise convs + activation of the stage input --------------------------------------------
+struct NoiseActArgs {
+  float* x;               // [B][T][C] ups output -> stage input (in place)
+  const float* har;       // [B][T_full] or null (no source)
+  const float* w;         // [C][k]
+  const float* bias;      // [C]
+  int B, T, C, k, stride, pad, T_full;
+  int act_kind;           // 0 lrelu 1 snake
+  float slope;
+  int n_act;              // snake: one activation per stack (alpha differs); lrelu: 1
+  const float* alpha[3];
+  bf16* act_hi[3];
+  bf16* act_lo[3];
+  bf16* pre;              // bf16 copy of x (snake masks)
+};
+void noise_add_act(const NoiseActArgs& a, cudaStream_t st);
+
+// backward of the noise conv: d_har[b][t] += ..., weight-gradient partials
+void noise_backward(const float* dx, const float* har, const float* w, int B, int T, int C, int k, int stride, int pad,
+                    int T_full, float* d_har, int accumulate_dhar, float* wpart, int rows_per_part, cudaStream_t st);
+int noise_backward_parts(int B, int T, int rows_per_part);
+void noise_wgrad_reduce(const float* wpart, int nparts, int C, int k, float* dW, cudaStream_t st);
+
+// ---- conv_post ------------------------------------------------------------------------------
+// audio[b][t] = tanh(sum_{c,tap} a[b][t-3+tap][c] * W[c][tap]), a = hi + lo
+void post_forward(const bf16* a_hi, const bf16* a_lo, const float* W, int B, int T, int C, int k, float* audio,
+                  cudaStream_t st);
+// d_pre = dy*(1-y^2); d_a = conv_post^T(d_pre); d_stage = d_a * act'(stage) * scale -> f32 + bf16
+// partials: colsum of d_stage (64-row blocks), dW_post, snake d(alpha)
+struct PostBwdArgs {
+  const float* dy;        // [B][T]
+  const float* audio;     // [B][T]
+  const float* W;         // [C][k]
+  const bf16* a_hi;       // [B][T][C] activation (wgrad operand, with lo)
+  const bf16* a_lo;
+  const bf16* mask_src;   // activated (lrelu sign) or pre-activation (snake)
+  const float* alpha;     // snake alpha [C]
+  int act_kind;
+  float slope, scale;
+  int B, T, C, k;
+  float* d_stage;         // [B][T][C] f32
+  bf16* d_stage_bf;       // [B][T][C]
+  float* colsum_part;     // [nblk][C]
+  float* w_part;          // [nblk][C*k]
+  float* alpha_part;      // [nblk][C]
+};
+int post_backward_blocks(int B, int T);
+void post_backward(const PostBwdArgs& a, cudaStream_t st);
+
+// generic [nparts][n] -> out[n] fixed-order reduction (optionally accumulating)
+void rows_reduce(const float* part, int nparts, int n, float* out, int accumulate, cudaStream_t st);
+
+}  // namespace wb

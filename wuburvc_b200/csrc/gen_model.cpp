@@ -1,0 +1,628 @@
+// gen_model.cpp — the generator training step on one GPU: buffers, launch plans, forward,
+// backward, AdamW, CUDA-graph capture.
+//
+// Data layout in HBM: every activation is channels-last [B][T][C].  Residual streams (pair inputs,
+// stage sums, their gradients) are fp32; GEMM operands are bf16 — forward operands as hi/lo pairs
+// (bf16x3 products), backward operands single bf16.  Parameters, gradients and AdamW moments live
+// in flat fp32 buffers laid out by the parameter table.
+#include "gen_model.h"
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+
+#include "small_kernels.cuh"
+
+namespace wb {
+
+// comm.cpp (no-ops without a communicator)
+int comm_bucket_ready(Gen& m, int bucket);
+int comm_join(Gen& m);
+void comm_destroy(Gen& m);
+
+namespace {
+
+constexpr int kWgradCtas = 296;  // 2 waves of 148 SMs for split-K weight gradients
+
+#define CK(x)                                                                                   \
+  do {                                                                                          \
+    cudaError_t e_ = (x);                                                                       \
+    if (e_ != cudaSuccess) {                                                                    \
+      fprintf(stderr, "wuburvc_b200: %s failed: %s (%s:%d)\n", #x, cudaGetErrorString(e_), __FILE__, \
+              __LINE__);                                                                        \
+      return false;                                                                             \
+    }                                                                                           \
+  } while (0)
+
+template <class T>
+bool dalloc(Gen& m, T** p, size_t n) {
+  *p = nullptr;
+  if (n == 0) return true;
+  void* q = nullptr;
+  if (cudaMalloc(&q, n * sizeof(T)) != cudaSuccess) {
+    fprintf(stderr, "wuburvc_b200: cudaMalloc of %zu bytes failed\n", n * sizeof(T));
+    return false;
+  }
+  cudaMemset(q, 0, n * sizeof(T));
+  m.allocs.push_back(q);
+  *p = static_cast<T*>(q);
+  return true;
+}
+
+Epi epi0(float slope) {
+  Epi e{};
+  e.scale = 1.f;
+  e.slope = slope;
+  return e;
+}
+
+const float* alpha_ptr(Gen& m, const std::string& name) {
+  const int i = m.pidx(name);
+  return i >= 0 ? m.P(i) : nullptr;
+}
+float* alpha_grad(Gen& m, const std::string& name) {
+  const int i = m.pidx(name);
+  return i >= 0 ? m.G(i) : nullptr;
+}
+
+// derived weights of one conv param
+bool make_weights(Gen& m, ConvWeights& w, const std::string& base, bool resblock, bool convT, int stride) {
+  const bool wn = m.cfg.weight_norm && (resblock || convT);
+  const std::string vname = resblock ? base + ".weight_v" : (wn ? base + ".weight_v" : base + ".weight");
+  w.pv = m.pidx(vname);
+  w.pg = wn ? m.pidx(base + ".weight_g") : -1;
+  w.pb = m.pidx(base + ".bias");
+  if (w.pv < 0 || (wn && w.pg < 0)) {
+    fprintf(stderr, "wuburvc_b200: missing parameter %s\n", vname.c_str());
+    return false;
+  }
+  const ParamEntry& p = m.table.e[w.pv];
+  w.rows = p.shape[0];
+  w.cols = p.shape[1];
+  w.k = p.shape[2];
+  w.convT = convT;
+  w.stride = stride;
+  const size_t n = (size_t)p.n;
+  if (!dalloc(m, &w.fwd_hi, n) || !dalloc(m, &w.fwd_lo, n) || !dalloc(m, &w.dg, n)) return false;
+  if (wn) {
+    if (!dalloc(m, &w.norm, (size_t)w.rows) || !dalloc(m, &w.dW, n)) return false;
+  } else {
+    w.dW = m.G(w.pv);
+  }
+  return true;
+}
+
+bool make_wgrad_job(Gen& m, WgradJob& j, int layout, int c_out, int k, float* dW) {
+  j.layout = layout;
+  j.c_out = c_out;
+  j.k = k;
+  j.dW = dW;
+  std::vector<int> tab(j.L.row_tap);
+  tab.insert(tab.end(), j.L.row_oc.begin(), j.L.row_oc.end());
+  if (!dalloc(m, &j.tab, tab.size())) return false;
+  CK(cudaMemcpy(j.tab, tab.data(), tab.size() * sizeof(int), cudaMemcpyHostToDevice));
+  return true;
+}
+
+bool run_wgrad(Gen& m, WgradJob& j) {
+  j.L.p.part = m.wg_part;
+  CK(j.L.run(m.stream));
+  const int rows = j.L.p.n_mtiles * 128;
+  wgrad_reduce(m.wg_part, j.L.splits, rows, j.L.p.n_total, j.tab, j.tab + rows, j.layout, j.c_out, j.k, j.dW, 0,
+               m.stream);
+  return true;
+}
+
+void prep(Gen& m, const ConvWeights& w) {
+  prep_weight(m.P(w.pv), w.pg >= 0 ? m.P(w.pg) : nullptr, w.rows, w.cols, w.k, w.convT, w.stride, w.fwd_hi,
+              w.fwd_lo, w.dg, w.norm, m.stream);
+}
+
+void finish_weight_grad(Gen& m, const ConvWeights& w) {
+  if (w.pg >= 0) wn_backward(w.dW, m.P(w.pv), m.P(w.pg), w.norm, w.rows, w.cols * w.k, m.G(w.pv), m.G(w.pg), m.stream);
+}
+
+}  // namespace
+
+// =============================================================================================
+// setup
+// =============================================================================================
+bool gen_setup(Gen& m) {
+  const WubuB200GenConfig& c = m.cfg;
+  m.B = m.opt.batch;
+  m.F = m.opt.frames;
+  m.nk = c.n_kernels;
+  m.nd = c.n_dilations;
+  m.upp = 1;
+  for (int L = 0; L < 4; ++L) m.upp *= c.upsample_rates[L];
+  m.T = m.F * m.upp;
+  m.dim = c.harmonic_num + 1;
+  const bool snake = c.activation == 1;
+  const int B = m.B;
+  CK(cudaSetDevice(m.opt.device));
+  CK(cudaStreamCreateWithFlags(&m.stream, cudaStreamNonBlocking));
+  if (!dalloc(m, &m.err, 1) || !dalloc(m, &m.state, 1)) return false;
+
+  m.table = build_param_table(c);
+  const size_t P = (size_t)m.table.total;
+  if (!dalloc(m, &m.params, P) || !dalloc(m, &m.grads, P) || !dalloc(m, &m.adam_m, P) || !dalloc(m, &m.adam_v, P))
+    return false;
+
+  // ---- inputs ----
+  if (!dalloc(m, &m.z, (size_t)B * c.in_channels * m.F) || !dalloc(m, &m.dldy, (size_t)B * m.T)) return false;
+  if (!dalloc(m, &m.z_hi, (size_t)B * m.F * c.in_channels) || !dalloc(m, &m.z_lo, (size_t)B * m.F * c.in_channels))
+    return false;
+  if (c.gin_channels && !dalloc(m, &m.g, (size_t)B * c.gin_channels)) return false;
+  if (c.nsf) {
+    if (!dalloc(m, &m.f0, (size_t)B * m.F) || !dalloc(m, &m.noise, (size_t)B * m.T * m.dim)) return false;
+    if (!dalloc(m, &m.har, (size_t)B * m.T) || !dalloc(m, &m.sw, (size_t)B * m.T * m.dim) ||
+        !dalloc(m, &m.d_har, (size_t)B * m.T) || !dalloc(m, &m.nsf_acc, (size_t)B * m.F))
+      return false;
+    m.nsf_parts = 256;
+    if (!dalloc(m, &m.nsf_part, (size_t)(m.nsf_parts + 1) * (m.dim + 1))) return false;
+  }
+
+  // ---- stage geometry ----
+  const int C0 = c.initial_channel;
+  int Tcur = m.F;
+  for (int L = 0; L < 4; ++L) {
+    StageBufs& s = m.sg[L];
+    s.su = c.upsample_rates[L];
+    s.ku = c.upsample_kernels[L];
+    s.pu = (s.ku - s.su) / 2;
+    s.Cin = C0 >> L;
+    s.C = C0 >> (L + 1);
+    s.T = Tcur * s.su;
+    s.rows = B * s.T;
+    Tcur = s.T;
+    if (L + 1 < 4) {
+      int sf = 1;
+      for (int i = L + 1; i < 4; ++i) sf *= c.upsample_rates[i];
+      s.sn = sf;
+      s.kn = 2 * sf;
+      s.pn = sf / 2;
+    } else {
+      s.sn = 1;
+      s.kn = 1;
+      s.pn = 0;
+    }
+  }
+  if (m.sg[3].T != m.T) return false;
+
+  // ---- derived weights ----
+  if (!make_weights(m, m.wpre, "dec.conv_pre", false, false, 1)) return false;
+  for (int L = 0; L < 4; ++L) {
+    StageBufs& s = m.sg[L];
+    if (!make_weights(m, s.wu, "dec.ups." + std::to_string(L), false, true, s.su)) return false;
+    for (int j = 0; j < m.nk; ++j)
+      for (int cp = 0; cp < m.nd; ++cp) {
+        const std::string R = "dec.resblocks." + std::to_string(L * m.nk + j);
+        if (!make_weights(m, s.st[j].w1[cp], R + ".convs1." + std::to_string(cp), true, false, 1)) return false;
+        if (!make_weights(m, s.st[j].w2[cp], R + ".convs2." + std::to_string(cp), true, false, 1)) return false;
+      }
+  }
+
+  // ---- activations ----
+  const size_t n_pre = (size_t)B * m.F * C0;
+  if (!dalloc(m, &m.pre_hi, n_pre) || !dalloc(m, &m.pre_lo, n_pre) || !dalloc(m, &m.d_pre_bf, n_pre)) return false;
+  if (snake && !dalloc(m, &m.pre_pre, n_pre)) return false;
+  if (c.gin_channels && !dalloc(m, &m.rowadd, (size_t)B * C0)) return false;
+  if (!dalloc(m, &m.audio, (size_t)B * m.T)) return false;
+  for (int L = 0; L < 4; ++L) {
+    StageBufs& s = m.sg[L];
+    const size_t n = (size_t)s.rows * s.C;
+    if (!dalloc(m, &s.x_in, n) || !dalloc(m, &s.sout, n) || !dalloc(m, &s.sa_hi, n) || !dalloc(m, &s.sa_lo, n))
+      return false;
+    if (!dalloc(m, &s.d_s, n) || !dalloc(m, &s.d_s_bf, n) || !dalloc(m, &s.d_x, n) || !dalloc(m, &s.d_x_bf, n))
+      return false;
+    const int nxa = snake ? m.nk : 1;
+    for (int q = 0; q < nxa; ++q)
+      if (!dalloc(m, &s.xa_hi[q], n) || !dalloc(m, &s.xa_lo[q], n)) return false;
+    if (snake && (!dalloc(m, &s.x_pre, n) || !dalloc(m, &s.s_pre, n))) return false;
+    const int tiles = B * ((s.T + 127) / 128);
+    for (int j = 0; j < m.nk; ++j) {
+      StackBufs& k = s.st[j];
+      k.tiles = tiles;
+      k.p[0] = s.x_in;
+      k.a1_hi[0] = s.xa_hi[snake ? j : 0];
+      k.a1_lo[0] = s.xa_lo[snake ? j : 0];
+      k.a1_pre[0] = s.x_pre;
+      for (int cp = 0; cp < m.nd; ++cp) {
+        if (cp > 0) {
+          if (!dalloc(m, &k.p[cp], n) || !dalloc(m, &k.a1_hi[cp], n) || !dalloc(m, &k.a1_lo[cp], n)) return false;
+          if (snake && !dalloc(m, &k.a1_pre[cp], n)) return false;
+        }
+        if (!dalloc(m, &k.a2_hi[cp], n) || !dalloc(m, &k.a2_lo[cp], n)) return false;
+        if (snake && !dalloc(m, &k.a2_pre[cp], n)) return false;
+        if (!dalloc(m, &k.cs_dc1[cp], (size_t)tiles * s.C) || !dalloc(m, &k.cs_dp[cp], (size_t)tiles * s.C))
+          return false;
+        if (snake && (!dalloc(m, &k.ap1[cp], (size_t)tiles * s.C) || !dalloc(m, &k.ap2[cp], (size_t)tiles * s.C)))
+          return false;
+      }
+      if (!dalloc(m, &k.d_c1, n)) return false;
+      for (int q = 0; q < 2; ++q)
+        if (!dalloc(m, &k.pp[q], n) || !dalloc(m, &k.pp_bf[q], n)) return false;
+    }
+    if (c.nsf) {
+      s.noise_parts = noise_backward_parts(B, s.T, 64);
+      if (!dalloc(m, &s.noise_wpart, (size_t)s.noise_parts * s.C * s.kn)) return false;
+    }
+  }
+
+  // ---- launch plans ----
+  m.wg_part_cap = 0;
+  // forward conv_pre
+  {
+    Epi e = epi0(c.lrelu_slope);
+    e.bias = m.P(m.wpre.pb);
+    e.rowadd = m.rowadd;
+    e.act_hi = m.pre_hi;
+    e.act_lo = m.pre_lo;
+    e.act_kind = c.activation;
+    e.act_alpha = alpha_ptr(m, "dec.ups_act.0.alpha");
+    e.pre_hi = m.pre_pre;
+    ConvGeom g{B, m.F, m.F, c.in_channels, C0, 7, 1, 3};
+    if (!plan_conv(m.pre_fwd, g, m.z_hi, m.z_lo, m.wpre.fwd_hi, m.wpre.fwd_lo, 1, e, m.err)) return false;
+  }
+  for (int L = 0; L < 4; ++L) {
+    StageBufs& s = m.sg[L];
+    const bool last = L == 3;
+    const int Tin = (L == 0) ? m.F : m.sg[L - 1].T;
+    const bf16* in_hi = (L == 0) ? m.pre_hi : m.sg[L - 1].sa_hi;
+    const bf16* in_lo = (L == 0) ? m.pre_lo : m.sg[L - 1].sa_lo;
+    {  // ups forward
+      Epi e = epi0(c.lrelu_slope);
+      e.bias = m.P(s.wu.pb);
+      e.out_f32 = s.x_in;
+      if (!plan_convT(s.up_fwd, B, Tin, s.Cin, s.C, s.ku, s.su, s.pu, in_hi, in_lo, s.wu.fwd_hi, s.wu.fwd_lo, 1, e,
+                      m.err))
+        return false;
+    }
+    for (int j = 0; j < m.nk; ++j) {
+      StackBufs& k = s.st[j];
+      const int kk = c.resblock_kernels[j];
+      const std::string R = std::to_string(L * m.nk + j);
+      for (int cp = 0; cp < m.nd; ++cp) {
+        const int dil = c.resblock_dilations[j][cp];
+        const std::string P = std::to_string(cp);
+        {  // conv1: bias -> act -> a2
+          Epi e = epi0(c.lrelu_slope);
+          e.bias = m.P(k.w1[cp].pb);
+          e.act_hi = k.a2_hi[cp];
+          e.act_lo = k.a2_lo[cp];
+          e.act_kind = c.activation;
+          e.act_alpha = alpha_ptr(m, "dec.resblocks." + R + ".alpha2." + P);
+          e.pre_hi = k.a2_pre[cp];
+          ConvGeom g{B, s.T, s.T, s.C, s.C, kk, dil, dil * (kk - 1) / 2};
+          if (!plan_conv(k.f1[cp], g, k.a1_hi[cp], k.a1_lo[cp], k.w1[cp].fwd_hi, k.w1[cp].fwd_lo, 1, e, m.err))
+            return false;
+        }
+        {  // conv2: bias + residual -> next pair input (+act) or stage sum
+          Epi e = epi0(c.lrelu_slope);
+          e.bias = m.P(k.w2[cp].pb);
+          e.res = k.p[cp];
+          e.act_kind = c.activation;
+          if (cp + 1 < m.nd) {
+            e.out_f32 = k.p[cp + 1];
+            e.act_hi = k.a1_hi[cp + 1];
+            e.act_lo = k.a1_lo[cp + 1];
+            e.act_alpha = alpha_ptr(m, "dec.resblocks." + R + ".alpha1." + std::to_string(cp + 1));
+            e.pre_hi = k.a1_pre[cp + 1];
+          } else {
+            e.scale = 1.f / (float)m.nk;
+            e.out_f32 = s.sout;
+            e.accumulate = j > 0;
+            if (j == m.nk - 1) {
+              e.act_hi = s.sa_hi;
+              e.act_lo = s.sa_lo;
+              e.pre_hi = s.s_pre;
+              e.slope = last ? c.final_slope : c.lrelu_slope;
+              e.act_alpha = alpha_ptr(m, last ? "dec.post_act.alpha" : "dec.ups_act." + std::to_string(L + 1) + ".alpha");
+            }
+          }
+          ConvGeom g{B, s.T, s.T, s.C, s.C, kk, 1, (kk - 1) / 2};
+          if (!plan_conv(k.f2[cp], g, k.a2_hi[cp], k.a2_lo[cp], k.w2[cp].fwd_hi, k.w2[cp].fwd_lo, 1, e, m.err))
+            return false;
+        }
+      }
+    }
+  }
+
+  // ---- backward plans ----
+  // gradient wrt each stage output: produced by conv_post bwd (L=3) or ups L+1 dgrad
+  m.post_blocks = post_backward_blocks(B, m.T);
+  if (!dalloc(m, &m.post_cs, (size_t)m.post_blocks * m.sg[3].C) ||
+      !dalloc(m, &m.post_wpart, (size_t)m.post_blocks * m.sg[3].C * 7))
+    return false;
+  if (snake && !dalloc(m, &m.post_ap, (size_t)m.post_blocks * m.sg[3].C)) return false;
+  m.sg[3].cs_ds = m.post_cs;
+  m.sg[3].cs_ds_tiles = m.post_blocks;
+  for (int L = 0; L < 4; ++L) {
+    StageBufs& s = m.sg[L];
+    for (int j = 0; j < m.nk; ++j) {
+      StackBufs& k = s.st[j];
+      const int kk = c.resblock_kernels[j];
+      const std::string R = std::to_string(L * m.nk + j);
+      for (int cp = m.nd - 1; cp >= 0; --cp) {
+        const int dil = c.resblock_dilations[j][cp];
+        const std::string P = std::to_string(cp);
+        const float* dp_out_f = (cp == m.nd - 1) ? s.d_s : k.pp[cp % 2];
+        const bf16* dp_out_b = (cp == m.nd - 1) ? s.d_s_bf : k.pp_bf[cp % 2];
+        (void)dp_out_f;
+        {  // conv2 dgrad -> d_c1 (mask of conv1's activation)
+          Epi e = epi0(c.lrelu_slope);
+          e.act_kind = c.activation;
+          e.mask_src = snake ? k.a2_pre[cp] : k.a2_hi[cp];
+          e.mask_alpha = alpha_ptr(m, "dec.resblocks." + R + ".alpha2." + P);
+          e.alpha_part = k.ap2[cp];
+          e.out_bf16 = k.d_c1;
+          e.colsum = k.cs_dc1[cp];
+          ConvGeom g{B, s.T, s.T, s.C, s.C, kk, 1, (kk - 1) / 2};
+          if (!plan_conv(k.d2[cp], g, dp_out_b, nullptr, k.w2[cp].dg, nullptr, 0, e, m.err)) return false;
+        }
+        {  // conv2 wgrad
+          ConvGeom g{B, s.T, s.T, s.C, s.C, kk, 1, (kk - 1) / 2};
+          if (!plan_wgrad(k.g2[cp].L, g, dp_out_b, k.a2_hi[cp], nullptr, ~size_t(0), kWgradCtas, m.err)) return false;
+          m.wg_part_cap = std::max(m.wg_part_cap, wgrad_part_floats(k.g2[cp].L));
+          if (!make_wgrad_job(m, k.g2[cp], 0, s.C, kk, k.w2[cp].dW)) return false;
+        }
+        {  // conv1 dgrad -> gradient wrt the pair input
+          Epi e = epi0(c.lrelu_slope);
+          e.act_kind = c.activation;
+          e.mask_src = snake ? k.a1_pre[cp] : k.a1_hi[cp];
+          e.mask_alpha = alpha_ptr(m, "dec.resblocks." + R + ".alpha1." + P);
+          e.alpha_part = k.ap1[cp];
+          e.res = (cp == m.nd - 1) ? s.d_s : k.pp[cp % 2];
+          e.colsum = k.cs_dp[cp];
+          if (cp > 0) {
+            e.out_f32 = k.pp[(cp - 1) % 2];
+            e.out_bf16 = k.pp_bf[(cp - 1) % 2];
+          } else {
+            e.out_f32 = s.d_x;
+            e.accumulate = j > 0;
+            e.out_bf16 = (j == m.nk - 1) ? s.d_x_bf : nullptr;
+          }
+          ConvGeom g{B, s.T, s.T, s.C, s.C, kk, dil, dil * (kk - 1) / 2};
+          if (!plan_conv(k.d1[cp], g, k.d_c1, nullptr, k.w1[cp].dg, nullptr, 0, e, m.err)) return false;
+        }
+        {  // conv1 wgrad
+          ConvGeom g{B, s.T, s.T, s.C, s.C, kk, dil, dil * (kk - 1) / 2};
+          if (!plan_wgrad(k.g1[cp].L, g, k.d_c1, k.a1_hi[cp], nullptr, ~size_t(0), kWgradCtas, m.err)) return false;
+          m.wg_part_cap = std::max(m.wg_part_cap, wgrad_part_floats(k.g1[cp].L));
+          if (!make_wgrad_job(m, k.g1[cp], 0, s.C, kk, k.w1[cp].dW)) return false;
+        }
+      }
+    }
+    // ups L input gradient -> gradient wrt the previous stage output (or conv_pre output)
+    {
+      const int Tin = (L == 0) ? m.F : m.sg[L - 1].T;
+      Epi e = epi0(c.lrelu_slope);
+      e.act_kind = c.activation;
+      e.mask_alpha = alpha_ptr(m, "dec.ups_act." + std::to_string(L) + ".alpha");
+      const int tiles = B * ((Tin + 127) / 128);
+      if (snake && !dalloc(m, &s.ap_up, (size_t)tiles * s.Cin)) return false;
+      s.ap_up_tiles = tiles;
+      e.alpha_part = s.ap_up;
+      if (L > 0) {
+        StageBufs& pv = m.sg[L - 1];
+        e.mask_src = snake ? pv.s_pre : pv.sa_hi;
+        e.scale = 1.f / (float)m.nk;
+        e.out_f32 = pv.d_s;
+        e.out_bf16 = pv.d_s_bf;
+        if (!dalloc(m, &pv.cs_ds, (size_t)tiles * pv.C)) return false;
+        pv.cs_ds_tiles = tiles;
+        e.colsum = pv.cs_ds;
+      } else {
+        e.mask_src = snake ? m.pre_pre : m.pre_hi;
+        e.out_bf16 = m.d_pre_bf;
+        if (!dalloc(m, &m.cs_pre, (size_t)tiles * C0)) return false;
+        m.cs_pre_tiles = tiles;
+        m.pre_tiles_per_item = (Tin + 127) / 128;
+        e.colsum = m.cs_pre;
+      }
+      if (!plan_convT_dgrad(s.up_dg, B, Tin, s.Cin, s.C, s.ku, s.su, s.pu, s.d_x_bf, s.wu.dg, e, m.err)) return false;
+      const bf16* xin = (L == 0) ? m.pre_hi : m.sg[L - 1].sa_hi;
+      if (!plan_convT_wgrad(s.up_wg.L, B, Tin, s.Cin, s.C, s.ku, s.su, s.pu, xin, s.d_x_bf, nullptr, ~size_t(0),
+                            kWgradCtas, m.err))
+        return false;
+      m.wg_part_cap = std::max(m.wg_part_cap, wgrad_part_floats(s.up_wg.L));
+      if (!make_wgrad_job(m, s.up_wg, 1, s.C, s.ku, s.wu.dW)) return false;
+    }
+  }
+  {  // conv_pre wgrad
+    ConvGeom g{B, m.F, m.F, c.in_channels, C0, 7, 1, 3};
+    if (!plan_wgrad(m.pre_wg.L, g, m.d_pre_bf, m.z_hi, nullptr, ~size_t(0), kWgradCtas, m.err)) return false;
+    m.wg_part_cap = std::max(m.wg_part_cap, wgrad_part_floats(m.pre_wg.L));
+    if (!make_wgrad_job(m, m.pre_wg, 0, C0, 7, m.wpre.dW)) return false;
+  }
+  if (!dalloc(m, &m.wg_part, m.wg_part_cap)) return false;
+  return true;
+}
+
+// =============================================================================================
+// forward
+// =============================================================================================
+bool gen_forward(Gen& m) {
+  const WubuB200GenConfig& c = m.cfg;
+  const bool snake = c.activation == 1;
+  cudaStream_t st = m.stream;
+  // weights for this step
+  prep(m, m.wpre);
+  for (int L = 0; L < 4; ++L) {
+    prep(m, m.sg[L].wu);
+    for (int j = 0; j < m.nk; ++j)
+      for (int cp = 0; cp < m.nd; ++cp) {
+        prep(m, m.sg[L].st[j].w1[cp]);
+        prep(m, m.sg[L].st[j].w2[cp]);
+      }
+  }
+  pack_z(m.z, m.B, c.in_channels, m.F, m.z_hi, m.z_lo, st);
+  if (c.nsf) {
+    NsfArgs a{};
+    a.f0 = m.f0;
+    a.noise = m.has_noise_input ? m.noise : nullptr;
+    a.lin_w = m.P(m.pidx("dec.m_source.l_linear.weight"));
+    a.lin_b = m.P(m.pidx("dec.m_source.l_linear.bias"));
+    a.har = m.har;
+    a.sw = m.sw;
+    a.acc = m.nsf_acc;
+    a.B = m.B;
+    a.F = m.F;
+    a.upp = m.upp;
+    a.dim = m.dim;
+    a.sr = (float)c.sample_rate;
+    a.sine_amp = c.sine_amp;
+    a.noise_std = c.noise_std;
+    a.seed = m.opt.seed;
+    a.stream = &m.state->noise_stream;
+    nsf_forward(a, st);
+  }
+  if (c.gin_channels)
+    cond_forward(m.P(m.pidx("dec.cond.weight")), m.P(m.pidx("dec.cond.bias")), m.g, m.B, c.initial_channel,
+                 c.gin_channels, m.rowadd, st);
+  CK(m.pre_fwd.run(st));
+  for (int L = 0; L < 4; ++L) {
+    StageBufs& s = m.sg[L];
+    CK(s.up_fwd.run(st));
+    NoiseActArgs na{};
+    na.x = s.x_in;
+    na.har = c.nsf ? m.har : nullptr;
+    if (c.nsf) {
+      na.w = m.P(m.pidx("dec.noise_convs." + std::to_string(L) + ".weight"));
+      na.bias = m.P(m.pidx("dec.noise_convs." + std::to_string(L) + ".bias"));
+    }
+    na.B = m.B;
+    na.T = s.T;
+    na.C = s.C;
+    na.k = s.kn;
+    na.stride = s.sn;
+    na.pad = s.pn;
+    na.T_full = m.T;
+    na.act_kind = c.activation;
+    na.slope = c.lrelu_slope;
+    na.n_act = snake ? m.nk : 1;
+    for (int q = 0; q < na.n_act; ++q) {
+      na.alpha[q] = snake ? alpha_ptr(m, "dec.resblocks." + std::to_string(L * m.nk + q) + ".alpha1.0") : nullptr;
+      na.act_hi[q] = s.xa_hi[q];
+      na.act_lo[q] = s.xa_lo[q];
+    }
+    na.pre = s.x_pre;
+    noise_add_act(na, st);
+    for (int j = 0; j < m.nk; ++j)
+      for (int cp = 0; cp < m.nd; ++cp) {
+        CK(s.st[j].f1[cp].run(st));
+        CK(s.st[j].f2[cp].run(st));
+      }
+  }
+  post_forward(m.sg[3].sa_hi, m.sg[3].sa_lo, m.P(m.pidx("dec.conv_post.weight")), m.B, m.T, m.sg[3].C, 7, m.audio,
+               st);
+  return true;
+}
+
+// =============================================================================================
+// backward
+// =============================================================================================
+bool gen_backward(Gen& m) {
+  const WubuB200GenConfig& c = m.cfg;
+  const bool snake = c.activation == 1;
+  cudaStream_t st = m.stream;
+  const int B = m.B;
+  {  // conv_post + tanh backward -> gradient wrt stage 3 output (/nk per stack)
+    StageBufs& s3 = m.sg[3];
+    PostBwdArgs a{};
+    a.dy = m.dldy;
+    a.audio = m.audio;
+    a.W = m.P(m.pidx("dec.conv_post.weight"));
+    a.a_hi = s3.sa_hi;
+    a.a_lo = s3.sa_lo;
+    a.mask_src = snake ? s3.s_pre : s3.sa_hi;
+    a.alpha = alpha_ptr(m, "dec.post_act.alpha");
+    a.act_kind = c.activation;
+    a.slope = c.final_slope;
+    a.scale = 1.f / (float)m.nk;
+    a.B = B;
+    a.T = m.T;
+    a.C = s3.C;
+    a.k = 7;
+    a.d_stage = s3.d_s;
+    a.d_stage_bf = s3.d_s_bf;
+    a.colsum_part = m.post_cs;
+    a.w_part = m.post_wpart;
+    a.alpha_part = m.post_ap;
+    post_backward(a, st);
+    rows_reduce(m.post_wpart, m.post_blocks, s3.C * 7, m.G(m.pidx("dec.conv_post.weight")), 0, st);
+    if (snake) rows_reduce(m.post_ap, m.post_blocks, s3.C, alpha_grad(m, "dec.post_act.alpha"), 0, st);
+  }
+  for (int L = 3; L >= 0; --L) {
+    StageBufs& s = m.sg[L];
+    for (int j = 0; j < m.nk; ++j) {
+      StackBufs& k = s.st[j];
+      const std::string R = std::to_string(L * m.nk + j);
+      for (int cp = m.nd - 1; cp >= 0; --cp) {
+        const std::string P = std::to_string(cp);
+        CK(k.d2[cp].run(st));
+        if (!run_wgrad(m, k.g2[cp])) return false;
+        CK(k.d1[cp].run(st));
+        if (!run_wgrad(m, k.g1[cp])) return false;
+        // biases: conv1 <- colsum(d_c1); conv2 <- colsum(grad wrt pair output)
+        colsum_reduce(k.cs_dc1[cp], k.tiles, s.C, m.G(k.w1[cp].pb), 0, st);
+        if (cp == m.nd - 1)
+          colsum_reduce(s.cs_ds, s.cs_ds_tiles, s.C, m.G(k.w2[cp].pb), 0, st);
+        else
+          colsum_reduce(k.cs_dp[cp + 1], k.tiles, s.C, m.G(k.w2[cp].pb), 0, st);
+        if (snake) {
+          colsum_reduce(k.ap1[cp], k.tiles, s.C, alpha_grad(m, "dec.resblocks." + R + ".alpha1." + P), 0, st);
+          colsum_reduce(k.ap2[cp], k.tiles, s.C, alpha_grad(m, "dec.resblocks." + R + ".alpha2." + P), 0, st);
+        }
+        finish_weight_grad(m, k.w1[cp]);
+        finish_weight_grad(m, k.w2[cp]);
+      }
+    }
+    // stage input gradient d_x: ups bias, noise conv, ups dgrad / wgrad
+    const int ub = m.pidx("dec.ups." + std::to_string(L) + ".bias");
+    for (int j = 0; j < m.nk; ++j) colsum_reduce(s.st[j].cs_dp[0], s.st[j].tiles, s.C, m.G(ub), j > 0, st);
+    if (c.nsf) {
+      const int nw = m.pidx("dec.noise_convs." + std::to_string(L) + ".weight");
+      const int nb = m.pidx("dec.noise_convs." + std::to_string(L) + ".bias");
+      CK(cudaMemcpyAsync(m.G(nb), m.G(ub), sizeof(float) * s.C, cudaMemcpyDeviceToDevice, st));
+      noise_backward(s.d_x, m.har, m.P(nw), B, s.T, s.C, s.kn, s.sn, s.pn, m.T, m.d_har, L < 3, s.noise_wpart, 64, st);
+      noise_wgrad_reduce(s.noise_wpart, s.noise_parts, s.C, s.kn, m.G(nw), st);
+    }
+    CK(s.up_dg.run(st));
+    if (!run_wgrad(m, s.up_wg)) return false;
+    finish_weight_grad(m, s.wu);
+    if (snake)
+      colsum_reduce(s.ap_up, s.ap_up_tiles, s.Cin, alpha_grad(m, "dec.ups_act." + std::to_string(L) + ".alpha"), 0, st);
+    if (comm_bucket_ready(m, 3 - L)) return false;  // this stage's gradients are final
+  }
+  // conv_pre, cond, source
+  if (!run_wgrad(m, m.pre_wg)) return false;
+  colsum_reduce(m.cs_pre, m.cs_pre_tiles, c.initial_channel, m.G(m.wpre.pb), 0, st);
+  if (c.gin_channels)
+    cond_backward(m.cs_pre, m.pre_tiles_per_item, B, c.initial_channel, m.g, c.gin_channels,
+                  m.G(m.pidx("dec.cond.weight")), m.G(m.pidx("dec.cond.bias")), st);
+  if (c.nsf)
+    nsf_backward(m.d_har, m.har, m.sw, B * m.T, m.dim, m.nsf_part, m.nsf_parts,
+                 m.G(m.pidx("dec.m_source.l_linear.weight")), m.G(m.pidx("dec.m_source.l_linear.bias")), st);
+  if (comm_bucket_ready(m, 4) || comm_join(m)) return false;
+  return true;
+}
+
+bool gen_adamw(Gen& m, float grad_scale, int bump_noise) {
+  step_bump(m.state, bump_noise, m.stream);
+  adamw(m.params, m.grads, m.adam_m, m.adam_v, m.table.total, m.opt.lr, m.opt.beta1, m.opt.beta2, m.opt.eps,
+        m.opt.weight_decay, m.state, grad_scale, m.stream);
+  return cudaGetLastError() == cudaSuccess;
+}
+
+void gen_free(Gen& m) {
+  if (m.stream) cudaStreamSynchronize(m.stream);
+  comm_destroy(m);
+  if (m.graph) cudaGraphExecDestroy(m.graph);
+  for (void* p : m.allocs) cudaFree(p);
+  m.allocs.clear();
+  if (m.stream) cudaStreamDestroy(m.stream);
+  m.stream = nullptr;
+}
+
+}  // namespace wb

@@ -1,0 +1,123 @@
+// gen_model.h — internal state of one generator training context (one GPU).
+#pragma once
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "conv_plan.h"
+#include "gen_kernels.cuh"
+#include "param_table.h"
+
+namespace wb {
+
+struct Comm;  // NCCL communicator + bucket plan (comm.cpp)
+
+// Derived GEMM weights of one convolution and where its gradient goes.
+struct ConvWeights {
+  int pv = -1, pg = -1, pb = -1;  // param indices (v or W, g, bias)
+  int rows = 0, cols = 0, k = 0;  // param dims: conv [C_out][C_in][k], convT [C_in][C_out][k]
+  int convT = 0, stride = 1;
+  bf16 *fwd_hi = nullptr, *fwd_lo = nullptr, *dg = nullptr;
+  float* norm = nullptr;  // ||v|| rows (weight norm)
+  float* dW = nullptr;    // gradient in param layout (grad buffer directly, or a temp under weight norm)
+};
+
+struct WgradJob {
+  WgradLaunch L;
+  int* tab = nullptr;  // device [row_tap | row_oc]
+  int layout = 0;      // 0 conv, 1 convT
+  int c_out = 0, k = 0;
+  float* dW = nullptr;
+};
+
+struct StackBufs {
+  // forward (index = pair)
+  bf16 *a1_hi[3] = {}, *a1_lo[3] = {}, *a1_pre[3] = {};  // activation of the pair input
+  float* p[3] = {};                                      // pair input (p[0] aliases the stage input)
+  bf16 *a2_hi[3] = {}, *a2_lo[3] = {}, *a2_pre[3] = {};  // activation of conv1's output
+  // backward
+  bf16* d_c1 = nullptr;
+  float* pp[2] = {};
+  bf16* pp_bf[2] = {};
+  float *cs_dc1[3] = {}, *cs_dp[3] = {}, *ap1[3] = {}, *ap2[3] = {};
+  int tiles = 0;
+  ConvWeights w1[3], w2[3];
+  ConvLaunch f1[3], f2[3], d2[3], d1[3];
+  WgradJob g1[3], g2[3];
+};
+
+struct StageBufs {
+  int T = 0, C = 0, Cin = 0, rows = 0, ku = 0, su = 0, pu = 0;
+  int kn = 0, sn = 0, pn = 0;
+  float* x_in = nullptr;
+  bf16 *xa_hi[3] = {}, *xa_lo[3] = {}, *x_pre = nullptr;
+  float* sout = nullptr;
+  bf16 *sa_hi = nullptr, *sa_lo = nullptr, *s_pre = nullptr;
+  float* d_s = nullptr;
+  bf16* d_s_bf = nullptr;
+  float* d_x = nullptr;
+  bf16* d_x_bf = nullptr;
+  float* cs_ds = nullptr;  // colsum partials of d_s (from its producer)
+  int cs_ds_tiles = 0;
+  float* ap_up = nullptr;  // snake alpha partials of the activation feeding ups L (from up_dg)
+  int ap_up_tiles = 0;
+  float* noise_wpart = nullptr;
+  int noise_parts = 0;
+  ConvWeights wu;
+  ConvLaunch up_fwd, up_dg;
+  WgradJob up_wg;
+  StackBufs st[3];
+};
+
+struct Gen {
+  WubuB200GenConfig cfg{};
+  WubuB200TrainOptions opt{};
+  ParamTable table;
+  int B = 0, F = 0, T = 0, dim = 0, upp = 0;
+  int nk = 3, nd = 3;
+  cudaStream_t stream = nullptr;
+  std::vector<void*> allocs;
+  int* err = nullptr;
+
+  float *params = nullptr, *grads = nullptr, *adam_m = nullptr, *adam_v = nullptr;
+  StepState* state = nullptr;  // device: noise stream + AdamW step
+
+  // inputs
+  float *z = nullptr, *f0 = nullptr, *g = nullptr, *noise = nullptr, *dldy = nullptr;
+  bool has_noise_input = false;
+  bf16 *z_hi = nullptr, *z_lo = nullptr;
+  // source
+  float *har = nullptr, *sw = nullptr, *d_har = nullptr, *nsf_part = nullptr;
+  double* nsf_acc = nullptr;
+  int nsf_parts = 0;
+  // conv_pre / cond
+  ConvWeights wpre;
+  float* rowadd = nullptr;
+  bf16 *pre_hi = nullptr, *pre_lo = nullptr, *pre_pre = nullptr;
+  bf16* d_pre_bf = nullptr;
+  float* cs_pre = nullptr;
+  int cs_pre_tiles = 0, pre_tiles_per_item = 0;
+  ConvLaunch pre_fwd;
+  WgradJob pre_wg;
+  // conv_post
+  float* audio = nullptr;
+  float *post_cs = nullptr, *post_wpart = nullptr, *post_ap = nullptr;
+  int post_blocks = 0;
+
+  StageBufs sg[4];
+  float* wg_part = nullptr;  // shared split-K scratch for the weight gradients
+  size_t wg_part_cap = 0;
+
+  // CUDA graph of the resident-input step
+  cudaGraphExec_t graph = nullptr;
+
+
+
+  Comm* comm = nullptr;  // owned; released by comm_destroy
+
+  int pidx(const std::string& n) const { return table.find(n); }
+  float* P(int i) { return params + table.e[i].off; }
+  float* G(int i) { return grads + table.e[i].off; }
+};
+
+}  // namespace wb

@@ -382,21 +382,31 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
-// explicit instantiations / launch wrappers (host)
+// launch wrappers (host).  The dynamic shared-memory limit is raised once, before any capture.
+static void raise_smem_limits() {
+  static bool done = false;
+  if (done) return;
+  done = true;
+  const int lim = 227 * 1024;
+  cudaFuncSetAttribute(tc_conv_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+  cudaFuncSetAttribute(tc_conv_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+  cudaFuncSetAttribute(tc_wgrad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+}
+
+void tc_kernels_init() { raise_smem_limits(); }
+
 cudaError_t launch_tc_conv(const TcMaps& maps, const TcConvParams& p, int kc, dim3 grid, size_t smem,
                            cudaStream_t st) {
-  if (kc == 64) {
-    cudaFuncSetAttribute(tc_conv_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  raise_smem_limits();
+  if (kc == 64)
     tc_conv_kernel<64><<<grid, 192, smem, st>>>(maps, p);
-  } else {
-    cudaFuncSetAttribute(tc_conv_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  else
     tc_conv_kernel<32><<<grid, 192, smem, st>>>(maps, p);
-  }
   return cudaGetLastError();
 }
 
 cudaError_t launch_tc_wgrad(const TcWgMaps& maps, const TcWgParams& p, dim3 grid, size_t smem, cudaStream_t st) {
-  cudaFuncSetAttribute(tc_wgrad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  raise_smem_limits();
   tc_wgrad_kernel<<<grid, 192, smem, st>>>(maps, p);
   return cudaGetLastError();
 }
