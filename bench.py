@@ -1,0 +1,294 @@
+#!/usr/bin/env python
+"""Generator train-step throughput: audio-seconds trained per second.
+
+Workload: the 40 kHz RVC v2 NSF-HiFiGAN generator training step (forward, backward with dL/dy
+given, AdamW), batch 16 per GPU, 32 frames (12,800 samples) per item, 9-harmonic sine source,
+cond(g), weight norm; GEMM operands bf16 (forward bf16x3 split) with fp32 accumulation.
+Synthetic seeded inputs of the configured shapes (z ~ N(0,1), g ~ N(0,1), f0 ~ U(80,400) Hz with
+20% unvoiced frames, dL/dy ~ N(0,1)).
+
+  python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+
+One process per GPU (torchrun for N > 1); gradients are all-reduced over NCCL inside the step.
+Rank 0 prints one JSON line.  `--impl reference` times the reference's own CPU trainer
+(src/wubu_train.c built from its sources into oracle/_ref) on this host's cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "generator train-step audio-sec/sec"
+UNIT = "audio-s/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="40k")
+    ap.add_argument("--batch", type=int, default=16)
+    ap.add_argument("--frames", type=int, default=32)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["bf16_tflops"], d.get("bf16_tflops_sustained", d["bf16_tflops"]), d["hbm_gbs"], "measured"
+    return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+def make_inputs(cfg, B, F, seed):
+    rng = np.random.default_rng(seed)
+    T = F * int(np.prod(cfg["upsample_rates"]))
+    z = rng.standard_normal((B, cfg["in_channels"], F), dtype=np.float32)
+    g = rng.standard_normal((B, cfg["gin_channels"]), dtype=np.float32)
+    f0 = rng.uniform(80, 400, (B, F)).astype(np.float32)
+    f0[rng.random((B, F)) < 0.2] = 0.0
+    dldy = rng.standard_normal((B, T), dtype=np.float32)
+    return z, f0, g, dldy
+
+
+class Clocks:
+    """Samples SM clocks and throttle reasons of one GPU while the timed region runs."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.proc = None
+        self.f = None
+
+    def __enter__(self):
+        try:
+            self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        time.sleep(0.2)
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.f:
+            return None
+        self.f.flush()
+        rows = []
+        for line in open(self.f.name):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        os.unlink(self.f.name)
+        if not rows:
+            return None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, r in rows for i, v in enumerate(r) if v.lower() == "active"})
+        load = [r[0] for r in rows]
+        return {"sm_mhz": statistics.median(load), "sm_max_mhz": max(r[1] for r in rows), "reasons": reasons,
+                "samples": len(rows)}
+
+
+def cpu_reference_step(ref, mel, dldy):
+    ref.forward(mel)
+    ref.backward(dldy)
+    ref.adamw()
+
+
+def time_reference(cfg_name, F, steps, warmup):
+    """The reference C trainer (decoder fwd + bwd + AdamW, one item per step) on host cores."""
+    from oracle import generator_ref as G
+    from oracle import ref_oracle
+    from wuburvc_b200 import model
+    if not ref_oracle.available():
+        return None, "oracle/_ref/libwubu_ref.so not built"
+    cfg = model.decoder_only(cfg_name)
+    P = G.init_params_ref(cfg, 1)
+    ref = ref_oracle.RefTrainer(P, cfg["upsample_rates"], cfg["upsample_kernels"])
+    T = F * model.hop(cfg)
+    mel = G.counter_normal(1, 1, 192 * F).reshape(192, F).astype(np.float32)
+    dldy = G.counter_normal(1, 2, T).astype(np.float32)
+    for _ in range(warmup):
+        cpu_reference_step(ref, mel, dldy)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        cpu_reference_step(ref, mel, dldy)
+    dt = (time.perf_counter() - t0) / steps
+    audio_s = T / cfg["sr"]
+    return {"value": audio_s / dt, "unit": UNIT, "cores": ref_oracle.RefTrainer.threads(), "kind": "reference",
+            "sec_per_item": dt,
+            "sample": f"1 item x {F} frames ({T} samples) per step, decoder fwd+bwd+AdamW of src/wubu_train.c "
+                      f"(no NSF source / cond / noise convs: the reference trainer has none), {steps} steps"}, None
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    res, why = time_reference(args.config, args.frames, args.steps, args.warmup)
+    if res is None:
+        print(json.dumps({"impl": "reference", "unavailable": why}))
+        return
+    ms = 1000.0 * res["sec_per_item"]
+    line = {"impl": "reference", "metric": METRIC, "value": res["value"], "unit": UNIT, "n_gpus": 0,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"{args.config} generator train step on the reference CPU trainer, "
+                                   f"1 item x {args.frames} frames per step (bounded sample of the batch-16 "
+                                   f"workload)", "frames": args.frames, "parallelism": "OpenMP host threads"},
+            "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": res["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+
+    import torch
+    import torch.distributed as dist
+    from wuburvc_b200 import Generator, model
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", init_method="env://", timeout=__import__("datetime").timedelta(seconds=300))
+    cfg = model.config(args.config)
+    B, F = args.batch, args.frames
+    gen = Generator(cfg, B, F, device=local)
+    if world > 1:
+        obj = [Generator.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        gen.attach_comm(rank, world, obj[0])
+    T = gen.T
+    z, f0, g, dldy = make_inputs(cfg, B, F, seed=1234 + rank)
+    gen.upload(z, f0, g, None, dldy)
+    stream = torch.cuda.ExternalStream(gen.stream, device=local)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{local}")
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident timing ----
+    for i in range(max(3, args.warmup)):
+        gen.step_async(i)
+    gen.sync()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        e0.record(stream)
+        for i in range(args.steps):
+            gen.step_async(1000 + i)
+        e1.record(stream)
+        gen.sync()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
+    audio_s = B * T / cfg["sr"]
+    value = world * audio_s / (ms / 1000.0)
+
+    # ---- end to end through the public API: pinned host inputs in, audio out, every step ----
+    pz = torch.from_numpy(z).pin_memory()
+    pf = torch.from_numpy(f0).pin_memory()
+    pg = torch.from_numpy(g).pin_memory()
+    pd = torch.from_numpy(dldy).pin_memory()
+    pa = torch.empty((B, T), dtype=torch.float32).pin_memory()
+    for i in range(2):
+        gen.train_step_raw(pz.data_ptr(), pf.data_ptr(), pg.data_ptr(), pd.data_ptr(), pa.data_ptr(), i)
+    barrier()
+    h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    h0.record(stream)
+    for i in range(args.steps):
+        gen.train_step_raw(pz.data_ptr(), pf.data_ptr(), pg.data_ptr(), pd.data_ptr(), pa.data_ptr(), 2000 + i)
+    h1.record(stream)
+    gen.sync()
+    barrier()
+    ms_e2e = max_over_ranks(h0.elapsed_time(h1)) / args.steps
+    e2e_value = world * audio_s / (ms_e2e / 1000.0)
+    h2d = (z.nbytes + f0.nbytes + g.nbytes + dldy.nbytes)
+    d2h = pa.numel() * 4
+
+    # ---- dominant kernel vs roofline (bf16 tensor peak, kernel timed alone) ----
+    pk, pk_sus, hbm, pk_src = peaks()
+    kms, kflops = gen.kernel_bench(0, 1, iters=20)
+    achieved = kflops / (kms / 1000.0) / 1e12
+    step_flops = model.train_flops_per_item(cfg, F) * B
+    step_tflops = step_flops / (ms / 1000.0) / 1e12
+    launches = gen.graph_kernels() * args.steps
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        res, why = time_reference(args.config, F, steps=2, warmup=1)
+        cpu = ({k: res[k] for k in ("value", "unit", "cores", "kind", "sample")} if res
+               else {"value": None, "unavailable": why})
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"{args.config} NSF-HiFiGAN generator train step (fwd + bwd + AdamW), "
+                                   f"batch {B}/GPU, {F} frames = {T} samples per item",
+                       "global_batch": B * world, "frames": F, "samples_per_item": T,
+                       "parallelism": f"dp{world}",
+                       "gemm": "tcgen05 bf16 operands, fp32 accumulate; forward bf16x3 split",
+                       "l2": "working set of several GB per step is larger than L2; no flush"},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": ms_e2e},
+            "gpu_launches": launches,
+            "roofline": {"bound": "tensor", "kernel": "tc_conv_kernel<64> forward conv1 (k=11) of stage 1, bf16x3",
+                         "achieved": achieved, "peak": pk, "unit": "TFLOP/s", "frac": achieved / pk,
+                         "peak_source": pk_src, "traffic": None, "launch_ms": kms,
+                         "algorithmic_flops_per_launch": kflops},
+            "step_roofline": {"algorithmic_tflops": step_tflops, "peak_sustained": pk_sus,
+                              "frac": step_tflops / pk_sus, "flops_per_step": step_flops},
+            "clocks": clk.summary(),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line))
+    gen.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

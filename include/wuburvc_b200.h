@@ -156,6 +156,16 @@ void* wubu_b200_gen_stream(WubuB200Gen* gen);
 /* Host synchronisation + device error word check. */
 int wubu_b200_gen_sync(WubuB200Gen* gen);
 
+/* Kernel launches in one captured step (the graph's kernel nodes); -1 before the first step. */
+int wubu_b200_gen_graph_kernels(WubuB200Gen* gen);
+
+/* Times `iters` back-to-back launches of one convolution of the step with CUDA events on the
+ * model stream.  which: 0 = forward conv1 of the largest-k stack of stage `stage` (bf16x3),
+ * 1 = its input-gradient conv, 2 = its weight gradient.  Returns the mean launch time (ms) and
+ * the algorithmic FLOPs of one launch (2*MACs of the convolution, not counting split terms). */
+int wubu_b200_gen_kernel_bench(WubuB200Gen* gen, int which, int stage, int iters, float* ms_per_launch,
+                               double* flops_per_launch);
+
 /* Data parallelism: one process per GPU.  Rank 0 creates the 128-byte NCCL unique id and the
  * caller ships it to the other ranks; every rank then attaches it.  Gradients are summed
  * over ranks in buckets on a communication stream while the backward runs, then scaled 1/world. */

@@ -1,0 +1,90 @@
+"""Host-side logic that needs no GPU: the native library loads and exports every symbol its
+header declares, the parameter table matches the reference registry, init is deterministic."""
+import os
+import re
+
+import numpy as np
+
+from oracle import generator_ref as G
+from wuburvc_b200 import flatten, init_params, model, param_table, param_total, unflatten
+from wuburvc_b200._lib import LIB_PATH, lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def header_functions():
+    txt = open(os.path.join(ROOT, "include", "wuburvc_b200.h")).read()
+    txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
+    return sorted(set(re.findall(r"\b(wubu_b200_\w+)\s*\(", txt)))
+
+
+def test_library_exports_every_header_symbol():
+    assert os.path.exists(LIB_PATH)
+    h = lib()
+    names = header_functions()
+    assert len(names) >= 25
+    for n in names:
+        assert hasattr(h, n), n
+
+
+def test_decoder_table_matches_reference_registry():
+    """Same tensor set and sizes as wubu_train_registry_build (src/wubu_train.c:131-210):
+    155 tensors / 14,327,424 floats for the 40 kHz decoder."""
+    cfg = model.decoder_only("40k")
+    t = param_table(cfg)
+    assert len(t) == 155
+    assert sum(x[4] for x in t) == 14327424
+    ref = G.param_names(cfg)
+    assert {x[0] for x in t} == set(ref)
+    for name, kind, shape, off, n in t:
+        assert n == int(np.prod(ref[name]))
+        assert off % 64 == 0
+
+
+def test_nsf_table_matches_upstream_generator():
+    cfg = model.config("40k")
+    t = param_table(cfg)
+    assert sum(x[4] for x in t) == 14490890  # upstream GeneratorNSF with weight_norm, gin 256, 9 harmonics
+    assert {x[0] for x in t} == set(G.param_names(cfg))
+    snake = model.config("48k_snake")
+    names = {x[0] for x in param_table(snake)}
+    assert "dec.post_act.alpha" in names and "dec.resblocks.11.alpha2.2" in names
+
+
+def test_table_order_is_backward_completion_order():
+    cfg = model.config("40k")
+    t = param_table(cfg)
+    offs = {n: o for n, _, _, o, _ in t}
+    assert offs["dec.conv_post.weight"] == 0
+    assert offs["dec.ups.3.bias"] < offs["dec.resblocks.6.convs1.0.bias"] < offs["dec.ups.0.bias"]
+    assert offs["dec.ups.0.bias"] < offs["dec.conv_pre.weight"] < offs["dec.m_source.l_linear.weight"]
+
+
+def test_init_is_deterministic_and_weight_normed():
+    cfg = model.config("40k")
+    a = init_params(cfg, 0)
+    b = init_params(cfg, 0)
+    assert np.array_equal(a, b)
+    named = unflatten(cfg, a)
+    v = named["dec.resblocks.4.convs2.1.weight_v"]
+    gg = named["dec.resblocks.4.convs2.1.weight_g"]
+    np.testing.assert_allclose(gg.reshape(-1), np.linalg.norm(v.reshape(v.shape[0], -1), axis=1), rtol=1e-5)
+    w = named["dec.conv_pre.weight"]
+    assert abs(w.std() - 0.01) < 5e-4
+    assert np.all(named["dec.ups.1.bias"] == 0)
+
+
+def test_flatten_roundtrip():
+    cfg = model.config("32k")
+    P = G.init_params_ref(cfg, 3)
+    flat = flatten(cfg, P)
+    back = unflatten(cfg, flat)
+    for k, v in P.items():
+        np.testing.assert_array_equal(back[k].reshape(-1), v.reshape(-1))
+    assert flat.size == param_total(cfg)
+
+
+def test_flops_match_survey():
+    assert abs(model.train_flops_per_item(model.config("40k"), 32) / 1e9 - 87.79) < 0.01
+    assert abs(model.train_flops_per_item(model.config("32k"), 40) / 1e9 - 92.27) < 0.01
+    assert abs(model.train_flops_per_item(model.config("48k"), 36) / 1e9 - 118.97) < 0.01

@@ -107,6 +107,9 @@ _SIGS = {
     "wubu_b200_gen_train_step_async": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_ulonglong]),
     "wubu_b200_gen_stream": (ctypes.c_void_p, [ctypes.c_void_p]),
     "wubu_b200_gen_sync": (ctypes.c_int, [ctypes.c_void_p]),
+    "wubu_b200_gen_graph_kernels": (ctypes.c_int, [ctypes.c_void_p]),
+    "wubu_b200_gen_kernel_bench": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                                  ctypes.c_void_p, ctypes.c_void_p]),
     "wubu_b200_nccl_unique_id": (ctypes.c_int, [ctypes.c_void_p]),
     "wubu_b200_gen_attach_comm": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
 }
@@ -270,6 +273,15 @@ class Generator:
     @property
     def stream(self) -> int:
         return L().wubu_b200_gen_stream(self.h) or 0
+
+    def graph_kernels(self) -> int:
+        return int(L().wubu_b200_gen_graph_kernels(self.h))
+
+    def kernel_bench(self, which: int, stage: int, iters: int = 20):
+        ms, fl = ctypes.c_float(), ctypes.c_double()
+        check(L().wubu_b200_gen_kernel_bench(self.h, which, stage, iters, ctypes.byref(ms), ctypes.byref(fl)),
+              "kernel_bench")
+        return ms.value, fl.value
 
     # ---- data parallel ----
     @staticmethod

@@ -64,6 +64,15 @@ int run_step_graph(Gen& m) {
       fprintf(stderr, "wuburvc_b200: step capture failed (%s)\n", cudaGetErrorString(e));
       return WUBU_B200_ERR_CUDA;
     }
+    size_t nn = 0;
+    cudaGraphGetNodes(g, nullptr, &nn);
+    std::vector<cudaGraphNode_t> nodes(nn);
+    cudaGraphGetNodes(g, nodes.data(), &nn);
+    m.graph_kernels = 0;
+    for (auto nd : nodes) {
+      cudaGraphNodeType t;
+      if (cudaGraphNodeGetType(nd, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) ++m.graph_kernels;
+    }
     const cudaError_t ie = cudaGraphInstantiate(&m.graph, g, 0);
     cudaGraphDestroy(g);
     if (ie != cudaSuccess) {
@@ -237,6 +246,47 @@ int wubu_b200_gen_sync(WubuB200Gen* gen) {
   if (!gen) return WUBU_B200_ERR_ARG;
   cudaSetDevice(gen->m.opt.device);
   return check_err(gen->m);
+}
+
+int wubu_b200_gen_graph_kernels(WubuB200Gen* gen) {
+  if (!gen) return WUBU_B200_ERR_ARG;
+  return gen->m.graph ? gen->m.graph_kernels : -1;
+}
+
+int wubu_b200_gen_kernel_bench(WubuB200Gen* gen, int which, int stage, int iters, float* ms_per_launch,
+                               double* flops_per_launch) {
+  if (!gen || stage < 0 || stage > 3 || iters < 1 || which < 0 || which > 2) return WUBU_B200_ERR_ARG;
+  Gen& m = gen->m;
+  cudaSetDevice(m.opt.device);
+  StageBufs& s = m.sg[stage];
+  int j = 0;
+  for (int q = 1; q < m.nk; ++q)
+    if (m.cfg.resblock_kernels[q] > m.cfg.resblock_kernels[j]) j = q;
+  StackBufs& k = s.st[j];
+  const double flops = 2.0 * s.rows * (double)s.C * s.C * m.cfg.resblock_kernels[j];
+  auto launch = [&]() -> bool {
+    if (which == 0) return k.f1[0].run(m.stream) == cudaSuccess;
+    if (which == 1) return k.d1[0].run(m.stream) == cudaSuccess;
+    k.g1[0].L.p.part = m.wg_part;
+    return k.g1[0].L.run(m.stream) == cudaSuccess;
+  };
+  for (int i = 0; i < 2; ++i)
+    if (!launch()) return WUBU_B200_ERR_CUDA;
+  cudaEvent_t a, b;
+  cudaEventCreate(&a);
+  cudaEventCreate(&b);
+  cudaEventRecord(a, m.stream);
+  for (int i = 0; i < iters; ++i)
+    if (!launch()) return WUBU_B200_ERR_CUDA;
+  cudaEventRecord(b, m.stream);
+  const int rc = check_err(m);
+  float ms = 0.f;
+  cudaEventElapsedTime(&ms, a, b);
+  cudaEventDestroy(a);
+  cudaEventDestroy(b);
+  if (ms_per_launch) *ms_per_launch = ms / (float)iters;
+  if (flops_per_launch) *flops_per_launch = flops;
+  return rc;
 }
 
 int wubu_b200_nccl_unique_id(void* out128) {

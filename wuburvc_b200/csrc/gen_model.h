@@ -110,6 +110,7 @@ struct Gen {
 
   // CUDA graph of the resident-input step
   cudaGraphExec_t graph = nullptr;
+  int graph_kernels = 0;  // kernel nodes in the captured step
 
 
 

@@ -387,7 +387,11 @@ static void raise_smem_limits() {
   static bool done = false;
   if (done) return;
   done = true;
-  const int lim = 227 * 1024;
+  // opt-in limit minus room for the kernels' static shared memory
+  int dev = 0, optin = 227 * 1024;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  const int lim = optin - 1024;
   cudaFuncSetAttribute(tc_conv_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
   cudaFuncSetAttribute(tc_conv_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
   cudaFuncSetAttribute(tc_wgrad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
