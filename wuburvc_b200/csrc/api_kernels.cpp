@@ -38,6 +38,11 @@ int finish(cudaStream_t st, int* derr) {
   return WUBU_B200_OK;
 }
 
+bool launched(cudaError_t e) {
+  if (e != cudaSuccess) fprintf(stderr, "wuburvc_b200: launch failed: %s\n", cudaGetErrorString(e));
+  return e == cudaSuccess;
+}
+
 Epi plain_epi(const float* bias, float* out) {
   Epi e{};
   e.bias = bias;
@@ -52,9 +57,9 @@ int run_wgrad(WgradLaunch& L, Scratch& s, int layout, int c_out, int k, float* d
   tab.insert(tab.end(), L.row_oc.begin(), L.row_oc.end());
   if (cudaMalloc(&s.tabs, tab.size() * sizeof(int)) != cudaSuccess) return WUBU_B200_ERR_CUDA;
   cudaMemcpy(s.tabs, tab.data(), tab.size() * sizeof(int), cudaMemcpyHostToDevice);
-  if (L.run(st) != cudaSuccess) return WUBU_B200_ERR_CUDA;
+  if (!launched(L.run(st))) return WUBU_B200_ERR_CUDA;
   const int rows = L.p.n_mtiles * 128;
-  wgrad_reduce(s.part, L.splits, rows, L.p.n_total, s.tabs, s.tabs + rows, layout, c_out, k, dw, 0, st);
+  wgrad_reduce(s.part, L.splits, rows, L.p.n_total, s.tabs, s.tabs + rows, layout, c_out, k, dw, 0, nullptr, 0, st);
   return finish(st, s.err);
 }
 
@@ -70,9 +75,9 @@ int wubu_b200_conv1d(const void* x_hi, const void* x_lo, const void* w_hi, const
   if (cudaMalloc(&s.err, sizeof(int)) != cudaSuccess) return WUBU_B200_ERR_CUDA;
   cudaMemsetAsync(s.err, 0, sizeof(int), st);
   ConvGeom g{B, T, T + 2 * pad - dil * (k - 1), C_in, C_out, k, dil, pad};
-  ConvLaunch L;
-  if (!plan_conv(L, g, x_hi, x_lo, w_hi, w_lo, split, plain_epi(bias, out), s.err)) return WUBU_B200_ERR_SHAPE;
-  if (L.run(st) != cudaSuccess) return WUBU_B200_ERR_CUDA;
+  ConvOp L;
+  if (!plan_conv_any(L, g, x_hi, x_lo, w_hi, w_lo, split, plain_epi(bias, out), s.err)) return WUBU_B200_ERR_SHAPE;
+  if (!launched(L.run(st))) return WUBU_B200_ERR_CUDA;
   return finish(st, s.err);
 }
 
@@ -101,7 +106,7 @@ int wubu_b200_convT(const void* x_hi, const void* x_lo, const void* wp_hi, const
   if (!plan_convT(L, B, T_in, C_in, C_out, k, stride, pad, x_hi, x_lo, wp_hi, wp_lo, split, plain_epi(bias, out),
                   s.err))
     return WUBU_B200_ERR_SHAPE;
-  if (L.run(st) != cudaSuccess) return WUBU_B200_ERR_CUDA;
+  if (!launched(L.run(st))) return WUBU_B200_ERR_CUDA;
   return finish(st, s.err);
 }
 
@@ -114,7 +119,7 @@ int wubu_b200_convT_dgrad(const void* dy, const void* wd, float* dx, int B, int 
   ConvLaunch L;
   if (!plan_convT_dgrad(L, B, T_in, C_in, C_out, k, stride, pad, dy, wd, plain_epi(nullptr, dx), s.err))
     return WUBU_B200_ERR_SHAPE;
-  if (L.run(st) != cudaSuccess) return WUBU_B200_ERR_CUDA;
+  if (!launched(L.run(st))) return WUBU_B200_ERR_CUDA;
   return finish(st, s.err);
 }
 

@@ -123,6 +123,101 @@ bool plan_conv(ConvLaunch& L, const ConvGeom& g, const void* x_hi, const void* x
   return finish_fwd(L, g.B, g.C_in, g.C_out, split, 1, err);
 }
 
+// No-swizzle view of a [B][T][C] bf16 tensor with an (8 channels, R rows, 1) box: each load lands in
+// shared memory as one core-matrix column (R rows x 16 bytes) of the K-major no-swizzle UMMA layout.
+static bool make_map_bf16_cm(CUtensorMap* m, const void* base, uint64_t T, uint64_t C, uint64_t B, uint32_t R) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {C, T, B};
+  cuuint64_t strides[2] = {C * 2, T * C * 2};
+  cuuint32_t box[3] = {8, R, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    fprintf(stderr, "wuburvc_b200: cuTensorMapEncodeTiled (core-matrix) failed (%d) T %llu C %llu B %llu R %u\n",
+            (int)r, (unsigned long long)T, (unsigned long long)C, (unsigned long long)B, R);
+    return false;
+  }
+  return true;
+}
+
+static int sm_count() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+  }
+  return n;
+}
+
+bool plan_conv2(Conv2Launch& L, const ConvGeom& g, const void* x_hi, const void* x_lo, const void* w_hi,
+                const void* w_lo, int split, const Epi& epi, int* err) {
+  memset(&L.p, 0, sizeof(L.p));
+  memset(&L.maps, 0, sizeof(L.maps));
+  TcConv2Params& p = L.p;
+  if (g.T_in != g.T_out || g.C_out > 256 || g.C_out % 32 || g.C_in % 32 || g.k > kMaxTaps2) return false;
+  const int span = g.dil * (g.k - 1);
+  // rows of the halo tile, rounded up to 8 so every core-matrix column (R x 16 B) starts on the
+  // 128-byte boundary a TMA shared-memory destination requires
+  const int R = (128 + span + 7) / 8 * 8;
+  if (R > 256) return false;
+  p.ntaps = g.k;
+  p.halo_start = -g.pad;
+  p.halo_rows = R;
+  for (int t = 0; t < g.k; ++t) {
+    p.tap_off[t] = (short)(g.dil * t);
+    p.tap_w[t] = (short)t;
+  }
+  p.tiles_per_item = (g.T_out + 127) / 128;
+  p.ntiles = g.B * p.tiles_per_item;
+  p.t_rows = g.T_out;
+  p.n = g.C_out;
+  p.split = split;
+  p.epi = epi;
+  p.err = err;
+  const int nA = split ? 2 : 1;
+  int kc = (g.C_in % 64 == 0) ? 64 : 32;
+  for (;;) {
+    const size_t a_sub = ((size_t)R * kc * 2 + 1023) / 1024 * 1024;
+    const size_t a_stage = nA * a_sub, w_stage = (size_t)nA * g.C_out * kc * 2;
+    p.a_stages = 2;
+    const long long room = (long long)kSmemBudget - 2048 - (long long)p.a_stages * a_stage;
+    p.w_stages = room > 0 ? (int)std::min<long long>(8, room / (long long)w_stage) : 0;
+    if (p.w_stages >= 3 || (p.w_stages >= 2 && kc == 32)) {
+      p.a_sub_bytes = (uint32_t)a_sub;
+      L.smem = p.a_stages * a_stage + p.w_stages * w_stage + 1024 + 512;
+      break;
+    }
+    if (kc == 32) return false;
+    kc = 32;
+  }
+  L.kc = kc;
+  p.n_chunks = g.C_in / kc;
+  p.tmem_cols = pow2_cols(2 * g.C_out);
+  if (p.tmem_cols > 512) return false;
+  if (!make_map_bf16_cm(&L.maps.a_hi, x_hi, g.T_in, g.C_in, g.B, R)) return false;
+  if (split && !make_map_bf16_cm(&L.maps.a_lo, x_lo, g.T_in, g.C_in, g.B, R)) return false;
+  const uint64_t wr = (uint64_t)g.C_in * 2, wt = wr * g.C_out;
+  if (!make_map_bf16_3d(&L.maps.w_hi, w_hi, g.C_in, g.C_out, g.k, wr, wt, kc, g.C_out, 1)) return false;
+  if (split && !make_map_bf16_3d(&L.maps.w_lo, w_lo, g.C_in, g.C_out, g.k, wr, wt, kc, g.C_out, 1)) return false;
+  int occ = (int)std::min<size_t>(2, (227 * 1024) / L.smem);
+  occ = std::min(occ, 512 / p.tmem_cols);
+  occ = std::max(occ, 1);
+  L.grid = std::min(p.ntiles, sm_count() * occ);
+  return true;
+}
+
+bool plan_conv_any(ConvOp& op, const ConvGeom& g, const void* x_hi, const void* x_lo, const void* w_hi,
+                   const void* w_lo, int split, const Epi& epi, int* err) {
+  static const bool force_v1 = getenv("WUBU_B200_CONV_V1") != nullptr;
+  op.v2 = !force_v1 && plan_conv2(op.c2, g, x_hi, x_lo, w_hi, w_lo, split, epi, err);
+  if (op.v2) return true;
+  return plan_conv(op.v1, g, x_hi, x_lo, w_hi, w_lo, split, epi, err);
+}
+
 bool plan_convT(ConvLaunch& L, int B, int T_in, int C_in, int C_out, int k, int s, int pad, const void* x_hi,
                 const void* x_lo, const void* wp_hi, const void* wp_lo, int split, const Epi& epi, int* err) {
   memset(&L.p, 0, sizeof(L.p));

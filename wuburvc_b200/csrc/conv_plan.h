@@ -28,6 +28,29 @@ struct ConvLaunch {
   cudaError_t run(cudaStream_t st) const { return launch_tc_conv(maps, p, kc, grid, smem, st); }
 };
 
+cudaError_t launch_tc_conv2(const TcConv2Maps& maps, const TcConv2Params& p, int kc, int grid, size_t smem,
+                            cudaStream_t st);
+
+struct Conv2Launch {
+  TcConv2Maps maps;
+  TcConv2Params p;
+  int grid = 0;
+  size_t smem = 0;
+  int kc = 64;
+  cudaError_t run(cudaStream_t st) const { return launch_tc_conv2(maps, p, kc, grid, smem, st); }
+};
+
+// A stride-1 convolution planned on the persistent halo kernel when its shape allows, else on
+// the general kernel.
+struct ConvOp {
+  bool v2 = false;
+  ConvLaunch v1;
+  Conv2Launch c2;
+  cudaError_t run(cudaStream_t st) const { return v2 ? c2.run(st) : v1.run(st); }
+  // rows of the [partials][C] column-sum buffers this launch writes (one per CTA or per tile)
+  int partials() const { return v2 ? c2.grid : (int)(v1.grid.x * v1.grid.z); }
+};
+
 struct WgradLaunch {
   TcWgMaps maps;
   TcWgParams p;
@@ -50,6 +73,13 @@ struct ConvGeom {
 //   w_hi/w_lo : [k][C_out][C_in] bf16
 bool plan_conv(ConvLaunch& L, const ConvGeom& g, const void* x_hi, const void* x_lo, const void* w_hi,
                const void* w_lo, int split, const Epi& epi, int* err);
+
+// Persistent halo-reuse plan (stride-1, T_in == T_out, C_out <= 256); false if the shape does not fit.
+bool plan_conv2(Conv2Launch& L, const ConvGeom& g, const void* x_hi, const void* x_lo, const void* w_hi,
+                const void* w_lo, int split, const Epi& epi, int* err);
+// plan_conv2 when possible (unless WUBU_B200_CONV_V1 is set), else plan_conv.
+bool plan_conv_any(ConvOp& op, const ConvGeom& g, const void* x_hi, const void* x_lo, const void* w_hi,
+                   const void* w_lo, int split, const Epi& epi, int* err);
 
 // ConvTranspose1d forward as polyphase conv: x [B][T_in][C_in], w (per-phase packed)
 // [n_phase_taps][C_out][C_in]; output [B][T_in*s][C_out].

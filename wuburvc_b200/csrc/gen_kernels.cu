@@ -1,5 +1,6 @@
 // gen_kernels.cu — bandwidth-bound kernels of the generator training step.
 #include "gen_kernels.cuh"
+#include "small_kernels.cuh"
 
 namespace wb {
 
@@ -298,17 +299,8 @@ __global__ void nsf_backward_kernel(const float* __restrict__ d_har, const float
   if (threadIdx.x == 0) part[(size_t)blockIdx.x * (dim + 1) + dim] = s;
 }
 
-__global__ void rows_reduce_kernel(const float* __restrict__ part, int nparts, int n, float* __restrict__ out,
-                                   int accumulate) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n) return;
-  float s = 0.f;
-  for (int p = 0; p < nparts; ++p) s += part[(size_t)p * n + i];
-  out[i] = accumulate ? out[i] + s : s;
-}
-
 void rows_reduce(const float* part, int nparts, int n, float* out, int accumulate, cudaStream_t st) {
-  rows_reduce_kernel<<<(n + 127) / 128, 128, 0, st>>>(part, nparts, n, out, accumulate);
+  col_reduce(part, nparts, n, out, accumulate, st);
 }
 
 __global__ void split_lin_kernel(const float* __restrict__ red, int dim, float* __restrict__ dw, float* __restrict__ db) {
@@ -324,195 +316,6 @@ void nsf_backward(const float* d_har, const float* har, const float* sw, int n, 
   float* red = part + (size_t)nparts * (dim + 1);
   rows_reduce(part, nparts, dim + 1, red, 0, st);
   split_lin_kernel<<<1, 32, 0, st>>>(red, dim, dlin_w, dlin_b);
-}
-
-// =============================================================================================
-// noise conv (+ activation of the stage input)
-// =============================================================================================
-__global__ void noise_add_act_kernel(NoiseActArgs a) {
-  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  const long long n = (long long)a.B * a.T * a.C;
-  if (i >= n) return;
-  const int c = (int)(i % a.C);
-  const long long row = i / a.C;
-  const int b = (int)(row / a.T), j = (int)(row % a.T);
-  float x = a.x[i];
-  if (a.har) {
-    float s = a.bias[c];
-    const float* h = a.har + (size_t)b * a.T_full;
-    const float* w = a.w + (size_t)c * a.k;
-    const int t0 = j * a.stride - a.pad;
-    for (int tap = 0; tap < a.k; ++tap) {
-      const int t = t0 + tap;
-      if (t >= 0 && t < a.T_full) s += w[tap] * h[t];
-    }
-    x += s;
-    a.x[i] = x;
-  }
-  if (a.pre) a.pre[i] = __float2bfloat16_rn(x);
-  for (int q = 0; q < a.n_act; ++q) {
-    const float al = a.alpha[q] ? a.alpha[q][c] : 1.f;
-    const float y = act_fwd(x, a.act_kind, a.slope, al);
-    bf16 hi, lo;
-    split_bf16(y, hi, lo);
-    a.act_hi[q][i] = hi;
-    a.act_lo[q][i] = lo;
-  }
-}
-
-void noise_add_act(const NoiseActArgs& a, cudaStream_t st) {
-  const long long n = (long long)a.B * a.T * a.C;
-  noise_add_act_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(a);
-}
-
-__global__ void noise_dhar_kernel(const float* __restrict__ dx, const float* __restrict__ w, int B, int T, int C, int k,
-                                  int stride, int pad, int T_full, float* __restrict__ d_har, int accumulate) {
-  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= (long long)B * T_full) return;
-  const int b = (int)(i / T_full), t = (int)(i % T_full);
-  // rows j with 0 <= t + pad - j*stride < k
-  int jhi = (t + pad) / stride;
-  int jlo = t + pad - k + 1;
-  jlo = jlo <= 0 ? 0 : (jlo + stride - 1) / stride;
-  if (jhi > T - 1) jhi = T - 1;
-  float s = 0.f;
-  for (int j = jlo; j <= jhi; ++j) {
-    const int tap = t + pad - j * stride;
-    const float* r = dx + ((size_t)b * T + j) * C;
-    for (int c = 0; c < C; ++c) s += r[c] * w[(size_t)c * k + tap];
-  }
-  d_har[i] = accumulate ? d_har[i] + s : s;
-}
-
-__global__ void noise_wgrad_kernel(const float* __restrict__ dx, const float* __restrict__ har, int B, int T, int C,
-                                   int k, int stride, int pad, int T_full, int rows_per_part, float* __restrict__ part) {
-  const long long r0 = (long long)blockIdx.x * rows_per_part;
-  const long long nrows = (long long)B * T;
-  const int nout = C * k;
-  for (int o = threadIdx.x; o < nout; o += blockDim.x) {
-    const int c = o / k, tap = o % k;
-    float s = 0.f;
-    for (long long r = r0; r < r0 + rows_per_part && r < nrows; ++r) {
-      const int b = (int)(r / T), j = (int)(r % T);
-      const int t = j * stride - pad + tap;
-      if (t >= 0 && t < T_full) s += dx[r * C + c] * har[(size_t)b * T_full + t];
-    }
-    part[(size_t)blockIdx.x * nout + o] = s;
-  }
-}
-
-int noise_backward_parts(int B, int T, int rows_per_part) {
-  return (int)(((long long)B * T + rows_per_part - 1) / rows_per_part);
-}
-
-void noise_backward(const float* dx, const float* har, const float* w, int B, int T, int C, int k, int stride, int pad,
-                    int T_full, float* d_har, int accumulate_dhar, float* wpart, int rows_per_part, cudaStream_t st) {
-  const long long n = (long long)B * T_full;
-  noise_dhar_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(dx, w, B, T, C, k, stride, pad, T_full, d_har,
-                                                                  accumulate_dhar);
-  const int parts = noise_backward_parts(B, T, rows_per_part);
-  noise_wgrad_kernel<<<parts, 256, 0, st>>>(dx, har, B, T, C, k, stride, pad, T_full, rows_per_part, wpart);
-}
-
-void noise_wgrad_reduce(const float* wpart, int nparts, int C, int k, float* dW, cudaStream_t st) {
-  rows_reduce(wpart, nparts, C * k, dW, 0, st);
-}
-
-// =============================================================================================
-// conv_post (C -> 1, k taps, pad k/2) + tanh
-// =============================================================================================
-__global__ void post_forward_kernel(const bf16* __restrict__ hi, const bf16* __restrict__ lo,
-                                    const float* __restrict__ W, int B, int T, int C, int k, float* __restrict__ audio) {
-  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= (long long)B * T) return;
-  const int b = (int)(i / T), t = (int)(i % T);
-  const int pad = k / 2;
-  float s = 0.f;
-  for (int tap = 0; tap < k; ++tap) {
-    const int r = t - pad + tap;
-    if (r < 0 || r >= T) continue;
-    const size_t base = ((size_t)b * T + r) * C;
-    for (int c = 0; c < C; ++c)
-      s += (__bfloat162float(hi[base + c]) + __bfloat162float(lo[base + c])) * W[(size_t)c * k + tap];
-  }
-  audio[i] = tanhf(s);
-}
-
-void post_forward(const bf16* a_hi, const bf16* a_lo, const float* W, int B, int T, int C, int k, float* audio,
-                  cudaStream_t st) {
-  const long long n = (long long)B * T;
-  post_forward_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(a_hi, a_lo, W, B, T, C, k, audio);
-}
-
-constexpr int kPostRows = 64;
-
-int post_backward_blocks(int B, int T) { return (int)(((long long)B * T + kPostRows - 1) / kPostRows); }
-
-__global__ void __launch_bounds__(256) post_backward_kernel(PostBwdArgs a) {
-  // lane = channel (C == 32), 8 warps x 8 rows each
-  __shared__ float red[8][32 * 9];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int c = lane;
-  const int k = a.k, pad = k / 2;
-  const long long nrows = (long long)a.B * a.T;
-  float cs = 0.f, as = 0.f, dw[16];
-  for (int q = 0; q < k; ++q) dw[q] = 0.f;
-  for (int rr = warp; rr < kPostRows; rr += 8) {
-    const long long row = (long long)blockIdx.x * kPostRows + rr;
-    if (row >= nrows) break;
-    const int b = (int)(row / a.T), t = (int)(row % a.T);
-    float dpre[16];
-    for (int q = 0; q < k; ++q) {
-      const int tt = t + pad - q;  // d_pre at t + pad - tap feeds input row t through tap q
-      float d = 0.f;
-      if (tt >= 0 && tt < a.T) {
-        const float y = a.audio[(size_t)b * a.T + tt];
-        d = a.dy[(size_t)b * a.T + tt] * (1.f - y * y);
-      }
-      dpre[q] = d;
-    }
-    float da = 0.f;
-    for (int q = 0; q < k; ++q) da += dpre[q] * a.W[(size_t)c * k + q];
-    const size_t off = (size_t)row * a.C + c;
-    const float xin = __bfloat162float(a.a_hi[off]) + __bfloat162float(a.a_lo[off]);
-    for (int q = 0; q < k; ++q) dw[q] += xin * dpre[q];
-    const float x = __bfloat162float(a.mask_src[off]);
-    float deriv;
-    if (a.act_kind == 1) {
-      const float al = a.alpha[c];
-      float sn, csn;
-      sincosf(al * x, &sn, &csn);
-      const float s2 = 2.f * sn * csn;
-      as += da * (x * s2 / al - sn * sn / (al * al));
-      deriv = 1.f + s2;
-    } else {
-      deriv = x > 0.f ? 1.f : a.slope;
-    }
-    const float ds = da * deriv * a.scale;
-    a.d_stage[off] = ds;
-    a.d_stage_bf[off] = __float2bfloat16_rn(ds);
-    cs += ds;
-  }
-  red[warp][c] = cs;
-  red[warp][32 + c] = as;
-  for (int q = 0; q < k; ++q) red[warp][64 + q * 32 + c] = dw[q];
-  __syncthreads();
-  const int nval = 64 + k * 32;
-  for (int o = threadIdx.x; o < nval; o += blockDim.x) {
-    float s = 0.f;
-    for (int w = 0; w < 8; ++w) s += red[w][o];
-    if (o < 32) a.colsum_part[(size_t)blockIdx.x * a.C + o] = s;
-    else if (o < 64) {
-      if (a.alpha_part) a.alpha_part[(size_t)blockIdx.x * a.C + (o - 32)] = s;
-    } else {
-      const int q = (o - 64) / 32, cc = (o - 64) % 32;
-      a.w_part[(size_t)blockIdx.x * (a.C * k) + (size_t)cc * k + q] = s;
-    }
-  }
-}
-
-void post_backward(const PostBwdArgs& a, cudaStream_t st) {
-  post_backward_kernel<<<post_backward_blocks(a.B, a.T), 256, 0, st>>>(a);
 }
 
 }  // namespace wb

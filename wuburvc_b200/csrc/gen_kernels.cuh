@@ -60,10 +60,13 @@ void nsf_backward(const float* d_har, const float* har, const float* sw, int n, 
                   float* dlin_w, float* dlin_b, cudaStream_t st);
 
 // ---- noise convs + activation of the stage input --------------------------------------------
+// w [C][k] -> wt [k][C] (noise-conv weights, read coalesced by the kernels below)
+void transpose_ck(const float* w, int C, int k, float* wt, cudaStream_t st);
+
 struct NoiseActArgs {
   float* x;               // [B][T][C] ups output -> stage input (in place)
   const float* har;       // [B][T_full] or null (no source)
-  const float* w;         // [C][k]
+  const float* w;         // [k][C] (transposed)
   const float* bias;      // [C]
   int B, T, C, k, stride, pad, T_full;
   int act_kind;           // 0 lrelu 1 snake
@@ -77,9 +80,11 @@ struct NoiseActArgs {
 void noise_add_act(const NoiseActArgs& a, cudaStream_t st);
 
 // backward of the noise conv: d_har[b][t] += ..., weight-gradient partials
-void noise_backward(const float* dx, const float* har, const float* w, int B, int T, int C, int k, int stride, int pad,
-                    int T_full, float* d_har, int accumulate_dhar, float* wpart, int rows_per_part, cudaStream_t st);
-int noise_backward_parts(int B, int T, int rows_per_part);
+//   wt [k][C] transposed weights; wpart [noise_backward_parts][C][k]
+void noise_backward(const float* dx, const float* har, const float* wt, int B, int T, int C, int k, int stride, int pad,
+                    int T_full, float* d_har, int accumulate_dhar, float* wpart, cudaStream_t st);
+int noise_rows_per_part(int k);
+int noise_backward_parts(int B, int T, int k);
 void noise_wgrad_reduce(const float* wpart, int nparts, int C, int k, float* dW, cudaStream_t st);
 
 // ---- conv_post ------------------------------------------------------------------------------

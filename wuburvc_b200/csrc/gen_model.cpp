@@ -92,24 +92,33 @@ bool make_weights(Gen& m, ConvWeights& w, const std::string& base, bool resblock
   return true;
 }
 
-bool make_wgrad_job(Gen& m, WgradJob& j, int layout, int c_out, int k, float* dW) {
+bool make_wgrad_job(Gen& m, WgradJob& j, int layout, int c_out, int k, const ConvWeights& w) {
   j.layout = layout;
   j.c_out = c_out;
   j.k = k;
-  j.dW = dW;
-  std::vector<int> tab(j.L.row_tap);
-  tab.insert(tab.end(), j.L.row_oc.begin(), j.L.row_oc.end());
-  if (!dalloc(m, &j.tab, tab.size())) return false;
-  CK(cudaMemcpy(j.tab, tab.data(), tab.size() * sizeof(int), cudaMemcpyHostToDevice));
+  j.w = &w;
+  j.dW = w.dW;
+  // inverse map (oc, tap) -> partial row, for the fused split-K reduction
+  std::vector<int> inv((size_t)c_out * k, -1);
+  for (size_t r = 0; r < j.L.row_tap.size(); ++r)
+    if (j.L.row_tap[r] >= 0) inv[(size_t)j.L.row_oc[r] * k + j.L.row_tap[r]] = (int)r;
+  for (int x : inv)
+    if (x < 0) return false;
+  if (!dalloc(m, &j.inv, inv.size())) return false;
+  CK(cudaMemcpy(j.inv, inv.data(), inv.size() * sizeof(int), cudaMemcpyHostToDevice));
   return true;
 }
 
+// weight gradient: split-K partials on the tensor cores, then one fused reduction straight into
+// the flat gradient buffer (with the weight-norm backward under weight norm)
 bool run_wgrad(Gen& m, WgradJob& j) {
   j.L.p.part = m.wg_part;
   CK(j.L.run(m.stream));
+  const ConvWeights& w = *j.w;
   const int rows = j.L.p.n_mtiles * 128;
-  wgrad_reduce(m.wg_part, j.L.splits, rows, j.L.p.n_total, j.tab, j.tab + rows, j.layout, j.c_out, j.k, j.dW, 0,
-               m.stream);
+  const bool wn = w.pg >= 0;
+  wgrad_finish(m.wg_part, j.L.splits, rows, j.L.p.n_total, j.inv, j.layout, j.c_out, j.k, w.rows, m.P(w.pv),
+               wn ? m.P(w.pg) : nullptr, w.norm, m.G(w.pv), wn ? m.G(w.pg) : nullptr, m.stream);
   return true;
 }
 
@@ -118,9 +127,6 @@ void prep(Gen& m, const ConvWeights& w) {
               w.fwd_lo, w.dg, w.norm, m.stream);
 }
 
-void finish_weight_grad(Gen& m, const ConvWeights& w) {
-  if (w.pg >= 0) wn_backward(w.dW, m.P(w.pv), m.P(w.pg), w.norm, w.rows, w.cols * w.k, m.G(w.pv), m.G(w.pg), m.stream);
-}
 
 }  // namespace
 
@@ -244,7 +250,8 @@ bool gen_setup(Gen& m) {
         if (!dalloc(m, &k.pp[q], n) || !dalloc(m, &k.pp_bf[q], n)) return false;
     }
     if (c.nsf) {
-      s.noise_parts = noise_backward_parts(B, s.T, 64);
+      s.noise_parts = noise_backward_parts(B, s.T, s.kn);
+      if (!dalloc(m, &s.noise_wt, (size_t)s.C * s.kn)) return false;
       if (!dalloc(m, &s.noise_wpart, (size_t)s.noise_parts * s.C * s.kn)) return false;
     }
   }
@@ -294,7 +301,7 @@ bool gen_setup(Gen& m) {
           e.act_alpha = alpha_ptr(m, "dec.resblocks." + R + ".alpha2." + P);
           e.pre_hi = k.a2_pre[cp];
           ConvGeom g{B, s.T, s.T, s.C, s.C, kk, dil, dil * (kk - 1) / 2};
-          if (!plan_conv(k.f1[cp], g, k.a1_hi[cp], k.a1_lo[cp], k.w1[cp].fwd_hi, k.w1[cp].fwd_lo, 1, e, m.err))
+          if (!plan_conv_any(k.f1[cp], g, k.a1_hi[cp], k.a1_lo[cp], k.w1[cp].fwd_hi, k.w1[cp].fwd_lo, 1, e, m.err))
             return false;
         }
         {  // conv2: bias + residual -> next pair input (+act) or stage sum
@@ -321,7 +328,7 @@ bool gen_setup(Gen& m) {
             }
           }
           ConvGeom g{B, s.T, s.T, s.C, s.C, kk, 1, (kk - 1) / 2};
-          if (!plan_conv(k.f2[cp], g, k.a2_hi[cp], k.a2_lo[cp], k.w2[cp].fwd_hi, k.w2[cp].fwd_lo, 1, e, m.err))
+          if (!plan_conv_any(k.f2[cp], g, k.a2_hi[cp], k.a2_lo[cp], k.w2[cp].fwd_hi, k.w2[cp].fwd_lo, 1, e, m.err))
             return false;
         }
       }
@@ -358,13 +365,13 @@ bool gen_setup(Gen& m) {
           e.out_bf16 = k.d_c1;
           e.colsum = k.cs_dc1[cp];
           ConvGeom g{B, s.T, s.T, s.C, s.C, kk, 1, (kk - 1) / 2};
-          if (!plan_conv(k.d2[cp], g, dp_out_b, nullptr, k.w2[cp].dg, nullptr, 0, e, m.err)) return false;
+          if (!plan_conv_any(k.d2[cp], g, dp_out_b, nullptr, k.w2[cp].dg, nullptr, 0, e, m.err)) return false;
         }
         {  // conv2 wgrad
           ConvGeom g{B, s.T, s.T, s.C, s.C, kk, 1, (kk - 1) / 2};
           if (!plan_wgrad(k.g2[cp].L, g, dp_out_b, k.a2_hi[cp], nullptr, ~size_t(0), kWgradCtas, m.err)) return false;
           m.wg_part_cap = std::max(m.wg_part_cap, wgrad_part_floats(k.g2[cp].L));
-          if (!make_wgrad_job(m, k.g2[cp], 0, s.C, kk, k.w2[cp].dW)) return false;
+          if (!make_wgrad_job(m, k.g2[cp], 0, s.C, kk, k.w2[cp])) return false;
         }
         {  // conv1 dgrad -> gradient wrt the pair input
           Epi e = epi0(c.lrelu_slope);
@@ -383,13 +390,13 @@ bool gen_setup(Gen& m) {
             e.out_bf16 = (j == m.nk - 1) ? s.d_x_bf : nullptr;
           }
           ConvGeom g{B, s.T, s.T, s.C, s.C, kk, dil, dil * (kk - 1) / 2};
-          if (!plan_conv(k.d1[cp], g, k.d_c1, nullptr, k.w1[cp].dg, nullptr, 0, e, m.err)) return false;
+          if (!plan_conv_any(k.d1[cp], g, k.d_c1, nullptr, k.w1[cp].dg, nullptr, 0, e, m.err)) return false;
         }
         {  // conv1 wgrad
           ConvGeom g{B, s.T, s.T, s.C, s.C, kk, dil, dil * (kk - 1) / 2};
           if (!plan_wgrad(k.g1[cp].L, g, k.d_c1, k.a1_hi[cp], nullptr, ~size_t(0), kWgradCtas, m.err)) return false;
           m.wg_part_cap = std::max(m.wg_part_cap, wgrad_part_floats(k.g1[cp].L));
-          if (!make_wgrad_job(m, k.g1[cp], 0, s.C, kk, k.w1[cp].dW)) return false;
+          if (!make_wgrad_job(m, k.g1[cp], 0, s.C, kk, k.w1[cp])) return false;
         }
       }
     }
@@ -426,16 +433,18 @@ bool gen_setup(Gen& m) {
                             kWgradCtas, m.err))
         return false;
       m.wg_part_cap = std::max(m.wg_part_cap, wgrad_part_floats(s.up_wg.L));
-      if (!make_wgrad_job(m, s.up_wg, 1, s.C, s.ku, s.wu.dW)) return false;
+      if (!make_wgrad_job(m, s.up_wg, 1, s.C, s.ku, s.wu)) return false;
     }
   }
   {  // conv_pre wgrad
     ConvGeom g{B, m.F, m.F, c.in_channels, C0, 7, 1, 3};
     if (!plan_wgrad(m.pre_wg.L, g, m.d_pre_bf, m.z_hi, nullptr, ~size_t(0), kWgradCtas, m.err)) return false;
     m.wg_part_cap = std::max(m.wg_part_cap, wgrad_part_floats(m.pre_wg.L));
-    if (!make_wgrad_job(m, m.pre_wg, 0, C0, 7, m.wpre.dW)) return false;
+    if (!make_wgrad_job(m, m.pre_wg, 0, C0, 7, m.wpre)) return false;
   }
   if (!dalloc(m, &m.wg_part, m.wg_part_cap)) return false;
+  m.red_scratch_n = (size_t)4 << 20;
+  if (!dalloc(m, &m.red_scratch, m.red_scratch_n)) return false;
   return true;
 }
 
@@ -446,6 +455,7 @@ bool gen_forward(Gen& m) {
   const WubuB200GenConfig& c = m.cfg;
   const bool snake = c.activation == 1;
   cudaStream_t st = m.stream;
+  set_reduce_scratch(m.red_scratch, m.red_scratch_n);
   // weights for this step
   prep(m, m.wpre);
   for (int L = 0; L < 4; ++L) {
@@ -488,7 +498,8 @@ bool gen_forward(Gen& m) {
     na.x = s.x_in;
     na.har = c.nsf ? m.har : nullptr;
     if (c.nsf) {
-      na.w = m.P(m.pidx("dec.noise_convs." + std::to_string(L) + ".weight"));
+      transpose_ck(m.P(m.pidx("dec.noise_convs." + std::to_string(L) + ".weight")), s.C, s.kn, s.noise_wt, st);
+      na.w = s.noise_wt;
       na.bias = m.P(m.pidx("dec.noise_convs." + std::to_string(L) + ".bias"));
     }
     na.B = m.B;
@@ -527,6 +538,7 @@ bool gen_backward(Gen& m) {
   const bool snake = c.activation == 1;
   cudaStream_t st = m.stream;
   const int B = m.B;
+  set_reduce_scratch(m.red_scratch, m.red_scratch_n);
   {  // conv_post + tanh backward -> gradient wrt stage 3 output (/nk per stack)
     StageBufs& s3 = m.sg[3];
     PostBwdArgs a{};
@@ -565,32 +577,29 @@ bool gen_backward(Gen& m) {
         CK(k.d1[cp].run(st));
         if (!run_wgrad(m, k.g1[cp])) return false;
         // biases: conv1 <- colsum(d_c1); conv2 <- colsum(grad wrt pair output)
-        colsum_reduce(k.cs_dc1[cp], k.tiles, s.C, m.G(k.w1[cp].pb), 0, st);
+        colsum_reduce(k.cs_dc1[cp], k.d2[cp].partials(), s.C, m.G(k.w1[cp].pb), 0, st);
         if (cp == m.nd - 1)
           colsum_reduce(s.cs_ds, s.cs_ds_tiles, s.C, m.G(k.w2[cp].pb), 0, st);
         else
-          colsum_reduce(k.cs_dp[cp + 1], k.tiles, s.C, m.G(k.w2[cp].pb), 0, st);
+          colsum_reduce(k.cs_dp[cp + 1], k.d1[cp + 1].partials(), s.C, m.G(k.w2[cp].pb), 0, st);
         if (snake) {
-          colsum_reduce(k.ap1[cp], k.tiles, s.C, alpha_grad(m, "dec.resblocks." + R + ".alpha1." + P), 0, st);
-          colsum_reduce(k.ap2[cp], k.tiles, s.C, alpha_grad(m, "dec.resblocks." + R + ".alpha2." + P), 0, st);
+          colsum_reduce(k.ap1[cp], k.d1[cp].partials(), s.C, alpha_grad(m, "dec.resblocks." + R + ".alpha1." + P), 0, st);
+          colsum_reduce(k.ap2[cp], k.d2[cp].partials(), s.C, alpha_grad(m, "dec.resblocks." + R + ".alpha2." + P), 0, st);
         }
-        finish_weight_grad(m, k.w1[cp]);
-        finish_weight_grad(m, k.w2[cp]);
       }
     }
     // stage input gradient d_x: ups bias, noise conv, ups dgrad / wgrad
     const int ub = m.pidx("dec.ups." + std::to_string(L) + ".bias");
-    for (int j = 0; j < m.nk; ++j) colsum_reduce(s.st[j].cs_dp[0], s.st[j].tiles, s.C, m.G(ub), j > 0, st);
+    for (int j = 0; j < m.nk; ++j) colsum_reduce(s.st[j].cs_dp[0], s.st[j].d1[0].partials(), s.C, m.G(ub), j > 0, st);
     if (c.nsf) {
       const int nw = m.pidx("dec.noise_convs." + std::to_string(L) + ".weight");
       const int nb = m.pidx("dec.noise_convs." + std::to_string(L) + ".bias");
       CK(cudaMemcpyAsync(m.G(nb), m.G(ub), sizeof(float) * s.C, cudaMemcpyDeviceToDevice, st));
-      noise_backward(s.d_x, m.har, m.P(nw), B, s.T, s.C, s.kn, s.sn, s.pn, m.T, m.d_har, L < 3, s.noise_wpart, 64, st);
+      noise_backward(s.d_x, m.har, s.noise_wt, B, s.T, s.C, s.kn, s.sn, s.pn, m.T, m.d_har, L < 3, s.noise_wpart, st);
       noise_wgrad_reduce(s.noise_wpart, s.noise_parts, s.C, s.kn, m.G(nw), st);
     }
     CK(s.up_dg.run(st));
     if (!run_wgrad(m, s.up_wg)) return false;
-    finish_weight_grad(m, s.wu);
     if (snake)
       colsum_reduce(s.ap_up, s.ap_up_tiles, s.Cin, alpha_grad(m, "dec.ups_act." + std::to_string(L) + ".alpha"), 0, st);
     if (comm_bucket_ready(m, 3 - L)) return false;  // this stage's gradients are final

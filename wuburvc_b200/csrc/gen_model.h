@@ -24,7 +24,8 @@ struct ConvWeights {
 
 struct WgradJob {
   WgradLaunch L;
-  int* tab = nullptr;  // device [row_tap | row_oc]
+  int* inv = nullptr;  // device [c_out][k] -> partial row
+  const ConvWeights* w = nullptr;
   int layout = 0;      // 0 conv, 1 convT
   int c_out = 0, k = 0;
   float* dW = nullptr;
@@ -42,7 +43,7 @@ struct StackBufs {
   float *cs_dc1[3] = {}, *cs_dp[3] = {}, *ap1[3] = {}, *ap2[3] = {};
   int tiles = 0;
   ConvWeights w1[3], w2[3];
-  ConvLaunch f1[3], f2[3], d2[3], d1[3];
+  ConvOp f1[3], f2[3], d2[3], d1[3];
   WgradJob g1[3], g2[3];
 };
 
@@ -62,6 +63,7 @@ struct StageBufs {
   float* ap_up = nullptr;  // snake alpha partials of the activation feeding ups L (from up_dg)
   int ap_up_tiles = 0;
   float* noise_wpart = nullptr;
+  float* noise_wt = nullptr;  // noise-conv weights transposed to [k][C]
   int noise_parts = 0;
   ConvWeights wu;
   ConvLaunch up_fwd, up_dg;
@@ -107,6 +109,8 @@ struct Gen {
   StageBufs sg[4];
   float* wg_part = nullptr;  // shared split-K scratch for the weight gradients
   size_t wg_part_cap = 0;
+  float* red_scratch = nullptr;  // two-pass deterministic reductions
+  size_t red_scratch_n = 0;
 
   // CUDA graph of the resident-input step
   cudaGraphExec_t graph = nullptr;

@@ -1,74 +1,7 @@
 // tc_conv.cu — tcgen05/TMEM implicit-GEMM kernels (sm_100a).  See tc_conv.cuh.
-#include "tc_conv.cuh"
+#include "tc_epilogue.cuh"
 
 namespace wb {
-
-// ---------------------------------------------------------------------------------------------
-// Epilogue helpers
-// ---------------------------------------------------------------------------------------------
-
-// Warp transpose-reduction: on return v[0] of lane l holds sum over lanes of the input v[l].
-WB_DEV float warp_colsum32(float* v, int lane) {
-#pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) {
-    const bool upper = (lane & off) != 0;
-#pragma unroll
-    for (int i = 0; i < off; ++i) {
-      float send = upper ? v[i] : v[i + off];
-      float keep = upper ? v[i + off] : v[i];
-      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
-    }
-  }
-  return v[0];
-}
-
-WB_DEV void load_bf16x32(const bf16* p, float* out) {
-  const uint4* q = reinterpret_cast<const uint4*>(p);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    uint4 u = q[i];
-    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float2 f = __bfloat1622float2(h[j]);
-      out[i * 8 + j * 2] = f.x;
-      out[i * 8 + j * 2 + 1] = f.y;
-    }
-  }
-}
-
-WB_DEV void store_bf16x32(bf16* p, const bf16* v) {
-  uint4* q = reinterpret_cast<uint4*>(p);
-  const uint4* s = reinterpret_cast<const uint4*>(v);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) q[i] = s[i];
-}
-
-WB_DEV void load_f32x32(const float* p, float* out) {
-  const float4* q = reinterpret_cast<const float4*>(p);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    float4 f = q[i];
-    out[i * 4] = f.x; out[i * 4 + 1] = f.y; out[i * 4 + 2] = f.z; out[i * 4 + 3] = f.w;
-  }
-}
-
-WB_DEV void store_f32x32(float* p, const float* v) {
-  float4* q = reinterpret_cast<float4*>(p);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) q[i] = make_float4(v[i * 4], v[i * 4 + 1], v[i * 4 + 2], v[i * 4 + 3]);
-}
-
-// Sums `v` (one row per thread, 32 columns) over the 128 rows of the CTA's four epilogue warps
-// and writes the 32 column sums to dst[0..31] (thread 0..31 of warp 0 store).
-WB_DEV void cta_colsum32(float* v, float* red /*smem [4][32]*/, int warp, int lane, float* dst,
-                         int epi_bar_threads) {
-  float s = warp_colsum32(v, lane);
-  red[warp * 32 + lane] = s;
-  asm volatile("bar.sync 1, %0;" ::"r"(epi_bar_threads));
-  if (warp == 0) dst[lane] = red[lane] + red[32 + lane] + red[64 + lane] + red[96 + lane];
-  asm volatile("bar.sync 1, %0;" ::"r"(epi_bar_threads));
-}
 
 // ---------------------------------------------------------------------------------------------
 // tc_conv kernel
@@ -167,100 +100,17 @@ __global__ void __launch_bounds__(192, 1)
     // ---------------- epilogue (warps 0..3 <-> TMEM lanes 0..127) ----------------
     const bool ok = mbar_wait(accf, 0, p.err, ERR_WAIT_ACC);
     tc_fence_after();
-    const Epi& e = p.epi;
     const int q = q0 + warp * 32 + lane;
     const int orow = q * p.out_stride + p.out_off[phase];
     const bool valid = ok && q < p.m_rows && orow >= 0 && orow < p.t_out;
     const size_t row_off = ((size_t)item * p.t_out + (valid ? orow : 0)) * p.n_total + n0;
     const size_t part_row = (size_t)(blockIdx.z * gridDim.x + blockIdx.x) * p.n_total + n0;
+    const float* ra = p.epi.rowadd ? p.epi.rowadd + (size_t)item * p.n_total + n0 : nullptr;
     for (int c0 = 0; c0 < N; c0 += 32) {
       float v[32];
       tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
       if (!ok) continue;
-      const size_t off = row_off + c0;
-      if (e.mask_src) {
-        float x[32];
-        if (valid) load_bf16x32(e.mask_src + off, x);
-        else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) x[i] = 0.f;
-        }
-        if (e.act_kind == 1) {
-          float ga[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float a = e.mask_alpha[n0 + c0 + i];
-            float sn, cs;
-            sincosf(a * x[i], &sn, &cs);
-            const float s2 = 2.f * sn * cs;                       // sin(2 a x)
-            ga[i] = valid ? v[i] * (x[i] * s2 / a - sn * sn / (a * a)) : 0.f;
-            v[i] *= 1.f + s2;
-          }
-          if (e.alpha_part) {
-            float tmp[32];
-            cta_colsum32(ga, red, warp, lane, tmp, 128);
-            if (warp == 0) e.alpha_part[part_row + c0 + lane] = tmp[lane];
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] *= (x[i] > 0.f) ? 1.f : e.slope;
-        }
-      }
-      if (e.bias) {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] += e.bias[n0 + c0 + i];
-      }
-      if (e.rowadd) {
-        const float* ra = e.rowadd + (size_t)item * p.n_total + n0 + c0;
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] += ra[i];
-      }
-      if (e.res && valid) {
-        float r[32];
-        load_f32x32(e.res + off, r);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] += r[i];
-      }
-#pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] *= e.scale;
-      if (e.colsum) {
-        float cv[32], tmp[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) cv[i] = valid ? v[i] : 0.f;
-        cta_colsum32(cv, red, warp, lane, tmp, 128);
-        if (warp == 0) e.colsum[part_row + c0 + lane] = tmp[lane];
-      }
-      if (!valid) continue;
-      if (e.accumulate) {
-        float r[32];
-        load_f32x32(e.out_f32 + off, r);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] += r[i];
-      }
-      if (e.out_f32) store_f32x32(e.out_f32 + off, v);
-      if (e.out_bf16) {
-        __align__(16) bf16 b[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) b[i] = __float2bfloat16_rn(v[i]);
-        store_bf16x32(e.out_bf16 + off, b);
-      }
-      if (e.pre_hi) {
-        __align__(16) bf16 b[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) b[i] = __float2bfloat16_rn(v[i]);
-        store_bf16x32(e.pre_hi + off, b);
-      }
-      if (e.act_hi) {
-        __align__(16) bf16 h[32];
-        __align__(16) bf16 l[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float a = (e.act_kind == 1) ? snake(v[i], e.act_alpha[n0 + c0 + i]) : lrelu(v[i], e.slope);
-          split_bf16(a, h[i], l[i]);
-        }
-        store_bf16x32(e.act_hi + off, h);
-        if (e.act_lo) store_bf16x32(e.act_lo + off, l);
-      }
+      epi_chunk(p.epi, v, valid, row_off + c0, n0 + c0, part_row + c0, ra ? ra + c0 : nullptr, warp, lane, red);
     }
   }
   tc_fence_before();
@@ -383,6 +233,8 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 // launch wrappers (host).  The dynamic shared-memory limit is raised once, before any capture.
+void tc_conv2_set_smem_limit(int lim);  // tc_conv2.cu
+
 static void raise_smem_limits() {
   static bool done = false;
   if (done) return;
@@ -392,9 +244,14 @@ static void raise_smem_limits() {
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
   const int lim = optin - 1024;
-  cudaFuncSetAttribute(tc_conv_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
-  cudaFuncSetAttribute(tc_conv_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
-  cudaFuncSetAttribute(tc_wgrad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+  cudaError_t e[3];
+  e[0] = cudaFuncSetAttribute(tc_conv_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+  e[1] = cudaFuncSetAttribute(tc_conv_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+  e[2] = cudaFuncSetAttribute(tc_wgrad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+  for (int i = 0; i < 3; ++i)
+    if (e[i] != cudaSuccess) fprintf(stderr, "wuburvc_b200: smem limit %d: %s\n", i, cudaGetErrorString(e[i]));
+  tc_conv2_set_smem_limit(lim);
+  cudaGetLastError();
 }
 
 void tc_kernels_init() { raise_smem_limits(); }

@@ -73,6 +73,37 @@ struct TcConvParams {
 };
 
 // ---------------------------------------------------------------------------------------------
+// persistent stride-1 conv kernel with halo reuse (tc_conv2)
+//   Each CTA loops over 128-row output tiles.  Per input-channel chunk it loads ONE halo tile
+//   (rows q0+sh_min .. q0+127+sh_max) in the no-swizzle core-matrix layout, so every tap's A operand
+//   is the same tile viewed at a 16-byte row offset; weight slices stream per (chunk, tap).  Two TMEM
+//   accumulators let the epilogue of one tile overlap the MMAs of the next.
+// ---------------------------------------------------------------------------------------------
+constexpr int kMaxTaps2 = 16;
+
+struct TcConv2Maps {
+  CUtensorMap a_hi, a_lo;   // no-swizzle (C_in, T, B) views with an 8-channel x R-row box
+  CUtensorMap w_hi, w_lo;   // 3-D (C_in, C_out, taps), 128B/64B swizzle
+};
+
+struct TcConv2Params {
+  int ntiles, tiles_per_item, t_rows;
+  int n;                    // C_out (GEMM N, <= 256), also the output channel pitch
+  int n_chunks;             // C_in / KC
+  int split;
+  int ntaps;
+  int halo_start;           // row offset of the halo tile relative to the tile's first output row
+  int halo_rows;            // 128 + taps span
+  short tap_off[kMaxTaps2]; // row offset of each tap inside the halo tile
+  short tap_w[kMaxTaps2];   // weight tap index
+  int a_stages, w_stages;
+  uint32_t a_sub_bytes;     // one A (hi or lo) halo tile, 1024-aligned
+  int tmem_cols;            // 2 accumulators
+  Epi epi;
+  int* err;
+};
+
+// ---------------------------------------------------------------------------------------------
 // weight-gradient kernel
 // ---------------------------------------------------------------------------------------------
 struct TcWgMaps {
