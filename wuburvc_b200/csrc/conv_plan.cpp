@@ -172,9 +172,13 @@ bool plan_conv2(Conv2Launch& L, const ConvGeom& g, const void* x_hi, const void*
     p.tap_w[t] = (short)t;
   }
   p.tiles_per_item = (g.T_out + 127) / 128;
-  p.ntiles = g.B * p.tiles_per_item;
+  const int mtiles = g.B * p.tiles_per_item;
+  // split N in two when the row tiles alone cannot fill the SMs
+  p.n_tiles = (mtiles < sm_count() && g.C_out >= 128) ? 2 : 1;
+  p.n = g.C_out / p.n_tiles;
+  p.n_total = g.C_out;
+  p.ntiles = mtiles * p.n_tiles;
   p.t_rows = g.T_out;
-  p.n = g.C_out;
   p.split = split;
   p.epi = epi;
   p.err = err;
@@ -182,7 +186,7 @@ bool plan_conv2(Conv2Launch& L, const ConvGeom& g, const void* x_hi, const void*
   int kc = (g.C_in % 64 == 0) ? 64 : 32;
   for (;;) {
     const size_t a_sub = ((size_t)R * kc * 2 + 1023) / 1024 * 1024;
-    const size_t a_stage = nA * a_sub, w_stage = (size_t)nA * g.C_out * kc * 2;
+    const size_t a_stage = nA * a_sub, w_stage = (size_t)nA * p.n * kc * 2;
     p.a_stages = 2;
     const long long room = (long long)kSmemBudget - 2048 - (long long)p.a_stages * a_stage;
     p.w_stages = room > 0 ? (int)std::min<long long>(8, room / (long long)w_stage) : 0;
@@ -196,17 +200,17 @@ bool plan_conv2(Conv2Launch& L, const ConvGeom& g, const void* x_hi, const void*
   }
   L.kc = kc;
   p.n_chunks = g.C_in / kc;
-  p.tmem_cols = pow2_cols(2 * g.C_out);
+  p.tmem_cols = pow2_cols(2 * p.n);
   if (p.tmem_cols > 512) return false;
   if (!make_map_bf16_cm(&L.maps.a_hi, x_hi, g.T_in, g.C_in, g.B, R)) return false;
   if (split && !make_map_bf16_cm(&L.maps.a_lo, x_lo, g.T_in, g.C_in, g.B, R)) return false;
   const uint64_t wr = (uint64_t)g.C_in * 2, wt = wr * g.C_out;
-  if (!make_map_bf16_3d(&L.maps.w_hi, w_hi, g.C_in, g.C_out, g.k, wr, wt, kc, g.C_out, 1)) return false;
-  if (split && !make_map_bf16_3d(&L.maps.w_lo, w_lo, g.C_in, g.C_out, g.k, wr, wt, kc, g.C_out, 1)) return false;
+  if (!make_map_bf16_3d(&L.maps.w_hi, w_hi, g.C_in, g.C_out, g.k, wr, wt, kc, p.n, 1)) return false;
+  if (split && !make_map_bf16_3d(&L.maps.w_lo, w_lo, g.C_in, g.C_out, g.k, wr, wt, kc, p.n, 1)) return false;
   int occ = (int)std::min<size_t>(2, (227 * 1024) / L.smem);
   occ = std::min(occ, 512 / p.tmem_cols);
   occ = std::max(occ, 1);
-  L.grid = std::min(p.ntiles, sm_count() * occ);
+  L.grid = std::min(p.ntiles, sm_count() * occ) / p.n_tiles * p.n_tiles;
   return true;
 }
 

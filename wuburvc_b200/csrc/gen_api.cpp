@@ -40,6 +40,26 @@ int check_err(Gen& m) {
   return WUBU_B200_OK;
 }
 
+// whole flat buffers between the reference tensor layouts and the device storage layouts
+void flat_to_internal(const ParamTable& t, const float* ref, float* dev) {
+  memset(dev, 0, sizeof(float) * (size_t)t.total);
+  for (const auto& e : t.e) to_internal(e, ref + e.off, dev + e.off);
+}
+void flat_to_reference(const ParamTable& t, const float* dev, float* ref) {
+  memset(ref, 0, sizeof(float) * (size_t)t.total);
+  for (const auto& e : t.e) to_reference(e, dev + e.off, ref + e.off);
+}
+
+int download_reference(Gen& m, const float* dsrc, float* host_flat) {
+  std::vector<float> tmp((size_t)m.table.total);
+  if (cudaMemcpyAsync(tmp.data(), dsrc, sizeof(float) * tmp.size(), cudaMemcpyDeviceToHost, m.stream) != cudaSuccess)
+    return WUBU_B200_ERR_CUDA;
+  const int rc = check_err(m);
+  if (rc) return rc;
+  flat_to_reference(m.table, tmp.data(), host_flat);
+  return 0;
+}
+
 int set_noise_stream(Gen& m, unsigned long long s) {
   // pageable source: staged before return, ordered on the model stream
   return cudaMemcpyAsync(&m.state->noise_stream, &s, sizeof(s), cudaMemcpyHostToDevice, m.stream) == cudaSuccess
@@ -131,9 +151,10 @@ WubuB200Gen* wubu_b200_gen_create(const WubuB200GenConfig* cfg, const WubuB200Tr
     delete h;
     return nullptr;
   }
-  std::vector<float> p((size_t)h->m.table.total);
+  std::vector<float> p((size_t)h->m.table.total), d(p.size());
   init_params(h->m.cfg, h->m.table, 0, p.data());
-  cudaMemcpy(h->m.params, p.data(), p.size() * sizeof(float), cudaMemcpyHostToDevice);
+  flat_to_internal(h->m.table, p.data(), d.data());
+  cudaMemcpy(h->m.params, d.data(), d.size() * sizeof(float), cudaMemcpyHostToDevice);
   return h;
 }
 
@@ -153,7 +174,9 @@ int wubu_b200_gen_set_params(WubuB200Gen* gen, const float* host_flat) {
   Gen& m = gen->m;
   cudaSetDevice(m.opt.device);
   const size_t bytes = sizeof(float) * (size_t)m.table.total;
-  if (cudaMemcpyAsync(m.params, host_flat, bytes, cudaMemcpyHostToDevice, m.stream) != cudaSuccess)
+  std::vector<float> d((size_t)m.table.total);
+  flat_to_internal(m.table, host_flat, d.data());
+  if (cudaMemcpyAsync(m.params, d.data(), bytes, cudaMemcpyHostToDevice, m.stream) != cudaSuccess)
     return WUBU_B200_ERR_CUDA;
   // a new parameter set restarts the optimiser
   cudaMemsetAsync(m.adam_m, 0, bytes, m.stream);
@@ -166,20 +189,14 @@ int wubu_b200_gen_get_params(WubuB200Gen* gen, float* host_flat) {
   if (!gen || !host_flat) return WUBU_B200_ERR_ARG;
   Gen& m = gen->m;
   cudaSetDevice(m.opt.device);
-  if (cudaMemcpyAsync(host_flat, m.params, sizeof(float) * (size_t)m.table.total, cudaMemcpyDeviceToHost, m.stream) !=
-      cudaSuccess)
-    return WUBU_B200_ERR_CUDA;
-  return check_err(m);
+  return download_reference(m, m.params, host_flat);
 }
 
 int wubu_b200_gen_get_grads(WubuB200Gen* gen, float* host_flat) {
   if (!gen || !host_flat) return WUBU_B200_ERR_ARG;
   Gen& m = gen->m;
   cudaSetDevice(m.opt.device);
-  if (cudaMemcpyAsync(host_flat, m.grads, sizeof(float) * (size_t)m.table.total, cudaMemcpyDeviceToHost, m.stream) !=
-      cudaSuccess)
-    return WUBU_B200_ERR_CUDA;
-  return check_err(m);
+  return download_reference(m, m.grads, host_flat);
 }
 
 int wubu_b200_gen_upload(WubuB200Gen* gen, const float* z, const float* f0, const float* g, const float* noise,

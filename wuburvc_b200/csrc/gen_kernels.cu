@@ -51,26 +51,35 @@ __device__ __forceinline__ float act_fwd(float x, int kind, float slope, float a
 // =============================================================================================
 // weights
 // =============================================================================================
+// Device storage of GEMM-fed weights is tap-major [k][C_out][C_in].  A weight-norm "row" is one dim-0
+// index of the reference tensor: conv r = out channel (elements (tap, in)), convT r = in channel
+// (elements (tap, out)).  Element i of row r: tap = i / cols, c = i % cols.
+__device__ __forceinline__ size_t wrow_addr(int i, int r, int rows, int cols, int is_convT) {
+  const int t = i / cols, c = i - t * cols;
+  return is_convT ? ((size_t)t * cols + c) * rows + r : ((size_t)t * rows + r) * cols + c;
+}
+
 __global__ void prep_weight_kernel(const float* __restrict__ v, const float* __restrict__ g, int rows, int cols, int k,
                                    int is_convT, int stride, bf16* __restrict__ fwd_hi, bf16* __restrict__ fwd_lo,
                                    bf16* __restrict__ dg, float* __restrict__ norm) {
   __shared__ float sh[32];
   const int r = blockIdx.x;
   const int per = cols * k;
-  const float* vr = v + (size_t)r * per;
   float scale = 1.f;
   if (g) {
     float s = 0.f;
-    for (int i = threadIdx.x; i < per; i += blockDim.x) s += vr[i] * vr[i];
+    for (int i = threadIdx.x; i < per; i += blockDim.x) {
+      const float x = v[wrow_addr(i, r, rows, cols, is_convT)];
+      s += x * x;
+    }
     s = block_sum(s, sh);
     const float n = sqrtf(s);
     scale = g[r] / n;
     if (threadIdx.x == 0 && norm) norm[r] = n;
   }
-  // phase-order position of each tap (ConvTranspose)
   for (int i = threadIdx.x; i < per; i += blockDim.x) {
-    const int c = i / k, t = i - c * k;
-    const float w = vr[i] * scale;
+    const int t = i / cols, c = i - t * cols;
+    const float w = v[wrow_addr(i, r, rows, cols, is_convT)] * scale;
     bf16 hi, lo;
     split_bf16(w, hi, lo);
     if (!is_convT) {
@@ -98,26 +107,87 @@ void prep_weight(const float* v, const float* g, int rows, int cols, int k, int 
   prep_weight_kernel<<<rows, 256, 0, st>>>(v, g, rows, cols, k, is_convT, stride, fwd_hi, fwd_lo, dg, norm);
 }
 
+__global__ void prep_weights_batched_kernel(const PrepDesc* __restrict__ descs, int ndesc) {
+  __shared__ float sh[32];
+  __shared__ int di;
+  if (threadIdx.x == 0) {
+    int lo = 0, hi = ndesc - 1;  // last descriptor with first <= blockIdx.x
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (descs[mid].first <= (int)blockIdx.x) lo = mid;
+      else hi = mid - 1;
+    }
+    di = lo;
+  }
+  __syncthreads();
+  const PrepDesc d = descs[di];
+  const int r = blockIdx.x - d.first;
+  const int rows = d.rows, cols = d.cols, k = d.k, is_convT = d.is_convT, stride = d.stride;
+  const int per = cols * k;
+  float scale = 1.f;
+  if (d.g) {
+    float s = 0.f;
+    for (int i = threadIdx.x; i < per; i += blockDim.x) {
+      const float x = d.v[wrow_addr(i, r, rows, cols, is_convT)];
+      s += x * x;
+    }
+    s = block_sum(s, sh);
+    const float n = sqrtf(s);
+    scale = d.g[r] / n;
+    if (threadIdx.x == 0 && d.norm) d.norm[r] = n;
+  }
+  for (int i = threadIdx.x; i < per; i += blockDim.x) {
+    const int t = i / cols, c = i - t * cols;
+    const float w = d.v[wrow_addr(i, r, rows, cols, is_convT)] * scale;
+    bf16 hi, lo;
+    split_bf16(w, hi, lo);
+    if (!is_convT) {
+      const size_t f = ((size_t)t * rows + r) * cols + c;
+      d.fwd_hi[f] = hi;
+      d.fwd_lo[f] = lo;
+      d.dg[((size_t)(k - 1 - t) * cols + c) * rows + r] = hi;
+    } else {
+      const int ph = t % stride, m = t / stride;
+      int n = 0;
+      for (int q = 0; q < ph; ++q) n += (k - q + stride - 1) / stride;
+      n += m;
+      const size_t f = ((size_t)n * cols + c) * rows + r;
+      d.fwd_hi[f] = hi;
+      d.fwd_lo[f] = lo;
+      d.dg[((size_t)t * rows + r) * cols + c] = hi;
+    }
+  }
+}
+
+void prep_weights_batched(const PrepDesc* descs, int ndesc, int total_rows, cudaStream_t st) {
+  prep_weights_batched_kernel<<<total_rows, 256, 0, st>>>(descs, ndesc);
+}
+
 __global__ void wn_backward_kernel(const float* __restrict__ dW, const float* __restrict__ v,
-                                   const float* __restrict__ g, const float* __restrict__ norm, int per,
-                                   float* __restrict__ dv, float* __restrict__ dgo) {
+                                   const float* __restrict__ g, const float* __restrict__ norm, int rows, int cols,
+                                   int k, int is_convT, float* __restrict__ dv, float* __restrict__ dgo) {
   __shared__ float sh[32];
   const int r = blockIdx.x;
-  const float* d = dW + (size_t)r * per;
-  const float* vr = v + (size_t)r * per;
+  const int per = cols * k;
   float s = 0.f;
-  for (int i = threadIdx.x; i < per; i += blockDim.x) s += d[i] * vr[i];
+  for (int i = threadIdx.x; i < per; i += blockDim.x) {
+    const size_t a = wrow_addr(i, r, rows, cols, is_convT);
+    s += dW[a] * v[a];
+  }
   s = block_sum(s, sh);
   const float n = norm[r];
   const float dgr = s / n;
   if (threadIdx.x == 0) dgo[r] = dgr;
   const float a = g[r] / n, b = dgr / n;
-  for (int i = threadIdx.x; i < per; i += blockDim.x) dv[(size_t)r * per + i] = a * (d[i] - b * vr[i]);
+  for (int i = threadIdx.x; i < per; i += blockDim.x) {
+    const size_t q = wrow_addr(i, r, rows, cols, is_convT);
+    dv[q] = a * (dW[q] - b * v[q]);
+  }
 }
 
-void wn_backward(const float* dW, const float* v, const float* g, const float* norm, int rows, int per_row, float* dv,
-                 float* dg, cudaStream_t st) {
-  wn_backward_kernel<<<rows, 256, 0, st>>>(dW, v, g, norm, per_row, dv, dg);
+void wn_backward(const float* dW, const float* v, const float* g, const float* norm, int rows, int cols, int k,
+                 int is_convT, float* dv, float* dg, cudaStream_t st) {
+  wn_backward_kernel<<<rows, 256, 0, st>>>(dW, v, g, norm, rows, cols, k, is_convT, dv, dg);
 }
 
 // Step state lives on the device so a captured step graph advances it by itself.

@@ -12,9 +12,22 @@ namespace wb {
 void prep_weight(const float* v, const float* g, int rows, int cols, int k, int is_convT, int stride,
                  bf16* fwd_hi, bf16* fwd_lo, bf16* dg, float* norm, cudaStream_t st);
 
+// All weight preparations of a step in one launch: block b handles dim-0 row (b - first[i]) of
+// descriptor i, where first[i] <= b < first[i] + rows.
+struct PrepDesc {
+  const float* v;
+  const float* g;
+  bf16 *fwd_hi, *fwd_lo, *dg;
+  float* norm;
+  int rows, cols, k, is_convT, stride, first;
+};
+void prep_weights_batched(const PrepDesc* descs, int ndesc, int total_rows, cudaStream_t st);
+
 // weight-norm backward: dg[r] = <dW[r], v[r]>/n[r];  dv[r] = g[r]/n[r] * (dW[r] - dg[r]/n[r] * v[r])
-void wn_backward(const float* dW, const float* v, const float* g, const float* norm, int rows, int per_row,
-                 float* dv, float* dg, cudaStream_t st);
+// over dim-0 rows of a tap-major [k][C_out][C_in] tensor (rows x cols = C_out x C_in for a conv,
+// C_in x C_out for a ConvTranspose).
+void wn_backward(const float* dW, const float* v, const float* g, const float* norm, int rows, int cols, int k,
+                 int is_convT, float* dv, float* dg, cudaStream_t st);
 
 // Per-context step state kept on the device (a captured step graph advances it itself).
 struct StepState {

@@ -115,10 +115,14 @@ bool run_wgrad(Gen& m, WgradJob& j) {
   j.L.p.part = m.wg_part;
   CK(j.L.run(m.stream));
   const ConvWeights& w = *j.w;
-  const int rows = j.L.p.n_mtiles * 128;
+  // partial rows are (tap * C_out + oc) x C_in: the first k*C_out rows of each split are exactly the
+  // tap-major device layout of the weight, so the split-K sum is a plain column reduction
+  const long long ld = (long long)j.L.p.n_mtiles * 128 * j.L.p.n_total;
+  const long long n = (long long)j.k * j.c_out * j.L.p.n_total;
   const bool wn = w.pg >= 0;
-  wgrad_finish(m.wg_part, j.L.splits, rows, j.L.p.n_total, j.inv, j.layout, j.c_out, j.k, w.rows, m.P(w.pv),
-               wn ? m.P(w.pg) : nullptr, w.norm, m.G(w.pv), wn ? m.G(w.pg) : nullptr, m.stream);
+  col_reduce_ld(m.wg_part, j.L.splits, n, ld, wn ? w.dW : m.G(w.pv), 0, m.stream);
+  if (wn)
+    wn_backward(w.dW, m.P(w.pv), m.P(w.pg), w.norm, w.rows, w.cols, w.k, w.convT, m.G(w.pv), m.G(w.pg), m.stream);
   return true;
 }
 
@@ -240,9 +244,12 @@ bool gen_setup(Gen& m) {
         }
         if (!dalloc(m, &k.a2_hi[cp], n) || !dalloc(m, &k.a2_lo[cp], n)) return false;
         if (snake && !dalloc(m, &k.a2_pre[cp], n)) return false;
-        if (!dalloc(m, &k.cs_dc1[cp], (size_t)tiles * s.C) || !dalloc(m, &k.cs_dp[cp], (size_t)tiles * s.C))
+        // column-sum partials: one row per tile (general kernel) or per CTA of the persistent kernel,
+        // which may split N in two (at most 2 * tiles rows)
+        if (!dalloc(m, &k.cs_dc1[cp], (size_t)2 * tiles * s.C) || !dalloc(m, &k.cs_dp[cp], (size_t)2 * tiles * s.C))
           return false;
-        if (snake && (!dalloc(m, &k.ap1[cp], (size_t)tiles * s.C) || !dalloc(m, &k.ap2[cp], (size_t)tiles * s.C)))
+        if (snake &&
+            (!dalloc(m, &k.ap1[cp], (size_t)2 * tiles * s.C) || !dalloc(m, &k.ap2[cp], (size_t)2 * tiles * s.C)))
           return false;
       }
       if (!dalloc(m, &k.d_c1, n)) return false;
@@ -366,6 +373,7 @@ bool gen_setup(Gen& m) {
           e.colsum = k.cs_dc1[cp];
           ConvGeom g{B, s.T, s.T, s.C, s.C, kk, 1, (kk - 1) / 2};
           if (!plan_conv_any(k.d2[cp], g, dp_out_b, nullptr, k.w2[cp].dg, nullptr, 0, e, m.err)) return false;
+          if (k.d2[cp].partials() > 2 * k.tiles) return false;  // partial buffers hold 2 * tiles rows
         }
         {  // conv2 wgrad
           ConvGeom g{B, s.T, s.T, s.C, s.C, kk, 1, (kk - 1) / 2};
@@ -391,6 +399,7 @@ bool gen_setup(Gen& m) {
           }
           ConvGeom g{B, s.T, s.T, s.C, s.C, kk, dil, dil * (kk - 1) / 2};
           if (!plan_conv_any(k.d1[cp], g, k.d_c1, nullptr, k.w1[cp].dg, nullptr, 0, e, m.err)) return false;
+          if (k.d1[cp].partials() > 2 * k.tiles) return false;
         }
         {  // conv1 wgrad
           ConvGeom g{B, s.T, s.T, s.C, s.C, kk, dil, dil * (kk - 1) / 2};
@@ -445,6 +454,40 @@ bool gen_setup(Gen& m) {
   if (!dalloc(m, &m.wg_part, m.wg_part_cap)) return false;
   m.red_scratch_n = (size_t)4 << 20;
   if (!dalloc(m, &m.red_scratch, m.red_scratch_n)) return false;
+  {  // one-launch weight preparation table
+    std::vector<PrepDesc> d;
+    int first = 0;
+    auto add = [&](const ConvWeights& w) {
+      PrepDesc p{};
+      p.v = m.P(w.pv);
+      p.g = w.pg >= 0 ? m.P(w.pg) : nullptr;
+      p.fwd_hi = w.fwd_hi;
+      p.fwd_lo = w.fwd_lo;
+      p.dg = w.dg;
+      p.norm = w.norm;
+      p.rows = w.rows;
+      p.cols = w.cols;
+      p.k = w.k;
+      p.is_convT = w.convT;
+      p.stride = w.stride;
+      p.first = first;
+      first += w.rows;
+      d.push_back(p);
+    };
+    add(m.wpre);
+    for (int L = 0; L < 4; ++L) {
+      add(m.sg[L].wu);
+      for (int j = 0; j < m.nk; ++j)
+        for (int cp = 0; cp < m.nd; ++cp) {
+          add(m.sg[L].st[j].w1[cp]);
+          add(m.sg[L].st[j].w2[cp]);
+        }
+    }
+    m.n_prep = (int)d.size();
+    m.prep_rows = first;
+    if (!dalloc(m, &m.prep_descs, d.size())) return false;
+    CK(cudaMemcpy(m.prep_descs, d.data(), d.size() * sizeof(PrepDesc), cudaMemcpyHostToDevice));
+  }
   return true;
 }
 
@@ -456,16 +499,8 @@ bool gen_forward(Gen& m) {
   const bool snake = c.activation == 1;
   cudaStream_t st = m.stream;
   set_reduce_scratch(m.red_scratch, m.red_scratch_n);
-  // weights for this step
-  prep(m, m.wpre);
-  for (int L = 0; L < 4; ++L) {
-    prep(m, m.sg[L].wu);
-    for (int j = 0; j < m.nk; ++j)
-      for (int cp = 0; cp < m.nd; ++cp) {
-        prep(m, m.sg[L].st[j].w1[cp]);
-        prep(m, m.sg[L].st[j].w2[cp]);
-      }
-  }
+  // GEMM weights for this step (weight norm + bf16 hi/lo + transposed layouts), one launch
+  prep_weights_batched(m.prep_descs, m.n_prep, m.prep_rows, st);
   pack_z(m.z, m.B, c.in_channels, m.F, m.z_hi, m.z_lo, st);
   if (c.nsf) {
     NsfArgs a{};

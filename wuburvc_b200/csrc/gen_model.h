@@ -109,6 +109,8 @@ struct Gen {
   StageBufs sg[4];
   float* wg_part = nullptr;  // shared split-K scratch for the weight gradients
   size_t wg_part_cap = 0;
+  PrepDesc* prep_descs = nullptr;  // device table: every GEMM weight's preparation, one launch
+  int n_prep = 0, prep_rows = 0;
   float* red_scratch = nullptr;  // two-pass deterministic reductions
   size_t red_scratch_n = 0;
 

@@ -40,6 +40,11 @@ ParamTable build_param_table(const WubuB200GenConfig& c) {
     p.n = (long long)d0 * d1 * d2;
     p.off = t.total;
     t.total += (p.n + 63) / 64 * 64;
+    // GEMM-fed convolutions are stored tap-major on the device
+    const bool ups = name.rfind("dec.ups.", 0) == 0;
+    const bool gemm_conv = name.rfind("dec.resblocks.", 0) == 0 || name == "dec.conv_pre.weight";
+    if (kind == P_CONVT_W || (kind == P_WN_V && ups)) p.internal = 2;
+    else if ((kind == P_CONV_W || kind == P_WN_V) && gemm_conv) p.internal = 1;
     t.e.push_back(p);
   };
   const bool snake = c.activation == 1;
@@ -94,6 +99,36 @@ ParamTable build_param_table(const WubuB200GenConfig& c) {
     add("dec.m_source.l_linear.bias", P_LIN_B, 1, 1, 1);
   }
   return t;
+}
+
+void to_internal(const ParamEntry& p, const float* ref, float* dev) {
+  const int d0 = p.shape[0], d1 = p.shape[1], k = p.shape[2];
+  if (p.internal == 0) {
+    memcpy(dev, ref, sizeof(float) * (size_t)p.n);
+  } else if (p.internal == 1) {  // ref [Co][Ci][k] -> [k][Co][Ci]
+    for (int o = 0; o < d0; ++o)
+      for (int i = 0; i < d1; ++i)
+        for (int t = 0; t < k; ++t) dev[((size_t)t * d0 + o) * d1 + i] = ref[((size_t)o * d1 + i) * k + t];
+  } else {  // ref [Ci][Co][k] -> [k][Co][Ci]
+    for (int i = 0; i < d0; ++i)
+      for (int o = 0; o < d1; ++o)
+        for (int t = 0; t < k; ++t) dev[((size_t)t * d1 + o) * d0 + i] = ref[((size_t)i * d1 + o) * k + t];
+  }
+}
+
+void to_reference(const ParamEntry& p, const float* dev, float* ref) {
+  const int d0 = p.shape[0], d1 = p.shape[1], k = p.shape[2];
+  if (p.internal == 0) {
+    memcpy(ref, dev, sizeof(float) * (size_t)p.n);
+  } else if (p.internal == 1) {
+    for (int o = 0; o < d0; ++o)
+      for (int i = 0; i < d1; ++i)
+        for (int t = 0; t < k; ++t) ref[((size_t)o * d1 + i) * k + t] = dev[((size_t)t * d0 + o) * d1 + i];
+  } else {
+    for (int i = 0; i < d0; ++i)
+      for (int o = 0; o < d1; ++o)
+        for (int t = 0; t < k; ++t) ref[((size_t)i * d1 + o) * k + t] = dev[((size_t)t * d1 + o) * d0 + i];
+  }
 }
 
 // counter-based generator shared with the device source-noise generator (splitmix64 finaliser)

@@ -14,7 +14,15 @@ struct ParamEntry {
   int kind;
   int shape[3];
   long long off, n;
+  // Device storage order of the tensor: 0 = reference layout, 1 = Conv1d weight stored tap-major
+  // [k][C_out][C_in], 2 = ConvTranspose1d weight stored tap-major [k][C_out][C_in].  Tap-major is the
+  // order the weight-gradient GEMM produces; the host API converts at set/get.
+  int internal = 0;
 };
+
+// reference layout <-> device storage layout of one tensor
+void to_internal(const ParamEntry& p, const float* ref, float* dev);
+void to_reference(const ParamEntry& p, const float* dev, float* ref);
 
 struct ParamTable {
   std::vector<ParamEntry> e;

@@ -174,6 +174,12 @@ void col_reduce(const float* part, int nparts, long long n, float* out, int accu
   col_reduce(part, nparts, n, out, accumulate, g_scratch, g_scratch_n, st);
 }
 
+void col_reduce_ld(const float* part, int nparts, long long n, long long ld, float* out, int accumulate,
+                   cudaStream_t st) {
+  col_reduce_impl(part, nparts, n, ld, out, accumulate, Scatter{0, 0, 0, 0, nullptr, nullptr}, g_scratch, g_scratch_n,
+                  st);
+}
+
 void colsum_reduce(const float* part, int tiles, int C, float* out, int accumulate, cudaStream_t st) {
   col_reduce(part, tiles, C, out, accumulate, g_scratch, g_scratch_n, st);
 }

@@ -30,6 +30,9 @@ void colsum_reduce(const float* part, int tiles, int C, float* out, int accumula
 // Scratch used by the overloads below (set by the training context before it enqueues work).
 void set_reduce_scratch(float* scratch, size_t floats);
 void col_reduce(const float* part, int nparts, long long n, float* out, int accumulate, cudaStream_t st);
+// parts of length n placed ld floats apart
+void col_reduce_ld(const float* part, int nparts, long long n, long long ld, float* out, int accumulate,
+                   cudaStream_t st);
 void colsum_reduce(const float* part, int tiles, int C, float* out, int accumulate, cudaStream_t st);
 void wgrad_reduce(const float* part, int splits, int rows, int n_total, const int* row_tap, const int* row_oc,
                   int layout, int c_out, int k, float* dw, int accumulate, cudaStream_t st);

@@ -87,8 +87,10 @@ struct TcConv2Maps {
 };
 
 struct TcConv2Params {
-  int ntiles, tiles_per_item, t_rows;
-  int n;                    // C_out (GEMM N, <= 256), also the output channel pitch
+  int ntiles, tiles_per_item, t_rows;  // ntiles counts (row tile, N tile) pairs
+  int n;                    // GEMM N per tile (<= 256)
+  int n_tiles;              // C_out / n; N tile = tile % n_tiles (grid is a multiple of n_tiles)
+  int n_total;              // C_out: output channel pitch
   int n_chunks;             // C_in / KC
   int split;
   int ntaps;

@@ -12,12 +12,18 @@ WB_DEV void mbar_arrive(uint64_t* bar) {
 
 }  // namespace
 
+// Warp roles: 0..7 epilogue (warp w reads TMEM lane quadrant w%4 and column half w/4), 8 TMA producer,
+// 9 TMEM allocation + MMA issue.
+constexpr int kConv2Threads = 320;
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
+
 template <int KC>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kConv2Threads, 1)
     tc_conv2_kernel(const __grid_constant__ TcConv2Maps maps, const __grid_constant__ TcConv2Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ float red[128];
+  __shared__ float red[2][128];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int N = p.n;
@@ -44,19 +50,21 @@ __global__ void __launch_bounds__(192, 1)
     for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], 1); }
     fence_barrier_init();
   }
-  if (warp == 5) tmem_alloc(tmem_slot, (uint32_t)p.tmem_cols);
+  if (warp == kMmaWarp) tmem_alloc(tmem_slot, (uint32_t)p.tmem_cols);
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == kProducerWarp) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       int a_it = 0, w_it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < p.ntiles && ok; tile += gridDim.x) {
-        const int item = tile / p.tiles_per_item;
-        const int q0 = (tile - item * p.tiles_per_item) * 128;
+        const int mtile = tile / p.n_tiles;
+        const int n0 = (tile - mtile * p.n_tiles) * N;
+        const int item = mtile / p.tiles_per_item;
+        const int q0 = (mtile - item * p.tiles_per_item) * 128;
         for (int c = 0; c < p.n_chunks && ok; ++c) {
           const int sa = a_it % AS;
           if (a_it >= AS && !mbar_wait(&a_empty[sa], ((a_it / AS) & 1) ^ 1, p.err, ERR_WAIT_EMPTY)) { ok = false; break; }
@@ -77,14 +85,14 @@ __global__ void __launch_bounds__(192, 1)
             if (w_it >= WS && !mbar_wait(&w_empty[sw], ((w_it / WS) & 1) ^ 1, p.err, ERR_WAIT_EMPTY)) { ok = false; break; }
             uint8_t* wd = w_base + (size_t)sw * w_stage;
             mbar_arrive_expect_tx(&w_full[sw], w_stage);
-            tma_load_3d(wd, &maps.w_hi, &w_full[sw], c * KC, 0, p.tap_w[t]);
-            if (p.split) tma_load_3d(wd + w_sub, &maps.w_lo, &w_full[sw], c * KC, 0, p.tap_w[t]);
+            tma_load_3d(wd, &maps.w_hi, &w_full[sw], c * KC, n0, p.tap_w[t]);
+            if (p.split) tma_load_3d(wd + w_sub, &maps.w_lo, &w_full[sw], c * KC, n0, p.tap_w[t]);
             ++w_it;
           }
         }
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == kMmaWarp) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       const uint32_t idesc = make_idesc_bf16(128, N, 0, 0);
@@ -137,44 +145,58 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   } else {
-    // ---------------- epilogue (warps 0..3 <-> TMEM lanes 0..127) ----------------
+    // ---------------- epilogue: 8 warps; warp w -> TMEM lanes 32*(w%4).., columns of half w/4 ----------------
+    const int qw = warp & 3, half = warp >> 2;
+    const int hw = N >= 64 ? N / 2 : N;  // columns per half (N = 32: the second half idles)
+    const int c_beg = half * hw, c_end = min(N, c_beg + hw);
     // column sums (bias / Snake-alpha gradients) accumulate over this CTA's tiles: one partial per CTA
-    float cs_acc[8], ap_acc[8];
+    float cs_acc[4], ap_acc[4];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) cs_acc[i] = ap_acc[i] = 0.f;
+    for (int i = 0; i < 4; ++i) cs_acc[i] = ap_acc[i] = 0.f;
     int t_it = 0;
     for (int tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x, ++t_it) {
       const int buf = t_it & 1;
       const bool ok = mbar_wait(&acc_full[buf], (t_it >> 1) & 1, p.err, ERR_WAIT_ACC);
       tc_fence_after();
       if (!ok) break;
-      const int item = tile / p.tiles_per_item;
-      const int q = (tile - item * p.tiles_per_item) * 128 + warp * 32 + lane;
+      const int mtile = tile / p.n_tiles;
+      const int n0 = (tile - mtile * p.n_tiles) * N;
+      const int item = mtile / p.tiles_per_item;
+      const int q = (mtile - item * p.tiles_per_item) * 128 + qw * 32 + lane;
       const bool valid = q < p.t_rows;
-      const size_t row_off = ((size_t)item * p.t_rows + (valid ? q : 0)) * N;
-      const size_t part_row = (size_t)tile * N;
-      const float* ra = p.epi.rowadd ? p.epi.rowadd + (size_t)item * N : nullptr;
+      const size_t row_off = ((size_t)item * p.t_rows + (valid ? q : 0)) * p.n_total + n0;
+      const size_t part_row = (size_t)tile * p.n_total + n0;  // unused: sums accumulate per CTA
+      const float* ra = p.epi.rowadd ? p.epi.rowadd + (size_t)item * p.n_total + n0 : nullptr;
 #pragma unroll 1
-      for (int c0 = 0; c0 < N; c0 += 32) {
+      for (int c0 = c_beg; c0 < c_end; c0 += 32) {
         float v[32];
-        tmem_ld32(tmem + (uint32_t)(buf * N) + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
-        epi_chunk(p.epi, v, valid, row_off + c0, c0, part_row + c0, ra ? ra + c0 : nullptr, warp, lane, red,
-                  &cs_acc[c0 >> 5], &ap_acc[c0 >> 5]);
+        tmem_ld32(tmem + (uint32_t)(buf * N) + ((uint32_t)(qw * 32) << 16) + (uint32_t)c0, v);
+        epi_chunk(p.epi, v, valid, row_off + c0, n0 + c0, part_row + c0, ra ? ra + c0 : nullptr, qw, lane,
+                  red[half], &cs_acc[(c0 - c_beg) >> 5], &ap_acc[(c0 - c_beg) >> 5], 1 + 2 * half);
       }
       tc_fence_before();
-      asm volatile("bar.sync 2, 128;" ::: "memory");
+      asm volatile("bar.sync 2, 256;" ::: "memory");
       if (warp == 0 && lane == 0) mbar_arrive(&acc_empty[buf]);
     }
-    if (warp == 0) {
-      for (int c0 = 0; c0 < N; c0 += 32) {
-        if (p.epi.colsum) p.epi.colsum[(size_t)blockIdx.x * N + c0 + lane] = cs_acc[c0 >> 5];
-        if (p.epi.alpha_part) p.epi.alpha_part[(size_t)blockIdx.x * N + c0 + lane] = ap_acc[c0 >> 5];
+    if (qw == 0) {
+      // this CTA's tiles all share one N tile (the grid is a multiple of n_tiles): its partial row
+      // holds the sums in that tile's columns and zeros elsewhere (written by half 0)
+      const int my_n0 = (blockIdx.x % p.n_tiles) * N;
+      for (int c = 0; c < p.n_total; c += 32) {
+        const int rel = c - my_n0;
+        const bool in_tile = rel >= 0 && rel < N;
+        const bool in_half = in_tile && rel >= c_beg && rel < c_end;
+        if (!in_half && (in_tile || half == 1)) continue;
+        const float cs = in_half ? cs_acc[(rel - c_beg) >> 5] : 0.f;
+        const float ap = in_half ? ap_acc[(rel - c_beg) >> 5] : 0.f;
+        if (p.epi.colsum) p.epi.colsum[(size_t)blockIdx.x * p.n_total + c + lane] = cs;
+        if (p.epi.alpha_part) p.epi.alpha_part[(size_t)blockIdx.x * p.n_total + c + lane] = ap;
       }
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, (uint32_t)p.tmem_cols);
   }
@@ -193,9 +215,9 @@ cudaError_t launch_tc_conv2(const TcConv2Maps& maps, const TcConv2Params& p, int
                             cudaStream_t st) {
   tc_kernels_init();
   if (kc == 64)
-    tc_conv2_kernel<64><<<grid, 192, smem, st>>>(maps, p);
+    tc_conv2_kernel<64><<<grid, kConv2Threads, smem, st>>>(maps, p);
   else
-    tc_conv2_kernel<32><<<grid, 192, smem, st>>>(maps, p);
+    tc_conv2_kernel<32><<<grid, kConv2Threads, smem, st>>>(maps, p);
   return cudaGetLastError();
 }
 

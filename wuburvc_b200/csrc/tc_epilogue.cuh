@@ -63,13 +63,14 @@ WB_DEV void store_f32x32(float* p, const float* v) {
 
 // Column sums of v over the 128 rows of the four epilogue warps; warp 0 lane l gets column l.
 // Named barrier 1 synchronises only the 128 epilogue threads.
-WB_DEV float cta_colsum32(float* v, float* red /*smem [128]*/, int warp, int lane) {
+WB_DEV float cta_colsum32(float* v, float* red /*smem [128]*/, int warp, int lane, int bar) {
+  // warp = index within a group of four epilogue warps; named barrier `bar` spans that group only
   const float s = warp_colsum32(v, lane);
   red[warp * 32 + lane] = s;
-  asm volatile("bar.sync 1, 128;" ::: "memory");
+  asm volatile("bar.sync %0, 128;" ::"r"(bar) : "memory");
   float t = 0.f;
   if (warp == 0) t = red[lane] + red[32 + lane] + red[64 + lane] + red[96 + lane];
-  asm volatile("bar.sync 1, 128;" ::: "memory");
+  asm volatile("bar.sync %0, 128;" ::"r"(bar) : "memory");
   return t;
 }
 
@@ -80,7 +81,8 @@ WB_DEV float cta_colsum32(float* v, float* red /*smem [128]*/, int warp, int lan
 //   cs_acc / ap_acc: when non-null (persistent kernels), warp 0 accumulates this tile's column sums
 //   there instead of writing a per-tile partial.
 WB_DEV void epi_chunk(const Epi& e, float* v, bool valid, size_t off, int col, size_t part_row, const float* rowadd_row,
-                      int warp, int lane, float* red, float* cs_acc = nullptr, float* ap_acc = nullptr) {
+                      int warp, int lane, float* red, float* cs_acc = nullptr, float* ap_acc = nullptr,
+                      int bar = 1) {
   if (e.mask_src) {
     float x[32];
     if (valid) load_bf16x32(e.mask_src + off, x);
@@ -100,7 +102,7 @@ WB_DEV void epi_chunk(const Epi& e, float* v, bool valid, size_t off, int col, s
         v[i] *= 1.f + s2;
       }
       if (e.alpha_part) {
-        const float t = cta_colsum32(ga, red, warp, lane);
+        const float t = cta_colsum32(ga, red, warp, lane, bar);
         if (warp == 0) {
           if (ap_acc) *ap_acc += t;
           else e.alpha_part[part_row + lane] = t;
@@ -131,7 +133,7 @@ WB_DEV void epi_chunk(const Epi& e, float* v, bool valid, size_t off, int col, s
     float cv[32];
 #pragma unroll
     for (int i = 0; i < 32; ++i) cv[i] = valid ? v[i] : 0.f;
-    const float t = cta_colsum32(cv, red, warp, lane);
+    const float t = cta_colsum32(cv, red, warp, lane, bar);
     if (warp == 0) {
       if (cs_acc) *cs_acc += t;
       else e.colsum[part_row + lane] = t;
