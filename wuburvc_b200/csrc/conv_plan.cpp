@@ -207,10 +207,8 @@ bool plan_conv2(Conv2Launch& L, const ConvGeom& g, const void* x_hi, const void*
   const uint64_t wr = (uint64_t)g.C_in * 2, wt = wr * g.C_out;
   if (!make_map_bf16_3d(&L.maps.w_hi, w_hi, g.C_in, g.C_out, g.k, wr, wt, kc, p.n, 1)) return false;
   if (split && !make_map_bf16_3d(&L.maps.w_lo, w_lo, g.C_in, g.C_out, g.k, wr, wt, kc, p.n, 1)) return false;
-  int occ = (int)std::min<size_t>(2, (227 * 1024) / L.smem);
-  occ = std::min(occ, 512 / p.tmem_cols);
-  occ = std::max(occ, 1);
-  L.grid = std::min(p.ntiles, sm_count() * occ) / p.n_tiles * p.n_tiles;
+  // one CTA per SM (320 threads x ~128 registers), persistent over its tiles
+  L.grid = std::min(p.ntiles, sm_count()) / p.n_tiles * p.n_tiles;
   return true;
 }
 

@@ -48,7 +48,7 @@ struct ConvOp {
   Conv2Launch c2;
   cudaError_t run(cudaStream_t st) const { return v2 ? c2.run(st) : v1.run(st); }
   // rows of the [partials][C] column-sum buffers this launch writes (one per CTA or per tile)
-  int partials() const { return v2 ? c2.grid : (int)(v1.grid.x * v1.grid.z); }
+  int partials() const { return v2 ? 2 * c2.grid : (int)(v1.grid.x * v1.grid.z); }
 };
 
 struct WgradLaunch {

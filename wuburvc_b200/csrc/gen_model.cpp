@@ -245,11 +245,11 @@ bool gen_setup(Gen& m) {
         if (!dalloc(m, &k.a2_hi[cp], n) || !dalloc(m, &k.a2_lo[cp], n)) return false;
         if (snake && !dalloc(m, &k.a2_pre[cp], n)) return false;
         // column-sum partials: one row per tile (general kernel) or per CTA of the persistent kernel,
-        // which may split N in two (at most 2 * tiles rows)
-        if (!dalloc(m, &k.cs_dc1[cp], (size_t)2 * tiles * s.C) || !dalloc(m, &k.cs_dp[cp], (size_t)2 * tiles * s.C))
+        // which may split N in two and writes two rows (epilogue groups) per CTA: at most 4 * tiles rows
+        if (!dalloc(m, &k.cs_dc1[cp], (size_t)4 * tiles * s.C) || !dalloc(m, &k.cs_dp[cp], (size_t)4 * tiles * s.C))
           return false;
         if (snake &&
-            (!dalloc(m, &k.ap1[cp], (size_t)2 * tiles * s.C) || !dalloc(m, &k.ap2[cp], (size_t)2 * tiles * s.C)))
+            (!dalloc(m, &k.ap1[cp], (size_t)4 * tiles * s.C) || !dalloc(m, &k.ap2[cp], (size_t)4 * tiles * s.C)))
           return false;
       }
       if (!dalloc(m, &k.d_c1, n)) return false;
@@ -373,7 +373,7 @@ bool gen_setup(Gen& m) {
           e.colsum = k.cs_dc1[cp];
           ConvGeom g{B, s.T, s.T, s.C, s.C, kk, 1, (kk - 1) / 2};
           if (!plan_conv_any(k.d2[cp], g, dp_out_b, nullptr, k.w2[cp].dg, nullptr, 0, e, m.err)) return false;
-          if (k.d2[cp].partials() > 2 * k.tiles) return false;  // partial buffers hold 2 * tiles rows
+          if (k.d2[cp].partials() > 4 * k.tiles) return false;  // partial buffers hold 4 * tiles rows
         }
         {  // conv2 wgrad
           ConvGeom g{B, s.T, s.T, s.C, s.C, kk, 1, (kk - 1) / 2};
@@ -399,7 +399,7 @@ bool gen_setup(Gen& m) {
           }
           ConvGeom g{B, s.T, s.T, s.C, s.C, kk, dil, dil * (kk - 1) / 2};
           if (!plan_conv_any(k.d1[cp], g, k.d_c1, nullptr, k.w1[cp].dg, nullptr, 0, e, m.err)) return false;
-          if (k.d1[cp].partials() > 2 * k.tiles) return false;
+          if (k.d1[cp].partials() > 4 * k.tiles) return false;
         }
         {  // conv1 wgrad
           ConvGeom g{B, s.T, s.T, s.C, s.C, kk, dil, dil * (kk - 1) / 2};

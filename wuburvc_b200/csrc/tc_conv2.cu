@@ -145,17 +145,17 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
       }
     }
   } else {
-    // ---------------- epilogue: 8 warps; warp w -> TMEM lanes 32*(w%4).., columns of half w/4 ----------------
-    const int qw = warp & 3, half = warp >> 2;
-    const int hw = N >= 64 ? N / 2 : N;  // columns per half (N = 32: the second half idles)
-    const int c_beg = half * hw, c_end = min(N, c_beg + hw);
-    // column sums (bias / Snake-alpha gradients) accumulate over this CTA's tiles: one partial per CTA
-    float cs_acc[4], ap_acc[4];
+    // ---------------- epilogue: two groups of 4 warps; group g drains TMEM accumulator g, i.e. every
+    // other tile, so two tiles' epilogues run concurrently (warp w reads TMEM lane quadrant w%4) ----------------
+    const int qw = warp & 3, grp = warp >> 2;
+    // column sums (bias / Snake-alpha gradients) accumulate over the group's tiles: one partial row
+    // per group, 2 per CTA
+    float cs_acc[8], ap_acc[8];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) cs_acc[i] = ap_acc[i] = 0.f;
-    int t_it = 0;
-    for (int tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x, ++t_it) {
-      const int buf = t_it & 1;
+    for (int i = 0; i < 8; ++i) cs_acc[i] = ap_acc[i] = 0.f;
+    int t_it = grp;
+    for (int tile = blockIdx.x + grp * gridDim.x; tile < p.ntiles; tile += 2 * gridDim.x, t_it += 2) {
+      const int buf = grp;
       const bool ok = mbar_wait(&acc_full[buf], (t_it >> 1) & 1, p.err, ERR_WAIT_ACC);
       tc_fence_after();
       if (!ok) break;
@@ -168,29 +168,27 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
       const size_t part_row = (size_t)tile * p.n_total + n0;  // unused: sums accumulate per CTA
       const float* ra = p.epi.rowadd ? p.epi.rowadd + (size_t)item * p.n_total + n0 : nullptr;
 #pragma unroll 1
-      for (int c0 = c_beg; c0 < c_end; c0 += 32) {
+      for (int c0 = 0; c0 < N; c0 += 32) {
         float v[32];
         tmem_ld32(tmem + (uint32_t)(buf * N) + ((uint32_t)(qw * 32) << 16) + (uint32_t)c0, v);
         epi_chunk(p.epi, v, valid, row_off + c0, n0 + c0, part_row + c0, ra ? ra + c0 : nullptr, qw, lane,
-                  red[half], &cs_acc[(c0 - c_beg) >> 5], &ap_acc[(c0 - c_beg) >> 5], 1 + 2 * half);
+                  red[grp], &cs_acc[c0 >> 5], &ap_acc[c0 >> 5], 1 + grp);
       }
       tc_fence_before();
-      asm volatile("bar.sync 2, 256;" ::: "memory");
-      if (warp == 0 && lane == 0) mbar_arrive(&acc_empty[buf]);
+      asm volatile("bar.sync %0, 128;" ::"r"(3 + grp) : "memory");
+      if (qw == 0 && lane == 0) mbar_arrive(&acc_empty[buf]);
     }
     if (qw == 0) {
-      // this CTA's tiles all share one N tile (the grid is a multiple of n_tiles): its partial row
-      // holds the sums in that tile's columns and zeros elsewhere (written by half 0)
+      // every tile of this CTA shares one N tile (the grid is a multiple of n_tiles): the group's partial
+      // row holds its sums in that tile's columns and zeros elsewhere
       const int my_n0 = (blockIdx.x % p.n_tiles) * N;
+      const size_t prow = (size_t)(2 * blockIdx.x + grp) * p.n_total;
       for (int c = 0; c < p.n_total; c += 32) {
         const int rel = c - my_n0;
-        const bool in_tile = rel >= 0 && rel < N;
-        const bool in_half = in_tile && rel >= c_beg && rel < c_end;
-        if (!in_half && (in_tile || half == 1)) continue;
-        const float cs = in_half ? cs_acc[(rel - c_beg) >> 5] : 0.f;
-        const float ap = in_half ? ap_acc[(rel - c_beg) >> 5] : 0.f;
-        if (p.epi.colsum) p.epi.colsum[(size_t)blockIdx.x * p.n_total + c + lane] = cs;
-        if (p.epi.alpha_part) p.epi.alpha_part[(size_t)blockIdx.x * p.n_total + c + lane] = ap;
+        const bool mine = rel >= 0 && rel < N;
+        const float cs = mine ? cs_acc[rel >> 5] : 0.f, ap = mine ? ap_acc[rel >> 5] : 0.f;
+        if (p.epi.colsum) p.epi.colsum[prow + c + lane] = cs;
+        if (p.epi.alpha_part) p.epi.alpha_part[prow + c + lane] = ap;
       }
     }
   }
