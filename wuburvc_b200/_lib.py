@@ -20,6 +20,7 @@ P = ctypes.POINTER
 SIGNATURES = {
     "wubu_b200_conv1d": (c_int, [c_void_p] * 4 + [c_void_p, c_void_p] + [c_int] * 8 + [c_void_p]),
     "wubu_b200_conv1d_wgrad": (c_int, [c_void_p, c_void_p, c_void_p] + [c_int] * 7 + [c_void_p]),
+    "wubu_b200_conv1d_wgrad_noalloc": (c_int, [c_void_p, c_void_p, c_void_p] + [c_int] * 7 + [c_void_p]),
     "wubu_b200_convT": (c_int, [c_void_p] * 4 + [c_void_p, c_void_p] + [c_int] * 8 + [c_void_p]),
     "wubu_b200_convT_dgrad": (c_int, [c_void_p, c_void_p, c_void_p] + [c_int] * 7 + [c_void_p]),
     "wubu_b200_convT_wgrad": (c_int, [c_void_p, c_void_p, c_void_p] + [c_int] * 7 + [c_void_p]),
