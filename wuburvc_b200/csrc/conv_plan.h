@@ -49,6 +49,11 @@ struct ConvOp {
   cudaError_t run(cudaStream_t st) const { return v2 ? c2.run(st) : v1.run(st); }
   // rows of the [partials][C] column-sum buffers this launch writes (one per CTA or per tile)
   int partials() const { return v2 ? 2 * c2.grid : (int)(v1.grid.x * v1.grid.z); }
+  // re-points the epilogue's column-sum partial buffer
+  void set_colsum(float* p) {
+    v1.p.epi.colsum = p;
+    c2.p.epi.colsum = p;
+  }
 };
 
 struct WgradLaunch {

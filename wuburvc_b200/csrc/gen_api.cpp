@@ -284,7 +284,6 @@ int wubu_b200_gen_kernel_bench(WubuB200Gen* gen, int which, int stage, int iters
   auto launch = [&]() -> bool {
     if (which == 0) return k.f1[0].run(m.stream) == cudaSuccess;
     if (which == 1) return k.d1[0].run(m.stream) == cudaSuccess;
-    k.g1[0].L.p.part = m.wg_part;
     return k.g1[0].L.run(m.stream) == cudaSuccess;
   };
   for (int i = 0; i < 2; ++i)

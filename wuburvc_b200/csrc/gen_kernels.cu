@@ -190,6 +190,42 @@ void wn_backward(const float* dW, const float* v, const float* g, const float* n
   wn_backward_kernel<<<rows, 256, 0, st>>>(dW, v, g, norm, rows, cols, k, is_convT, dv, dg);
 }
 
+__global__ void wn_backward_batched_kernel(const WnDesc* __restrict__ descs, int ndesc) {
+  __shared__ float sh[32];
+  __shared__ int di;
+  if (threadIdx.x == 0) {
+    int lo = 0, hi = ndesc - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (descs[mid].first <= (int)blockIdx.x) lo = mid;
+      else hi = mid - 1;
+    }
+    di = lo;
+  }
+  __syncthreads();
+  const WnDesc d = descs[di];
+  const int r = blockIdx.x - d.first;
+  const int per = d.cols * d.k;
+  float s = 0.f;
+  for (int i = threadIdx.x; i < per; i += blockDim.x) {
+    const size_t a = wrow_addr(i, r, d.rows, d.cols, d.is_convT);
+    s += d.dW[a] * d.v[a];
+  }
+  s = block_sum(s, sh);
+  const float n = d.norm[r];
+  const float dgr = s / n;
+  if (threadIdx.x == 0) d.dg[r] = dgr;
+  const float a = d.g[r] / n, b = dgr / n;
+  for (int i = threadIdx.x; i < per; i += blockDim.x) {
+    const size_t q = wrow_addr(i, r, d.rows, d.cols, d.is_convT);
+    d.dv[q] = a * (d.dW[q] - b * d.v[q]);
+  }
+}
+
+void wn_backward_batched(const WnDesc* descs, int ndesc, int total_rows, cudaStream_t st) {
+  if (ndesc > 0 && total_rows > 0) wn_backward_batched_kernel<<<total_rows, 256, 0, st>>>(descs, ndesc);
+}
+
 // Step state lives on the device so a captured step graph advances it by itself.
 __global__ void step_bump_kernel(StepState* s, int bump_noise) {
   s->adam_t += 1;

@@ -23,6 +23,14 @@ struct PrepDesc {
 };
 void prep_weights_batched(const PrepDesc* descs, int ndesc, int total_rows, cudaStream_t st);
 
+// Weight-norm backward of many tensors in one launch (block = one dim-0 row of one tensor).
+struct WnDesc {
+  const float *dW, *v, *g, *norm;
+  float *dv, *dg;
+  int rows, cols, k, is_convT, first;
+};
+void wn_backward_batched(const WnDesc* descs, int ndesc, int total_rows, cudaStream_t st);
+
 // weight-norm backward: dg[r] = <dW[r], v[r]>/n[r];  dv[r] = g[r]/n[r] * (dW[r] - dg[r]/n[r] * v[r])
 // over dim-0 rows of a tap-major [k][C_out][C_in] tensor (rows x cols = C_out x C_in for a conv,
 // C_in x C_out for a ConvTranspose).

@@ -22,6 +22,7 @@ void comm_destroy(Gen& m);
 
 namespace {
 
+constexpr size_t kWgBatchBytes = (size_t)48 << 20;  // split-K partials reduced per batch (L2-sized)
 constexpr int kWgradCtas = 296;  // 2 waves of 148 SMs for split-K weight gradients
 
 #define CK(x)                                                                                   \
@@ -98,30 +99,121 @@ bool make_wgrad_job(Gen& m, WgradJob& j, int layout, int c_out, int k, const Con
   j.k = k;
   j.w = &w;
   j.dW = w.dW;
-  // inverse map (oc, tap) -> partial row, for the fused split-K reduction
-  std::vector<int> inv((size_t)c_out * k, -1);
+  // every (oc, tap) must own a partial row
+  std::vector<char> seen((size_t)c_out * k, 0);
   for (size_t r = 0; r < j.L.row_tap.size(); ++r)
-    if (j.L.row_tap[r] >= 0) inv[(size_t)j.L.row_oc[r] * k + j.L.row_tap[r]] = (int)r;
-  for (int x : inv)
-    if (x < 0) return false;
-  if (!dalloc(m, &j.inv, inv.size())) return false;
-  CK(cudaMemcpy(j.inv, inv.data(), inv.size() * sizeof(int), cudaMemcpyHostToDevice));
+    if (j.L.row_tap[r] >= 0) seen[(size_t)j.L.row_oc[r] * k + j.L.row_tap[r]] = 1;
+  for (char x : seen)
+    if (!x) return false;
+  if (!dalloc(m, &j.part, wgrad_part_floats(j.L))) return false;
+  j.L.p.part = j.part;
   return true;
 }
 
-// weight gradient: split-K partials on the tensor cores, then one fused reduction straight into
-// the flat gradient buffer (with the weight-norm backward under weight norm)
-bool run_wgrad(Gen& m, WgradJob& j) {
-  j.L.p.part = m.wg_part;
-  CK(j.L.run(m.stream));
+// The split-K reduction of a weight gradient: partial rows are (tap * C_out + oc) x C_in, so the first
+// k*C_out rows of each split are exactly the tap-major device layout of the weight and the sum over
+// splits is a plain column reduction.  Under weight norm it lands in the dW temp (then wn backward).
+ReduceDesc wgrad_desc(Gen& m, const WgradJob& j) {
   const ConvWeights& w = *j.w;
-  // partial rows are (tap * C_out + oc) x C_in: the first k*C_out rows of each split are exactly the
-  // tap-major device layout of the weight, so the split-K sum is a plain column reduction
-  const long long ld = (long long)j.L.p.n_mtiles * 128 * j.L.p.n_total;
-  const long long n = (long long)j.k * j.c_out * j.L.p.n_total;
-  const bool wn = w.pg >= 0;
-  col_reduce_ld(m.wg_part, j.L.splits, n, ld, wn ? w.dW : m.G(w.pv), 0, m.stream);
-  if (wn)
+  ReduceDesc d{};
+  d.part = j.part;
+  d.out = w.pg >= 0 ? w.dW : m.G(w.pv);
+  d.ld = (long long)j.L.p.n_mtiles * 128 * j.L.p.n_total;
+  d.n = (long long)j.k * j.c_out * j.L.p.n_total;
+  d.nparts = j.L.splits;
+  return d;
+}
+
+WnDesc wn_desc(Gen& m, const ConvWeights& w) {
+  WnDesc d{};
+  d.dW = w.dW;
+  d.v = m.P(w.pv);
+  d.g = m.P(w.pg);
+  d.norm = w.norm;
+  d.dv = m.G(w.pv);
+  d.dg = m.G(w.pg);
+  d.rows = w.rows;
+  d.cols = w.cols;
+  d.k = w.k;
+  d.is_convT = w.convT;
+  return d;
+}
+
+ReduceDesc colsum_desc(const float* part, int nparts, int C, float* out) {
+  ReduceDesc d{};
+  d.part = part;
+  d.out = out;
+  d.ld = C;
+  d.n = C;
+  d.nparts = nparts;
+  return d;
+}
+
+// Uploads a batch of column reductions (with their chunk scratch and counters) for one launch.
+bool upload_reduce_table(Gen& m, std::vector<ReduceDesc>& v, ReduceDesc** dev, int* n, int* blocks) {
+  size_t sc_total = 0, ct_total = 0;
+  int first = 0;
+  std::vector<size_t> sc_off(v.size()), ct_off(v.size());
+  for (size_t i = 0; i < v.size(); ++i) {
+    size_t sf = 0, cn = 0;
+    first += reduce_desc_shape(v[i], first, &sf, &cn);
+    sc_off[i] = sc_total;
+    ct_off[i] = ct_total;
+    sc_total += sf;
+    ct_total += cn;
+  }
+  float* sc = nullptr;
+  unsigned int* ct = nullptr;
+  if (sc_total && !dalloc(m, &sc, sc_total)) return false;
+  if (ct_total) {
+    if (!dalloc(m, &ct, ct_total)) return false;
+    CK(cudaMemset(ct, 0, ct_total * sizeof(unsigned int)));
+  }
+  for (size_t i = 0; i < v.size(); ++i)
+    if (v[i].nchunks > 1) {
+      v[i].scratch = sc + sc_off[i];
+      v[i].counter = ct + ct_off[i];
+    }
+  *n = (int)v.size();
+  *blocks = first;
+  if (v.empty()) return true;
+  if (!dalloc(m, dev, v.size())) return false;
+  CK(cudaMemcpy(*dev, v.data(), v.size() * sizeof(ReduceDesc), cudaMemcpyHostToDevice));
+  return true;
+}
+
+bool upload_wn_table(Gen& m, std::vector<WnDesc>& v, WnDesc** dev, int* n, int* rows) {
+  int first = 0;
+  for (WnDesc& d : v) {
+    d.first = first;
+    first += d.rows;
+  }
+  *n = (int)v.size();
+  *rows = first;
+  if (v.empty()) return true;
+  if (!dalloc(m, dev, v.size())) return false;
+  CK(cudaMemcpy(*dev, v.data(), v.size() * sizeof(WnDesc), cudaMemcpyHostToDevice));
+  return true;
+}
+
+// split-K partials into the job's own buffer; the batched reductions follow the group's last job
+bool run_wgrad(Gen& m, StageBufs& s, const WgradJob& j) {
+  CK(j.L.run(m.stream));
+  if (j.flush >= 0) {
+    const WgradBatch& b = s.wg_batches[j.flush];
+    reduce_batched(b.wg_d, b.wg_n, b.wg_blocks, m.stream);
+    wn_backward_batched(b.wn_d, b.wn_n, b.wn_rows, m.stream);
+  }
+  return true;
+}
+
+// conv_pre's weight gradient (kernel + reduction + weight norm; a handful of launches, once per step)
+bool run_pre_wgrad(Gen& m) {
+  CK(m.pre_wg.L.run(m.stream));
+  const ReduceDesc d = wgrad_desc(m, m.pre_wg);
+  col_reduce_ld(d.part, d.nparts, d.n, d.ld, d.out, 0, m.stream);
+  const ConvWeights& w = m.wpre;
+  if (w.pg >= 0)
     wn_backward(w.dW, m.P(w.pv), m.P(w.pg), w.norm, w.rows, w.cols, w.k, w.convT, m.G(w.pv), m.G(w.pg), m.stream);
   return true;
 }
@@ -264,7 +356,6 @@ bool gen_setup(Gen& m) {
   }
 
   // ---- launch plans ----
-  m.wg_part_cap = 0;
   // forward conv_pre
   {
     Epi e = epi0(c.lrelu_slope);
@@ -378,7 +469,6 @@ bool gen_setup(Gen& m) {
         {  // conv2 wgrad
           ConvGeom g{B, s.T, s.T, s.C, s.C, kk, 1, (kk - 1) / 2};
           if (!plan_wgrad(k.g2[cp].L, g, dp_out_b, k.a2_hi[cp], nullptr, ~size_t(0), kWgradCtas, m.err)) return false;
-          m.wg_part_cap = std::max(m.wg_part_cap, wgrad_part_floats(k.g2[cp].L));
           if (!make_wgrad_job(m, k.g2[cp], 0, s.C, kk, k.w2[cp])) return false;
         }
         {  // conv1 dgrad -> gradient wrt the pair input
@@ -404,7 +494,6 @@ bool gen_setup(Gen& m) {
         {  // conv1 wgrad
           ConvGeom g{B, s.T, s.T, s.C, s.C, kk, dil, dil * (kk - 1) / 2};
           if (!plan_wgrad(k.g1[cp].L, g, k.d_c1, k.a1_hi[cp], nullptr, ~size_t(0), kWgradCtas, m.err)) return false;
-          m.wg_part_cap = std::max(m.wg_part_cap, wgrad_part_floats(k.g1[cp].L));
           if (!make_wgrad_job(m, k.g1[cp], 0, s.C, kk, k.w1[cp])) return false;
         }
       }
@@ -441,17 +530,81 @@ bool gen_setup(Gen& m) {
       if (!plan_convT_wgrad(s.up_wg.L, B, Tin, s.Cin, s.C, s.ku, s.su, s.pu, xin, s.d_x_bf, nullptr, ~size_t(0),
                             kWgradCtas, m.err))
         return false;
-      m.wg_part_cap = std::max(m.wg_part_cap, wgrad_part_floats(s.up_wg.L));
       if (!make_wgrad_job(m, s.up_wg, 1, s.C, s.ku, s.wu)) return false;
     }
   }
   {  // conv_pre wgrad
     ConvGeom g{B, m.F, m.F, c.in_channels, C0, 7, 1, 3};
     if (!plan_wgrad(m.pre_wg.L, g, m.d_pre_bf, m.z_hi, nullptr, ~size_t(0), kWgradCtas, m.err)) return false;
-    m.wg_part_cap = std::max(m.wg_part_cap, wgrad_part_floats(m.pre_wg.L));
     if (!make_wgrad_job(m, m.pre_wg, 0, C0, 7, m.wpre)) return false;
   }
-  if (!dalloc(m, &m.wg_part, m.wg_part_cap)) return false;
+  // ---- batched per-stage reductions ----
+  for (int L = 0; L < 4; ++L) {
+    StageBufs& s = m.sg[L];
+    // the stacks' input-gradient column sums side by side: the ups bias sums them in one pass
+    int slot = 0;
+    for (int j = 0; j < m.nk; ++j) slot = std::max(slot, s.st[j].d1[0].partials());
+    if (!dalloc(m, &s.cs_dx, (size_t)m.nk * slot * s.C)) return false;
+    for (int j = 0; j < m.nk; ++j) {
+      s.st[j].cs_dp[0] = s.cs_dx + (size_t)j * slot * s.C;
+      s.st[j].d1[0].set_colsum(s.st[j].cs_dp[0]);
+    }
+    // weight gradients in execution order, grouped while their partials fit the L2 budget
+    std::vector<WgradJob*> jobs;
+    for (int j = 0; j < m.nk; ++j)
+      for (int cp = m.nd - 1; cp >= 0; --cp) {
+        jobs.push_back(&s.st[j].g2[cp]);
+        jobs.push_back(&s.st[j].g1[cp]);
+      }
+    jobs.push_back(&s.up_wg);
+    {
+      std::vector<ReduceDesc> wg;
+      std::vector<WnDesc> wn;
+      size_t bytes = 0;
+      for (size_t i = 0; i < jobs.size(); ++i) {
+        WgradJob& jb = *jobs[i];
+        wg.push_back(wgrad_desc(m, jb));
+        if (jb.w->pg >= 0) wn.push_back(wn_desc(m, *jb.w));
+        bytes += wgrad_part_floats(jb.L) * sizeof(float);
+        const size_t next = i + 1 < jobs.size() ? wgrad_part_floats(jobs[i + 1]->L) * sizeof(float) : 0;
+        if (i + 1 == jobs.size() || bytes + next > kWgBatchBytes) {
+          WgradBatch bt;
+          if (!upload_reduce_table(m, wg, &bt.wg_d, &bt.wg_n, &bt.wg_blocks) ||
+              !upload_wn_table(m, wn, &bt.wn_d, &bt.wn_n, &bt.wn_rows))
+            return false;
+          jb.flush = (int)s.wg_batches.size();
+          s.wg_batches.push_back(bt);
+          wg.clear();
+          wn.clear();
+          bytes = 0;
+        }
+      }
+    }
+    std::vector<ReduceDesc> cs;
+    for (int j = 0; j < m.nk; ++j) {
+      StackBufs& k = s.st[j];
+      const std::string R = std::to_string(L * m.nk + j);
+      for (int cp = m.nd - 1; cp >= 0; --cp) {
+        const std::string P = std::to_string(cp);
+        cs.push_back(colsum_desc(k.cs_dc1[cp], k.d2[cp].partials(), s.C, m.G(k.w1[cp].pb)));
+        if (cp == m.nd - 1)
+          cs.push_back(colsum_desc(s.cs_ds, s.cs_ds_tiles, s.C, m.G(k.w2[cp].pb)));
+        else
+          cs.push_back(colsum_desc(k.cs_dp[cp + 1], k.d1[cp + 1].partials(), s.C, m.G(k.w2[cp].pb)));
+        if (snake) {
+          cs.push_back(colsum_desc(k.ap1[cp], k.d1[cp].partials(), s.C,
+                                   alpha_grad(m, "dec.resblocks." + R + ".alpha1." + P)));
+          cs.push_back(colsum_desc(k.ap2[cp], k.d2[cp].partials(), s.C,
+                                   alpha_grad(m, "dec.resblocks." + R + ".alpha2." + P)));
+        }
+      }
+    }
+    cs.push_back(colsum_desc(s.cs_dx, m.nk * slot, s.C, m.G(m.pidx("dec.ups." + std::to_string(L) + ".bias"))));
+    if (snake)
+      cs.push_back(
+          colsum_desc(s.ap_up, s.ap_up_tiles, s.Cin, alpha_grad(m, "dec.ups_act." + std::to_string(L) + ".alpha")));
+    if (!upload_reduce_table(m, cs, &s.cs_d, &s.cs_n, &s.cs_blocks)) return false;
+  }
   m.red_scratch_n = (size_t)4 << 20;
   if (!dalloc(m, &m.red_scratch, m.red_scratch_n)) return false;
   {  // one-launch weight preparation table
@@ -604,43 +757,31 @@ bool gen_backward(Gen& m) {
     StageBufs& s = m.sg[L];
     for (int j = 0; j < m.nk; ++j) {
       StackBufs& k = s.st[j];
-      const std::string R = std::to_string(L * m.nk + j);
       for (int cp = m.nd - 1; cp >= 0; --cp) {
-        const std::string P = std::to_string(cp);
         CK(k.d2[cp].run(st));
-        if (!run_wgrad(m, k.g2[cp])) return false;
+        if (!run_wgrad(m, s, k.g2[cp])) return false;
         CK(k.d1[cp].run(st));
-        if (!run_wgrad(m, k.g1[cp])) return false;
-        // biases: conv1 <- colsum(d_c1); conv2 <- colsum(grad wrt pair output)
-        colsum_reduce(k.cs_dc1[cp], k.d2[cp].partials(), s.C, m.G(k.w1[cp].pb), 0, st);
-        if (cp == m.nd - 1)
-          colsum_reduce(s.cs_ds, s.cs_ds_tiles, s.C, m.G(k.w2[cp].pb), 0, st);
-        else
-          colsum_reduce(k.cs_dp[cp + 1], k.d1[cp + 1].partials(), s.C, m.G(k.w2[cp].pb), 0, st);
-        if (snake) {
-          colsum_reduce(k.ap1[cp], k.d1[cp].partials(), s.C, alpha_grad(m, "dec.resblocks." + R + ".alpha1." + P), 0, st);
-          colsum_reduce(k.ap2[cp], k.d2[cp].partials(), s.C, alpha_grad(m, "dec.resblocks." + R + ".alpha2." + P), 0, st);
-        }
+        if (!run_wgrad(m, s, k.g1[cp])) return false;
       }
     }
-    // stage input gradient d_x: ups bias, noise conv, ups dgrad / wgrad
-    const int ub = m.pidx("dec.ups." + std::to_string(L) + ".bias");
-    for (int j = 0; j < m.nk; ++j) colsum_reduce(s.st[j].cs_dp[0], s.st[j].d1[0].partials(), s.C, m.G(ub), j > 0, st);
+    // stage input gradient d_x: noise conv, ups dgrad / wgrad
     if (c.nsf) {
       const int nw = m.pidx("dec.noise_convs." + std::to_string(L) + ".weight");
-      const int nb = m.pidx("dec.noise_convs." + std::to_string(L) + ".bias");
-      CK(cudaMemcpyAsync(m.G(nb), m.G(ub), sizeof(float) * s.C, cudaMemcpyDeviceToDevice, st));
       noise_backward(s.d_x, m.har, s.noise_wt, B, s.T, s.C, s.kn, s.sn, s.pn, m.T, m.d_har, L < 3, s.noise_wpart, st);
       noise_wgrad_reduce(s.noise_wpart, s.noise_parts, s.C, s.kn, m.G(nw), st);
     }
     CK(s.up_dg.run(st));
-    if (!run_wgrad(m, s.up_wg)) return false;
-    if (snake)
-      colsum_reduce(s.ap_up, s.ap_up_tiles, s.Cin, alpha_grad(m, "dec.ups_act." + std::to_string(L) + ".alpha"), 0, st);
+    if (!run_wgrad(m, s, s.up_wg)) return false;
+    reduce_batched(s.cs_d, s.cs_n, s.cs_blocks, st);  // every bias / Snake-alpha gradient of the stage
+    if (c.nsf) {  // the noise conv's bias is added where the ups bias is: same gradient
+      const int ub = m.pidx("dec.ups." + std::to_string(L) + ".bias");
+      const int nb = m.pidx("dec.noise_convs." + std::to_string(L) + ".bias");
+      CK(cudaMemcpyAsync(m.G(nb), m.G(ub), sizeof(float) * s.C, cudaMemcpyDeviceToDevice, st));
+    }
     if (comm_bucket_ready(m, 3 - L)) return false;  // this stage's gradients are final
   }
   // conv_pre, cond, source
-  if (!run_wgrad(m, m.pre_wg)) return false;
+  if (!run_pre_wgrad(m)) return false;
   colsum_reduce(m.cs_pre, m.cs_pre_tiles, c.initial_channel, m.G(m.wpre.pb), 0, st);
   if (c.gin_channels)
     cond_backward(m.cs_pre, m.pre_tiles_per_item, B, c.initial_channel, m.g, c.gin_channels,

@@ -7,6 +7,7 @@
 #include "conv_plan.h"
 #include "gen_kernels.cuh"
 #include "param_table.h"
+#include "small_kernels.cuh"
 
 namespace wb {
 
@@ -24,11 +25,20 @@ struct ConvWeights {
 
 struct WgradJob {
   WgradLaunch L;
-  int* inv = nullptr;  // device [c_out][k] -> partial row
+  float* part = nullptr;  // this job's split-K partials (reduced later in a batched launch)
+  int flush = -1;         // WgradBatch of the stage to launch after this job's kernel (-1: none)
   const ConvWeights* w = nullptr;
   int layout = 0;      // 0 conv, 1 convT
   int c_out = 0, k = 0;
   float* dW = nullptr;
+};
+
+// Split-K reductions of several weight gradients (one launch) and their weight-norm backward (one).
+struct WgradBatch {
+  ReduceDesc* wg_d = nullptr;
+  int wg_n = 0, wg_blocks = 0;
+  WnDesc* wn_d = nullptr;
+  int wn_n = 0, wn_rows = 0;
 };
 
 struct StackBufs {
@@ -69,6 +79,12 @@ struct StageBufs {
   ConvLaunch up_fwd, up_dg;
   WgradJob up_wg;
   StackBufs st[3];
+  float* cs_dx = nullptr;  // the stacks' cs_dp[0] partial slots, contiguous (ups / noise-conv bias)
+  // batched reductions (device descriptor tables): the weight gradients in groups whose split-K
+  // partials stay L2-sized, and all of the stage's bias / Snake-alpha column sums at its end
+  std::vector<WgradBatch> wg_batches;
+  ReduceDesc* cs_d = nullptr;
+  int cs_n = 0, cs_blocks = 0;
 };
 
 struct Gen {
@@ -107,8 +123,6 @@ struct Gen {
   int post_blocks = 0;
 
   StageBufs sg[4];
-  float* wg_part = nullptr;  // shared split-K scratch for the weight gradients
-  size_t wg_part_cap = 0;
   PrepDesc* prep_descs = nullptr;  // device table: every GEMM weight's preparation, one launch
   int n_prep = 0, prep_rows = 0;
   float* red_scratch = nullptr;  // two-pass deterministic reductions

@@ -162,6 +162,77 @@ void wgrad_finish(const float* part, int splits, int rows, int n_total, const in
                                                            norm, dv, dg);
 }
 
+__global__ void __launch_bounds__(256) reduce_batched_kernel(const ReduceDesc* __restrict__ descs, int ndesc) {
+  __shared__ float sh[kYLanes][33];
+  __shared__ int di, last;
+  const int tx = threadIdx.x, ty = threadIdx.y;
+  if (tx == 0 && ty == 0) {
+    int lo = 0, hi = ndesc - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (descs[mid].first_block <= (int)blockIdx.x) lo = mid;
+      else hi = mid - 1;
+    }
+    di = lo;
+  }
+  __syncthreads();
+  const ReduceDesc d = descs[di];
+  const int b = blockIdx.x - d.first_block;
+  const int cb = b % d.colblocks, ch = b / d.colblocks;
+  const long long j = (long long)cb * 32 + tx;
+  const int p0 = d.nchunks == 1 ? 0 : ch * kReduceChunk;
+  const int p1 = d.nchunks == 1 ? d.nparts : min(d.nparts, p0 + kReduceChunk);
+  float s = 0.f;
+  if (j < d.n) {
+#pragma unroll 4
+    for (int p = p0 + ty; p < p1; p += kYLanes) s += d.part[(long long)p * d.ld + j];
+  }
+  sh[ty][tx] = s;
+  __syncthreads();
+  float t = 0.f;
+  if (ty == 0) {
+#pragma unroll
+    for (int y = 0; y < kYLanes; ++y) t += sh[y][tx];
+  }
+  if (d.nchunks == 1) {
+    if (ty == 0 && j < d.n) d.out[j] = t;
+    return;
+  }
+  if (ty == 0 && j < d.n) d.scratch[(long long)ch * d.n + j] = t;
+  __threadfence();
+  __syncthreads();
+  if (tx == 0 && ty == 0) last = atomicAdd(&d.counter[cb], 1u) == (unsigned)(d.nchunks - 1);
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  // last block of this column group: chunk sums in chunk order
+  s = 0.f;
+  if (j < d.n)
+    for (int c = ty; c < d.nchunks; c += kYLanes) s += __ldcg(&d.scratch[(long long)c * d.n + j]);
+  sh[ty][tx] = s;
+  __syncthreads();
+  if (ty == 0 && j < d.n) {
+    t = 0.f;
+#pragma unroll
+    for (int y = 0; y < kYLanes; ++y) t += sh[y][tx];
+    d.out[j] = t;
+  }
+  if (tx == 0 && ty == 0) d.counter[cb] = 0u;
+}
+
+int reduce_desc_shape(ReduceDesc& d, int first_block, size_t* scratch_floats, size_t* counters) {
+  d.first_block = first_block;
+  d.colblocks = (int)((d.n + 31) / 32);
+  d.nchunks = d.nparts > 2 * kReduceChunk ? (d.nparts + kReduceChunk - 1) / kReduceChunk : 1;
+  *scratch_floats = d.nchunks > 1 ? (size_t)d.nchunks * d.n : 0;
+  *counters = d.nchunks > 1 ? (size_t)d.colblocks : 0;
+  return d.colblocks * d.nchunks;
+}
+
+void reduce_batched(const ReduceDesc* descs, int ndesc, int total_blocks, cudaStream_t st) {
+  if (ndesc > 0 && total_blocks > 0) reduce_batched_kernel<<<total_blocks, dim3(32, kYLanes), 0, st>>>(descs, ndesc);
+}
+
 static float* g_scratch = nullptr;
 static size_t g_scratch_n = 0;
 

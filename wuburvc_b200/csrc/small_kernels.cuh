@@ -23,6 +23,25 @@ void wgrad_finish(const float* part, int splits, int rows, int n_total, const in
                   int dim0_rows, const float* v, const float* g, const float* norm, float* dv, float* dg,
                   cudaStream_t st);
 
+// Many column reductions in one launch: out_i[j] = sum_{p < nparts_i} part_i[p * ld_i + j], j < n_i.
+// A descriptor is served by colblocks x nchunks blocks (32 columns x up to kReduceChunk parts each);
+// with several chunks, each block stores its chunk sum in `scratch` [nchunks][n] and the last block of
+// a column group (counted in `counter`, which it resets) adds the chunk sums in chunk order, so the
+// result does not depend on block scheduling.
+constexpr int kReduceChunk = 64;
+struct ReduceDesc {
+  const float* part;
+  float* out;
+  long long ld, n;
+  int nparts, first_block, colblocks, nchunks;
+  float* scratch;          // nchunks * n floats when nchunks > 1
+  unsigned int* counter;   // colblocks zeroed words when nchunks > 1
+};
+// Fills the launch shape of d (first_block = blocks already in the table); returns its block count and
+// the scratch floats / counters it needs.
+int reduce_desc_shape(ReduceDesc& d, int first_block, size_t* scratch_floats, size_t* counters);
+void reduce_batched(const ReduceDesc* descs, int ndesc, int total_blocks, cudaStream_t st);
+
 // column sums of per-tile partials part[tiles][C]
 void colsum_reduce(const float* part, int tiles, int C, float* out, int accumulate, float* scratch,
                    size_t scratch_floats, cudaStream_t st);
