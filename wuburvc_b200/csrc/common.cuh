@@ -21,9 +21,15 @@ enum : int {
   ERR_BAD_SHAPE = 4,
 };
 
-// Upper bound on mbarrier polls before a kernel declares a timeout.  Each
-// try_wait may suspend for a while, so this is a few seconds of waiting.
-constexpr uint32_t kWaitLimit = 1u << 24;
+// Time after which a bounded mbarrier wait gives up and the kernel reports a timeout (ns of
+// %globaltimer; far above any legitimate wait, short enough that a broken pipeline ends quickly).
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+
+WB_DEV unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
 WB_DEV uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -56,7 +62,9 @@ WB_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Bounded wait: returns false (and records `code`) if the phase never flips.
 WB_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i)
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_ns();
+  while (global_ns() - t0 < kWaitLimitNs)
     if (mbar_try_wait(bar, parity)) return true;
   if (err) atomicCAS(err, 0, code);
   return false;
@@ -98,6 +106,75 @@ WB_DEV void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t i
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
+}
+
+// ---- warp-converged issue ----------------------------------------------------------------------
+// The producer and MMA roles run their loops with all 32 lanes converged, so descriptors and
+// coordinates are warp-uniform values (uniform registers); one lane chosen by elect.sync (the lowest,
+// i.e. always the same lane) issues the asynchronous instruction.  Issuing from a lane-0-only branch
+// instead makes every tcgen05.mma pay a register-to-uniform conversion of its operands.
+WB_DEV void umma_f16_warp(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+WB_DEV void umma_commit_warp(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(smem_u32(bar))
+      : "memory");
+}
+
+WB_DEV void mbar_expect_tx_warp(uint64_t* bar, uint32_t bytes) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n\t}" ::"r"(smem_u32(bar)),
+      "r"(bytes)
+      : "memory");
+}
+
+WB_DEV void tma_load_3d_warp(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];\n\t}" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Bounded wait by a converged warp; every lane gets the same verdict.  The spin loop lives inside one
+// asm block so the compiler sees no divergent control flow around the issuing code (a C++ loop here
+// makes it treat descriptors as per-lane values and every tcgen05.mma pays for uniformising them).
+WB_DEV bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* err, int code) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t.reg .u64 t0, t1;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "@p bra WB_WAIT_DONE;\n\t"
+      "mov.u64 t0, %%globaltimer;\n"
+      "WB_WAIT_LOOP:\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "@p bra WB_WAIT_DONE;\n\t"
+      "mov.u64 t1, %%globaltimer;\n\t"
+      "sub.u64 t1, t1, t0;\n\t"
+      "setp.lt.u64 q, t1, %3;\n\t"
+      "@q bra WB_WAIT_LOOP;\n"
+      "WB_WAIT_DONE:\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity), "l"(kWaitLimitNs)
+      : "memory");
+  const bool ok = __all_sync(0xffffffffu, done != 0);
+  if (!ok && err && (threadIdx.x & 31) == 0) atomicCAS(err, 0, code);
+  return ok;
 }
 
 // Arrive on `bar` once every previously issued tcgen05.mma of this thread completes.

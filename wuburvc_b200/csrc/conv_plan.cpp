@@ -165,12 +165,9 @@ bool plan_conv2(Conv2Launch& L, const ConvGeom& g, const void* x_hi, const void*
   const int R = (128 + span + 7) / 8 * 8;
   if (R > 256) return false;
   p.ntaps = g.k;
+  p.dil = g.dil;
   p.halo_start = -g.pad;
   p.halo_rows = R;
-  for (int t = 0; t < g.k; ++t) {
-    p.tap_off[t] = (short)(g.dil * t);
-    p.tap_w[t] = (short)t;
-  }
   p.tiles_per_item = (g.T_out + 127) / 128;
   const int mtiles = g.B * p.tiles_per_item;
   // split N in two when the row tiles alone cannot fill the SMs
@@ -183,16 +180,32 @@ bool plan_conv2(Conv2Launch& L, const ConvGeom& g, const void* x_hi, const void*
   p.epi = epi;
   p.err = err;
   const int nA = split ? 2 : 1;
+  // weights: resident (every chunk and tap of the CTA's N tile loaded once) when they fit beside two
+  // A stages, else a ring of stages holding w_group taps each (fewer, larger stages: each stage costs
+  // the MMA warp one barrier round trip)
   int kc = (g.C_in % 64 == 0) ? 64 : 32;
   for (;;) {
     const size_t a_sub = ((size_t)R * kc * 2 + 1023) / 1024 * 1024;
-    const size_t a_stage = nA * a_sub, w_stage = (size_t)nA * p.n * kc * 2;
+    const size_t a_stage = nA * a_sub, w_tap = (size_t)nA * p.n * kc * 2;
+    const long long nch = g.C_in / kc;
     p.a_stages = 2;
     const long long room = (long long)kSmemBudget - 2048 - (long long)p.a_stages * a_stage;
-    p.w_stages = room > 0 ? (int)std::min<long long>(8, room / (long long)w_stage) : 0;
-    if (p.w_stages >= 3 || (p.w_stages >= 2 && kc == 32)) {
+    const long long total_w = nch * g.k * (long long)w_tap;
+    if (room > 0 && total_w <= room) {
+      p.w_resident = 1;
+      p.w_group = g.k;
+      p.w_stages = 1;
       p.a_sub_bytes = (uint32_t)a_sub;
-      L.smem = p.a_stages * a_stage + p.w_stages * w_stage + 1024 + 512;
+      L.smem = p.a_stages * a_stage + (size_t)total_w + 1024 + 512;
+      break;
+    }
+    const long long G = room > 0 ? std::min<long long>(g.k, room / (2 * (long long)w_tap)) : 0;
+    if (G >= 1) {
+      p.w_resident = 0;
+      p.w_group = (int)G;
+      p.w_stages = (int)std::min<long long>(4, room / (G * (long long)w_tap));
+      p.a_sub_bytes = (uint32_t)a_sub;
+      L.smem = p.a_stages * a_stage + (size_t)p.w_stages * G * w_tap + 1024 + 512;
       break;
     }
     if (kc == 32) return false;

@@ -94,11 +94,12 @@ struct TcConv2Params {
   int n_chunks;             // C_in / KC
   int split;
   int ntaps;
+  int dil;                  // tap t reads halo rows t*dil .. t*dil+127
   int halo_start;           // row offset of the halo tile relative to the tile's first output row
   int halo_rows;            // 128 + taps span
-  short tap_off[kMaxTaps2]; // row offset of each tap inside the halo tile
-  short tap_w[kMaxTaps2];   // weight tap index
   int a_stages, w_stages;
+  int w_group;              // taps per weight stage
+  int w_resident;           // every weight tap of the CTA's N tile is loaded once and kept
   uint32_t a_sub_bytes;     // one A (hi or lo) halo tile, 1024-aligned
   int tmem_cols;            // 2 accumulators
   Epi epi;

@@ -18,20 +18,28 @@ constexpr int kConv2Threads = 320;
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
 
-template <int KC>
+// Shared memory: [A stages][W stages or resident W][barriers].  A stage = halo tile (hi[, lo]) of one
+// channel chunk; a weight stage holds `w_group` taps of one chunk, each tap hi[, lo] (N x KC, swizzled);
+// resident weights hold every (chunk, tap) of the CTA's N tile in the same per-tap layout, loaded once.
+template <int KC, bool SPLIT>
 __global__ void __launch_bounds__(kConv2Threads, 1)
     tc_conv2_kernel(const __grid_constant__ TcConv2Maps maps, const __grid_constant__ TcConv2Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ float red[2][128];
 
+  constexpr int nA = SPLIT ? 2 : 1;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int N = p.n;
-  const int nA = p.split ? 2 : 1;
-  const uint32_t a_stage = nA * p.a_sub_bytes;
-  const uint32_t w_sub = (uint32_t)N * KC * 2u;
-  const uint32_t w_stage = nA * w_sub;
-  const int AS = p.a_stages, WS = p.w_stages;
+  const int ntaps = p.ntaps, nch = p.n_chunks, G = p.w_group, dil = p.dil;
+  const bool resident = p.w_resident != 0;
+  const int ngroups = resident ? 1 : (ntaps + G - 1) / G;
+  const uint32_t a_sub = p.a_sub_bytes;
+  const uint32_t a_stage = nA * a_sub;
+  const uint32_t w_sub = (uint32_t)N * KC * 2u;  // one tap, hi or lo
+  const uint32_t w_tap = nA * w_sub;
+  const uint32_t w_stage = resident ? (uint32_t)(nch * ntaps) * w_tap : (uint32_t)G * w_tap;
+  const int AS = p.a_stages, WS = resident ? 1 : p.w_stages;
 
   uint8_t* a_base = smem;
   uint8_t* w_base = smem + (size_t)AS * a_stage;
@@ -55,94 +63,115 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  // Producer and MMA roles: whole warps with a warp-uniform `ok` flag instead of early exits (a
+  // break out of these loops makes the compiler treat the issuing code as divergent, which costs
+  // the MMA issue rate); after a timed-out wait the loops run on without issuing anything.
   if (warp == kProducerWarp) {
     // ---------------- TMA producer ----------------
-    if (lane == 0) {
-      int a_it = 0, w_it = 0;
-      bool ok = true;
-      for (int tile = blockIdx.x; tile < p.ntiles && ok; tile += gridDim.x) {
-        const int mtile = tile / p.n_tiles;
-        const int n0 = (tile - mtile * p.n_tiles) * N;
-        const int item = mtile / p.tiles_per_item;
-        const int q0 = (mtile - item * p.tiles_per_item) * 128;
-        for (int c = 0; c < p.n_chunks && ok; ++c) {
-          const int sa = a_it % AS;
-          if (a_it >= AS && !mbar_wait(&a_empty[sa], ((a_it / AS) & 1) ^ 1, p.err, ERR_WAIT_EMPTY)) { ok = false; break; }
+    bool ok = true;
+    const int n0_cta = (blockIdx.x % p.n_tiles) * N;  // every tile of this CTA has this N tile
+    if (resident) {
+      mbar_expect_tx_warp(&w_full[0], (uint32_t)(nch * ntaps) * w_tap);
+      for (int c = 0; c < nch; ++c)
+        for (int t = 0; t < ntaps; ++t) {
+          uint8_t* wd = w_base + (size_t)(c * ntaps + t) * w_tap;
+          tma_load_3d_warp(wd, &maps.w_hi, &w_full[0], c * KC, n0_cta, t);
+          if (SPLIT) tma_load_3d_warp(wd + w_sub, &maps.w_lo, &w_full[0], c * KC, n0_cta, t);
+        }
+    }
+    int sa = 0, sw = 0;
+    uint32_t aph = 0, wph = 0;
+    int a_uses = 0, w_uses = 0;
+    const uint32_t colb = (uint32_t)p.halo_rows * 16u;  // 8-channel core-matrix column: R rows x 16 B
+    for (int tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x) {
+      const int mtile = tile / p.n_tiles;
+      const int item = mtile / p.tiles_per_item;
+      const int q0 = (mtile - item * p.tiles_per_item) * 128;
+      for (int c = 0; c < nch; ++c) {
+        if (ok && a_uses >= AS) ok = mbar_wait_warp(&a_empty[sa], aph ^ 1u, p.err, ERR_WAIT_EMPTY);
+        if (ok) {
           uint8_t* ad = a_base + (size_t)sa * a_stage;
-          mbar_arrive_expect_tx(&a_full[sa], (uint32_t)nA * (uint32_t)p.halo_rows * KC * 2u);
-          // one box of R rows x 8 channels per core-matrix column: column j lands at j * R * 16 bytes
-          const uint32_t colb = (uint32_t)p.halo_rows * 16u;
+          mbar_expect_tx_warp(&a_full[sa], nA * (uint32_t)p.halo_rows * KC * 2u);
 #pragma unroll
           for (int j = 0; j < KC / 8; ++j) {
-            tma_load_3d(ad + j * colb, &maps.a_hi, &a_full[sa], c * KC + j * 8, q0 + p.halo_start, item);
-            if (p.split)
-              tma_load_3d(ad + p.a_sub_bytes + j * colb, &maps.a_lo, &a_full[sa], c * KC + j * 8, q0 + p.halo_start,
-                          item);
+            tma_load_3d_warp(ad + j * colb, &maps.a_hi, &a_full[sa], c * KC + j * 8, q0 + p.halo_start, item);
+            if (SPLIT)
+              tma_load_3d_warp(ad + a_sub + j * colb, &maps.a_lo, &a_full[sa], c * KC + j * 8, q0 + p.halo_start,
+                               item);
           }
-          ++a_it;
-          for (int t = 0; t < p.ntaps; ++t) {
-            const int sw = w_it % WS;
-            if (w_it >= WS && !mbar_wait(&w_empty[sw], ((w_it / WS) & 1) ^ 1, p.err, ERR_WAIT_EMPTY)) { ok = false; break; }
+        }
+        ++a_uses;
+        if (++sa == AS) { sa = 0; aph ^= 1u; }
+        if (resident) continue;
+        for (int g = 0; g < ngroups; ++g) {
+          const int t0 = g * G, nt = min(G, ntaps - t0);
+          if (ok && w_uses >= WS) ok = mbar_wait_warp(&w_empty[sw], wph ^ 1u, p.err, ERR_WAIT_EMPTY);
+          if (ok) {
             uint8_t* wd = w_base + (size_t)sw * w_stage;
-            mbar_arrive_expect_tx(&w_full[sw], w_stage);
-            tma_load_3d(wd, &maps.w_hi, &w_full[sw], c * KC, n0, p.tap_w[t]);
-            if (p.split) tma_load_3d(wd + w_sub, &maps.w_lo, &w_full[sw], c * KC, n0, p.tap_w[t]);
-            ++w_it;
+            mbar_expect_tx_warp(&w_full[sw], (uint32_t)nt * w_tap);
+            for (int j = 0; j < nt; ++j) {
+              tma_load_3d_warp(wd + j * w_tap, &maps.w_hi, &w_full[sw], c * KC, n0_cta, t0 + j);
+              if (SPLIT) tma_load_3d_warp(wd + j * w_tap + w_sub, &maps.w_lo, &w_full[sw], c * KC, n0_cta, t0 + j);
+            }
           }
+          ++w_uses;
+          if (++sw == WS) { sw = 0; wph ^= 1u; }
         }
       }
     }
   } else if (warp == kMmaWarp) {
     // ---------------- MMA issuer ----------------
-    if (lane == 0) {
-      const uint32_t idesc = make_idesc_bf16(128, N, 0, 0);
-      constexpr uint32_t wlayout = (KC == 64) ? 2u : 4u;
-      constexpr uint32_t wsbo = (KC == 64) ? 1024u : 512u;
-      const uint32_t a_lbo = (uint32_t)p.halo_rows * 16u;  // stride between 8-channel core-matrix columns
-      const uint32_t abase = smem_u32(a_base), wbase = smem_u32(w_base);
-      int a_it = 0, w_it = 0, t_it = 0;
-      bool ok = true;
-      for (int tile = blockIdx.x; tile < p.ntiles && ok; tile += gridDim.x, ++t_it) {
-        const int buf = t_it & 1;
-        if (t_it >= 2 && !mbar_wait(&acc_empty[buf], ((t_it >> 1) & 1) ^ 1, p.err, ERR_WAIT_ACC)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t d = tmem + (uint32_t)(buf * N);
-        bool first = true;
-        for (int c = 0; c < p.n_chunks && ok; ++c) {
-          const int sa = a_it % AS;
-          if (!mbar_wait(&a_full[sa], (a_it / AS) & 1, p.err, ERR_WAIT_FULL)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t ah = abase + (uint32_t)sa * a_stage;
-          const uint32_t al = ah + p.a_sub_bytes;
-          for (int t = 0; t < p.ntaps; ++t) {
-            const int sw = w_it % WS;
-            if (!mbar_wait(&w_full[sw], (w_it / WS) & 1, p.err, ERR_WAIT_FULL)) { ok = false; break; }
-            tc_fence_after();
-            const uint32_t wh = wbase + (uint32_t)sw * w_stage;
-            const uint32_t wl = wh + w_sub;
-            const uint32_t toff = (uint32_t)p.tap_off[t] * 16u;
+    const uint32_t idesc = make_idesc_bf16(128, N, 0, 0);
+    constexpr uint32_t wlayout = (KC == 64) ? 2u : 4u;
+    constexpr uint32_t wsbo = (KC == 64) ? 1024u : 512u;
+    const uint32_t a_lbo = (uint32_t)p.halo_rows * 16u;  // stride between 8-channel core-matrix columns
+    // descriptors are built once; a tap / k-step / stage moves the 14-bit start-address field
+    const uint64_t da0 = make_sdesc(smem_u32(a_base), a_lbo, 128, 0);
+    const uint64_t dw0 = make_sdesc(smem_u32(w_base), 16, wsbo, wlayout);
+    const uint32_t tap_step = (uint32_t)dil;             // 16-byte units per tap (dil rows)
+    const uint32_t k_step_a = (2u * a_lbo) >> 4;          // two core-matrix columns
+    bool ok = true;
+    if (resident) ok = mbar_wait_warp(&w_full[0], 0, p.err, ERR_WAIT_FULL);
+    int sa = 0, sw = 0, t_it = 0;
+    uint32_t aph = 0, wph = 0;
+    for (int tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x, ++t_it) {
+      const int buf = t_it & 1;
+      if (ok && t_it >= 2) ok = mbar_wait_warp(&acc_empty[buf], ((t_it >> 1) & 1) ^ 1, p.err, ERR_WAIT_ACC);
+      tc_fence_after();
+      const uint32_t d = tmem + (uint32_t)(buf * N);
+      for (int c = 0; c < nch; ++c) {
+        if (ok) ok = mbar_wait_warp(&a_full[sa], aph, p.err, ERR_WAIT_FULL);
+        const uint64_t dah = da0 + (uint64_t)((sa * a_stage) >> 4);
+        const uint64_t dal = dah + (uint64_t)(a_sub >> 4);
+        for (int g = 0; g < ngroups; ++g) {
+          const int t0 = resident ? 0 : g * G;
+          const int nt = resident ? ntaps : min(G, ntaps - t0);
+          if (!resident && ok) ok = mbar_wait_warp(&w_full[sw], wph, p.err, ERR_WAIT_FULL);
+          if (ok) {
+            const uint32_t wst = resident ? (uint32_t)(c * ntaps) * w_tap : (uint32_t)sw * w_stage;
+            for (int j = 0; j < nt; ++j) {
+              const uint64_t dwh = dw0 + (uint64_t)((wst + (uint32_t)j * w_tap) >> 4);
+              const uint64_t dwl = dwh + (uint64_t)(w_sub >> 4);
+              const uint32_t at = (uint32_t)(t0 + j) * tap_step;
+              const uint32_t acc0 = (c | t0 | j) ? 1u : 0u;
 #pragma unroll
-            for (int k = 0; k < KC / 16; ++k) {
-              const uint32_t aoff = toff + (uint32_t)k * 2u * a_lbo;
-              const uint64_t dah = make_sdesc(ah + aoff, a_lbo, 128, 0);
-              const uint64_t dwh = make_sdesc(wh + (uint32_t)k * 32u, 16, wsbo, wlayout);
-              umma_f16(d, dah, dwh, idesc, first ? 0u : 1u);
-              first = false;
-              if (p.split) {
-                const uint64_t dal = make_sdesc(al + aoff, a_lbo, 128, 0);
-                const uint64_t dwl = make_sdesc(wl + (uint32_t)k * 32u, 16, wsbo, wlayout);
-                umma_f16(d, dal, dwh, idesc, 1);
-                umma_f16(d, dah, dwl, idesc, 1);
+              for (int k = 0; k < KC / 16; ++k) {
+                const uint64_t ao = at + (uint32_t)k * k_step_a;
+                umma_f16_warp(d, dah + ao, dwh + 2u * k, idesc, k ? 1u : acc0);
+                if (SPLIT) {
+                  umma_f16_warp(d, dal + ao, dwh + 2u * k, idesc, 1);
+                  umma_f16_warp(d, dah + ao, dwl + 2u * k, idesc, 1);
+                }
               }
             }
-            umma_commit(&w_empty[sw]);
-            ++w_it;
+            if (!resident) umma_commit_warp(&w_empty[sw]);
           }
-          umma_commit(&a_empty[sa]);
-          ++a_it;
+          if (!resident && ++sw == WS) { sw = 0; wph ^= 1u; }
         }
-        if (ok) umma_commit(&acc_full[buf]);
+        if (ok) umma_commit_warp(&a_empty[sa]);
+        if (++sa == AS) { sa = 0; aph ^= 1u; }
       }
+      if (ok) umma_commit_warp(&acc_full[buf]);
     }
   } else {
     // ---------------- epilogue: two groups of 4 warps; group g drains TMEM accumulator g, i.e. every
@@ -154,11 +183,11 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
 #pragma unroll
     for (int i = 0; i < 8; ++i) cs_acc[i] = ap_acc[i] = 0.f;
     int t_it = grp;
+    bool ok = true;
     for (int tile = blockIdx.x + grp * gridDim.x; tile < p.ntiles; tile += 2 * gridDim.x, t_it += 2) {
       const int buf = grp;
-      const bool ok = mbar_wait(&acc_full[buf], (t_it >> 1) & 1, p.err, ERR_WAIT_ACC);
+      if (ok) ok = mbar_wait_warp(&acc_full[buf], (t_it >> 1) & 1, p.err, ERR_WAIT_ACC);
       tc_fence_after();
-      if (!ok) break;
       const int mtile = tile / p.n_tiles;
       const int n0 = (tile - mtile * p.n_tiles) * N;
       const int item = mtile / p.tiles_per_item;
@@ -170,8 +199,12 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
 #pragma unroll 1
       for (int c0 = 0; c0 < N; c0 += 32) {
         float v[32];
-        tmem_ld32(tmem + (uint32_t)(buf * N) + ((uint32_t)(qw * 32) << 16) + (uint32_t)c0, v);
-        epi_chunk(p.epi, v, valid, row_off + c0, n0 + c0, part_row + c0, ra ? ra + c0 : nullptr, qw, lane,
+        if (ok) tmem_ld32(tmem + (uint32_t)(buf * N) + ((uint32_t)(qw * 32) << 16) + (uint32_t)c0, v);
+        else
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = 0.f;
+        // the chunk's named barriers are reached by the whole group whether or not the wait succeeded
+        epi_chunk(p.epi, v, valid && ok, row_off + c0, n0 + c0, part_row + c0, ra ? ra + c0 : nullptr, qw, lane,
                   red[grp], &cs_acc[c0 >> 5], &ap_acc[c0 >> 5], 1 + grp);
       }
       tc_fence_before();
@@ -201,10 +234,13 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
 }
 
 void tc_conv2_set_smem_limit(int lim) {
-  const cudaError_t a = cudaFuncSetAttribute(tc_conv2_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
-  const cudaError_t b = cudaFuncSetAttribute(tc_conv2_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
-  if (a != cudaSuccess || b != cudaSuccess)
-    fprintf(stderr, "wuburvc_b200: tc_conv2 smem limit: %s / %s\n", cudaGetErrorString(a), cudaGetErrorString(b));
+  const cudaError_t e[4] = {
+      cudaFuncSetAttribute(tc_conv2_kernel<64, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim),
+      cudaFuncSetAttribute(tc_conv2_kernel<64, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim),
+      cudaFuncSetAttribute(tc_conv2_kernel<32, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim),
+      cudaFuncSetAttribute(tc_conv2_kernel<32, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim)};
+  for (int i = 0; i < 4; ++i)
+    if (e[i] != cudaSuccess) fprintf(stderr, "wuburvc_b200: tc_conv2 smem limit %d: %s\n", i, cudaGetErrorString(e[i]));
 }
 
 void tc_kernels_init();  // tc_conv.cu
@@ -212,10 +248,13 @@ void tc_kernels_init();  // tc_conv.cu
 cudaError_t launch_tc_conv2(const TcConv2Maps& maps, const TcConv2Params& p, int kc, int grid, size_t smem,
                             cudaStream_t st) {
   tc_kernels_init();
-  if (kc == 64)
-    tc_conv2_kernel<64><<<grid, kConv2Threads, smem, st>>>(maps, p);
-  else
-    tc_conv2_kernel<32><<<grid, kConv2Threads, smem, st>>>(maps, p);
+  if (kc == 64) {
+    if (p.split) tc_conv2_kernel<64, true><<<grid, kConv2Threads, smem, st>>>(maps, p);
+    else tc_conv2_kernel<64, false><<<grid, kConv2Threads, smem, st>>>(maps, p);
+  } else {
+    if (p.split) tc_conv2_kernel<32, true><<<grid, kConv2Threads, smem, st>>>(maps, p);
+    else tc_conv2_kernel<32, false><<<grid, kConv2Threads, smem, st>>>(maps, p);
+  }
   return cudaGetLastError();
 }
 
