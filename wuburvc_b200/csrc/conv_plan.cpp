@@ -32,6 +32,9 @@ int pow2_cols(int n) {
 }
 
 constexpr size_t kSmemBudget = 220 * 1024;
+// the persistent conv keeps ~24 KB of static shared memory (epilogue vectors, column sums, the
+// epilogue warps' store staging)
+constexpr size_t kSmemBudget2 = 200 * 1024;
 
 }  // namespace
 
@@ -189,7 +192,7 @@ bool plan_conv2(Conv2Launch& L, const ConvGeom& g, const void* x_hi, const void*
     const size_t a_stage = nA * a_sub, w_tap = (size_t)nA * p.n * kc * 2;
     const long long nch = g.C_in / kc;
     p.a_stages = 2;
-    const long long room = (long long)kSmemBudget - 2048 - (long long)p.a_stages * a_stage;
+    const long long room = (long long)kSmemBudget2 - 2048 - (long long)p.a_stages * a_stage;
     const long long total_w = nch * g.k * (long long)w_tap;
     if (room > 0 && total_w <= room) {
       p.w_resident = 1;

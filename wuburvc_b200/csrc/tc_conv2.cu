@@ -21,12 +21,16 @@ constexpr int kMmaWarp = 9;
 // Shared memory: [A stages][W stages or resident W][barriers].  A stage = halo tile (hi[, lo]) of one
 // channel chunk; a weight stage holds `w_group` taps of one chunk, each tap hi[, lo] (N x KC, swizzled);
 // resident weights hold every (chunk, tap) of the CTA's N tile in the same per-tap layout, loaded once.
-template <int KC, bool SPLIT>
+template <int KC, bool SPLIT, uint32_t F>
 __global__ void __launch_bounds__(kConv2Threads, 1)
     tc_conv2_kernel(const __grid_constant__ TcConv2Maps maps, const __grid_constant__ TcConv2Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ float red[2][128];
+  // epilogue vectors of this CTA's N tile, and the groups' running column sums
+  __shared__ __align__(16) float s_bias[256], s_aalpha[256], s_malpha[256];
+  __shared__ float s_csum[2][256], s_asum[2][256];
+  __shared__ uint4 s_stage[8][128];  // per epilogue warp: 32 rows x 64 B of outgoing data
 
   constexpr int nA = SPLIT ? 2 : 1;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -59,6 +63,14 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
     fence_barrier_init();
   }
   if (warp == kMmaWarp) tmem_alloc(tmem_slot, (uint32_t)p.tmem_cols);
+  if (threadIdx.x < 256) {
+    const int i = threadIdx.x, col = (blockIdx.x % p.n_tiles) * N + i;
+    const bool in_tile = i < N;
+    s_bias[i] = (in_tile && p.epi.bias) ? p.epi.bias[col] : 0.f;
+    s_aalpha[i] = (in_tile && p.epi.act_alpha) ? p.epi.act_alpha[col] : 1.f;
+    s_malpha[i] = (in_tile && p.epi.mask_alpha) ? p.epi.mask_alpha[col] : 1.f;
+    s_csum[0][i] = s_csum[1][i] = s_asum[0][i] = s_asum[1][i] = 0.f;
+  }
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
@@ -177,51 +189,64 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
     // ---------------- epilogue: two groups of 4 warps; group g drains TMEM accumulator g, i.e. every
     // other tile, so two tiles' epilogues run concurrently (warp w reads TMEM lane quadrant w%4) ----------------
     const int qw = warp & 3, grp = warp >> 2;
-    // column sums (bias / Snake-alpha gradients) accumulate over the group's tiles: one partial row
-    // per group, 2 per CTA
-    float cs_acc[8], ap_acc[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) cs_acc[i] = ap_acc[i] = 0.f;
+    const Epi& e = p.epi;
+    const int n0 = (blockIdx.x % p.n_tiles) * N;  // every tile of this CTA has this N tile
+    const float* bias = e.bias ? s_bias : nullptr;
+    const float* aal = e.act_alpha ? s_aalpha : nullptr;
+    const float* mal = e.mask_alpha ? s_malpha : nullptr;
     int t_it = grp;
     bool ok = true;
     for (int tile = blockIdx.x + grp * gridDim.x; tile < p.ntiles; tile += 2 * gridDim.x, t_it += 2) {
       const int buf = grp;
-      if (ok) ok = mbar_wait_warp(&acc_full[buf], (t_it >> 1) & 1, p.err, ERR_WAIT_ACC);
-      tc_fence_after();
       const int mtile = tile / p.n_tiles;
-      const int n0 = (tile - mtile * p.n_tiles) * N;
       const int item = mtile / p.tiles_per_item;
       const int q = (mtile - item * p.tiles_per_item) * 128 + qw * 32 + lane;
       const bool valid = q < p.t_rows;
       const size_t row_off = ((size_t)item * p.t_rows + (valid ? q : 0)) * p.n_total + n0;
-      const size_t part_row = (size_t)tile * p.n_total + n0;  // unused: sums accumulate per CTA
-      const float* ra = p.epi.rowadd ? p.epi.rowadd + (size_t)item * p.n_total + n0 : nullptr;
+      const float* ra = e.rowadd ? e.rowadd + (size_t)item * p.n_total + n0 : nullptr;
+      const int wrow0 = (mtile - item * p.tiles_per_item) * 128 + qw * 32;  // warp's first output row
+      RowOut o;
+      o.stage = s_stage[warp];
+      o.off0 = ((size_t)item * p.t_rows + wrow0) * p.n_total + n0;
+      o.pitch = (size_t)p.n_total;
+      o.rows_valid = ok ? max(0, min(32, p.t_rows - wrow0)) : 0;
+      o.lane = lane;
+      // the first chunk's inputs are in flight while the accumulator is still being computed
+      EpiIn in;
+      epi_load<F>(e, valid, row_off, in);
+      if (ok) ok = mbar_wait_warp(&acc_full[buf], (t_it >> 1) & 1, p.err, ERR_WAIT_ACC);
+      tc_fence_after();
 #pragma unroll 1
       for (int c0 = 0; c0 < N; c0 += 32) {
+        if (c0) epi_load<F>(e, valid, row_off + c0, in);
         float v[32];
         if (ok) tmem_ld32(tmem + (uint32_t)(buf * N) + ((uint32_t)(qw * 32) << 16) + (uint32_t)c0, v);
         else
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = 0.f;
         // the chunk's named barriers are reached by the whole group whether or not the wait succeeded
-        epi_chunk(p.epi, v, valid && ok, row_off + c0, n0 + c0, part_row + c0, ra ? ra + c0 : nullptr, qw, lane,
-                  red[grp], &cs_acc[c0 >> 5], &ap_acc[c0 >> 5], 1 + grp);
+        float cs = 0.f, ap = 0.f;
+        epi_finish<F>(e, v, in, valid && ok, row_off + c0, 0, ra ? ra + c0 : nullptr, bias ? bias + c0 : nullptr,
+                   aal ? aal + c0 : nullptr, mal ? mal + c0 : nullptr, qw, lane, red[grp], &cs, &ap, 1 + grp, true,
+                   o);
+        o.off0 += 32;
+        if (qw == 0) {  // column sums accumulate over the group's tiles (warp 0 holds this tile's)
+          s_csum[grp][c0 + lane] += cs;
+          s_asum[grp][c0 + lane] += ap;
+        }
       }
       tc_fence_before();
       asm volatile("bar.sync %0, 128;" ::"r"(3 + grp) : "memory");
       if (qw == 0 && lane == 0) mbar_arrive(&acc_empty[buf]);
     }
     if (qw == 0) {
-      // every tile of this CTA shares one N tile (the grid is a multiple of n_tiles): the group's partial
-      // row holds its sums in that tile's columns and zeros elsewhere
-      const int my_n0 = (blockIdx.x % p.n_tiles) * N;
+      // one partial row per group (2 per CTA): its sums in this CTA's N tile, zeros elsewhere
       const size_t prow = (size_t)(2 * blockIdx.x + grp) * p.n_total;
       for (int c = 0; c < p.n_total; c += 32) {
-        const int rel = c - my_n0;
+        const int rel = c - n0;
         const bool mine = rel >= 0 && rel < N;
-        const float cs = mine ? cs_acc[rel >> 5] : 0.f, ap = mine ? ap_acc[rel >> 5] : 0.f;
-        if (p.epi.colsum) p.epi.colsum[prow + c + lane] = cs;
-        if (p.epi.alpha_part) p.epi.alpha_part[prow + c + lane] = ap;
+        if (e.colsum) e.colsum[prow + c + lane] = mine ? s_csum[grp][rel + lane] : 0.f;
+        if (e.alpha_part) e.alpha_part[prow + c + lane] = mine ? s_asum[grp][rel + lane] : 0.f;
       }
     }
   }
@@ -233,14 +258,36 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
   }
 }
 
+// Instantiated (KC, SPLIT, epilogue feature set) combinations: the forward (bf16x3) and input-gradient
+// epilogues of the resblock convolutions, plus a generic kernel for any other epilogue.
+#define WB_CONV2_KERNELS(X)                                                                     \
+  X(64, true, kEpiGeneric) X(64, true, kEpiAct) X(64, true, kEpiAct | kEpiSnake)                 \
+  X(64, true, kEpiRes | kEpiAct) X(64, true, kEpiRes | kEpiAct | kEpiSnake) X(64, true, kEpiRes)  \
+  X(64, true, 0u) X(64, false, kEpiGeneric) X(64, false, kEpiMask | kEpiColsum)                 \
+  X(64, false, kEpiMask | kEpiColsum | kEpiSnake) X(64, false, kEpiMask | kEpiRes | kEpiColsum)  \
+  X(64, false, kEpiMask | kEpiRes | kEpiColsum | kEpiSnake)                                      \
+  X(32, true, kEpiGeneric) X(32, true, kEpiAct) X(32, true, kEpiAct | kEpiSnake)                 \
+  X(32, true, kEpiRes | kEpiAct) X(32, true, kEpiRes | kEpiAct | kEpiSnake) X(32, true, kEpiRes)  \
+  X(32, true, 0u) X(32, false, kEpiGeneric) X(32, false, kEpiMask | kEpiColsum)                 \
+  X(32, false, kEpiMask | kEpiColsum | kEpiSnake) X(32, false, kEpiMask | kEpiRes | kEpiColsum)  \
+  X(32, false, kEpiMask | kEpiRes | kEpiColsum | kEpiSnake)
+
+// `lim` = opt-in shared memory minus 1 KB; the kernels' own static shared memory comes off it too
 void tc_conv2_set_smem_limit(int lim) {
-  const cudaError_t e[4] = {
-      cudaFuncSetAttribute(tc_conv2_kernel<64, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim),
-      cudaFuncSetAttribute(tc_conv2_kernel<64, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim),
-      cudaFuncSetAttribute(tc_conv2_kernel<32, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim),
-      cudaFuncSetAttribute(tc_conv2_kernel<32, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim)};
-  for (int i = 0; i < 4; ++i)
-    if (e[i] != cudaSuccess) fprintf(stderr, "wuburvc_b200: tc_conv2 smem limit %d: %s\n", i, cudaGetErrorString(e[i]));
+  int i = 0;
+#define WB_SET(kc, sp, f)                                                                          \
+  {                                                                                                \
+    const void* k = (const void*)tc_conv2_kernel<kc, sp, f>;                                       \
+    cudaFuncAttributes fa{};                                                                       \
+    cudaError_t e = cudaFuncGetAttributes(&fa, k);                                                 \
+    if (e == cudaSuccess)                                                                          \
+      e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,                     \
+                               lim + 1024 - (int)fa.sharedSizeBytes);                              \
+    if (e != cudaSuccess) fprintf(stderr, "wuburvc_b200: tc_conv2 smem limit %d: %s\n", i, cudaGetErrorString(e)); \
+    ++i;                                                                                           \
+  }
+  WB_CONV2_KERNELS(WB_SET)
+#undef WB_SET
 }
 
 void tc_kernels_init();  // tc_conv.cu
@@ -248,12 +295,24 @@ void tc_kernels_init();  // tc_conv.cu
 cudaError_t launch_tc_conv2(const TcConv2Maps& maps, const TcConv2Params& p, int kc, int grid, size_t smem,
                             cudaStream_t st) {
   tc_kernels_init();
-  if (kc == 64) {
-    if (p.split) tc_conv2_kernel<64, true><<<grid, kConv2Threads, smem, st>>>(maps, p);
-    else tc_conv2_kernel<64, false><<<grid, kConv2Threads, smem, st>>>(maps, p);
-  } else {
-    if (p.split) tc_conv2_kernel<32, true><<<grid, kConv2Threads, smem, st>>>(maps, p);
-    else tc_conv2_kernel<32, false><<<grid, kConv2Threads, smem, st>>>(maps, p);
+  const bool split = p.split != 0;
+  const uint32_t f = epi_features(p.epi);
+  bool done = false;
+#define WB_LAUNCH(kc_, sp, f_)                                                                     \
+  if (!done && kc == kc_ && split == sp && f == (f_)) {                                             \
+    tc_conv2_kernel<kc_, sp, f_><<<grid, kConv2Threads, smem, st>>>(maps, p);                      \
+    done = true;                                                                                   \
+  }
+  WB_CONV2_KERNELS(WB_LAUNCH)
+#undef WB_LAUNCH
+  if (!done) {  // any other epilogue: the generic instantiation
+    if (kc == 64) {
+      if (split) tc_conv2_kernel<64, true, kEpiGeneric><<<grid, kConv2Threads, smem, st>>>(maps, p);
+      else tc_conv2_kernel<64, false, kEpiGeneric><<<grid, kConv2Threads, smem, st>>>(maps, p);
+    } else {
+      if (split) tc_conv2_kernel<32, true, kEpiGeneric><<<grid, kConv2Threads, smem, st>>>(maps, p);
+      else tc_conv2_kernel<32, false, kEpiGeneric><<<grid, kConv2Threads, smem, st>>>(maps, p);
+    }
   }
   return cudaGetLastError();
 }

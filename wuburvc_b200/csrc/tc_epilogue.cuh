@@ -24,41 +24,74 @@ WB_DEV float warp_colsum32(float* v, int lane) {
   return v[0];
 }
 
-WB_DEV void load_bf16x32(const bf16* p, float* out) {
-  const uint4* q = reinterpret_cast<const uint4*>(p);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    uint4 u = q[i];
-    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float2 f = __bfloat1622float2(h[j]);
-      out[i * 8 + j * 2] = f.x;
-      out[i * 8 + j * 2 + 1] = f.y;
-    }
-  }
+// bf16 pairs packed in 32-bit words: element 2i in the low half.  Conversions stay in registers
+// (no arrays whose address is taken, which would put them on the stack).
+WB_DEV float bf16lo_f(uint32_t w) { return __uint_as_float(w << 16); }
+WB_DEV float bf16hi_f(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+// two floats -> packed bf16x2 (round to nearest even), one conversion instruction
+WB_DEV uint32_t pack_bf16(float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  uint32_t u;
+  memcpy(&u, &h, sizeof(u));
+  return u;
 }
 
-WB_DEV void store_bf16x32(bf16* p, const bf16* v) {
+WB_DEV void store_packed16(bf16* p, const uint32_t* w) {  // 16 words = 32 bf16 = 64 bytes
   uint4* q = reinterpret_cast<uint4*>(p);
-  const uint4* s = reinterpret_cast<const uint4*>(v);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) q[i] = s[i];
-}
-
-WB_DEV void load_f32x32(const float* p, float* out) {
-  const float4* q = reinterpret_cast<const float4*>(p);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    float4 f = q[i];
-    out[i * 4] = f.x; out[i * 4 + 1] = f.y; out[i * 4 + 2] = f.z; out[i * 4 + 3] = f.w;
-  }
+  for (int i = 0; i < 4; ++i) q[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
 }
 
 WB_DEV void store_f32x32(float* p, const float* v) {
   float4* q = reinterpret_cast<float4*>(p);
 #pragma unroll
   for (int i = 0; i < 8; ++i) q[i] = make_float4(v[i * 4], v[i * 4 + 1], v[i * 4 + 2], v[i * 4 + 3]);
+}
+
+// A warp's 32 rows x 64 bytes leave through its 2 KB staging buffer: each lane writes its row
+// (16-byte pieces XOR-swizzled by row, conflict-free), then the warp stores 8 rows x 64 B per
+// instruction, contiguous where the rows are (512 B when a row is 64 B).  Rows >= rows_valid are
+// not stored.  g0 = address of the warp's row 0 at this column piece.
+WB_DEV void stage_put64(uint4* st, int lane, const uint32_t* w, char* g0, size_t pitch_bytes, int rows_valid) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    st[lane * 4 + (i ^ ((lane >> 1) & 3))] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+  __syncwarp();
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int r = 8 * j + (lane >> 2), sg = lane & 3;
+    const uint4 x = st[r * 4 + (sg ^ ((r >> 1) & 3))];
+    if (r < rows_valid) *reinterpret_cast<uint4*>(g0 + (size_t)r * pitch_bytes + sg * 16) = x;
+  }
+  __syncwarp();
+}
+
+// Where the chunk's outputs go: the thread's own row (stage == null), or the warp's staging buffer.
+struct RowOut {
+  uint4* stage;    // warp's 2 KB staging buffer, or null for direct per-row stores
+  size_t off0;     // element offset of the warp's row 0 at this chunk (staged path)
+  size_t pitch;    // elements per row
+  int rows_valid;  // rows of the warp that exist (staged path)
+  int lane;
+};
+
+WB_DEV void out_bf16x32(const RowOut& o, bf16* base, size_t off, const uint32_t* w) {
+  if (o.stage) stage_put64(o.stage, o.lane, w, reinterpret_cast<char*>(base + o.off0), o.pitch * 2, o.rows_valid);
+  else store_packed16(base + off, w);
+}
+
+WB_DEV void out_f32x32(const RowOut& o, float* base, size_t off, const float* v) {
+  if (o.stage) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint32_t w[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) w[i] = __float_as_uint(v[16 * h + i]);
+      stage_put64(o.stage, o.lane, w, reinterpret_cast<char*>(base + o.off0 + 16 * h), o.pitch * 4, o.rows_valid);
+    }
+  } else {
+    store_f32x32(base + off, v);
+  }
 }
 
 // Column sums of v over the 128 rows of the four epilogue warps; warp 0 lane l gets column l.
@@ -74,27 +107,76 @@ WB_DEV float cta_colsum32(float* v, float* red /*smem [128]*/, int warp, int lan
   return t;
 }
 
-// Applies the epilogue to one 32-column chunk of one row.
+// Compile-time epilogue feature sets.  A kernel instantiated for a feature set F contains only that
+// set's code (smaller code, fewer registers); kEpiGeneric keeps every feature a run-time check.
+enum : uint32_t {
+  kEpiMask = 1u,     // activation-derivative mask from mask_src
+  kEpiSnake = 2u,    // Snake (else LeakyReLU) for the mask and the activation
+  kEpiRes = 4u,      // fp32 residual
+  kEpiColsum = 8u,   // column-sum partials of the result (bias gradient)
+  kEpiAct = 16u,     // activated bf16 hi/lo output
+  kEpiGeneric = 1u << 31,
+};
+
+// The feature set of an epilogue, as the kernels' template argument expects it.
+inline uint32_t epi_features(const Epi& e) {
+  const bool snake = e.act_kind == 1 && (e.mask_src || e.act_hi);
+  return (e.mask_src ? kEpiMask : 0u) | (snake ? kEpiSnake : 0u) | (e.res ? kEpiRes : 0u) |
+         (e.colsum ? kEpiColsum : 0u) | (e.act_hi ? kEpiAct : 0u);
+}
+
+#define WB_EPI_HAS(bit, runtime) ((F & kEpiGeneric) ? (runtime) : ((F & (bit)) != 0))
+
+// Per-row inputs of one 32-column chunk, loaded before they are needed (ideally before the
+// accumulator is ready) so their memory latency overlaps the wait.
+struct EpiIn {
+  uint4 m[4];   // mask source (bf16)
+  float4 r[8];  // residual
+};
+
+template <uint32_t F>
+WB_DEV void epi_load(const Epi& e, bool valid, size_t off, EpiIn& in) {
+  if (WB_EPI_HAS(kEpiMask, e.mask_src != nullptr) && valid) {
+    const uint4* q = reinterpret_cast<const uint4*>(e.mask_src + off);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) in.m[i] = __ldcs(q + i);
+  }
+  if (WB_EPI_HAS(kEpiRes, e.res != nullptr) && valid) {
+    const float4* q = reinterpret_cast<const float4*>(e.res + off);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) in.r[i] = __ldcs(q + i);
+  }
+}
+
+// Applies the epilogue to one 32-column chunk of one row (inputs from epi_load).
 //   off      element offset of (row, column c0) in every [B][T][n_total] tensor
 //   col      global column index of the chunk's first column (bias / alpha index)
 //   part_row offset of this tile's row in the [tiles][n_total] partial buffers (+col)
+//   bias / act_alpha / mask_alpha: the vectors at `col` (shared-memory copies in the persistent
+//   kernel, else e's global vectors offset by col)
 //   cs_acc / ap_acc: when non-null (persistent kernels), warp 0 accumulates this tile's column sums
 //   there instead of writing a per-tile partial.
-WB_DEV void epi_chunk(const Epi& e, float* v, bool valid, size_t off, int col, size_t part_row, const float* rowadd_row,
-                      int warp, int lane, float* red, float* cs_acc = nullptr, float* ap_acc = nullptr,
-                      int bar = 1) {
-  if (e.mask_src) {
+template <uint32_t F>
+WB_DEV void epi_finish(const Epi& e, float* v, const EpiIn& in, bool valid, size_t off, size_t part_row,
+                       const float* rowadd_row, const float* bias, const float* act_alpha, const float* mask_alpha,
+                       int warp, int lane, float* red, float* cs_acc, float* ap_acc, int bar,
+                       bool bias16 = false, const RowOut& o = RowOut{}) {
+  if (WB_EPI_HAS(kEpiMask, e.mask_src != nullptr)) {
     float x[32];
-    if (valid) load_bf16x32(e.mask_src + off, x);
-    else {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) x[i] = 0.f;
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t w[4] = {in.m[i].x, in.m[i].y, in.m[i].z, in.m[i].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        x[8 * i + 2 * j] = valid ? bf16lo_f(w[j]) : 0.f;
+        x[8 * i + 2 * j + 1] = valid ? bf16hi_f(w[j]) : 0.f;
+      }
     }
-    if (e.act_kind == 1) {
+    if (WB_EPI_HAS(kEpiSnake, e.act_kind == 1)) {
       float ga[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        const float a = e.mask_alpha[col + i];
+        const float a = mask_alpha[i];
         float sn, cs;
         sincosf(a * x[i], &sn, &cs);
         const float s2 = 2.f * sn * cs;  // sin(2 a x)
@@ -113,23 +195,36 @@ WB_DEV void epi_chunk(const Epi& e, float* v, bool valid, size_t off, int col, s
       for (int i = 0; i < 32; ++i) v[i] *= (x[i] > 0.f) ? 1.f : e.slope;
     }
   }
-  if (e.bias) {
+  if (bias && bias16) {  // 16-byte aligned copy (the persistent kernel's shared memory)
+    const float4* b4 = reinterpret_cast<const float4*>(bias);
 #pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] += e.bias[col + i];
+    for (int i = 0; i < 8; ++i) {
+      const float4 b = b4[i];
+      v[4 * i] += b.x;
+      v[4 * i + 1] += b.y;
+      v[4 * i + 2] += b.z;
+      v[4 * i + 3] += b.w;
+    }
+  } else if (bias) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] += bias[i];
   }
   if (rowadd_row) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] += rowadd_row[i];
   }
-  if (e.res && valid) {
-    float r[32];
-    load_f32x32(e.res + off, r);
+  if (WB_EPI_HAS(kEpiRes, e.res != nullptr) && valid) {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] += r[i];
+    for (int i = 0; i < 8; ++i) {
+      v[4 * i] += in.r[i].x;
+      v[4 * i + 1] += in.r[i].y;
+      v[4 * i + 2] += in.r[i].z;
+      v[4 * i + 3] += in.r[i].w;
+    }
   }
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] *= e.scale;
-  if (e.colsum) {
+  if (WB_EPI_HAS(kEpiColsum, e.colsum != nullptr)) {
     float cv[32];
 #pragma unroll
     for (int i = 0; i < 32; ++i) cv[i] = valid ? v[i] : 0.f;
@@ -139,32 +234,55 @@ WB_DEV void epi_chunk(const Epi& e, float* v, bool valid, size_t off, int col, s
       else e.colsum[part_row + lane] = t;
     }
   }
-  if (!valid) return;
-  if (e.accumulate) {
-    float r[32];
-    load_f32x32(e.out_f32 + off, r);
+  if (!valid && !o.stage) return;  // (the staged path needs every lane of the warp below)
+  if (e.accumulate && valid) {  // previous value of the fp32 output (stack accumulation)
+    const float4* q = reinterpret_cast<const float4*>(e.out_f32 + off);
 #pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] += r[i];
-  }
-  if (e.out_f32) store_f32x32(e.out_f32 + off, v);
-  if (e.out_bf16 || e.pre_hi) {
-    __align__(16) bf16 b[32];
-#pragma unroll
-    for (int i = 0; i < 32; ++i) b[i] = __float2bfloat16_rn(v[i]);
-    if (e.out_bf16) store_bf16x32(e.out_bf16 + off, b);
-    if (e.pre_hi) store_bf16x32(e.pre_hi + off, b);
-  }
-  if (e.act_hi) {
-    __align__(16) bf16 h[32];
-    __align__(16) bf16 l[32];
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const float a = (e.act_kind == 1) ? snake(v[i], e.act_alpha[col + i]) : lrelu(v[i], e.slope);
-      split_bf16(a, h[i], l[i]);
+    for (int i = 0; i < 8; ++i) {
+      const float4 a = __ldcs(q + i);
+      v[4 * i] += a.x;
+      v[4 * i + 1] += a.y;
+      v[4 * i + 2] += a.z;
+      v[4 * i + 3] += a.w;
     }
-    store_bf16x32(e.act_hi + off, h);
-    if (e.act_lo) store_bf16x32(e.act_lo + off, l);
   }
+  if (e.out_f32) out_f32x32(o, e.out_f32, off, v);
+  if (e.out_bf16 || e.pre_hi) {
+    uint32_t b[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) b[i] = pack_bf16(v[2 * i], v[2 * i + 1]);
+    if (e.out_bf16) out_bf16x32(o, e.out_bf16, off, b);
+    if (e.pre_hi) out_bf16x32(o, e.pre_hi, off, b);
+  }
+  if (WB_EPI_HAS(kEpiAct, e.act_hi != nullptr)) {
+    uint32_t h[16], l[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float a0, a1;
+      if (WB_EPI_HAS(kEpiSnake, e.act_kind == 1)) {
+        a0 = snake(v[2 * i], act_alpha[2 * i]);
+        a1 = snake(v[2 * i + 1], act_alpha[2 * i + 1]);
+      } else {
+        a0 = lrelu(v[2 * i], e.slope);
+        a1 = lrelu(v[2 * i + 1], e.slope);
+      }
+      h[i] = pack_bf16(a0, a1);
+      l[i] = pack_bf16(a0 - bf16lo_f(h[i]), a1 - bf16hi_f(h[i]));
+    }
+    out_bf16x32(o, e.act_hi, off, h);
+    if (e.act_lo) out_bf16x32(o, e.act_lo, off, l);
+  }
+}
+
+// One-shot form (load + finish) with the epilogue's global bias / alpha vectors.
+WB_DEV void epi_chunk(const Epi& e, float* v, bool valid, size_t off, int col, size_t part_row, const float* rowadd_row,
+                      int warp, int lane, float* red, float* cs_acc = nullptr, float* ap_acc = nullptr,
+                      int bar = 1) {
+  EpiIn in;
+  epi_load<kEpiGeneric>(e, valid, off, in);
+  epi_finish<kEpiGeneric>(e, v, in, valid, off, part_row, rowadd_row, e.bias ? e.bias + col : nullptr,
+             e.act_alpha ? e.act_alpha + col : nullptr, e.mask_alpha ? e.mask_alpha + col : nullptr, warp, lane, red,
+             cs_acc, ap_acc, bar);
 }
 
 }  // namespace wb
