@@ -150,6 +150,16 @@ WB_DEV void tma_load_3d_warp(void* dst, const CUtensorMap* map, uint64_t* bar, i
       : "memory");
 }
 
+WB_DEV void tma_load_4d_warp(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];\n\t}" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // Bounded wait by a converged warp; every lane gets the same verdict.  The spin loop lives inside one
 // asm block so the compiler sees no divergent control flow around the issuing code (a C++ loop here
 // makes it treat descriptors as per-lane values and every tcgen05.mma pays for uniformising them).

@@ -126,16 +126,19 @@ bool plan_conv(ConvLaunch& L, const ConvGeom& g, const void* x_hi, const void* x
   return finish_fwd(L, g.B, g.C_in, g.C_out, split, 1, err);
 }
 
-// No-swizzle view of a [B][T][C] bf16 tensor with an (8 channels, R rows, 1) box: each load lands in
-// shared memory as one core-matrix column (R rows x 16 bytes) of the K-major no-swizzle UMMA layout.
-static bool make_map_bf16_cm(CUtensorMap* m, const void* base, uint64_t T, uint64_t C, uint64_t B, uint32_t R) {
+// No-swizzle core-matrix view of a [B][T][C] bf16 tensor: dimensions (8 channels, T, C/8 channel
+// groups, B) with the channel group outermost in the box, so one (8, R, KC/8, 1) box lands in shared
+// memory as KC/8 core-matrix columns of R rows x 16 bytes each (column j at j * R * 16 bytes): the
+// K-major no-swizzle UMMA layout of a KC-channel halo tile, in a single TMA instruction.
+static bool make_map_bf16_cm(CUtensorMap* m, const void* base, uint64_t T, uint64_t C, uint64_t B, uint32_t R,
+                             uint32_t kc) {
   auto fn = encode_fn();
   if (!fn) return false;
-  cuuint64_t dims[3] = {C, T, B};
-  cuuint64_t strides[2] = {C * 2, T * C * 2};
-  cuuint32_t box[3] = {8, R, 1};
-  cuuint32_t es[3] = {1, 1, 1};
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+  cuuint64_t dims[4] = {8, T, C / 8, B};
+  cuuint64_t strides[3] = {C * 2, 16, T * C * 2};
+  cuuint32_t box[4] = {8, R, kc / 8, 1};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, es,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
@@ -218,8 +221,8 @@ bool plan_conv2(Conv2Launch& L, const ConvGeom& g, const void* x_hi, const void*
   p.n_chunks = g.C_in / kc;
   p.tmem_cols = pow2_cols(2 * p.n);
   if (p.tmem_cols > 512) return false;
-  if (!make_map_bf16_cm(&L.maps.a_hi, x_hi, g.T_in, g.C_in, g.B, R)) return false;
-  if (split && !make_map_bf16_cm(&L.maps.a_lo, x_lo, g.T_in, g.C_in, g.B, R)) return false;
+  if (!make_map_bf16_cm(&L.maps.a_hi, x_hi, g.T_in, g.C_in, g.B, R, kc)) return false;
+  if (split && !make_map_bf16_cm(&L.maps.a_lo, x_lo, g.T_in, g.C_in, g.B, R, kc)) return false;
   const uint64_t wr = (uint64_t)g.C_in * 2, wt = wr * g.C_out;
   if (!make_map_bf16_3d(&L.maps.w_hi, w_hi, g.C_in, g.C_out, g.k, wr, wt, kc, p.n, 1)) return false;
   if (split && !make_map_bf16_3d(&L.maps.w_lo, w_lo, g.C_in, g.C_out, g.k, wr, wt, kc, p.n, 1)) return false;
@@ -350,9 +353,13 @@ static bool finish_wgrad(WgradLaunch& L, int B, int T_rows, int C_in, int C_out,
   int splits = std::max(1, std::min(p.total_kblocks, (target_ctas + base - 1) / base));
   p.kb_per_split = (p.total_kblocks + splits - 1) / splits;
   splits = (p.total_kblocks + p.kb_per_split - 1) / p.kb_per_split;
-  const size_t stage = 128 * 64 * 2 + (size_t)n_tile * 64 * 2;
-  p.stages = (int)std::min<size_t>(6, (kSmemBudget - 1024 - 256) / stage);
-  L.smem = p.stages * stage + 1024 + 256;
+  // stages of kb_group 64-row blocks: about three stages, each as many blocks as fit
+  const size_t kb = 128 * 64 * 2 + (size_t)n_tile * 64 * 2;
+  const size_t room = kSmemBudget - 1024 - 256;
+  p.kb_group = (int)std::max<size_t>(1, std::min<size_t>(8, room / (3 * kb)));
+  p.stages = (int)std::min<size_t>(4, room / (p.kb_group * kb));
+  if (p.stages < 2) return false;
+  L.smem = p.stages * p.kb_group * kb + 1024 + 256;
   p.tmem_cols = pow2_cols(n_tile);
   p.err = err;
   p.part = part;

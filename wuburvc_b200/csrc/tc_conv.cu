@@ -122,7 +122,11 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 // ---------------------------------------------------------------------------------------------
-// tc_wgrad kernel: partial dW tiles over a K (time) range
+// tc_wgrad kernel: partial dW tiles over a K (time) range.  A pipeline stage holds `kb_group` blocks
+// of 64 time rows (every atom of the M tile's dOut views + the activation rows), so the MMA warp
+// pays one barrier round trip per kb_group x 4 MMAs.  Producer and MMA run as converged warps with
+// elect.sync issue and a warp-uniform `ok` flag.  The partial tile leaves through the (then idle)
+// pipeline shared memory as coalesced row pieces.
 // ---------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(192, 1)
     tc_wgrad_kernel(const __grid_constant__ TcWgMaps maps, const __grid_constant__ TcWgParams p) {
@@ -134,24 +138,26 @@ __global__ void __launch_bounds__(192, 1)
   const int nbase = blockIdx.z * p.n_in;
   const int kb0 = split * p.kb_per_split;
   const int kb1 = min(p.total_kblocks, kb0 + p.kb_per_split);
-  const int ksteps = max(0, kb1 - kb0);
+  const int nkb = max(0, kb1 - kb0);
+  const int G = p.kb_group;
+  const int ngroups = (nkb + G - 1) / G;
   const int S = p.stages;
   const uint32_t atom_a_bytes = 64u * (uint32_t)p.atom_m * 2u;
   const uint32_t a_bytes = 128u * 64u * 2u;
   const int atom_n = p.n_in / p.n_atoms;
   const uint32_t atom_b_bytes = 64u * (uint32_t)atom_n * 2u;
   const uint32_t b_bytes = (uint32_t)p.n_in * 64u * 2u;
-  const uint32_t stage_bytes = a_bytes + b_bytes;
+  const uint32_t kb_bytes = a_bytes + b_bytes;
+  const uint32_t stage_bytes = (uint32_t)G * kb_bytes;
 
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * stage_bytes);
   uint64_t* empty = full + S;
   uint64_t* accf = empty + S;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accf + 1);
 
-  int n_used = 0;
-  uint32_t load_bytes = b_bytes;
+  uint32_t kb_load = b_bytes;
   for (int j = 0; j < p.m_atoms; ++j)
-    if (p.atom_tap[mt][j] >= 0) { ++n_used; load_bytes += atom_a_bytes; }
+    if (p.atom_tap[mt][j] >= 0) kb_load += atom_a_bytes;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
@@ -164,64 +170,82 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 4) {
-    if (lane == 0) {
-      for (int ks = 0; ks < ksteps; ++ks) {
-        const int s = ks % S;
-        if (ks >= S && !mbar_wait(&empty[s], ((ks / S) & 1) ^ 1, p.err, ERR_WAIT_EMPTY)) break;
-        const int kb = kb0 + ks;
-        const int item = kb / p.kblocks_per_item;
-        const int t0 = (kb - item * p.kblocks_per_item) * 64;
+    // ---------------- TMA producer ----------------
+    bool ok = true;
+    int s = 0;
+    uint32_t ph = 0;
+    for (int g = 0; g < ngroups; ++g) {
+      if (ok && g >= S) ok = mbar_wait_warp(&empty[s], ph ^ 1u, p.err, ERR_WAIT_EMPTY);
+      if (ok) {
+        const int kbg = kb0 + g * G, nk = min(G, kb1 - kbg);
         uint8_t* st = smem + (size_t)s * stage_bytes;
-        mbar_arrive_expect_tx(&full[s], load_bytes);
-        for (int j = 0; j < p.m_atoms; ++j) {
-          if (p.atom_tap[mt][j] < 0) continue;
-          tma_load_3d(st + j * atom_a_bytes, &maps.d[p.atom_map[mt][j]], &full[s], p.atom_oc0[mt][j],
-                      t0 + p.atom_shift[mt][j], item);
+        mbar_expect_tx_warp(&full[s], (uint32_t)nk * kb_load);
+        for (int i = 0; i < nk; ++i) {
+          const int kb = kbg + i;
+          const int item = kb / p.kblocks_per_item;
+          const int t0 = (kb - item * p.kblocks_per_item) * 64;
+          uint8_t* kd = st + (size_t)i * kb_bytes;
+          for (int j = 0; j < p.m_atoms; ++j) {
+            if (p.atom_tap[mt][j] < 0) continue;
+            tma_load_3d_warp(kd + j * atom_a_bytes, &maps.d[p.atom_map[mt][j]], &full[s], p.atom_oc0[mt][j],
+                             t0 + p.atom_shift[mt][j], item);
+          }
+          for (int j = 0; j < p.n_atoms; ++j)
+            tma_load_3d_warp(kd + a_bytes + j * atom_b_bytes, &maps.x, &full[s], nbase + j * atom_n, t0, item);
         }
-        for (int j = 0; j < p.n_atoms; ++j)
-          tma_load_3d(st + a_bytes + j * atom_b_bytes, &maps.x, &full[s], nbase + j * atom_n, t0, item);
       }
+      if (++s == S) { s = 0; ph ^= 1u; }
     }
   } else if (warp == 5) {
-    if (lane == 0) {
-      const uint32_t idesc = make_idesc_bf16(128, p.n_in, 1, 1);
-      const uint32_t la = (p.atom_m == 64) ? 2u : 4u, sboa = (uint32_t)p.atom_m * 16u;
-      const uint32_t lb = (atom_n == 64) ? 2u : 4u, sbob = (uint32_t)atom_n * 16u;
-      const uint32_t sbase = smem_u32(smem);
-      bool ok = true;
-      for (int ks = 0; ks < ksteps; ++ks) {
-        const int s = ks % S;
-        if (!mbar_wait(&full[s], (ks / S) & 1, p.err, ERR_WAIT_FULL)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t ab = sbase + (uint32_t)s * stage_bytes;
-        const uint32_t bb = ab + a_bytes;
+    // ---------------- MMA issuer ----------------
+    const uint32_t idesc = make_idesc_bf16(128, p.n_in, 1, 1);
+    const uint32_t la = (p.atom_m == 64) ? 2u : 4u, sboa = (uint32_t)p.atom_m * 16u;
+    const uint32_t lb = (atom_n == 64) ? 2u : 4u, sbob = (uint32_t)atom_n * 16u;
+    // descriptors built once; a k-step / block / stage moves the 14-bit start-address field
+    const uint64_t da0 = make_sdesc(smem_u32(smem), atom_a_bytes, sboa, la);
+    const uint64_t db0 = make_sdesc(smem_u32(smem) + a_bytes, atom_b_bytes, sbob, lb);
+    const uint32_t ka = (2u * sboa) >> 4, kbb = (2u * sbob) >> 4;
+    bool ok = true;
+    int s = 0;
+    uint32_t ph = 0;
+    for (int g = 0; g < ngroups; ++g) {
+      if (ok) ok = mbar_wait_warp(&full[s], ph, p.err, ERR_WAIT_FULL);
+      if (ok) {
+        const int nk = min(G, kb1 - (kb0 + g * G));
+        const uint32_t sbase = ((uint32_t)s * stage_bytes) >> 4;
+        for (int i = 0; i < nk; ++i) {
+          const uint32_t kbase = sbase + (((uint32_t)i * kb_bytes) >> 4);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {  // 64 time rows = 4 x K16
-          const uint64_t da = make_sdesc(ab + (uint32_t)k * 2u * sboa, atom_a_bytes, sboa, la);
-          const uint64_t db = make_sdesc(bb + (uint32_t)k * 2u * sbob, atom_b_bytes, sbob, lb);
-          umma_f16(tmem, da, db, idesc, (ks | k) != 0);
+          for (int k = 0; k < 4; ++k)  // 64 time rows = 4 x K16
+            umma_f16_warp(tmem, da0 + kbase + k * ka, db0 + kbase + k * kbb, idesc, (g | i | k) != 0);
         }
-        umma_commit(&empty[s]);
+        umma_commit_warp(&empty[s]);
       }
-      if (ok) umma_commit(accf);
+      if (++s == S) { s = 0; ph ^= 1u; }
     }
+    if (ok) umma_commit_warp(accf);
   } else {
-    bool ok = ksteps > 0 ? mbar_wait(accf, 0, p.err, ERR_WAIT_ACC) : true;
+    // ---------------- epilogue: 4 warps, TMEM lane quadrant = warp ----------------
+    bool ok = nkb > 0 ? mbar_wait_warp(accf, 0, p.err, ERR_WAIT_ACC) : true;
     tc_fence_after();
-    const int m = warp * 32 + lane;
-    float* dst = p.part + ((size_t)split * p.n_mtiles * 128 + (size_t)mt * 128 + m) * p.n_total + nbase;
+    // the pipeline buffers are idle once the accumulator is complete: 2 KB staging per warp
+    uint4* stage = reinterpret_cast<uint4*>(smem) + warp * 128;
+    char* dst = reinterpret_cast<char*>(p.part + ((size_t)split * p.n_mtiles * 128 + (size_t)mt * 128 + warp * 32) *
+                                                     p.n_total + nbase);
     for (int c0 = 0; c0 < p.n_in; c0 += 32) {
       float v[32];
-      if (ksteps > 0) tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
+      if (nkb > 0 && ok) tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
       else {
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = 0.f;
       }
-      if (!ok) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = 0.f;
+      for (int h = 0; h < 2; ++h) {
+        uint32_t w[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) w[i] = __float_as_uint(v[16 * h + i]);
+        stage_put64(stage, lane, w, dst + (size_t)(c0 + 16 * h) * 4, (size_t)p.n_total * 4, 32);
       }
-      store_f32x32(dst + c0, v);
     }
   }
   tc_fence_before();

@@ -126,6 +126,7 @@ struct TcWgParams {
   int m_atoms;         // 128 / atom_m
   int atom_m;          // 32 or 64 (dOut channels per atom)
   int stages;
+  int kb_group;        // 64-row K blocks per pipeline stage
   int tmem_cols;
   // per M tile: atoms (tap, oc0) packed along M
   int n_mtiles;

@@ -94,7 +94,6 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
     int sa = 0, sw = 0;
     uint32_t aph = 0, wph = 0;
     int a_uses = 0, w_uses = 0;
-    const uint32_t colb = (uint32_t)p.halo_rows * 16u;  // 8-channel core-matrix column: R rows x 16 B
     for (int tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x) {
       const int mtile = tile / p.n_tiles;
       const int item = mtile / p.tiles_per_item;
@@ -102,15 +101,11 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
       for (int c = 0; c < nch; ++c) {
         if (ok && a_uses >= AS) ok = mbar_wait_warp(&a_empty[sa], aph ^ 1u, p.err, ERR_WAIT_EMPTY);
         if (ok) {
+          // one box per operand: KC/8 core-matrix columns of R rows (column j at j * R * 16 bytes)
           uint8_t* ad = a_base + (size_t)sa * a_stage;
           mbar_expect_tx_warp(&a_full[sa], nA * (uint32_t)p.halo_rows * KC * 2u);
-#pragma unroll
-          for (int j = 0; j < KC / 8; ++j) {
-            tma_load_3d_warp(ad + j * colb, &maps.a_hi, &a_full[sa], c * KC + j * 8, q0 + p.halo_start, item);
-            if (SPLIT)
-              tma_load_3d_warp(ad + a_sub + j * colb, &maps.a_lo, &a_full[sa], c * KC + j * 8, q0 + p.halo_start,
-                               item);
-          }
+          tma_load_4d_warp(ad, &maps.a_hi, &a_full[sa], 0, q0 + p.halo_start, c * (KC / 8), item);
+          if (SPLIT) tma_load_4d_warp(ad + a_sub, &maps.a_lo, &a_full[sa], 0, q0 + p.halo_start, c * (KC / 8), item);
         }
         ++a_uses;
         if (++sa == AS) { sa = 0; aph ^= 1u; }
