@@ -318,6 +318,15 @@ bool plan_convT_dgrad(ConvLaunch& L, int B, int T_in, int C_in, int C_out, int k
 // ------------------------------------------------------------------------------------------------
 // weight gradients
 // ------------------------------------------------------------------------------------------------
+// Time rows per weight-gradient K block: the largest of 256 / 128 / 64 for which two pipeline stages
+// (128 dOut rows + n_tile activation channels, bf16) fit in shared memory.
+static int wgrad_kb_rows(int n_tile) {
+  const size_t room = kSmemBudget - 1024 - 256;
+  for (int kr = 256; kr > 64; kr >>= 1)
+    if ((size_t)(128 + n_tile) * kr * 2 * 2 <= room) return kr;
+  return 64;
+}
+
 static bool finish_wgrad(WgradLaunch& L, int B, int T_rows, int C_in, int C_out, int n_atoms_total,
                          const int* a_map, const int* a_shift, const int* a_oc0, const int* a_tap, float* part,
                          size_t cap, int target_ctas, int* err) {
@@ -346,7 +355,8 @@ static bool finish_wgrad(WgradLaunch& L, int B, int T_rows, int C_in, int C_out,
   p.n_atoms = n_tile / atom_n;
   p.c_out = C_out;
   p.t_rows = T_rows;
-  p.kblocks_per_item = (T_rows + 63) / 64;
+  p.kb_rows = wgrad_kb_rows(n_tile);
+  p.kblocks_per_item = (T_rows + p.kb_rows - 1) / p.kb_rows;
   p.total_kblocks = B * p.kblocks_per_item;
   const int n_ntiles = C_in / n_tile;
   const int base = p.n_mtiles * n_ntiles;
@@ -354,7 +364,7 @@ static bool finish_wgrad(WgradLaunch& L, int B, int T_rows, int C_in, int C_out,
   p.kb_per_split = (p.total_kblocks + splits - 1) / splits;
   splits = (p.total_kblocks + p.kb_per_split - 1) / p.kb_per_split;
   // stages of kb_group 64-row blocks: about three stages, each as many blocks as fit
-  const size_t kb = 128 * 64 * 2 + (size_t)n_tile * 64 * 2;
+  const size_t kb = (size_t)(128 + n_tile) * p.kb_rows * 2;
   const size_t room = kSmemBudget - 1024 - 256;
   p.kb_group = (int)std::max<size_t>(1, std::min<size_t>(8, room / (3 * kb)));
   p.stages = (int)std::min<size_t>(4, room / (p.kb_group * kb));
@@ -395,13 +405,14 @@ bool plan_wgrad(WgradLaunch& L, const ConvGeom& g, const void* dy, const void* x
       aoc.push_back(c * atom_m);
       atap.push_back(t);
     }
-  if (!make_map_bf16_3d(&L.maps.d[0], dy, g.C_out, g.T_out, g.B, (uint64_t)g.C_out * 2,
-                        (uint64_t)g.C_out * 2 * g.T_out, atom_m, 64, 1))
-    return false;
   const int n_tile = std::min(g.C_in, 256);
   const int atom_n = std::min(n_tile, 64);
+  const int kr = wgrad_kb_rows(n_tile);
+  if (!make_map_bf16_3d(&L.maps.d[0], dy, g.C_out, g.T_out, g.B, (uint64_t)g.C_out * 2,
+                        (uint64_t)g.C_out * 2 * g.T_out, atom_m, kr, 1))
+    return false;
   if (!make_map_bf16_3d(&L.maps.x, x, g.C_in, g.T_in, g.B, (uint64_t)g.C_in * 2, (uint64_t)g.C_in * 2 * g.T_in,
-                        atom_n, 64, 1))
+                        atom_n, kr, 1))
     return false;
   return finish_wgrad(L, g.B, g.T_in, g.C_in, g.C_out, (int)am.size(), am.data(), ash.data(), aoc.data(),
                       atap.data(), part, cap, target_ctas, err);
@@ -415,11 +426,12 @@ bool plan_convT_wgrad(WgradLaunch& L, int B, int T_in, int C_in, int C_out, int 
   const int T_out = T_in * s;
   const int atom_m = std::min(C_out, 64);
   const int oc_chunks = C_out / atom_m;
+  const int kr = wgrad_kb_rows(std::min(C_in, 256));
   for (int r = 0; r < s; ++r) {
     const uint64_t rows = (uint64_t)(T_out - r + s - 1) / s;
     const char* base = static_cast<const char*>(dy) + (size_t)r * C_out * 2;
     if (!make_map_bf16_3d(&L.maps.d[r], base, C_out, rows, B, (uint64_t)s * C_out * 2, (uint64_t)T_out * C_out * 2,
-                          atom_m, 64, 1))
+                          atom_m, kr, 1))
       return false;
   }
   std::vector<int> am, ash, aoc, atap;
@@ -434,7 +446,7 @@ bool plan_convT_wgrad(WgradLaunch& L, int B, int T_in, int C_in, int C_out, int 
     }
   const int n_tile = std::min(C_in, 256);
   const int atom_n = std::min(n_tile, 64);
-  if (!make_map_bf16_3d(&L.maps.x, x, C_in, T_in, B, (uint64_t)C_in * 2, (uint64_t)C_in * 2 * T_in, atom_n, 64, 1))
+  if (!make_map_bf16_3d(&L.maps.x, x, C_in, T_in, B, (uint64_t)C_in * 2, (uint64_t)C_in * 2 * T_in, atom_n, kr, 1))
     return false;
   return finish_wgrad(L, B, T_in, C_in, C_out, (int)am.size(), am.data(), ash.data(), aoc.data(), atap.data(), part,
                       cap, target_ctas, err);

@@ -142,11 +142,12 @@ __global__ void __launch_bounds__(192, 1)
   const int G = p.kb_group;
   const int ngroups = (nkb + G - 1) / G;
   const int S = p.stages;
-  const uint32_t atom_a_bytes = 64u * (uint32_t)p.atom_m * 2u;
-  const uint32_t a_bytes = 128u * 64u * 2u;
+  const int KR = p.kb_rows;  // time rows per K block (64, 128 or 256)
+  const uint32_t atom_a_bytes = (uint32_t)KR * (uint32_t)p.atom_m * 2u;
+  const uint32_t a_bytes = 128u * (uint32_t)KR * 2u;
   const int atom_n = p.n_in / p.n_atoms;
-  const uint32_t atom_b_bytes = 64u * (uint32_t)atom_n * 2u;
-  const uint32_t b_bytes = (uint32_t)p.n_in * 64u * 2u;
+  const uint32_t atom_b_bytes = (uint32_t)KR * (uint32_t)atom_n * 2u;
+  const uint32_t b_bytes = (uint32_t)p.n_in * (uint32_t)KR * 2u;
   const uint32_t kb_bytes = a_bytes + b_bytes;
   const uint32_t stage_bytes = (uint32_t)G * kb_bytes;
 
@@ -155,9 +156,18 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* accf = empty + S;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accf + 1);
 
+  // this M tile's atoms (dOut view, row shift, first channel), hoisted out of the parameter tables
+  int a_map[4], a_shift[4], a_oc0[4];
+  bool a_use[4];
   uint32_t kb_load = b_bytes;
-  for (int j = 0; j < p.m_atoms; ++j)
-    if (p.atom_tap[mt][j] >= 0) kb_load += atom_a_bytes;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    a_use[j] = j < p.m_atoms && p.atom_tap[mt][j] >= 0;
+    a_map[j] = p.atom_map[mt][j];
+    a_shift[j] = p.atom_shift[mt][j];
+    a_oc0[j] = p.atom_oc0[mt][j];
+    if (a_use[j]) kb_load += atom_a_bytes;
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
@@ -183,13 +193,12 @@ __global__ void __launch_bounds__(192, 1)
         for (int i = 0; i < nk; ++i) {
           const int kb = kbg + i;
           const int item = kb / p.kblocks_per_item;
-          const int t0 = (kb - item * p.kblocks_per_item) * 64;
+          const int t0 = (kb - item * p.kblocks_per_item) * KR;
           uint8_t* kd = st + (size_t)i * kb_bytes;
-          for (int j = 0; j < p.m_atoms; ++j) {
-            if (p.atom_tap[mt][j] < 0) continue;
-            tma_load_3d_warp(kd + j * atom_a_bytes, &maps.d[p.atom_map[mt][j]], &full[s], p.atom_oc0[mt][j],
-                             t0 + p.atom_shift[mt][j], item);
-          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            if (a_use[j])
+              tma_load_3d_warp(kd + j * atom_a_bytes, &maps.d[a_map[j]], &full[s], a_oc0[j], t0 + a_shift[j], item);
           for (int j = 0; j < p.n_atoms; ++j)
             tma_load_3d_warp(kd + a_bytes + j * atom_b_bytes, &maps.x, &full[s], nbase + j * atom_n, t0, item);
         }
@@ -215,8 +224,7 @@ __global__ void __launch_bounds__(192, 1)
         const uint32_t sbase = ((uint32_t)s * stage_bytes) >> 4;
         for (int i = 0; i < nk; ++i) {
           const uint32_t kbase = sbase + (((uint32_t)i * kb_bytes) >> 4);
-#pragma unroll
-          for (int k = 0; k < 4; ++k)  // 64 time rows = 4 x K16
+          for (int k = 0; k < KR / 16; ++k)  // KR time rows = KR/16 x K16
             umma_f16_warp(tmem, da0 + kbase + k * ka, db0 + kbase + k * kbb, idesc, (g | i | k) != 0);
         }
         umma_commit_warp(&empty[s]);

@@ -126,7 +126,8 @@ struct TcWgParams {
   int m_atoms;         // 128 / atom_m
   int atom_m;          // 32 or 64 (dOut channels per atom)
   int stages;
-  int kb_group;        // 64-row K blocks per pipeline stage
+  int kb_group;        // K blocks per pipeline stage
+  int kb_rows;         // time rows per K block (64, 128 or 256)
   int tmem_cols;
   // per M tile: atoms (tap, oc0) packed along M
   int n_mtiles;
