@@ -28,44 +28,132 @@ void transpose_ck(const float* w, int C, int k, float* wt, cudaStream_t st) {
 
 // =============================================================================================
 // noise conv (+ activation of the stage input); weights transposed wt[tap][C]
+//   x[b][j][c] += bias[c] + sum_tap wt[tap][c] * har[b][j*stride - pad + tap]
+// Block = 32 channels (lanes) x 64 rows of one item (8 warps x 8 rows); the weights of the 32
+// channels and the har window of the 64 rows sit in shared memory.
 // =============================================================================================
-__global__ void noise_add_act_kernel(NoiseActArgs a) {
-  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  const long long n = (long long)a.B * a.T * a.C;
-  if (i >= n) return;
-  const int c = (int)(i % a.C);
-  const long long row = i / a.C;
-  const int b = (int)(row / a.T), j = (int)(row % a.T);
-  float x = a.x[i];
+constexpr int kNaRowsPerWarp = 8;
+constexpr int kNaRows = 8 * kNaRowsPerWarp;
+
+__global__ void __launch_bounds__(256) noise_add_act_kernel(NoiseActArgs a) {
+  extern __shared__ float sh[];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int c = blockIdx.y * 32 + lane;
+  const int b = blockIdx.z;
+  const int j0 = blockIdx.x * kNaRows;
+  float* ws = sh;                 // [k][32]
+  float* hs = sh + a.k * 32;      // har window, (kNaRows - 1) * stride + k samples from j0 * stride - pad
   if (a.har) {
-    float s = a.bias[c];
-    const float* h = a.har + (size_t)b * a.T_full;
-    const int t0 = j * a.stride - a.pad;
-    for (int tap = 0; tap < a.k; ++tap) {
-      const int t = t0 + tap;
-      if (t >= 0 && t < a.T_full) s += a.w[(size_t)tap * a.C + c] * h[t];
+    const int hw = (kNaRows - 1) * a.stride + a.k, h0 = j0 * a.stride - a.pad;
+    for (int i = threadIdx.x; i < a.k * 32; i += blockDim.x)
+      ws[i] = a.w[(size_t)(i >> 5) * a.C + blockIdx.y * 32 + (i & 31)];
+    for (int i = threadIdx.x; i < hw; i += blockDim.x) {
+      const int t = h0 + i;
+      hs[i] = (t >= 0 && t < a.T_full) ? a.har[(size_t)b * a.T_full + t] : 0.f;
     }
-    x += s;
-    a.x[i] = x;
   }
-  if (a.pre) a.pre[i] = __float2bfloat16_rn(x);
-  for (int q = 0; q < a.n_act; ++q) {
-    const float al = a.alpha[q] ? a.alpha[q][c] : 1.f;
-    const float y = act_fwd2(x, a.act_kind, a.slope, al);
-    bf16 hi, lo;
-    split_bf16(y, hi, lo);
-    a.act_hi[q][i] = hi;
-    a.act_lo[q][i] = lo;
+  __syncthreads();
+  const int jw = j0 + w * kNaRowsPerWarp;  // this warp's first row
+  const int nr = max(0, min(kNaRowsPerWarp, a.T - jw));
+  float x[kNaRowsPerWarp];
+#pragma unroll
+  for (int r = 0; r < kNaRowsPerWarp; ++r) x[r] = r < nr ? a.x[((size_t)b * a.T + jw + r) * a.C + c] : 0.f;
+  if (a.har) {
+    float acc[kNaRowsPerWarp];
+    const float bc = a.bias[c];
+#pragma unroll
+    for (int r = 0; r < kNaRowsPerWarp; ++r) acc[r] = bc;
+    const float* hw0 = hs + (w * kNaRowsPerWarp) * a.stride;
+    for (int tap = 0; tap < a.k; ++tap) {
+      const float wv = ws[tap * 32 + lane];
+#pragma unroll
+      for (int r = 0; r < kNaRowsPerWarp; ++r) acc[r] += wv * hw0[r * a.stride + tap];
+    }
+#pragma unroll
+    for (int r = 0; r < kNaRowsPerWarp; ++r) {
+      x[r] += acc[r];
+      if (r < nr) a.x[((size_t)b * a.T + jw + r) * a.C + c] = x[r];
+    }
+  }
+  float al[3];
+#pragma unroll
+  for (int q = 0; q < 3; ++q) al[q] = (q < a.n_act && a.alpha[q]) ? a.alpha[q][c] : 1.f;
+#pragma unroll
+  for (int r = 0; r < kNaRowsPerWarp; ++r) {
+    if (r >= nr) break;
+    const size_t i = ((size_t)b * a.T + jw + r) * a.C + c;
+    if (a.pre) a.pre[i] = __float2bfloat16_rn(x[r]);
+    for (int q = 0; q < a.n_act; ++q) {
+      const float y = act_fwd2(x[r], a.act_kind, a.slope, al[q]);
+      bf16 hi, lo;
+      split_bf16(y, hi, lo);
+      a.act_hi[q][i] = hi;
+      a.act_lo[q][i] = lo;
+    }
   }
 }
 
 void noise_add_act(const NoiseActArgs& a, cudaStream_t st) {
-  const long long n = (long long)a.B * a.T * a.C;
-  noise_add_act_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(a);
+  const dim3 grid((unsigned)((a.T + kNaRows - 1) / kNaRows), (unsigned)(a.C / 32), (unsigned)a.B);
+  const size_t smem = a.har ? sizeof(float) * ((size_t)a.k * 32 + (size_t)(kNaRows - 1) * a.stride + a.k) : 0;
+  noise_add_act_kernel<<<grid, 256, smem, st>>>(a);
 }
 
-__global__ void noise_dhar_kernel(const float* __restrict__ dx, const float* __restrict__ wt, int B, int T, int C, int k,
-                                  int stride, int pad, int T_full, float* __restrict__ d_har, int accumulate) {
+size_t noise_act_smem(int k, int stride) {
+  return sizeof(float) * ((size_t)k * 32 + (size_t)(kNaRows - 1) * stride + k);
+}
+
+// ---- noise-conv backward ------------------------------------------------------------------------
+// Phase 1: g[row][tap] = sum_c dx[row][c] * wt[tap][c] (warp per (row, group of 16 taps), lanes over
+// channels, transpose-reduction across lanes).  Phase 2: d_har[b][t] (+)= overlap-add of g over the
+// rows j whose window covers t (tap = t + pad - j*stride).
+__device__ __forceinline__ float warp_colsum16(float* v, int lane) {
+  // v[0..15] per lane; on return lane q < 16 holds sum over lanes of v[q]
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    const bool upper = (lane & off) != 0;
+    const int n = off < 16 ? off : 16;
+#pragma unroll
+    for (int i = 0; i < n; ++i) {
+      if (off == 16) {
+        v[i] += __shfl_xor_sync(0xffffffffu, v[i], 16);
+      } else {
+        const float send = upper ? v[i] : v[i + off];
+        const float keep = upper ? v[i + off] : v[i];
+        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+      }
+    }
+  }
+  return v[0];
+}
+
+__global__ void __launch_bounds__(256) noise_g_kernel(const float* __restrict__ dx, const float* __restrict__ wt,
+                                                      long long rows, int C, int k, float* __restrict__ g) {
+  const int lane = threadIdx.x & 31;
+  const int ngroups = (k + 15) / 16;
+  const long long wid = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const long long row = wid / ngroups;
+  const int grp = (int)(wid - row * ngroups);
+  if (row >= rows) return;
+  float v[16];
+#pragma unroll
+  for (int q = 0; q < 16; ++q) v[q] = 0.f;
+  const float* xr = dx + (size_t)row * C;
+  for (int c = lane; c < C; c += 32) {
+    const float x = xr[c];
+#pragma unroll
+    for (int q = 0; q < 16; ++q) {
+      const int tap = grp * 16 + q;
+      if (tap < k) v[q] += x * wt[(size_t)tap * C + c];
+    }
+  }
+  const float sum = warp_colsum16(v, lane);
+  const int tap = grp * 16 + lane;
+  if (lane < 16 && tap < k) g[(size_t)row * k + tap] = sum;
+}
+
+__global__ void noise_dhar_kernel(const float* __restrict__ g, int B, int T, int k, int stride, int pad, int T_full,
+                                  float* __restrict__ d_har, int accumulate) {
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (long long)B * T_full) return;
   const int b = (int)(i / T_full), t = (int)(i % T_full);
@@ -75,72 +163,69 @@ __global__ void noise_dhar_kernel(const float* __restrict__ dx, const float* __r
   jlo = jlo <= 0 ? 0 : (jlo + stride - 1) / stride;
   if (jhi > T - 1) jhi = T - 1;
   float s = 0.f;
-  for (int j = jlo; j <= jhi; ++j) {
-    const int tap = t + pad - j * stride;
-    const float4* r = reinterpret_cast<const float4*>(dx + ((size_t)b * T + j) * C);
-    const float4* w = reinterpret_cast<const float4*>(wt + (size_t)tap * C);
-    for (int c4 = 0; c4 < C / 4; ++c4) {
-      const float4 x = r[c4], y = w[c4];
-      s += x.x * y.x + x.y * y.y + x.z * y.z + x.w * y.w;
-    }
-  }
+  for (int j = jlo; j <= jhi; ++j) s += g[((size_t)b * T + j) * k + (t + pad - j * stride)];
   d_har[i] = accumulate ? d_har[i] + s : s;
 }
 
+// dW partials part[b * row_blocks + rb][c][tap] = sum over the block's rows of dx[row][c] * har[...]
+// Block = 32 channels (lanes) x kNwRows rows of one item; har window in shared memory.
+//   k <= 16: the warps split the rows, every thread keeps all k taps, shared-memory reduce at the end.
+//   k > 16 : the warps split the taps (tap = warp + 8q), every thread walks all rows of the block.
 constexpr int kNoiseTaps = 16;
-
-int noise_rows_per_part(int k) { return k <= kNoiseTaps ? 512 : 64; }
+constexpr int kNwRows = 128;
 
 int noise_backward_parts(int B, int T, int k) {
-  const int r = noise_rows_per_part(k);
-  return (int)(((long long)B * T + r - 1) / r);
+  (void)k;
+  return B * ((T + kNwRows - 1) / kNwRows);
 }
 
-// dW partials part[chunk][c][tap].  Block = 32 channels (lanes) x 8 warps.
-//   k <= 16: the warps split the chunk's rows, every thread keeps all k taps, smem reduce at the end.
-//   k > 16 : the warps split the taps (tap = warp + 8q), every thread walks all rows of the chunk.
 __global__ void __launch_bounds__(256) noise_wgrad_kernel(const float* __restrict__ dx, const float* __restrict__ har,
                                                           int B, int T, int C, int k, int stride, int pad, int T_full,
-                                                          int rows_per_part, float* __restrict__ part) {
+                                                          float* __restrict__ part) {
+  extern __shared__ float hs[];  // har window: (kNwRows - 1) * stride + k samples from j0 * stride - pad
   __shared__ float red[8][kNoiseTaps][33];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int c = blockIdx.x * 32 + lane;
-  const long long r0 = (long long)blockIdx.y * rows_per_part;
-  const long long r1 = min((long long)B * T, r0 + rows_per_part);
+  const int nrb = (T + kNwRows - 1) / kNwRows;
+  const int b = blockIdx.y / nrb, rb = blockIdx.y % nrb;
+  const int j0 = rb * kNwRows, nrows = min(kNwRows, T - j0);
+  const int hw = (kNwRows - 1) * stride + k, h0 = j0 * stride - pad;
+  for (int i = threadIdx.x; i < hw; i += blockDim.x) {
+    const int t = h0 + i;
+    hs[i] = (t >= 0 && t < T_full) ? har[(size_t)b * T_full + t] : 0.f;
+  }
+  __syncthreads();
   float acc[kNoiseTaps];
 #pragma unroll
   for (int q = 0; q < kNoiseTaps; ++q) acc[q] = 0.f;
+  const float* xb = dx + ((size_t)b * T + j0) * C + c;
   float* o = part + (size_t)blockIdx.y * C * k + (size_t)c * k;
   if (k <= kNoiseTaps) {
-    for (long long r = r0 + w; r < r1; r += 8) {
-      const int b = (int)(r / T), j = (int)(r % T);
-      const float x = dx[r * C + c];
-      const int t0 = j * stride - pad;
-      const float* h = har + (size_t)b * T_full;
+#pragma unroll 4
+    for (int jl = w; jl < nrows; jl += 8) {
+      const float x = xb[(size_t)jl * C];
+      const float* h = hs + jl * stride;
 #pragma unroll
       for (int q = 0; q < kNoiseTaps; ++q)
-        if (q < k && t0 + q >= 0 && t0 + q < T_full) acc[q] += x * h[t0 + q];
+        if (q < k) acc[q] += x * h[q];
     }
 #pragma unroll
     for (int q = 0; q < kNoiseTaps; ++q) red[w][q][lane] = acc[q];
     __syncthreads();
     for (int q = w; q < k; q += 8) {
-      float s = 0.f;
+      float sum = 0.f;
 #pragma unroll
-      for (int y = 0; y < 8; ++y) s += red[y][q][lane];
-      o[q] = s;
+      for (int y = 0; y < 8; ++y) sum += red[y][q][lane];
+      o[q] = sum;
     }
   } else {
-    for (long long r = r0; r < r1; ++r) {
-      const int b = (int)(r / T), j = (int)(r % T);
-      const float x = dx[r * C + c];
-      const int t0 = j * stride - pad;
-      const float* h = har + (size_t)b * T_full;
+#pragma unroll 4
+    for (int jl = 0; jl < nrows; ++jl) {
+      const float x = xb[(size_t)jl * C];
+      const float* h = hs + jl * stride + w;
 #pragma unroll
-      for (int q = 0; q < kNoiseTaps; ++q) {
-        const int tap = w + 8 * q;
-        if (tap < k && t0 + tap >= 0 && t0 + tap < T_full) acc[q] += x * h[t0 + tap];
-      }
+      for (int q = 0; q < kNoiseTaps; ++q)
+        if (w + 8 * q < k) acc[q] += x * h[8 * q];
     }
 #pragma unroll
     for (int q = 0; q < kNoiseTaps; ++q) {
@@ -151,13 +236,16 @@ __global__ void __launch_bounds__(256) noise_wgrad_kernel(const float* __restric
 }
 
 void noise_backward(const float* dx, const float* har, const float* wt, int B, int T, int C, int k, int stride, int pad,
-                    int T_full, float* d_har, int accumulate_dhar, float* wpart, cudaStream_t st) {
+                    int T_full, float* d_har, int accumulate_dhar, float* wpart, float* g, cudaStream_t st) {
+  const long long rows = (long long)B * T;
+  const long long warps = rows * ((k + 15) / 16);
+  noise_g_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(dx, wt, rows, C, k, g);
   const long long n = (long long)B * T_full;
-  noise_dhar_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(dx, wt, B, T, C, k, stride, pad, T_full, d_har,
+  noise_dhar_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(g, B, T, k, stride, pad, T_full, d_har,
                                                                   accumulate_dhar);
-  const int parts = noise_backward_parts(B, T, k);
-  noise_wgrad_kernel<<<dim3(C / 32, parts), 256, 0, st>>>(dx, har, B, T, C, k, stride, pad, T_full,
-                                                          noise_rows_per_part(k), wpart);
+  const size_t smem = sizeof(float) * ((size_t)(kNwRows - 1) * stride + k);
+  noise_wgrad_kernel<<<dim3(C / 32, noise_backward_parts(B, T, k)), 256, smem, st>>>(dx, har, B, T, C, k, stride, pad,
+                                                                                     T_full, wpart);
 }
 
 void noise_wgrad_reduce(const float* wpart, int nparts, int C, int k, float* dW, cudaStream_t st) {
@@ -170,27 +258,60 @@ void noise_wgrad_reduce(const float* wpart, int nparts, int C, int k, float* dW,
 constexpr int kPostK = 7;
 constexpr int kPostC = 32;
 
+// Warp = 16 consecutive output rows of one item, lane = channel: the 22-row input window is read
+// once (coalesced), each lane forms its channel's 16 partial sums, and one transpose-reduction per
+// half gives lane r the output of row r.
+constexpr int kPostWarpRows = 16;
+
+__device__ __forceinline__ float warp_colsum32_post(float* v, int lane) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    const bool upper = (lane & off) != 0;
+#pragma unroll
+    for (int i = 0; i < off; ++i) {
+      const float send = upper ? v[i] : v[i + off];
+      const float keep = upper ? v[i + off] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+    }
+  }
+  return v[0];
+}
+
 __global__ void __launch_bounds__(256) post_forward_kernel(const bf16* __restrict__ hi, const bf16* __restrict__ lo,
                                                            const float* __restrict__ W, int B, int T,
                                                            float* __restrict__ audio) {
   const int lane = threadIdx.x & 31;
-  const long long warps = (long long)gridDim.x * 8;
+  constexpr int pad = kPostK / 2, win = kPostWarpRows + kPostK - 1;
   float w[kPostK];
 #pragma unroll
   for (int q = 0; q < kPostK; ++q) w[q] = W[lane * kPostK + q];
-  for (long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5); row < (long long)B * T; row += warps) {
-    const int t = (int)(row % T);
-    float s = 0.f;
+  const int wpi = (T + kPostWarpRows - 1) / kPostWarpRows;  // warps per item
+  const long long nw = (long long)B * wpi;
+  for (long long gw = (long long)blockIdx.x * 8 + (threadIdx.x >> 5); gw < nw; gw += (long long)gridDim.x * 8) {
+    const int b = (int)(gw / wpi), t0 = (int)(gw % wpi) * kPostWarpRows;
+    const size_t base = (size_t)b * T;
+    float x[win];
 #pragma unroll
-    for (int q = 0; q < kPostK; ++q) {
-      const int r = t - kPostK / 2 + q;
+    for (int i = 0; i < win; ++i) {
+      const int r = t0 - pad + i;
+      x[i] = 0.f;
       if (r >= 0 && r < T) {
-        const size_t off = (size_t)(row - t + r) * kPostC + lane;
-        s += (__bfloat162float(hi[off]) + __bfloat162float(lo[off])) * w[q];
+        const size_t off = (base + r) * kPostC + lane;
+        x[i] = __bfloat162float(hi[off]) + __bfloat162float(lo[off]);
       }
     }
-    s = warp_sum(s);
-    if (lane == 0) audio[row] = tanhf(s);
+    float v[32];
+#pragma unroll
+    for (int r = 0; r < 32; ++r) {
+      float acc = 0.f;
+      if (r < kPostWarpRows) {
+#pragma unroll
+        for (int q = 0; q < kPostK; ++q) acc += x[r + q] * w[q];
+      }
+      v[r] = acc;
+    }
+    const float s = warp_colsum32_post(v, lane);  // lane r: row t0 + r
+    if (lane < kPostWarpRows && t0 + lane < T) audio[base + t0 + lane] = tanhf(s);
   }
 }
 
@@ -218,30 +339,61 @@ __global__ void __launch_bounds__(256) post_backward_kernel(PostBwdArgs a) {
   float cs = 0.f, as = 0.f, dw[kPostK];
 #pragma unroll
   for (int q = 0; q < kPostK; ++q) dw[q] = 0.f;
-  for (int rr = warp; rr < kPostRows; rr += 8) {
-    const long long row = (long long)blockIdx.x * kPostRows + rr;
-    if (row >= nrows) break;
-    const int t = (int)(row % a.T);
-    const long long rb = row - t;  // first row of this item
-    float dpre[kPostK];
+  // warp = 8 consecutive rows; the 14 values dy * (1 - y^2) they need are formed once (one per lane)
+  // and broadcast by shuffles when the rows share an item
+  const long long wrow0 = (long long)blockIdx.x * kPostRows + warp * 8;
+  const int t0w = (int)(wrow0 % a.T);
+  const bool same_item = t0w + 7 < a.T && wrow0 + 7 < nrows;
+  float dval = 0.f;
+  if (same_item && lane < 8 + kPostK - 1) {
+    const int tt = t0w - pad + lane;
+    if (tt >= 0 && tt < a.T) {
+      const long long rb = wrow0 - t0w;
+      const float y = a.audio[rb + tt];
+      dval = a.dy[rb + tt] * (1.f - y * y);
+    }
+  }
+  float xin8[8], xm8[8];
 #pragma unroll
-    for (int q = 0; q < kPostK; ++q) {
-      const int tt = t + pad - q;  // output sample fed by input row t through tap q
-      float d = 0.f;
-      if (tt >= 0 && tt < a.T) {
-        const float y = a.audio[rb + tt];
-        d = a.dy[rb + tt] * (1.f - y * y);
+  for (int r = 0; r < 8; ++r) {
+    const long long row = wrow0 + r;
+    xin8[r] = xm8[r] = 0.f;
+    if (row < nrows) {
+      const size_t off = (size_t)row * kPostC + c;
+      xin8[r] = __bfloat162float(a.a_hi[off]) + __bfloat162float(a.a_lo[off]);
+      xm8[r] = __bfloat162float(a.mask_src[off]);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    const long long row = wrow0 + r;
+    if (row >= nrows) break;
+    float dpre[kPostK];
+    if (same_item) {
+#pragma unroll
+      for (int q = 0; q < kPostK; ++q) dpre[q] = __shfl_sync(0xffffffffu, dval, r + 2 * pad - q);
+    } else {
+      const int t = (int)(row % a.T);
+      const long long rb = row - t;
+#pragma unroll
+      for (int q = 0; q < kPostK; ++q) {
+        const int tt = t + pad - q;  // output sample fed by input row t through tap q
+        float d = 0.f;
+        if (tt >= 0 && tt < a.T) {
+          const float y = a.audio[rb + tt];
+          d = a.dy[rb + tt] * (1.f - y * y);
+        }
+        dpre[q] = d;
       }
-      dpre[q] = d;
     }
     float da = 0.f;
 #pragma unroll
     for (int q = 0; q < kPostK; ++q) da += dpre[q] * w[q];
     const size_t off = (size_t)row * kPostC + c;
-    const float xin = __bfloat162float(a.a_hi[off]) + __bfloat162float(a.a_lo[off]);
+    const float xin = xin8[r];
 #pragma unroll
     for (int q = 0; q < kPostK; ++q) dw[q] += xin * dpre[q];
-    const float x = __bfloat162float(a.mask_src[off]);
+    const float x = xm8[r];
     float deriv;
     if (a.act_kind == 1) {
       const float al = a.alpha[c];

@@ -156,7 +156,12 @@ bool upload_reduce_table(Gen& m, std::vector<ReduceDesc>& v, ReduceDesc** dev, i
   std::vector<size_t> sc_off(v.size()), ct_off(v.size());
   for (size_t i = 0; i < v.size(); ++i) {
     size_t sf = 0, cn = 0;
-    first += reduce_desc_shape(v[i], first, &sf, &cn);
+    const int nb = reduce_desc_shape(v[i], first, &sf, &cn);
+    if (nb < 0) {
+      fprintf(stderr, "wuburvc_b200: reduction shape not float4-aligned (n %lld ld %lld)\n", v[i].n, v[i].ld);
+      return false;
+    }
+    first += nb;
     sc_off[i] = sc_total;
     ct_off[i] = ct_total;
     sc_total += sf;
@@ -352,6 +357,12 @@ bool gen_setup(Gen& m) {
       s.noise_parts = noise_backward_parts(B, s.T, s.kn);
       if (!dalloc(m, &s.noise_wt, (size_t)s.C * s.kn)) return false;
       if (!dalloc(m, &s.noise_wpart, (size_t)s.noise_parts * s.C * s.kn)) return false;
+      if (!dalloc(m, &s.noise_g, (size_t)B * s.T * s.kn)) return false;
+      // the noise kernels' shared-memory windows stay within the default 48 KB
+      if (noise_act_smem(s.kn, s.sn) > 48 * 1024 || sizeof(float) * ((size_t)127 * s.sn + s.kn) > 30 * 1024) {
+        fprintf(stderr, "wuburvc_b200: noise conv of stage %d too large (k=%d stride=%d)\n", L, s.kn, s.sn);
+        return false;
+      }
     }
   }
 
@@ -767,7 +778,8 @@ bool gen_backward(Gen& m) {
     // stage input gradient d_x: noise conv, ups dgrad / wgrad
     if (c.nsf) {
       const int nw = m.pidx("dec.noise_convs." + std::to_string(L) + ".weight");
-      noise_backward(s.d_x, m.har, s.noise_wt, B, s.T, s.C, s.kn, s.sn, s.pn, m.T, m.d_har, L < 3, s.noise_wpart, st);
+      noise_backward(s.d_x, m.har, s.noise_wt, B, s.T, s.C, s.kn, s.sn, s.pn, m.T, m.d_har, L < 3, s.noise_wpart,
+                     s.noise_g, st);
       noise_wgrad_reduce(s.noise_wpart, s.noise_parts, s.C, s.kn, m.G(nw), st);
     }
     CK(s.up_dg.run(st));

@@ -73,6 +73,7 @@ struct StageBufs {
   float* ap_up = nullptr;  // snake alpha partials of the activation feeding ups L (from up_dg)
   int ap_up_tiles = 0;
   float* noise_wpart = nullptr;
+  float* noise_g = nullptr;  // noise-conv input-gradient rows [B*T][k]
   float* noise_wt = nullptr;  // noise-conv weights transposed to [k][C]
   int noise_parts = 0;
   ConvWeights wu;

@@ -162,8 +162,11 @@ void wgrad_finish(const float* part, int splits, int rows, int n_total, const in
                                                            norm, dv, dg);
 }
 
+// Block = 32 lanes x 8 part-lanes; a lane owns 4 consecutive columns (float4 loads of the partials),
+// so a block covers 128 columns.  n and ld are multiples of 4 and the partial / scratch buffers
+// 16-byte aligned; outputs are written per element (they may sit anywhere in the gradient buffer).
 __global__ void __launch_bounds__(256) reduce_batched_kernel(const ReduceDesc* __restrict__ descs, int ndesc) {
-  __shared__ float sh[kYLanes][33];
+  __shared__ float4 sh[kYLanes][32];
   __shared__ int di, last;
   const int tx = threadIdx.x, ty = threadIdx.y;
   if (tx == 0 && ty == 0) {
@@ -179,26 +182,35 @@ __global__ void __launch_bounds__(256) reduce_batched_kernel(const ReduceDesc* _
   const ReduceDesc d = descs[di];
   const int b = blockIdx.x - d.first_block;
   const int cb = b % d.colblocks, ch = b / d.colblocks;
-  const long long j = (long long)cb * 32 + tx;
+  const long long j = ((long long)cb * 32 + tx) * 4;
+  const bool in = j < d.n;
   const int p0 = d.nchunks == 1 ? 0 : ch * kReduceChunk;
   const int p1 = d.nchunks == 1 ? d.nparts : min(d.nparts, p0 + kReduceChunk);
-  float s = 0.f;
-  if (j < d.n) {
+  float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (in) {
 #pragma unroll 4
-    for (int p = p0 + ty; p < p1; p += kYLanes) s += d.part[(long long)p * d.ld + j];
+    for (int p = p0 + ty; p < p1; p += kYLanes) {
+      const float4 x = __ldcs(reinterpret_cast<const float4*>(d.part + (long long)p * d.ld + j));
+      s.x += x.x; s.y += x.y; s.z += x.z; s.w += x.w;
+    }
   }
   sh[ty][tx] = s;
   __syncthreads();
-  float t = 0.f;
+  float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
   if (ty == 0) {
 #pragma unroll
-    for (int y = 0; y < kYLanes; ++y) t += sh[y][tx];
+    for (int y = 0; y < kYLanes; ++y) {
+      const float4 x = sh[y][tx];
+      t.x += x.x; t.y += x.y; t.z += x.z; t.w += x.w;
+    }
   }
   if (d.nchunks == 1) {
-    if (ty == 0 && j < d.n) d.out[j] = t;
+    if (ty == 0 && in) {
+      d.out[j] = t.x; d.out[j + 1] = t.y; d.out[j + 2] = t.z; d.out[j + 3] = t.w;
+    }
     return;
   }
-  if (ty == 0 && j < d.n) d.scratch[(long long)ch * d.n + j] = t;
+  if (ty == 0 && in) *reinterpret_cast<float4*>(d.scratch + (long long)ch * d.n + j) = t;
   __threadfence();
   __syncthreads();
   if (tx == 0 && ty == 0) last = atomicAdd(&d.counter[cb], 1u) == (unsigned)(d.nchunks - 1);
@@ -206,23 +218,31 @@ __global__ void __launch_bounds__(256) reduce_batched_kernel(const ReduceDesc* _
   if (!last) return;
   __threadfence();
   // last block of this column group: chunk sums in chunk order
-  s = 0.f;
-  if (j < d.n)
-    for (int c = ty; c < d.nchunks; c += kYLanes) s += __ldcg(&d.scratch[(long long)c * d.n + j]);
+  s = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (in)
+    for (int c = ty; c < d.nchunks; c += kYLanes) {
+      const float4 x = __ldcg(reinterpret_cast<const float4*>(d.scratch + (long long)c * d.n + j));
+      s.x += x.x; s.y += x.y; s.z += x.z; s.w += x.w;
+    }
   sh[ty][tx] = s;
   __syncthreads();
-  if (ty == 0 && j < d.n) {
-    t = 0.f;
+  if (ty == 0 && in) {
+    t = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-    for (int y = 0; y < kYLanes; ++y) t += sh[y][tx];
-    d.out[j] = t;
+    for (int y = 0; y < kYLanes; ++y) {
+      const float4 x = sh[y][tx];
+      t.x += x.x; t.y += x.y; t.z += x.z; t.w += x.w;
+    }
+    d.out[j] = t.x; d.out[j + 1] = t.y; d.out[j + 2] = t.z; d.out[j + 3] = t.w;
   }
   if (tx == 0 && ty == 0) d.counter[cb] = 0u;
 }
 
 int reduce_desc_shape(ReduceDesc& d, int first_block, size_t* scratch_floats, size_t* counters) {
+  // the kernel reads the partials as float4: columns and pitch in multiples of 4, 16-byte base
+  if (d.n % 4 || d.ld % 4 || reinterpret_cast<uintptr_t>(d.part) % 16) return -1;
   d.first_block = first_block;
-  d.colblocks = (int)((d.n + 31) / 32);
+  d.colblocks = (int)((d.n + 127) / 128);
   d.nchunks = d.nparts > 2 * kReduceChunk ? (d.nparts + kReduceChunk - 1) / kReduceChunk : 1;
   *scratch_floats = d.nchunks > 1 ? (size_t)d.nchunks * d.n : 0;
   *counters = d.nchunks > 1 ? (size_t)d.colblocks : 0;

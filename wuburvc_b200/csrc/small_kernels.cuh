@@ -24,7 +24,7 @@ void wgrad_finish(const float* part, int splits, int rows, int n_total, const in
                   cudaStream_t st);
 
 // Many column reductions in one launch: out_i[j] = sum_{p < nparts_i} part_i[p * ld_i + j], j < n_i.
-// A descriptor is served by colblocks x nchunks blocks (32 columns x up to kReduceChunk parts each);
+// A descriptor is served by colblocks x nchunks blocks (128 columns x up to kReduceChunk parts each);
 // with several chunks, each block stores its chunk sum in `scratch` [nchunks][n] and the last block of
 // a column group (counted in `counter`, which it resets) adds the chunk sums in chunk order, so the
 // result does not depend on block scheduling.
@@ -38,7 +38,8 @@ struct ReduceDesc {
   unsigned int* counter;   // colblocks zeroed words when nchunks > 1
 };
 // Fills the launch shape of d (first_block = blocks already in the table); returns its block count and
-// the scratch floats / counters it needs.
+// the scratch floats / counters it needs, or -1 when n or ld is not a multiple of 4 or part is not
+// 16-byte aligned (the kernel reads float4 partials).
 int reduce_desc_shape(ReduceDesc& d, int first_block, size_t* scratch_floats, size_t* counters);
 void reduce_batched(const ReduceDesc* descs, int ndesc, int total_blocks, cudaStream_t st);
 
