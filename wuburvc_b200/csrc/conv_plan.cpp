@@ -187,36 +187,46 @@ bool plan_conv2(Conv2Launch& L, const ConvGeom& g, const void* x_hi, const void*
   p.err = err;
   const int nA = split ? 2 : 1;
   // weights: resident (every chunk and tap of the CTA's N tile loaded once) when they fit beside two
-  // A stages, else a ring of stages holding w_group taps each (fewer, larger stages: each stage costs
-  // the MMA warp one barrier round trip)
-  int kc = (g.C_in % 64 == 0) ? 64 : 32;
-  for (;;) {
-    const size_t a_sub = ((size_t)R * kc * 2 + 1023) / 1024 * 1024;
-    const size_t a_stage = nA * a_sub, w_tap = (size_t)nA * p.n * kc * 2;
-    const long long nch = g.C_in / kc;
-    p.a_stages = 2;
-    const long long room = (long long)kSmemBudget2 - 2048 - (long long)p.a_stages * a_stage;
+  // A stages, else a ring of stages holding w_group taps each.  The wider channel chunk is preferred:
+  // a tap then carries twice the MMAs for the same loop overhead of the MMA warp.
+  struct Opt {
+    int kc = 0, resident = 0, G = 0, WS = 0;
+    size_t a_sub = 0, smem = 0;
+    long long score = -1;
+  } best;
+  for (int kc_try : {64, 32}) {
+    if (g.C_in % kc_try) continue;
+    Opt o;
+    o.kc = kc_try;
+    o.a_sub = ((size_t)R * kc_try * 2 + 1023) / 1024 * 1024;
+    const size_t a_stage = nA * o.a_sub, w_tap = (size_t)nA * p.n * kc_try * 2;
+    const long long nch = g.C_in / kc_try;
+    const long long room = (long long)kSmemBudget2 - 2048 - 2 * (long long)a_stage;
     const long long total_w = nch * g.k * (long long)w_tap;
     if (room > 0 && total_w <= room) {
-      p.w_resident = 1;
-      p.w_group = g.k;
-      p.w_stages = 1;
-      p.a_sub_bytes = (uint32_t)a_sub;
-      L.smem = p.a_stages * a_stage + (size_t)total_w + 1024 + 512;
-      break;
+      o.resident = 1;
+      o.G = g.k;
+      o.WS = 1;
+      o.smem = 2 * a_stage + (size_t)total_w + 1024 + 512;
+      o.score = 1LL << 40;  // no weight waits at all
+    } else {
+      const long long G = room > 0 ? std::min<long long>(g.k, room / (2 * (long long)w_tap)) : 0;
+      if (G < 1) continue;
+      o.G = (int)G;
+      o.WS = (int)std::min<long long>(4, room / (G * (long long)w_tap));
+      o.smem = 2 * a_stage + (size_t)o.WS * G * w_tap + 1024 + 512;
+      o.score = (long long)kc_try * 1000 + G;
     }
-    const long long G = room > 0 ? std::min<long long>(g.k, room / (2 * (long long)w_tap)) : 0;
-    if (G >= 1) {
-      p.w_resident = 0;
-      p.w_group = (int)G;
-      p.w_stages = (int)std::min<long long>(4, room / (G * (long long)w_tap));
-      p.a_sub_bytes = (uint32_t)a_sub;
-      L.smem = p.a_stages * a_stage + (size_t)p.w_stages * G * w_tap + 1024 + 512;
-      break;
-    }
-    if (kc == 32) return false;
-    kc = 32;
+    if (o.score > best.score) best = o;
   }
+  if (best.score < 0) return false;
+  const int kc = best.kc;
+  p.a_stages = 2;
+  p.w_resident = best.resident;
+  p.w_group = best.G;
+  p.w_stages = best.WS;
+  p.a_sub_bytes = (uint32_t)best.a_sub;
+  L.smem = best.smem;
   L.kc = kc;
   p.n_chunks = g.C_in / kc;
   p.tmem_cols = pow2_cols(2 * p.n);

@@ -272,7 +272,7 @@ int wubu_b200_gen_graph_kernels(WubuB200Gen* gen) {
 
 int wubu_b200_gen_kernel_bench(WubuB200Gen* gen, int which, int stage, int iters, float* ms_per_launch,
                                double* flops_per_launch) {
-  if (!gen || stage < 0 || stage > 3 || iters < 1 || which < 0 || which > 2) return WUBU_B200_ERR_ARG;
+  if (!gen || stage < 0 || stage > 3 || iters < 1 || which < 0 || which > 4) return WUBU_B200_ERR_ARG;
   Gen& m = gen->m;
   cudaSetDevice(m.opt.device);
   StageBufs& s = m.sg[stage];
@@ -284,6 +284,8 @@ int wubu_b200_gen_kernel_bench(WubuB200Gen* gen, int which, int stage, int iters
   auto launch = [&]() -> bool {
     if (which == 0) return k.f1[0].run(m.stream) == cudaSuccess;
     if (which == 1) return k.d1[0].run(m.stream) == cudaSuccess;
+    if (which == 3) return k.f2[0].run(m.stream) == cudaSuccess;
+    if (which == 4) return k.d2[0].run(m.stream) == cudaSuccess;
     return k.g1[0].L.run(m.stream) == cudaSuccess;
   };
   for (int i = 0; i < 2; ++i)

@@ -235,11 +235,40 @@ __global__ void __launch_bounds__(256) noise_wgrad_kernel(const float* __restric
   }
 }
 
+// Phase 1 for few taps (k <= 8): thread per row, float4 walk over the row's channels.
+__global__ void __launch_bounds__(256) noise_g_small_kernel(const float* __restrict__ dx, const float* __restrict__ wt,
+                                                            long long rows, int C, int k, float* __restrict__ g) {
+  const long long row = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= rows) return;
+  float acc[8];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) acc[q] = 0.f;
+  const float4* x4 = reinterpret_cast<const float4*>(dx + (size_t)row * C);
+  const float4* w4 = reinterpret_cast<const float4*>(wt);
+  const int c4n = C / 4;
+  for (int c4 = 0; c4 < c4n; ++c4) {
+    const float4 x = x4[c4];
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      if (q < k) {
+        const float4 w = w4[(size_t)q * c4n + c4];
+        acc[q] += x.x * w.x + x.y * w.y + x.z * w.z + x.w * w.w;
+      }
+  }
+#pragma unroll
+  for (int q = 0; q < 8; ++q)
+    if (q < k) g[(size_t)row * k + q] = acc[q];
+}
+
 void noise_backward(const float* dx, const float* har, const float* wt, int B, int T, int C, int k, int stride, int pad,
                     int T_full, float* d_har, int accumulate_dhar, float* wpart, float* g, cudaStream_t st) {
   const long long rows = (long long)B * T;
-  const long long warps = rows * ((k + 15) / 16);
-  noise_g_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(dx, wt, rows, C, k, g);
+  if (k <= 8) {
+    noise_g_small_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, st>>>(dx, wt, rows, C, k, g);
+  } else {
+    const long long warps = rows * ((k + 15) / 16);
+    noise_g_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(dx, wt, rows, C, k, g);
+  }
   const long long n = (long long)B * T_full;
   noise_dhar_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(g, B, T, k, stride, pad, T_full, d_har,
                                                                   accumulate_dhar);
