@@ -60,15 +60,18 @@ bool make_map_bf16_3d(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1
   return true;
 }
 
-// choose K chunk / stages for the forward-type kernel
-static void pick_fwd_tiling(int c_in, int n_tile, int split, int& kc, int& stages, size_t& smem) {
+// choose K chunk / stages for the forward-type kernel: about three stages, each holding as many
+// (tap, chunk) steps as fit (every stage costs the MMA warp one barrier round trip)
+static void pick_fwd_tiling(int c_in, int n_tile, int split, int& kc, int& stages, int& kgroup, size_t& smem) {
   kc = (c_in % 64 == 0) ? 64 : 32;
   for (;;) {
     const int nA = split ? 2 : 1;
-    const size_t stage = (size_t)nA * (128 * kc * 2 + (size_t)n_tile * kc * 2);
-    stages = (int)std::min<size_t>(8, (kSmemBudget - 1024 - 256) / stage);
+    const size_t step = (size_t)nA * (128 * kc * 2 + (size_t)n_tile * kc * 2);
+    const size_t room = kSmemBudget - 1024 - 256;
+    kgroup = (int)std::max<size_t>(1, std::min<size_t>(4, room / (3 * step)));
+    stages = (int)std::min<size_t>(8, room / (kgroup * step));
     if (stages >= 3 || kc == 32) {
-      smem = stages * stage + 1024 /*align*/ + 256 /*barriers*/;
+      smem = stages * kgroup * step + 1024 /*align*/ + 256 /*barriers*/;
       return;
     }
     kc = 32;
@@ -81,7 +84,7 @@ static bool finish_fwd(ConvLaunch& L, int B, int c_in, int n_total, int split, i
   while (n_total % n_tile) n_tile -= 16;
   if (n_tile < 16 || n_tile % 16 || n_total % 32) return false;
   if (c_in % 32) return false;
-  pick_fwd_tiling(c_in, n_tile, split, L.kc, p.stages, L.smem);
+  pick_fwd_tiling(c_in, n_tile, split, L.kc, p.stages, p.kgroup, L.smem);
   p.n_tile = n_tile;
   p.n_total = n_total;
   p.n_chunks = c_in / L.kc;
@@ -114,9 +117,9 @@ bool plan_conv(ConvLaunch& L, const ConvGeom& g, const void* x_hi, const void* x
   p.epi = epi;
   int n_tile = std::min(g.C_out, 256);
   while (g.C_out % n_tile) n_tile -= 16;
-  int kc, stages;
+  int kc, stages, kgroup;
   size_t smem;
-  pick_fwd_tiling(g.C_in, n_tile, split, kc, stages, smem);
+  pick_fwd_tiling(g.C_in, n_tile, split, kc, stages, kgroup, smem);
   const uint64_t rs = (uint64_t)g.C_in * 2, is = rs * g.T_in;
   if (!make_map_bf16_3d(&L.maps.a[0], x_hi, g.C_in, g.T_in, g.B, rs, is, kc, 128, 1)) return false;
   if (split && !make_map_bf16_3d(&L.maps.a[1], x_lo, g.C_in, g.T_in, g.B, rs, is, kc, 128, 1)) return false;
@@ -273,9 +276,9 @@ bool plan_convT(ConvLaunch& L, int B, int T_in, int C_in, int C_out, int k, int 
   p.lo_base = 1;
   p.epi = epi;
   int n_tile = std::min(C_out, 256);
-  int kc, stages;
+  int kc, stages, kgroup;
   size_t smem;
-  pick_fwd_tiling(C_in, n_tile, split, kc, stages, smem);
+  pick_fwd_tiling(C_in, n_tile, split, kc, stages, kgroup, smem);
   const uint64_t rs = (uint64_t)C_in * 2, is = rs * T_in;
   if (!make_map_bf16_3d(&L.maps.a[0], x_hi, C_in, T_in, B, rs, is, kc, 128, 1)) return false;
   if (split && !make_map_bf16_3d(&L.maps.a[1], x_lo, C_in, T_in, B, rs, is, kc, 128, 1)) return false;
@@ -310,9 +313,9 @@ bool plan_convT_dgrad(ConvLaunch& L, int B, int T_in, int C_in, int C_out, int k
   p.lo_base = 0;
   p.epi = epi;
   int n_tile = std::min(C_in, 256);
-  int kc, stages;
+  int kc, stages, kgroup;
   size_t smem;
-  pick_fwd_tiling(C_out, n_tile, 0, kc, stages, smem);
+  pick_fwd_tiling(C_out, n_tile, 0, kc, stages, kgroup, smem);
   for (int r = 0; r < s; ++r) {
     const uint64_t rows = (uint64_t)(T_out - r + s - 1) / s;
     const char* base = static_cast<const char*>(dy) + (size_t)r * C_out * 2;

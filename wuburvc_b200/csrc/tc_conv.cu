@@ -23,11 +23,13 @@ __global__ void __launch_bounds__(192, 1)
   const int tap0 = p.tap_start[phase];
   const int ntaps = p.tap_start[phase + 1] - tap0;
   const int ksteps = ntaps * p.n_chunks;
-  const int S = p.stages;
+  const int S = p.stages, G = p.kgroup;  // a pipeline stage holds G consecutive (tap, chunk) steps
+  const int ngroups = (ksteps + G - 1) / G;
   const int nA = p.split ? 2 : 1;
   constexpr uint32_t a_bytes = 128u * KC * 2u;
   const uint32_t w_bytes = (uint32_t)N * KC * 2u;
-  const uint32_t stage_bytes = nA * (a_bytes + w_bytes);
+  const uint32_t step_bytes = nA * (a_bytes + w_bytes);
+  const uint32_t stage_bytes = (uint32_t)G * step_bytes;
 
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * stage_bytes);
   uint64_t* empty = full + S;
@@ -44,61 +46,69 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  // producer / MMA: converged warps, elect.sync issue, warp-uniform `ok` (no early exits)
   if (warp == 4) {
     // ---------------- TMA producer ----------------
-    if (lane == 0) {
-      for (int ks = 0; ks < ksteps; ++ks) {
-        const int s = ks % S;
-        if (ks >= S && !mbar_wait(&empty[s], ((ks / S) & 1) ^ 1, p.err, ERR_WAIT_EMPTY)) break;
-        const int t = ks / p.n_chunks, c = ks - t * p.n_chunks;
-        const int ti = tap0 + t;
-        const int mi = p.tap_map[ti];
-        const int row = q0 + p.tap_shift[ti];
+    bool ok = true;
+    int s = 0;
+    uint32_t ph = 0;
+    for (int g = 0; g < ngroups; ++g) {
+      if (ok && g >= S) ok = mbar_wait_warp(&empty[s], ph ^ 1u, p.err, ERR_WAIT_EMPTY);
+      if (ok) {
+        const int ks0 = g * G, nk = min(G, ksteps - ks0);
         uint8_t* st = smem + (size_t)s * stage_bytes;
-        mbar_arrive_expect_tx(&full[s], stage_bytes);
-        tma_load_3d(st, &maps.a[mi], &full[s], c * KC, row, item);
-        if (p.split) tma_load_3d(st + a_bytes, &maps.a[p.lo_base + mi], &full[s], c * KC, row, item);
-        uint8_t* wd = st + nA * a_bytes;
-        tma_load_3d(wd, &maps.w_hi, &full[s], c * KC, n0, p.tap_w[ti]);
-        if (p.split) tma_load_3d(wd + w_bytes, &maps.w_lo, &full[s], c * KC, n0, p.tap_w[ti]);
+        mbar_expect_tx_warp(&full[s], (uint32_t)nk * step_bytes);
+        for (int i = 0; i < nk; ++i) {
+          const int ks = ks0 + i;
+          const int t = ks / p.n_chunks, c = ks - t * p.n_chunks;
+          const int ti = tap0 + t;
+          const int mi = p.tap_map[ti];
+          const int row = q0 + p.tap_shift[ti];
+          uint8_t* sd = st + (size_t)i * step_bytes;
+          tma_load_3d_warp(sd, &maps.a[mi], &full[s], c * KC, row, item);
+          if (p.split) tma_load_3d_warp(sd + a_bytes, &maps.a[p.lo_base + mi], &full[s], c * KC, row, item);
+          uint8_t* wd = sd + nA * a_bytes;
+          tma_load_3d_warp(wd, &maps.w_hi, &full[s], c * KC, n0, p.tap_w[ti]);
+          if (p.split) tma_load_3d_warp(wd + w_bytes, &maps.w_lo, &full[s], c * KC, n0, p.tap_w[ti]);
+        }
       }
+      if (++s == S) { s = 0; ph ^= 1u; }
     }
   } else if (warp == 5) {
     // ---------------- MMA issuer ----------------
-    if (lane == 0) {
-      const uint32_t idesc = make_idesc_bf16(128, N, 0, 0);
-      constexpr uint32_t layout = (KC == 64) ? 2u : 4u;        // 128B / 64B swizzle
-      constexpr uint32_t sbo = (KC == 64) ? 1024u : 512u;       // 8 rows x row bytes
-      const uint32_t sbase = smem_u32(smem);
-      bool ok = true;
-      for (int ks = 0; ks < ksteps && ok; ++ks) {
-        const int s = ks % S;
-        if (!mbar_wait(&full[s], (ks / S) & 1, p.err, ERR_WAIT_FULL)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t a_hi = sbase + (uint32_t)s * stage_bytes;
-        const uint32_t a_lo = a_hi + a_bytes;
-        const uint32_t w_hi = a_hi + nA * a_bytes;
-        const uint32_t w_lo = w_hi + w_bytes;
+    const uint32_t idesc = make_idesc_bf16(128, N, 0, 0);
+    constexpr uint32_t layout = (KC == 64) ? 2u : 4u;        // 128B / 64B swizzle
+    constexpr uint32_t sbo = (KC == 64) ? 1024u : 512u;       // 8 rows x row bytes
+    const uint64_t d0 = make_sdesc(smem_u32(smem), 16, sbo, layout);
+    bool ok = true;
+    int s = 0;
+    uint32_t ph = 0;
+    for (int g = 0; g < ngroups; ++g) {
+      if (ok) ok = mbar_wait_warp(&full[s], ph, p.err, ERR_WAIT_FULL);
+      if (ok) {
+        const int nk = min(G, ksteps - g * G);
+        for (int i = 0; i < nk; ++i) {
+          const uint64_t dah = d0 + (((uint32_t)s * stage_bytes + (uint32_t)i * step_bytes) >> 4);
+          const uint64_t dal = dah + (a_bytes >> 4);
+          const uint64_t dwh = dah + ((nA * a_bytes) >> 4);
+          const uint64_t dwl = dwh + (w_bytes >> 4);
 #pragma unroll
-        for (int k = 0; k < KC / 16; ++k) {
-          const uint32_t koff = (uint32_t)k * 32u;
-          const uint64_t dah = make_sdesc(a_hi + koff, 16, sbo, layout);
-          const uint64_t dwh = make_sdesc(w_hi + koff, 16, sbo, layout);
-          umma_f16(tmem, dah, dwh, idesc, (ks | k) != 0);
-          if (p.split) {
-            const uint64_t dal = make_sdesc(a_lo + koff, 16, sbo, layout);
-            const uint64_t dwl = make_sdesc(w_lo + koff, 16, sbo, layout);
-            umma_f16(tmem, dal, dwh, idesc, 1);
-            umma_f16(tmem, dah, dwl, idesc, 1);
+          for (int k = 0; k < KC / 16; ++k) {  // K16 step = 32 bytes along the swizzled row
+            umma_f16_warp(tmem, dah + 2u * k, dwh + 2u * k, idesc, (g | i | k) != 0);
+            if (p.split) {
+              umma_f16_warp(tmem, dal + 2u * k, dwh + 2u * k, idesc, 1);
+              umma_f16_warp(tmem, dah + 2u * k, dwl + 2u * k, idesc, 1);
+            }
           }
         }
-        umma_commit(&empty[s]);
+        umma_commit_warp(&empty[s]);
       }
-      if (ok) umma_commit(accf);
+      if (++s == S) { s = 0; ph ^= 1u; }
     }
+    if (ok) umma_commit_warp(accf);
   } else {
     // ---------------- epilogue (warps 0..3 <-> TMEM lanes 0..127) ----------------
-    const bool ok = mbar_wait(accf, 0, p.err, ERR_WAIT_ACC);
+    const bool ok = mbar_wait_warp(accf, 0, p.err, ERR_WAIT_ACC);
     tc_fence_after();
     const int q = q0 + warp * 32 + lane;
     const int orow = q * p.out_stride + p.out_off[phase];
@@ -108,8 +118,11 @@ __global__ void __launch_bounds__(192, 1)
     const float* ra = p.epi.rowadd ? p.epi.rowadd + (size_t)item * p.n_total + n0 : nullptr;
     for (int c0 = 0; c0 < N; c0 += 32) {
       float v[32];
-      tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
-      if (!ok) continue;
+      if (ok) tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
+      else
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = 0.f;
+      // every epilogue warp reaches the chunk's named barriers, whether or not the wait succeeded
       epi_chunk(p.epi, v, valid, row_off + c0, n0 + c0, part_row + c0, ra ? ra + c0 : nullptr, warp, lane, red);
     }
   }

@@ -60,6 +60,7 @@ struct TcConvParams {
   int split;           // bf16x3 forward
   int lo_base;
   int stages;
+  int kgroup;          // (tap, chunk) steps per pipeline stage
   int tmem_cols;
   int t_out;           // output rows per item
   int out_stride;      // output row = q * out_stride + out_off[phase]
