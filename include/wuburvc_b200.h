@@ -130,6 +130,12 @@ int wubu_b200_gen_param_count(const WubuB200GenConfig* cfg);
 long long wubu_b200_gen_param_total(const WubuB200GenConfig* cfg);
 int wubu_b200_gen_param_info(const WubuB200GenConfig* cfg, int index, char* name, int name_cap, int* shape3,
                              long long* offset, long long* numel);
+/* Data-parallel gradient buckets (host only, no GPU needed): writes the end offset (floats, in the
+ * flat gradient buffer) of each all-reduce bucket into ends[0..n) and returns n (5: stages 3, 2, 1, 0
+ * in backward-completion order, then conv_pre / cond / source), or a negative error code.  Bucket b
+ * spans [ends[b-1], ends[b]) (ends[-1] = 0) and may be empty. */
+int wubu_b200_gen_bucket_plan(const WubuB200GenConfig* cfg, long long* ends, int cap);
+
 /* Deterministic init: conv weights / v ~ N(0, 0.01), g = ||v|| per dim-0 row, biases 0,
  * Snake alpha 1, l_linear weight U(-1/3, 1/3). */
 int wubu_b200_gen_init_params(const WubuB200GenConfig* cfg, unsigned long long seed, float* host_flat);

@@ -93,6 +93,7 @@ _SIGS = {
     "wubu_b200_gen_param_info": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_char_p, ctypes.c_int,
                                                 ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
     "wubu_b200_gen_init_params": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_ulonglong, ctypes.c_void_p]),
+    "wubu_b200_gen_bucket_plan": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]),
     "wubu_b200_gen_create": (ctypes.c_void_p, [ctypes.c_void_p, ctypes.c_void_p]),
     "wubu_b200_gen_destroy": (None, [ctypes.c_void_p]),
     "wubu_b200_gen_set_params": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
@@ -157,6 +158,21 @@ def param_table(cfg: dict) -> List[Tuple[str, str, Tuple[int, int, int], int, in
 def param_total(cfg: dict) -> int:
     c = GenConfig.from_dict(cfg)
     return int(L().wubu_b200_gen_param_total(ctypes.byref(c)))
+
+
+def bucket_plan(cfg: dict) -> List[Tuple[int, int]]:
+    """Data-parallel all-reduce buckets [(start, end)] of the flat gradient buffer, in the order the
+    backward finishes them (host only)."""
+    c = GenConfig.from_dict(cfg)
+    ends = (ctypes.c_longlong * 16)()
+    n = L().wubu_b200_gen_bucket_plan(ctypes.byref(c), ends, 16)
+    if n < 0:
+        raise ValueError("invalid generator config")
+    out, prev = [], 0
+    for i in range(n):
+        out.append((prev, int(ends[i])))
+        prev = int(ends[i])
+    return out
 
 
 def init_params(cfg: dict, seed: int = 0) -> np.ndarray:

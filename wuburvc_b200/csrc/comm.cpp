@@ -72,24 +72,48 @@ struct Comm {
 };
 
 // Bucket boundaries: end of conv_post + stage 3, stage 2, stage 1, stage 0, and the rest.
-static std::vector<std::pair<long long, long long>> make_buckets(const Gen& m) {
+// Gradient all-reduce buckets, in the order the backward finishes them: stage 3's parameters, then
+// stages 2, 1, 0 (each ends at its ups layer), then everything else (conv_pre, cond, source).  The
+// flat buffer is laid out in that order, so bucket b is the contiguous range [first, second).  Every
+// bucket is kept (possibly empty) so that bucket index b always means stage 3 - b.
+static std::vector<std::pair<long long, long long>> plan_buckets(const ParamTable& t) {
   std::vector<long long> ends;
   for (int L = 3; L >= 0; --L) {
     const std::string key = "dec.ups." + std::to_string(L) + ".bias";
     long long end = 0;
-    for (const auto& e : m.table.e)
+    for (const auto& e : t.e)
       if (e.name == key || e.name == "dec.ups_act." + std::to_string(L) + ".alpha") end = std::max(end, e.off + e.n);
     ends.push_back((end + 63) / 64 * 64);
   }
-  ends.push_back(m.table.total);
+  ends.push_back(t.total);
   std::vector<std::pair<long long, long long>> b;
   long long prev = 0;
   for (long long e : ends) {
-    if (e > prev) b.push_back({prev, e});
-    prev = std::max(prev, e);
+    const long long end = std::min(std::max(e, prev), t.total);
+    b.push_back({prev, end});
+    prev = end;
   }
   return b;
 }
+
+static std::vector<std::pair<long long, long long>> make_buckets(const Gen& m) { return plan_buckets(m.table); }
+
+}  // namespace wb
+
+int wubu_b200_gen_bucket_plan(const WubuB200GenConfig* cfg, long long* ends, int cap) {
+  using namespace wb;
+  if (!cfg || !config_valid(*cfg)) return WUBU_B200_ERR_ARG;
+  const ParamTable t = build_param_table(*cfg);
+  if (t.e.empty()) return WUBU_B200_ERR_ARG;
+  const auto b = plan_buckets(t);
+  if (ends) {
+    if (cap < (int)b.size()) return WUBU_B200_ERR_ARG;
+    for (size_t i = 0; i < b.size(); ++i) ends[i] = b[i].second;
+  }
+  return (int)b.size();
+}
+
+namespace wb {
 
 int comm_bucket_count(Gen& m) { return m.comm ? (int)m.comm->buckets.size() : 0; }
 
@@ -102,6 +126,7 @@ int comm_bucket_ready(Gen& m, int b) {
   if (cudaEventRecord(c->ready[b], m.stream) != cudaSuccess) return WUBU_B200_ERR_CUDA;
   if (cudaStreamWaitEvent(c->cs, c->ready[b], 0) != cudaSuccess) return WUBU_B200_ERR_CUDA;
   const auto& r = c->buckets[b];
+  if (r.second <= r.first) return 0;  // empty bucket: every rank skips it alike
   const int rc = api.AllReduce(m.grads + r.first, m.grads + r.first, (size_t)(r.second - r.first), ncclFloat32,
                                ncclSum, c->comm, c->cs);
   if (rc != ncclSuccess) {
