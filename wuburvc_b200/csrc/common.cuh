@@ -187,6 +187,20 @@ WB_DEV bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* err, int code) {
   return ok;
 }
 
+// Non-blocking test by a converged warp: has the phase with this parity completed?  (One
+// mbarrier.test_wait; lets the MMA warp look at the next stage while it issues the current one.)
+WB_DEV bool mbar_poll_warp(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return __all_sync(0xffffffffu, done != 0);
+}
+
 // Arrive on `bar` once every previously issued tcgen05.mma of this thread completes.
 WB_DEV void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(

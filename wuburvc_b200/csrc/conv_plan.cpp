@@ -232,7 +232,8 @@ bool plan_conv2(Conv2Launch& L, const ConvGeom& g, const void* x_hi, const void*
   L.smem = best.smem;
   L.kc = kc;
   p.n_chunks = g.C_in / kc;
-  p.tmem_cols = pow2_cols(2 * p.n);
+  // two accumulators (double buffering) of n columns, 2n under the two-MMA bf16x3 split
+  p.tmem_cols = pow2_cols(2 * p.n * (split ? 2 : 1));
   if (p.tmem_cols > 512) return false;
   if (!make_map_bf16_cm(&L.maps.a_hi, x_hi, g.T_in, g.C_in, g.B, R, kc)) return false;
   if (split && !make_map_bf16_cm(&L.maps.a_lo, x_lo, g.T_in, g.C_in, g.B, R, kc)) return false;

@@ -128,7 +128,12 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
     }
   } else if (warp == kMmaWarp) {
     // ---------------- MMA issuer ----------------
+    // bf16x3 as two MMAs per K16 step: A_hi x [W_hi | W_lo] (N = 2N: the tap's hi and lo weight tiles
+    // are adjacent rows in shared memory) into accumulator columns [0, 2N), then A_lo x W_hi added to
+    // columns [N, 2N); the epilogue sums the two halves.  Fewer operand reads from shared memory than
+    // three N-wide MMAs, and a wider (more efficient) first MMA.
     const uint32_t idesc = make_idesc_bf16(128, N, 0, 0);
+    const uint32_t idesc2 = make_idesc_bf16(128, 2 * N, 0, 0);
     constexpr uint32_t wlayout = (KC == 64) ? 2u : 4u;
     constexpr uint32_t wsbo = (KC == 64) ? 1024u : 512u;
     const uint32_t a_lbo = (uint32_t)p.halo_rows * 16u;  // stride between 8-channel core-matrix columns
@@ -141,39 +146,55 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
     if (resident) ok = mbar_wait_warp(&w_full[0], 0, p.err, ERR_WAIT_FULL);
     int sa = 0, sw = 0, t_it = 0;
     uint32_t aph = 0, wph = 0;
+    bool w_ready = false;  // weight stage sw known complete (polled ahead)
     for (int tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x, ++t_it) {
       const int buf = t_it & 1;
       if (ok && t_it >= 2) ok = mbar_wait_warp(&acc_empty[buf], ((t_it >> 1) & 1) ^ 1, p.err, ERR_WAIT_ACC);
       tc_fence_after();
-      const uint32_t d = tmem + (uint32_t)(buf * N);
+      const uint32_t d = tmem + (uint32_t)(buf * N * nA);  // nA = 2: accumulator of 2N columns
       for (int c = 0; c < nch; ++c) {
         if (ok) ok = mbar_wait_warp(&a_full[sa], aph, p.err, ERR_WAIT_FULL);
         const uint64_t dah = da0 + (uint64_t)((sa * a_stage) >> 4);
         const uint64_t dal = dah + (uint64_t)(a_sub >> 4);
-        for (int g = 0; g < ngroups; ++g) {
-          const int t0 = resident ? 0 : g * G;
-          const int nt = resident ? ntaps : min(G, ntaps - t0);
-          if (!resident && ok) ok = mbar_wait_warp(&w_full[sw], wph, p.err, ERR_WAIT_FULL);
-          if (ok) {
-            const uint32_t wst = resident ? (uint32_t)(c * ntaps) * w_tap : (uint32_t)sw * w_stage;
-            for (int j = 0; j < nt; ++j) {
-              const uint64_t dwh = dw0 + (uint64_t)((wst + (uint32_t)j * w_tap) >> 4);
-              const uint64_t dwl = dwh + (uint64_t)(w_sub >> 4);
-              const uint32_t at = (uint32_t)(t0 + j) * tap_step;
-              const uint32_t acc0 = (c | t0 | j) ? 1u : 0u;
+        // one tap: KC/16 K16 steps, 3 MMAs each under the bf16x3 split
+        auto issue_tap = [&](uint32_t w_off, int t, uint32_t acc0) {
+          const uint64_t dwh = dw0 + (uint64_t)(w_off >> 4);
+          const uint64_t dwl = dwh + (uint64_t)(w_sub >> 4);
+          const uint32_t at = (uint32_t)t * tap_step;
 #pragma unroll
-              for (int k = 0; k < KC / 16; ++k) {
-                const uint64_t ao = at + (uint32_t)k * k_step_a;
-                umma_f16_warp(d, dah + ao, dwh + 2u * k, idesc, k ? 1u : acc0);
-                if (SPLIT) {
-                  umma_f16_warp(d, dal + ao, dwh + 2u * k, idesc, 1);
-                  umma_f16_warp(d, dah + ao, dwl + 2u * k, idesc, 1);
-                }
-              }
+          for (int k = 0; k < KC / 16; ++k) {
+            const uint64_t ao = at + (uint32_t)k * k_step_a;
+            if (SPLIT) {
+              umma_f16_warp(d, dah + ao, dwh + 2u * k, idesc2, k ? 1u : acc0);
+              umma_f16_warp(d + (uint32_t)N, dal + ao, dwh + 2u * k, idesc, 1);
+            } else {
+              umma_f16_warp(d, dah + ao, dwh + 2u * k, idesc, k ? 1u : acc0);
             }
-            if (!resident) umma_commit_warp(&w_empty[sw]);
           }
-          if (!resident && ++sw == WS) { sw = 0; wph ^= 1u; }
+          (void)dwl;
+        };
+        if (resident) {
+          if (ok) {
+            const uint32_t wst = (uint32_t)(c * ntaps) * w_tap;
+            for (int t = 0; t < ntaps; ++t) issue_tap(wst + (uint32_t)t * w_tap, t, (c | t) ? 1u : 0u);
+          }
+        } else {
+          for (int g = 0; g < ngroups; ++g) {
+            const int t0 = g * G, nt = min(G, ntaps - t0);
+            if (ok && !w_ready) ok = mbar_wait_warp(&w_full[sw], wph, p.err, ERR_WAIT_FULL);
+            // look at the next weight stage now, so its (usually complete) wait is off the issue path
+            int sw2 = sw + 1;
+            uint32_t ph2 = wph;
+            if (sw2 == WS) { sw2 = 0; ph2 ^= 1u; }
+            w_ready = mbar_poll_warp(&w_full[sw2], ph2);
+            if (ok) {
+              const uint32_t wst = (uint32_t)sw * w_stage;
+              for (int j = 0; j < nt; ++j) issue_tap(wst + (uint32_t)j * w_tap, t0 + j, (c | t0 | j) ? 1u : 0u);
+              umma_commit_warp(&w_empty[sw]);
+            }
+            sw = sw2;
+            wph = ph2;
+          }
         }
         if (ok) umma_commit_warp(&a_empty[sa]);
         if (++sa == AS) { sa = 0; aph ^= 1u; }
@@ -215,8 +236,16 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
       for (int c0 = 0; c0 < N; c0 += 32) {
         if (c0) epi_load<F>(e, valid, row_off + c0, in);
         float v[32];
-        if (ok) tmem_ld32(tmem + (uint32_t)(buf * N) + ((uint32_t)(qw * 32) << 16) + (uint32_t)c0, v);
-        else
+        if (ok) {
+          const uint32_t ta = tmem + (uint32_t)(buf * N * nA) + ((uint32_t)(qw * 32) << 16) + (uint32_t)c0;
+          tmem_ld32(ta, v);
+          if (SPLIT) {  // [0, N) holds hi*hi, [N, 2N) hi*lo + lo*hi: their sum is the bf16x3 product
+            float u[32];
+            tmem_ld32(ta + (uint32_t)N, u);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] += u[i];
+          }
+        } else
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = 0.f;
         // the chunk's named barriers are reached by the whole group whether or not the wait succeeded
