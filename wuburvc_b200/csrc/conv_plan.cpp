@@ -78,10 +78,17 @@ static void pick_fwd_tiling(int c_in, int n_tile, int split, int& kc, int& stage
   }
 }
 
+// GEMM N per CTA of the general conv kernel: up to 256 columns, 128 under the bf16x3 split (its
+// first MMA is 2N wide)
+static int fwd_n_tile(int n_total, int split) {
+  int n_tile = std::min(n_total, split ? 128 : 256);
+  while (n_tile > 16 && n_total % n_tile) n_tile -= 16;
+  return n_tile;
+}
+
 static bool finish_fwd(ConvLaunch& L, int B, int c_in, int n_total, int split, int nphase, int* err) {
   TcConvParams& p = L.p;
-  int n_tile = std::min(n_total, 256);
-  while (n_total % n_tile) n_tile -= 16;
+  const int n_tile = fwd_n_tile(n_total, split);
   if (n_tile < 16 || n_tile % 16 || n_total % 32) return false;
   if (c_in % 32) return false;
   pick_fwd_tiling(c_in, n_tile, split, L.kc, p.stages, p.kgroup, L.smem);
@@ -89,7 +96,7 @@ static bool finish_fwd(ConvLaunch& L, int B, int c_in, int n_total, int split, i
   p.n_total = n_total;
   p.n_chunks = c_in / L.kc;
   p.split = split;
-  p.tmem_cols = pow2_cols(n_tile);
+  p.tmem_cols = pow2_cols(n_tile * (split ? 2 : 1));  // 2n columns under the two-MMA bf16x3 split
   p.tiles_per_item = (p.m_rows + 127) / 128;
   p.err = err;
   L.grid = dim3(B * p.tiles_per_item, n_total / n_tile, nphase);
@@ -115,8 +122,7 @@ bool plan_conv(ConvLaunch& L, const ConvGeom& g, const void* x_hi, const void* x
   }
   p.lo_base = 1;
   p.epi = epi;
-  int n_tile = std::min(g.C_out, 256);
-  while (g.C_out % n_tile) n_tile -= 16;
+  const int n_tile = fwd_n_tile(g.C_out, split);
   int kc, stages, kgroup;
   size_t smem;
   pick_fwd_tiling(g.C_in, n_tile, split, kc, stages, kgroup, smem);
@@ -276,7 +282,7 @@ bool plan_convT(ConvLaunch& L, int B, int T_in, int C_in, int C_out, int k, int 
   p.tap_start[s] = n;
   p.lo_base = 1;
   p.epi = epi;
-  int n_tile = std::min(C_out, 256);
+  const int n_tile = fwd_n_tile(C_out, split);
   int kc, stages, kgroup;
   size_t smem;
   pick_fwd_tiling(C_in, n_tile, split, kc, stages, kgroup, smem);

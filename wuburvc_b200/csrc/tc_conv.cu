@@ -76,7 +76,10 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else if (warp == 5) {
     // ---------------- MMA issuer ----------------
+    // bf16x3 as A_hi x [W_hi | W_lo] (2N wide: the tiles are adjacent rows) + A_lo x W_hi into the
+    // upper N columns; the epilogue adds the halves
     const uint32_t idesc = make_idesc_bf16(128, N, 0, 0);
+    const uint32_t idesc2 = make_idesc_bf16(128, 2 * N, 0, 0);
     constexpr uint32_t layout = (KC == 64) ? 2u : 4u;        // 128B / 64B swizzle
     constexpr uint32_t sbo = (KC == 64) ? 1024u : 512u;       // 8 rows x row bytes
     const uint64_t d0 = make_sdesc(smem_u32(smem), 16, sbo, layout);
@@ -94,12 +97,14 @@ __global__ void __launch_bounds__(192, 1)
           const uint64_t dwl = dwh + (w_bytes >> 4);
 #pragma unroll
           for (int k = 0; k < KC / 16; ++k) {  // K16 step = 32 bytes along the swizzled row
-            umma_f16_warp(tmem, dah + 2u * k, dwh + 2u * k, idesc, (g | i | k) != 0);
             if (p.split) {
-              umma_f16_warp(tmem, dal + 2u * k, dwh + 2u * k, idesc, 1);
-              umma_f16_warp(tmem, dah + 2u * k, dwl + 2u * k, idesc, 1);
+              umma_f16_warp(tmem, dah + 2u * k, dwh + 2u * k, idesc2, (g | i | k) != 0);
+              umma_f16_warp(tmem + (uint32_t)N, dal + 2u * k, dwh + 2u * k, idesc, 1);
+            } else {
+              umma_f16_warp(tmem, dah + 2u * k, dwh + 2u * k, idesc, (g | i | k) != 0);
             }
           }
+          (void)dwl;
         }
         umma_commit_warp(&empty[s]);
       }
@@ -118,8 +123,15 @@ __global__ void __launch_bounds__(192, 1)
     const float* ra = p.epi.rowadd ? p.epi.rowadd + (size_t)item * p.n_total + n0 : nullptr;
     for (int c0 = 0; c0 < N; c0 += 32) {
       float v[32];
-      if (ok) tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
-      else
+      if (ok) {
+        tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
+        if (p.split) {  // [0, N) holds hi*hi, [N, 2N) hi*lo + lo*hi
+          float u[32];
+          tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(N + c0), u);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] += u[i];
+        }
+      } else
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = 0.f;
       // every epilogue warp reaches the chunk's named barriers, whether or not the wait succeeded
