@@ -172,6 +172,11 @@ def run_reference(args, rank):
     print(json.dumps(line))
 
 
+# dram__bytes_read.sum + dram__bytes_write.sum of one launch of the roofline kernel, from the ncu
+# capture summarised in profiles/ (None until captured)
+TRAFFIC_BYTES = None
+
+
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -286,10 +291,14 @@ def main():
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": ms_e2e},
             "gpu_launches": launches,
-            "roofline": {"bound": "tensor", "kernel": "tc_conv_kernel<64> forward conv1 (k=11) of stage 1, bf16x3",
+            "roofline": {"bound": "tensor",
+                         "kernel": "tc_conv2_kernel (persistent conv) forward conv1, k=11 dil=1, stage 1 "
+                                   "(51200 rows x 128 ch), bf16x3 = 2 MMAs per K16 step",
                          "achieved": achieved, "peak": pk, "unit": "TFLOP/s", "frac": achieved / pk,
-                         "peak_source": pk_src, "traffic": None, "launch_ms": kms,
-                         "algorithmic_flops_per_launch": kflops},
+                         "peak_source": pk_src, "traffic": TRAFFIC_BYTES, "launch_ms": kms,
+                         "algorithmic_flops_per_launch": kflops,
+                         "issued_tensor_tflops": achieved * 3.0,
+                         "note": "achieved counts algorithmic FLOPs; the bf16x3 forward issues 3x that tensor work"},
             "step_roofline": {"algorithmic_tflops": step_tflops, "peak_sustained": pk_sus,
                               "frac": step_tflops / pk_sus, "flops_per_step": step_flops},
             "clocks": clk.summary(),

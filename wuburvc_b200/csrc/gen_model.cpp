@@ -814,8 +814,10 @@ bool gen_adamw(Gen& m, float grad_scale, int bump_noise) {
 
 void gen_free(Gen& m) {
   if (m.stream) cudaStreamSynchronize(m.stream);
-  comm_destroy(m);
+  // the captured step holds the NCCL all-reduces: release it before the communicator
   if (m.graph) cudaGraphExecDestroy(m.graph);
+  m.graph = nullptr;
+  comm_destroy(m);
   for (void* p : m.allocs) cudaFree(p);
   m.allocs.clear();
   if (m.stream) cudaStreamDestroy(m.stream);
