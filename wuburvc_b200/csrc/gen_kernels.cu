@@ -59,54 +59,6 @@ __device__ __forceinline__ size_t wrow_addr(int i, int r, int rows, int cols, in
   return is_convT ? ((size_t)t * cols + c) * rows + r : ((size_t)t * rows + r) * cols + c;
 }
 
-__global__ void prep_weight_kernel(const float* __restrict__ v, const float* __restrict__ g, int rows, int cols, int k,
-                                   int is_convT, int stride, bf16* __restrict__ fwd_hi, bf16* __restrict__ fwd_lo,
-                                   bf16* __restrict__ dg, float* __restrict__ norm) {
-  __shared__ float sh[32];
-  const int r = blockIdx.x;
-  const int per = cols * k;
-  float scale = 1.f;
-  if (g) {
-    float s = 0.f;
-    for (int i = threadIdx.x; i < per; i += blockDim.x) {
-      const float x = v[wrow_addr(i, r, rows, cols, is_convT)];
-      s += x * x;
-    }
-    s = block_sum(s, sh);
-    const float n = sqrtf(s);
-    scale = g[r] / n;
-    if (threadIdx.x == 0 && norm) norm[r] = n;
-  }
-  for (int i = threadIdx.x; i < per; i += blockDim.x) {
-    const int t = i / cols, c = i - t * cols;
-    const float w = v[wrow_addr(i, r, rows, cols, is_convT)] * scale;
-    bf16 hi, lo;
-    split_bf16(w, hi, lo);
-    if (!is_convT) {
-      // r = out channel, c = in channel
-      const size_t f = ((size_t)t * rows + r) * cols + c;
-      fwd_hi[f] = hi;
-      fwd_lo[f] = lo;
-      dg[((size_t)(k - 1 - t) * cols + c) * rows + r] = hi;
-    } else {
-      // r = in channel, c = out channel
-      const int ph = t % stride, m = t / stride;
-      int n = 0;
-      for (int q = 0; q < ph; ++q) n += (k - q + stride - 1) / stride;
-      n += m;
-      const size_t f = ((size_t)n * cols + c) * rows + r;
-      fwd_hi[f] = hi;
-      fwd_lo[f] = lo;
-      dg[((size_t)t * rows + r) * cols + c] = hi;
-    }
-  }
-}
-
-void prep_weight(const float* v, const float* g, int rows, int cols, int k, int is_convT, int stride, bf16* fwd_hi,
-                 bf16* fwd_lo, bf16* dg, float* norm, cudaStream_t st) {
-  prep_weight_kernel<<<rows, 256, 0, st>>>(v, g, rows, cols, k, is_convT, stride, fwd_hi, fwd_lo, dg, norm);
-}
-
 __global__ void prep_weights_batched_kernel(const PrepDesc* __restrict__ descs, int ndesc) {
   __shared__ float sh[32];
   __shared__ int di;
@@ -122,7 +74,7 @@ __global__ void prep_weights_batched_kernel(const PrepDesc* __restrict__ descs, 
   __syncthreads();
   const PrepDesc d = descs[di];
   const int r = blockIdx.x - d.first;
-  const int rows = d.rows, cols = d.cols, k = d.k, is_convT = d.is_convT, stride = d.stride;
+  const int rows = d.rows, cols = d.cols, k = d.k, is_convT = d.is_convT;
   const int per = cols * k;
   float scale = 1.f;
   if (d.g) {
@@ -136,27 +88,58 @@ __global__ void prep_weights_batched_kernel(const PrepDesc* __restrict__ descs, 
     scale = d.g[r] / n;
     if (threadIdx.x == 0 && d.norm) d.norm[r] = n;
   }
+  // only row-contiguous layouts here (coalesced); the transposed ones come from prep_transpose
   for (int i = threadIdx.x; i < per; i += blockDim.x) {
     const int t = i / cols, c = i - t * cols;
     const float w = d.v[wrow_addr(i, r, rows, cols, is_convT)] * scale;
     bf16 hi, lo;
     split_bf16(w, hi, lo);
+    const size_t f = ((size_t)t * rows + r) * cols + c;  // [t][r][c]
     if (!is_convT) {
-      const size_t f = ((size_t)t * rows + r) * cols + c;
-      d.fwd_hi[f] = hi;
+      d.fwd_hi[f] = hi;  // conv: r = out channel, c = in channel
       d.fwd_lo[f] = lo;
-      d.dg[((size_t)(k - 1 - t) * cols + c) * rows + r] = hi;
     } else {
-      const int ph = t % stride, m = t / stride;
-      int n = 0;
-      for (int q = 0; q < ph; ++q) n += (k - q + stride - 1) / stride;
-      n += m;
-      const size_t f = ((size_t)n * cols + c) * rows + r;
-      d.fwd_hi[f] = hi;
-      d.fwd_lo[f] = lo;
-      d.dg[((size_t)t * rows + r) * cols + c] = hi;
+      d.dg[f] = hi;      // convT: r = in channel, c = out channel
+      d.lo_tmp[f] = lo;
     }
   }
+}
+
+// Batched bf16 [R][C] -> [C][R] transposes through 32 x 32 shared-memory tiles.
+__global__ void __launch_bounds__(256) prep_transpose_kernel(const TransDesc* __restrict__ descs, int ndesc) {
+  __shared__ unsigned short tile[32][33];
+  __shared__ int di;
+  if (threadIdx.x == 0 && threadIdx.y == 0) {
+    int lo = 0, hi = ndesc - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (descs[mid].first <= (int)blockIdx.x) lo = mid;
+      else hi = mid - 1;
+    }
+    di = lo;
+  }
+  __syncthreads();
+  const TransDesc d = descs[di];
+  const int b = blockIdx.x - d.first;
+  const int tc = (d.C + 31) / 32;
+  const int r0 = (b / tc) * 32, c0 = (b % tc) * 32;
+  const unsigned short* src = reinterpret_cast<const unsigned short*>(d.src);
+  unsigned short* dst = reinterpret_cast<unsigned short*>(d.dst);
+  for (int y = threadIdx.y; y < 32; y += 8) {
+    const int r = r0 + y, c = c0 + threadIdx.x;
+    if (r < d.R && c < d.C) tile[y][threadIdx.x] = src[(size_t)r * d.C + c];
+  }
+  __syncthreads();
+  for (int y = threadIdx.y; y < 32; y += 8) {
+    const int c = c0 + y, r = r0 + threadIdx.x;
+    if (r < d.R && c < d.C) dst[(size_t)c * d.R + r] = tile[threadIdx.x][y];
+  }
+}
+
+int prep_transpose_blocks(int R, int C) { return ((R + 31) / 32) * ((C + 31) / 32); }
+
+void prep_transpose_batched(const TransDesc* descs, int ndesc, int total_blocks, cudaStream_t st) {
+  if (ndesc > 0 && total_blocks > 0) prep_transpose_kernel<<<total_blocks, dim3(32, 8), 0, st>>>(descs, ndesc);
 }
 
 void prep_weights_batched(const PrepDesc* descs, int ndesc, int total_rows, cudaStream_t st) {

@@ -9,19 +9,28 @@ namespace wb {
 //   conv  (param [C_out][C_in][k]):  fwd [k][C_out][C_in] hi/lo,  dgrad [k][C_in][C_out] (taps flipped)
 //   convT (param [C_in][C_out][k]):  fwd [k][C_out][C_in] hi/lo in phase order, dgrad [k][C_in][C_out]
 // `norm` receives ||v|| per dim-0 row under weight norm.
-void prep_weight(const float* v, const float* g, int rows, int cols, int k, int is_convT, int stride,
-                 bf16* fwd_hi, bf16* fwd_lo, bf16* dg, float* norm, cudaStream_t st);
-
 // All weight preparations of a step in one launch: block b handles dim-0 row (b - first[i]) of
 // descriptor i, where first[i] <= b < first[i] + rows.
+// Writes only the row-contiguous layouts [k][rows][cols] (conv: fwd_hi / fwd_lo; ConvTranspose: dg
+// and lo_tmp); the transposed layouts follow from prep_transpose_batched.
 struct PrepDesc {
   const float* v;
   const float* g;
-  bf16 *fwd_hi, *fwd_lo, *dg;
+  bf16 *fwd_hi, *fwd_lo, *dg, *lo_tmp;
   float* norm;
   int rows, cols, k, is_convT, stride, first;
 };
 void prep_weights_batched(const PrepDesc* descs, int ndesc, int total_rows, cudaStream_t st);
+
+// bf16 dst[C][R] = src[R][C] for many (src, dst) pairs in one launch; descriptor i owns blocks
+// [first_i, first_i + prep_transpose_blocks(R_i, C_i)).
+struct TransDesc {
+  const bf16* src;
+  bf16* dst;
+  int R, C, first;
+};
+int prep_transpose_blocks(int R, int C);
+void prep_transpose_batched(const TransDesc* descs, int ndesc, int total_blocks, cudaStream_t st);
 
 // Weight-norm backward of many tensors in one launch (block = one dim-0 row of one tensor).
 struct WnDesc {

@@ -85,6 +85,7 @@ bool make_weights(Gen& m, ConvWeights& w, const std::string& base, bool resblock
   w.stride = stride;
   const size_t n = (size_t)p.n;
   if (!dalloc(m, &w.fwd_hi, n) || !dalloc(m, &w.fwd_lo, n) || !dalloc(m, &w.dg, n)) return false;
+  if (convT && !dalloc(m, &w.lo_tmp, n)) return false;
   if (wn) {
     if (!dalloc(m, &w.norm, (size_t)w.rows) || !dalloc(m, &w.dW, n)) return false;
   } else {
@@ -221,11 +222,6 @@ bool run_pre_wgrad(Gen& m) {
   if (w.pg >= 0)
     wn_backward(w.dW, m.P(w.pv), m.P(w.pg), w.norm, w.rows, w.cols, w.k, w.convT, m.G(w.pv), m.G(w.pg), m.stream);
   return true;
-}
-
-void prep(Gen& m, const ConvWeights& w) {
-  prep_weight(m.P(w.pv), w.pg >= 0 ? m.P(w.pg) : nullptr, w.rows, w.cols, w.k, w.convT, w.stride, w.fwd_hi,
-              w.fwd_lo, w.dg, w.norm, m.stream);
 }
 
 
@@ -628,6 +624,7 @@ bool gen_setup(Gen& m) {
       p.fwd_hi = w.fwd_hi;
       p.fwd_lo = w.fwd_lo;
       p.dg = w.dg;
+      p.lo_tmp = w.lo_tmp;
       p.norm = w.norm;
       p.rows = w.rows;
       p.cols = w.cols;
@@ -651,6 +648,35 @@ bool gen_setup(Gen& m) {
     m.prep_rows = first;
     if (!dalloc(m, &m.prep_descs, d.size())) return false;
     CK(cudaMemcpy(m.prep_descs, d.data(), d.size() * sizeof(PrepDesc), cudaMemcpyHostToDevice));
+    // transposed layouts, one [rows][cols] -> [cols][rows] per tap:
+    //   conv:  dg[k-1-t] = fwd_hi[t]^T;  ConvTranspose: fwd_hi[n(t)] = dg[t]^T, fwd_lo[n(t)] = lo_tmp[t]^T
+    //   with n(t) the tap's place in the polyphase order (phase t % stride, then t / stride)
+    std::vector<TransDesc> td;
+    int tb = 0;
+    for (const PrepDesc& p : d) {
+      const size_t plane = (size_t)p.rows * p.cols;
+      for (int t = 0; t < p.k; ++t) {
+        auto push = [&](const bf16* src, bf16* dst) {
+          TransDesc x{src, dst, p.rows, p.cols, tb};
+          tb += prep_transpose_blocks(p.rows, p.cols);
+          td.push_back(x);
+        };
+        if (!p.is_convT) {
+          push(p.fwd_hi + t * plane, p.dg + (size_t)(p.k - 1 - t) * plane);
+        } else {
+          const int ph = t % p.stride, mm = t / p.stride;
+          int n = 0;
+          for (int q = 0; q < ph; ++q) n += (p.k - q + p.stride - 1) / p.stride;
+          n += mm;
+          push(p.dg + t * plane, p.fwd_hi + (size_t)n * plane);
+          push(p.lo_tmp + t * plane, p.fwd_lo + (size_t)n * plane);
+        }
+      }
+    }
+    m.n_trans = (int)td.size();
+    m.trans_blocks = tb;
+    if (!dalloc(m, &m.trans_descs, td.size())) return false;
+    CK(cudaMemcpy(m.trans_descs, td.data(), td.size() * sizeof(TransDesc), cudaMemcpyHostToDevice));
   }
   return true;
 }
@@ -665,6 +691,7 @@ bool gen_forward(Gen& m) {
   set_reduce_scratch(m.red_scratch, m.red_scratch_n);
   // GEMM weights for this step (weight norm + bf16 hi/lo + transposed layouts), one launch
   prep_weights_batched(m.prep_descs, m.n_prep, m.prep_rows, st);
+  prep_transpose_batched(m.trans_descs, m.n_trans, m.trans_blocks, st);
   pack_z(m.z, m.B, c.in_channels, m.F, m.z_hi, m.z_lo, st);
   if (c.nsf) {
     NsfArgs a{};
