@@ -45,6 +45,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--only-device", action="store_true",
                     help="time only the device-resident steps (for profiler launch lists)")
+    ap.add_argument("--kernel", default=None, metavar="WHICH,STAGE",
+                    help="time one convolution of the step alone (kernel_bench: which 0 f1, 1 d1, 2 g1, 3 f2, "
+                         "4 d2) inside an NVTX range 'kb<which><stage>' and exit")
     return ap.parse_args()
 
 
@@ -204,6 +207,18 @@ def main():
     z, f0, g, dldy = make_inputs(cfg, B, F, seed=1234 + rank)
     gen.upload(z, f0, g, None, dldy)
     stream = torch.cuda.ExternalStream(gen.stream, device=local)
+    if args.kernel:  # one convolution alone (for a profiler capture)
+        which, stage = (int(x) for x in args.kernel.split(","))
+        gen.forward(0)
+        gen.backward()
+        gen.sync()
+        torch.cuda.nvtx.range_push(f"kb{which}{stage}")
+        kms, kflops = gen.kernel_bench(which, stage, iters=5)
+        torch.cuda.nvtx.range_pop()
+        print(json.dumps({"kernel": {"which": which, "stage": stage, "batch": B, "launch_ms": kms,
+                                     "algorithmic_tflops": kflops / (kms / 1000.0) / 1e12}}))
+        gen.close()
+        return
 
     def barrier():
         if world > 1:
