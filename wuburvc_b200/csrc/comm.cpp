@@ -117,13 +117,13 @@ namespace wb {
 
 int comm_bucket_count(Gen& m) { return m.comm ? (int)m.comm->buckets.size() : 0; }
 
-// Called on the main stream after bucket `b`'s gradients are final: the comm stream waits for
+// Called once bucket `b`'s gradients are final on stream `producer`: the comm stream waits for
 // them and all-reduces them in place.
-int comm_bucket_ready(Gen& m, int b) {
+int comm_bucket_ready(Gen& m, int b, cudaStream_t producer) {
   Comm* c = m.comm;
   if (!c || c->world <= 1) return 0;
   NcclApi& api = nccl();
-  if (cudaEventRecord(c->ready[b], m.stream) != cudaSuccess) return WUBU_B200_ERR_CUDA;
+  if (cudaEventRecord(c->ready[b], producer) != cudaSuccess) return WUBU_B200_ERR_CUDA;
   if (cudaStreamWaitEvent(c->cs, c->ready[b], 0) != cudaSuccess) return WUBU_B200_ERR_CUDA;
   const auto& r = c->buckets[b];
   if (r.second <= r.first) return 0;  // empty bucket: every rank skips it alike
@@ -149,7 +149,7 @@ int comm_world(Gen& m) { return m.comm ? m.comm->world : 1; }
 
 int comm_allreduce_grads(Gen& m) {
   for (int b = 0; b < comm_bucket_count(m); ++b) {
-    const int rc = comm_bucket_ready(m, b);
+    const int rc = comm_bucket_ready(m, b, m.stream);
     if (rc) return rc;
   }
   return comm_join(m);

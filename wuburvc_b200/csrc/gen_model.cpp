@@ -16,7 +16,7 @@
 namespace wb {
 
 // comm.cpp (no-ops without a communicator)
-int comm_bucket_ready(Gen& m, int bucket);
+int comm_bucket_ready(Gen& m, int bucket, cudaStream_t producer);
 int comm_join(Gen& m);
 void comm_destroy(Gen& m);
 
@@ -203,12 +203,28 @@ bool upload_wn_table(Gen& m, std::vector<WnDesc>& v, WnDesc** dev, int* n, int* 
 }
 
 // split-K partials into the job's own buffer; the batched reductions follow the group's last job
+// fork: the side stream waits for everything enqueued on the main stream so far; join: the reverse
+bool fork_side(Gen& m) {
+  const cudaEvent_t e = m.evs[(size_t)(m.ev_next++) % m.evs.size()];
+  CK(cudaEventRecord(e, m.stream));
+  CK(cudaStreamWaitEvent(m.side, e, 0));
+  return true;
+}
+
+bool join_side(Gen& m) {
+  const cudaEvent_t e = m.evs[(size_t)(m.ev_next++) % m.evs.size()];
+  CK(cudaEventRecord(e, m.side));
+  CK(cudaStreamWaitEvent(m.stream, e, 0));
+  return true;
+}
+
 bool run_wgrad(Gen& m, StageBufs& s, const WgradJob& j) {
   CK(j.L.run(m.stream));
-  if (j.flush >= 0) {
+  if (j.flush >= 0) {  // the group's reductions overlap the next convolutions
     const WgradBatch& b = s.wg_batches[j.flush];
-    reduce_batched(b.wg_d, b.wg_n, b.wg_blocks, m.stream);
-    wn_backward_batched(b.wn_d, b.wn_n, b.wn_rows, m.stream);
+    if (!fork_side(m)) return false;
+    reduce_batched(b.wg_d, b.wg_n, b.wg_blocks, m.side);
+    wn_backward_batched(b.wn_d, b.wn_n, b.wn_rows, m.side);
   }
   return true;
 }
@@ -244,6 +260,9 @@ bool gen_setup(Gen& m) {
   const int B = m.B;
   CK(cudaSetDevice(m.opt.device));
   CK(cudaStreamCreateWithFlags(&m.stream, cudaStreamNonBlocking));
+  CK(cudaStreamCreateWithFlags(&m.side, cudaStreamNonBlocking));
+  m.evs.resize(64);
+  for (auto& e : m.evs) CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
   if (!dalloc(m, &m.err, 1) || !dalloc(m, &m.state, 1)) return false;
 
   m.table = build_param_table(c);
@@ -760,6 +779,7 @@ bool gen_forward(Gen& m) {
 // backward
 // =============================================================================================
 bool gen_backward(Gen& m) {
+  m.ev_next = 0;
   const WubuB200GenConfig& c = m.cfg;
   const bool snake = c.activation == 1;
   cudaStream_t st = m.stream;
@@ -811,13 +831,17 @@ bool gen_backward(Gen& m) {
     }
     CK(s.up_dg.run(st));
     if (!run_wgrad(m, s, s.up_wg)) return false;
-    reduce_batched(s.cs_d, s.cs_n, s.cs_blocks, st);  // every bias / Snake-alpha gradient of the stage
+    // every bias / Snake-alpha gradient of the stage, on the side stream after the stage's kernels
+    if (!fork_side(m)) return false;
+    reduce_batched(s.cs_d, s.cs_n, s.cs_blocks, m.side);
     if (c.nsf) {  // the noise conv's bias is added where the ups bias is: same gradient
       const int ub = m.pidx("dec.ups." + std::to_string(L) + ".bias");
       const int nb = m.pidx("dec.noise_convs." + std::to_string(L) + ".bias");
-      CK(cudaMemcpyAsync(m.G(nb), m.G(ub), sizeof(float) * s.C, cudaMemcpyDeviceToDevice, st));
+      CK(cudaMemcpyAsync(m.G(nb), m.G(ub), sizeof(float) * s.C, cudaMemcpyDeviceToDevice, m.side));
     }
-    if (comm_bucket_ready(m, 3 - L)) return false;  // this stage's gradients are final
+    // this stage's gradients are final once the side stream gets here (noise-conv weight gradient
+    // and everything before the fork are on the main stream, which the side stream waited for)
+    if (comm_bucket_ready(m, 3 - L, m.side)) return false;
   }
   // conv_pre, cond, source
   if (!run_pre_wgrad(m)) return false;
@@ -828,8 +852,8 @@ bool gen_backward(Gen& m) {
   if (c.nsf)
     nsf_backward(m.d_har, m.har, m.sw, B * m.T, m.dim, m.nsf_part, m.nsf_parts,
                  m.G(m.pidx("dec.m_source.l_linear.weight")), m.G(m.pidx("dec.m_source.l_linear.bias")), st);
-  if (comm_bucket_ready(m, 4) || comm_join(m)) return false;
-  return true;
+  if (comm_bucket_ready(m, 4, m.stream) || comm_join(m)) return false;
+  return join_side(m);  // AdamW (main stream) needs every reduction
 }
 
 bool gen_adamw(Gen& m, float grad_scale, int bump_noise) {
@@ -845,6 +869,13 @@ void gen_free(Gen& m) {
   if (m.graph) cudaGraphExecDestroy(m.graph);
   m.graph = nullptr;
   comm_destroy(m);
+  if (m.side) {
+    cudaStreamSynchronize(m.side);
+    cudaStreamDestroy(m.side);
+    m.side = nullptr;
+  }
+  for (auto e : m.evs) cudaEventDestroy(e);
+  m.evs.clear();
   for (void* p : m.allocs) cudaFree(p);
   m.allocs.clear();
   if (m.stream) cudaStreamDestroy(m.stream);

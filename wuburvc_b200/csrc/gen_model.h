@@ -96,6 +96,11 @@ struct Gen {
   int B = 0, F = 0, T = 0, dim = 0, upp = 0;
   int nk = 3, nd = 3;
   cudaStream_t stream = nullptr;
+  // the backward's reductions (split-K sums, weight-norm backward, bias / alpha column sums) run on
+  // a second stream, overlapping the next convolutions; `evs` is a pool for the fork / join edges
+  cudaStream_t side = nullptr;
+  std::vector<cudaEvent_t> evs;
+  int ev_next = 0;
   std::vector<void*> allocs;
   int* err = nullptr;
 
