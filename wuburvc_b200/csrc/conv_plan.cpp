@@ -5,6 +5,7 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -135,29 +136,6 @@ bool plan_conv(ConvLaunch& L, const ConvGeom& g, const void* x_hi, const void* x
   return finish_fwd(L, g.B, g.C_in, g.C_out, split, 1, err);
 }
 
-// No-swizzle core-matrix view of a [B][T][C] bf16 tensor: dimensions (8 channels, T, C/8 channel
-// groups, B) with the channel group outermost in the box, so one (8, R, KC/8, 1) box lands in shared
-// memory as KC/8 core-matrix columns of R rows x 16 bytes each (column j at j * R * 16 bytes): the
-// K-major no-swizzle UMMA layout of a KC-channel halo tile, in a single TMA instruction.
-static bool make_map_bf16_cm(CUtensorMap* m, const void* base, uint64_t T, uint64_t C, uint64_t B, uint32_t R,
-                             uint32_t kc) {
-  auto fn = encode_fn();
-  if (!fn) return false;
-  cuuint64_t dims[4] = {8, T, C / 8, B};
-  cuuint64_t strides[3] = {C * 2, 16, T * C * 2};
-  cuuint32_t box[4] = {8, R, kc / 8, 1};
-  cuuint32_t es[4] = {1, 1, 1, 1};
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, es,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) {
-    fprintf(stderr, "wuburvc_b200: cuTensorMapEncodeTiled (core-matrix) failed (%d) T %llu C %llu B %llu R %u\n",
-            (int)r, (unsigned long long)T, (unsigned long long)C, (unsigned long long)B, R);
-    return false;
-  }
-  return true;
-}
-
 static int sm_count() {
   static int n = 0;
   if (!n) {
@@ -175,9 +153,8 @@ bool plan_conv2(Conv2Launch& L, const ConvGeom& g, const void* x_hi, const void*
   TcConv2Params& p = L.p;
   if (g.T_in != g.T_out || g.C_out > 256 || g.C_out % 32 || g.C_in % 32 || g.k > kMaxTaps2) return false;
   const int span = g.dil * (g.k - 1);
-  // rows of the halo tile, rounded up to 8 so every core-matrix column (R x 16 B) starts on the
-  // 128-byte boundary a TMA shared-memory destination requires
-  const int R = (128 + span + 7) / 8 * 8;
+  // rows of the halo tile, a multiple of 16 so each tile is a whole number of 1 KB swizzle atoms
+  const int R = (128 + span + 15) / 16 * 16;
   if (R > 256) return false;
   p.ntaps = g.k;
   p.dil = g.dil;
@@ -241,8 +218,9 @@ bool plan_conv2(Conv2Launch& L, const ConvGeom& g, const void* x_hi, const void*
   // two accumulators (double buffering) of n columns, 2n under the two-MMA bf16x3 split
   p.tmem_cols = pow2_cols(2 * p.n * (split ? 2 : 1));
   if (p.tmem_cols > 512) return false;
-  if (!make_map_bf16_cm(&L.maps.a_hi, x_hi, g.T_in, g.C_in, g.B, R, kc)) return false;
-  if (split && !make_map_bf16_cm(&L.maps.a_lo, x_lo, g.T_in, g.C_in, g.B, R, kc)) return false;
+  const uint64_t xs = (uint64_t)g.C_in * 2, xt = xs * g.T_in;
+  if (!make_map_bf16_3d(&L.maps.a_hi, x_hi, g.C_in, g.T_in, g.B, xs, xt, kc, R, 1)) return false;
+  if (split && !make_map_bf16_3d(&L.maps.a_lo, x_lo, g.C_in, g.T_in, g.B, xs, xt, kc, R, 1)) return false;
   const uint64_t wr = (uint64_t)g.C_in * 2, wt = wr * g.C_out;
   if (!make_map_bf16_3d(&L.maps.w_hi, w_hi, g.C_in, g.C_out, g.k, wr, wt, kc, p.n, 1)) return false;
   if (split && !make_map_bf16_3d(&L.maps.w_lo, w_lo, g.C_in, g.C_out, g.k, wr, wt, kc, p.n, 1)) return false;
@@ -411,10 +389,78 @@ size_t wgrad_part_floats(const WgradLaunch& L) {
   return (size_t)L.splits * L.p.n_mtiles * 128 * L.p.n_total;
 }
 
+// Halo-mode weight gradient (C_out % 128 == 0): see TcWgParams.  tg = taps per CTA so that tg
+// accumulators of n_in columns fill TMEM; K blocks of 128 time rows; the halo tile of 128 channels x
+// R rows arrives as one 4-D box (8 ch, R rows, 16 groups, 1).
+static bool plan_wgrad_halo(WgradLaunch& L, const ConvGeom& g, const void* dy, const void* x, float* part, size_t cap,
+                            int target_ctas, int* err) {
+  TcWgParams& p = L.p;
+  int n_tile = std::min(g.C_in, 256);
+  while (g.C_in % n_tile) n_tile -= 16;
+  if (n_tile % 64) return false;
+  const int tg = std::min(4, 512 / n_tile);
+  const int kr = 128;  // K block rows; the halo kernel is compiled for 128 (kHaloKR)
+  const int R = (kr + (tg - 1) * g.dil + 7) / 8 * 8;
+  if (R > 256) return false;
+  p.halo = 1;
+  p.tg = tg;
+  p.ntaps = g.k;
+  p.dil = g.dil;
+  p.pad = g.pad;
+  p.oc_chunks = g.C_out / 128;
+  p.halo_rows = R;
+  p.n_in = n_tile;
+  p.n_total = g.C_in;
+  p.n_atoms = n_tile / 64;
+  p.c_out = g.C_out;
+  p.t_rows = g.T_in;
+  p.kb_rows = kr;
+  p.kb_group = 1;
+  p.kblocks_per_item = (g.T_in + kr - 1) / kr;
+  p.total_kblocks = g.B * p.kblocks_per_item;
+  p.n_mtiles = g.k * g.C_out / 128;  // partial rows: tap * C_out + oc
+  const int tap_groups = (g.k + tg - 1) / tg;
+  const int n_ntiles = g.C_in / n_tile;
+  const int base = tap_groups * p.oc_chunks * n_ntiles;
+  int splits = std::max(1, std::min(p.total_kblocks, (target_ctas + base - 1) / base));
+  p.kb_per_split = (p.total_kblocks + splits - 1) / splits;
+  splits = (p.total_kblocks + p.kb_per_split - 1) / p.kb_per_split;
+  const size_t stage = (size_t)128 * R * 2 + (size_t)n_tile * kr * 2;
+  const size_t room = kSmemBudget - 1024 - 256;
+  p.stages = (int)std::min<size_t>(3, room / stage);
+  if (p.stages < 2) return false;
+  L.smem = p.stages * stage + 1024 + 256;
+  p.tmem_cols = pow2_cols(tg * n_tile);
+  if (p.tmem_cols > 512) return false;
+  p.err = err;
+  p.part = part;
+  L.splits = splits;
+  L.grid = dim3(tap_groups * p.oc_chunks, splits, n_ntiles);
+  if ((size_t)splits * p.n_mtiles * 128 * g.C_in > cap) return false;
+  L.row_tap.assign((size_t)p.n_mtiles * 128, -1);
+  L.row_oc.assign((size_t)p.n_mtiles * 128, 0);
+  for (int r = 0; r < p.n_mtiles * 128; ++r) {
+    L.row_tap[r] = r / g.C_out;
+    L.row_oc[r] = r % g.C_out;
+  }
+  // dOut halo: (C_out, T, B) with a 64-channel x R-row SW128 box (two per 128-channel chunk)
+  if (!make_map_bf16_3d(&L.maps.d[0], dy, g.C_out, g.T_out, g.B, (uint64_t)g.C_out * 2,
+                        (uint64_t)g.C_out * 2 * g.T_out, 64, R, 1))
+    return false;
+  return make_map_bf16_3d(&L.maps.x, x, g.C_in, g.T_in, g.B, (uint64_t)g.C_in * 2, (uint64_t)g.C_in * 2 * g.T_in,
+                          64, kr, 1);
+}
+
 bool plan_wgrad(WgradLaunch& L, const ConvGeom& g, const void* dy, const void* x, float* part, size_t cap,
                 int target_ctas, int* err) {
   memset(&L.p, 0, sizeof(L.p));
   memset(&L.maps, 0, sizeof(L.maps));
+  if (g.C_out % 128 == 0 && g.T_in == g.T_out && !getenv("WUBU_B200_WGRAD_ATOMS")) {
+    // a halo CTA carries tg taps' MMAs per K block: half the CTAs keep the split-K partials small
+    if (plan_wgrad_halo(L, g, dy, x, part, cap, std::max(1, target_ctas / 2), err)) return true;
+    memset(&L.p, 0, sizeof(L.p));
+    memset(&L.maps, 0, sizeof(L.maps));
+  }
   const int atom_m = std::min(g.C_out, 64);
   const int oc_chunks = g.C_out / atom_m;
   std::vector<int> am, ash, aoc, atap;

@@ -289,6 +289,134 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// ---------------------------------------------------------------------------------------------
+// tc_wgrad halo kernel (see TcWgParams): CTA = 128 output channels x tg taps x n_in input channels;
+// per K block of kb_rows time rows one dOut halo (two SW128 MN-major atoms of 64 channels x R rows)
+// and one activation tile (SW128 MN-major atoms of 64 channels); tap t's A operand starts
+// (tg - 1 - (t - tb)) * dil rows into the halo.
+// ---------------------------------------------------------------------------------------------
+constexpr int kHaloKR = 128;  // time rows per K block of the halo weight gradient
+
+__global__ void __launch_bounds__(192, 1)
+    tc_wgrad_halo_kernel(const __grid_constant__ TcWgMaps maps, const __grid_constant__ TcWgParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int oc0 = (blockIdx.x % p.oc_chunks) * 128;
+  const int tb = (blockIdx.x / p.oc_chunks) * p.tg;  // first tap of this CTA
+  const int nt = min(p.tg, p.ntaps - tb);
+  const int split = blockIdx.y;
+  const int nbase = blockIdx.z * p.n_in;
+  const int kb0 = split * p.kb_per_split;
+  const int kb1 = min(p.total_kblocks, kb0 + p.kb_per_split);
+  const int nkb = max(0, kb1 - kb0);
+  const int S = p.stages;
+  const int KR = kHaloKR, R = p.halo_rows, N = p.n_in;
+  const uint32_t a_bytes = 128u * (uint32_t)R * 2u;
+  const uint32_t atom_b_bytes = (uint32_t)KR * 64u * 2u;
+  const uint32_t b_bytes = (uint32_t)N * (uint32_t)KR * 2u;
+  const uint32_t stage_bytes = a_bytes + b_bytes;
+
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * stage_bytes);
+  uint64_t* empty = full + S;
+  uint64_t* accf = empty + S;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accf + 1);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    mbar_init(accf, 1);
+    fence_barrier_init();
+  }
+  if (warp == 5) tmem_alloc(tmem_slot, (uint32_t)p.tmem_cols);
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    // ---------------- TMA producer ----------------
+    bool ok = true;
+    int s = 0;
+    uint32_t ph = 0;
+    for (int i = 0; i < nkb; ++i) {
+      if (ok && i >= S) ok = mbar_wait_warp(&empty[s], ph ^ 1u, p.err, ERR_WAIT_EMPTY);
+      if (ok) {
+        const int kb = kb0 + i;
+        const int item = kb / p.kblocks_per_item;
+        const int t0 = (kb - item * p.kblocks_per_item) * KR;
+        uint8_t* st = smem + (size_t)s * stage_bytes;
+        mbar_expect_tx_warp(&full[s], stage_bytes);
+        // dOut rows t0 + pad - (tb + tg - 1) * dil ... : every tap's window, once (two 64-channel atoms)
+        const int hr = t0 + p.pad - (tb + p.tg - 1) * p.dil;
+        tma_load_3d_warp(st, &maps.d[0], &full[s], oc0, hr, item);
+        tma_load_3d_warp(st + a_bytes / 2, &maps.d[0], &full[s], oc0 + 64, hr, item);
+        for (int j = 0; j < p.n_atoms; ++j)
+          tma_load_3d_warp(st + a_bytes + j * atom_b_bytes, &maps.x, &full[s], nbase + j * 64, t0, item);
+      }
+      if (++s == S) { s = 0; ph ^= 1u; }
+    }
+  } else if (warp == 5) {
+    // ---------------- MMA issuer ----------------
+    const uint32_t idesc = make_idesc_bf16(128, N, 1, 1);
+    // A: SW128 MN-major atoms of 64 channels x R time rows (128-byte rows, next atom at LBO = R * 128 B,
+    // 8-row groups at SBO = 1024 B); the swizzle follows the absolute address, so a tap's operand is
+    // the atom started (tg - 1 - j) * dil rows in.  B: SW128 MN-major atoms of 64 channels x KR rows.
+    const uint64_t da0 = make_sdesc(smem_u32(smem), (uint32_t)R * 128u, 1024, 2);
+    const uint64_t db0 = make_sdesc(smem_u32(smem) + a_bytes, atom_b_bytes, 1024, 2);
+    bool ok = true;
+    int s = 0;
+    uint32_t ph = 0;
+    for (int i = 0; i < nkb; ++i) {
+      if (ok) ok = mbar_wait_warp(&full[s], ph, p.err, ERR_WAIT_FULL);
+      if (ok) {
+        const uint32_t sb = ((uint32_t)s * stage_bytes) >> 4;
+        // straight-line issue: K blocks are kHaloKR rows, at most 4 taps
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if (j < nt) {
+            const uint32_t toff = (uint32_t)((p.tg - 1 - j) * p.dil) * 8u;  // rows of 128 B, in 16-B units
+            const uint32_t d = tmem + (uint32_t)(j * N);
+#pragma unroll
+            for (int k = 0; k < kHaloKR / 16; ++k)  // K16 step = 16 rows = 2048 B
+              umma_f16_warp(d, da0 + sb + toff + (uint32_t)k * 128u, db0 + sb + (uint32_t)k * 128u, idesc,
+                            (i | k) != 0);
+          }
+        }
+        umma_commit_warp(&empty[s]);
+      }
+      if (++s == S) { s = 0; ph ^= 1u; }
+    }
+    if (ok) umma_commit_warp(accf);
+  } else {
+    // ---------------- epilogue: 4 warps, TMEM lane quadrant = warp; one partial row block per tap ----------------
+    const bool ok = nkb > 0 ? mbar_wait_warp(accf, 0, p.err, ERR_WAIT_ACC) : true;
+    tc_fence_after();
+    uint4* stage = reinterpret_cast<uint4*>(smem) + warp * 128;  // pipeline buffers are idle now
+    for (int j = 0; j < nt; ++j) {
+      const size_t row0 = (size_t)split * p.n_mtiles * 128 + (size_t)(tb + j) * p.c_out + oc0 + warp * 32;
+      char* dst = reinterpret_cast<char*>(p.part + row0 * p.n_total + nbase);
+      for (int c0 = 0; c0 < N; c0 += 32) {
+        float v[32];
+        if (nkb > 0 && ok) tmem_ld32(tmem + (uint32_t)(j * N) + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
+        else
+#pragma unroll
+          for (int q = 0; q < 32; ++q) v[q] = 0.f;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint32_t w[16];
+#pragma unroll
+          for (int q = 0; q < 16; ++q) w[q] = __float_as_uint(v[16 * h + q]);
+          stage_put64(stage, lane, w, dst + (size_t)(c0 + 16 * h) * 4, (size_t)p.n_total * 4, 32);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, (uint32_t)p.tmem_cols);
+  }
+}
+
 // launch wrappers (host).  The dynamic shared-memory limit is raised once, before any capture.
 void tc_conv2_set_smem_limit(int lim);  // tc_conv2.cu
 
@@ -305,6 +433,8 @@ static void raise_smem_limits() {
   e[0] = cudaFuncSetAttribute(tc_conv_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
   e[1] = cudaFuncSetAttribute(tc_conv_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
   e[2] = cudaFuncSetAttribute(tc_wgrad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+  const cudaError_t eh = cudaFuncSetAttribute(tc_wgrad_halo_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+  if (eh != cudaSuccess) fprintf(stderr, "wuburvc_b200: smem limit (wgrad halo): %s\n", cudaGetErrorString(eh));
   for (int i = 0; i < 3; ++i)
     if (e[i] != cudaSuccess) fprintf(stderr, "wuburvc_b200: smem limit %d: %s\n", i, cudaGetErrorString(e[i]));
   tc_conv2_set_smem_limit(lim);
@@ -325,7 +455,8 @@ cudaError_t launch_tc_conv(const TcMaps& maps, const TcConvParams& p, int kc, di
 
 cudaError_t launch_tc_wgrad(const TcWgMaps& maps, const TcWgParams& p, dim3 grid, size_t smem, cudaStream_t st) {
   raise_smem_limits();
-  tc_wgrad_kernel<<<grid, 192, smem, st>>>(maps, p);
+  if (p.halo) tc_wgrad_halo_kernel<<<grid, 192, smem, st>>>(maps, p);
+  else tc_wgrad_kernel<<<grid, 192, smem, st>>>(maps, p);
   return cudaGetLastError();
 }
 

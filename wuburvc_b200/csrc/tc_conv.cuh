@@ -76,14 +76,15 @@ struct TcConvParams {
 // ---------------------------------------------------------------------------------------------
 // persistent stride-1 conv kernel with halo reuse (tc_conv2)
 //   Each CTA loops over 128-row output tiles.  Per input-channel chunk it loads ONE halo tile
-//   (rows q0+sh_min .. q0+127+sh_max) in the no-swizzle core-matrix layout, so every tap's A operand
-//   is the same tile viewed at a 16-byte row offset; weight slices stream per (chunk, tap).  Two TMEM
-//   accumulators let the epilogue of one tile overlap the MMAs of the next.
+//   (rows q0+sh_min .. q0+127+sh_max) with one swizzled TMA box; the swizzle is a function of the
+//   absolute shared-memory address, so every tap's A operand is the same tile started tap*dil rows
+//   further on.  Weights are resident or stream in multi-tap stages.  Two TMEM accumulators let the
+//   epilogue of one tile overlap the MMAs of the next.
 // ---------------------------------------------------------------------------------------------
 constexpr int kMaxTaps2 = 16;
 
 struct TcConv2Maps {
-  CUtensorMap a_hi, a_lo;   // no-swizzle (C_in, T, B) views with an 8-channel x R-row box
+  CUtensorMap a_hi, a_lo;   // (C_in, T, B) views with a KC-channel x R-row box, 128B/64B swizzle
   CUtensorMap w_hi, w_lo;   // 3-D (C_in, C_out, taps), 128B/64B swizzle
 };
 
@@ -138,6 +139,11 @@ struct TcWgParams {
   short atom_tap[64][4];         // tap index (for the partial layout); -1 = unused atom
   float* part;                   // [split][n_mtiles*128][n_total] fp32 partials
   int* err;
+  // halo mode (C_out a multiple of 128, stride-1 conv): a CTA owns 128 output channels x `tg` taps,
+  // one TMEM accumulator per tap; the dOut halo of a K block (kb_rows + (tg-1)*dil rows) is loaded once
+  // (SW128 MN-major) and every tap reads it at its own row offset.
+  // blockIdx.x = tap_group * oc_chunks + oc chunk.  Partial rows stay tap * c_out + oc.
+  int halo, tg, ntaps, dil, pad, oc_chunks, halo_rows;
 };
 
 }  // namespace wb

@@ -19,7 +19,8 @@ constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
 
 // Shared memory: [A stages][W stages or resident W][barriers].  A stage = halo tile (hi[, lo]) of one
-// channel chunk; a weight stage holds `w_group` taps of one chunk, each tap hi[, lo] (N x KC, swizzled);
+// channel chunk (R x KC, swizzled); a weight stage holds `w_group` taps of one chunk, each tap hi[, lo]
+// (N x KC, swizzled);
 // resident weights hold every (chunk, tap) of the CTA's N tile in the same per-tap layout, loaded once.
 template <int KC, bool SPLIT, uint32_t F>
 __global__ void __launch_bounds__(kConv2Threads, 1)
@@ -101,11 +102,11 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
       for (int c = 0; c < nch; ++c) {
         if (ok && a_uses >= AS) ok = mbar_wait_warp(&a_empty[sa], aph ^ 1u, p.err, ERR_WAIT_EMPTY);
         if (ok) {
-          // one box per operand: KC/8 core-matrix columns of R rows (column j at j * R * 16 bytes)
+          // one swizzled box per operand: R rows of KC channels
           uint8_t* ad = a_base + (size_t)sa * a_stage;
           mbar_expect_tx_warp(&a_full[sa], nA * (uint32_t)p.halo_rows * KC * 2u);
-          tma_load_4d_warp(ad, &maps.a_hi, &a_full[sa], 0, q0 + p.halo_start, c * (KC / 8), item);
-          if (SPLIT) tma_load_4d_warp(ad + a_sub, &maps.a_lo, &a_full[sa], 0, q0 + p.halo_start, c * (KC / 8), item);
+          tma_load_3d_warp(ad, &maps.a_hi, &a_full[sa], c * KC, q0 + p.halo_start, item);
+          if (SPLIT) tma_load_3d_warp(ad + a_sub, &maps.a_lo, &a_full[sa], c * KC, q0 + p.halo_start, item);
         }
         ++a_uses;
         if (++sa == AS) { sa = 0; aph ^= 1u; }
@@ -136,12 +137,14 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
     const uint32_t idesc2 = make_idesc_bf16(128, 2 * N, 0, 0);
     constexpr uint32_t wlayout = (KC == 64) ? 2u : 4u;
     constexpr uint32_t wsbo = (KC == 64) ? 1024u : 512u;
-    const uint32_t a_lbo = (uint32_t)p.halo_rows * 16u;  // stride between 8-channel core-matrix columns
+    // A: the halo tile in the swizzled K-major layout TMA writes (rows of KC channels, 8-row swizzle
+    // atoms).  The swizzle is a function of the absolute shared-memory address, so a tap's operand is
+    // the same tile started tap*dil rows further on (measured exact for any start row).
     // descriptors are built once; a tap / k-step / stage moves the 14-bit start-address field
-    const uint64_t da0 = make_sdesc(smem_u32(a_base), a_lbo, 128, 0);
+    const uint64_t da0 = make_sdesc(smem_u32(a_base), 16, wsbo, wlayout);
     const uint64_t dw0 = make_sdesc(smem_u32(w_base), 16, wsbo, wlayout);
-    const uint32_t tap_step = (uint32_t)dil;             // 16-byte units per tap (dil rows)
-    const uint32_t k_step_a = (2u * a_lbo) >> 4;          // two core-matrix columns
+    const uint32_t tap_step = (uint32_t)dil * (KC * 2u / 16u);  // 16-byte units per tap (dil rows)
+    const uint32_t k_step_a = 2u;                                 // K16 step = 32 bytes along the row
     bool ok = true;
     if (resident) ok = mbar_wait_warp(&w_full[0], 0, p.err, ERR_WAIT_FULL);
     int sa = 0, sw = 0, t_it = 0;
