@@ -398,7 +398,7 @@ static bool plan_wgrad_halo(WgradLaunch& L, const ConvGeom& g, const void* dy, c
   int n_tile = std::min(g.C_in, 256);
   while (g.C_in % n_tile) n_tile -= 16;
   if (n_tile % 64) return false;
-  const int tg = std::min(4, 512 / n_tile);
+  const int tg = std::min(2, 512 / n_tile);  // 2 taps per CTA: more CTAs per split, smaller partials
   const int kr = 128;  // K block rows; the halo kernel is compiled for 128 (kHaloKR)
   const int R = (kr + (tg - 1) * g.dil + 7) / 8 * 8;
   if (R > 256) return false;
