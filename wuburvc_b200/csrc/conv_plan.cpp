@@ -389,9 +389,9 @@ size_t wgrad_part_floats(const WgradLaunch& L) {
   return (size_t)L.splits * L.p.n_mtiles * 128 * L.p.n_total;
 }
 
-// Halo-mode weight gradient (C_out % 128 == 0): see TcWgParams.  tg = taps per CTA so that tg
-// accumulators of n_in columns fill TMEM; K blocks of 128 time rows; the halo tile of 128 channels x
-// R rows arrives as one 4-D box (8 ch, R rows, 16 groups, 1).
+// Halo-mode weight gradient (C_out % 128 == 0): see TcWgParams.  tg = 2 taps per CTA (at most
+// 512 / n_in accumulator columns); K blocks of 128 time rows; the halo tile of 128 channels x
+// R rows arrives as two SW128 boxes of 64 channels.
 static bool plan_wgrad_halo(WgradLaunch& L, const ConvGeom& g, const void* dy, const void* x, float* part, size_t cap,
                             int target_ctas, int* err) {
   TcWgParams& p = L.p;
