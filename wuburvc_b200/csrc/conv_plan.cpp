@@ -35,7 +35,7 @@ int pow2_cols(int n) {
 constexpr size_t kSmemBudget = 220 * 1024;
 // the persistent conv keeps ~24 KB of static shared memory (epilogue vectors, column sums, the
 // epilogue warps' store staging)
-constexpr size_t kSmemBudget2 = 200 * 1024;
+constexpr size_t kSmemBudget2 = 202 * 1024;  // dynamic <= budget - 512, plus 24 KB static <= 227 KB
 
 }  // namespace
 
