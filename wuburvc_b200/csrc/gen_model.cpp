@@ -567,12 +567,12 @@ bool gen_setup(Gen& m) {
   // ---- batched per-stage reductions ----
   for (int L = 0; L < 4; ++L) {
     StageBufs& s = m.sg[L];
-    // the stacks' input-gradient column sums side by side: the ups bias sums them in one pass
-    int slot = 0;
-    for (int j = 0; j < m.nk; ++j) slot = std::max(slot, s.st[j].d1[0].partials());
-    if (!dalloc(m, &s.cs_dx, (size_t)m.nk * slot * s.C)) return false;
+    // the stacks accumulate their input gradients into d_x in order; the last stack's epilogue
+    // takes the column sums of the finished sum (the ups bias gradient), the others none
+    const int slot = s.st[m.nk - 1].d1[0].partials();
+    if (!dalloc(m, &s.cs_dx, (size_t)slot * s.C)) return false;
     for (int j = 0; j < m.nk; ++j) {
-      s.st[j].cs_dp[0] = s.cs_dx + (size_t)j * slot * s.C;
+      s.st[j].cs_dp[0] = (j == m.nk - 1) ? s.cs_dx : nullptr;
       s.st[j].d1[0].set_colsum(s.st[j].cs_dp[0]);
     }
     // weight gradients in execution order, grouped while their partials fit the L2 budget
@@ -625,7 +625,7 @@ bool gen_setup(Gen& m) {
         }
       }
     }
-    cs.push_back(colsum_desc(s.cs_dx, m.nk * slot, s.C, m.G(m.pidx("dec.ups." + std::to_string(L) + ".bias"))));
+    cs.push_back(colsum_desc(s.cs_dx, slot, s.C, m.G(m.pidx("dec.ups." + std::to_string(L) + ".bias"))));
     if (snake)
       cs.push_back(
           colsum_desc(s.ap_up, s.ap_up_tiles, s.Cin, alpha_grad(m, "dec.ups_act." + std::to_string(L) + ".alpha")));

@@ -237,7 +237,6 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
       tc_fence_after();
 #pragma unroll 1
       for (int c0 = 0; c0 < N; c0 += 32) {
-        if (c0) epi_load<F>(e, valid, row_off + c0, in);
         float v[32];
         if (ok) {
           const uint32_t ta = tmem + (uint32_t)(buf * N * nA) + ((uint32_t)(qw * 32) << 16) + (uint32_t)c0;
@@ -255,7 +254,7 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
         float cs = 0.f, ap = 0.f;
         epi_finish<F>(e, v, in, valid && ok, row_off + c0, 0, ra ? ra + c0 : nullptr, bias ? bias + c0 : nullptr,
                    aal ? aal + c0 : nullptr, mal ? mal + c0 : nullptr, qw, lane, red[grp], &cs, &ap, 1 + grp, true,
-                   o);
+                   o, c0 + 32 < N, row_off + c0 + 32);
         o.off0 += 32;
         if (qw == 0) {  // column sums accumulate over the group's tiles (warp 0 holds this tile's)
           s_csum[grp][c0 + lane] += cs;
@@ -286,18 +285,21 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
 }
 
 // Instantiated (KC, SPLIT, epilogue feature set) combinations: the forward (bf16x3) and input-gradient
-// epilogues of the resblock convolutions, plus a generic kernel for any other epilogue.
+// epilogues of the resblock convolutions (with and without column sums), plus a generic kernel for
+// any other epilogue.
 #define WB_CONV2_KERNELS(X)                                                                     \
   X(64, true, kEpiGeneric) X(64, true, kEpiAct) X(64, true, kEpiAct | kEpiSnake)                 \
   X(64, true, kEpiRes | kEpiAct) X(64, true, kEpiRes | kEpiAct | kEpiSnake) X(64, true, kEpiRes)  \
   X(64, true, 0u) X(64, false, kEpiGeneric) X(64, false, kEpiMask | kEpiColsum)                 \
   X(64, false, kEpiMask | kEpiColsum | kEpiSnake) X(64, false, kEpiMask | kEpiRes | kEpiColsum)  \
-  X(64, false, kEpiMask | kEpiRes | kEpiColsum | kEpiSnake)                                      \
+  X(64, false, kEpiMask | kEpiRes | kEpiColsum | kEpiSnake) X(64, false, kEpiMask | kEpiRes)     \
+  X(64, false, kEpiMask | kEpiRes | kEpiSnake)                                                   \
   X(32, true, kEpiGeneric) X(32, true, kEpiAct) X(32, true, kEpiAct | kEpiSnake)                 \
   X(32, true, kEpiRes | kEpiAct) X(32, true, kEpiRes | kEpiAct | kEpiSnake) X(32, true, kEpiRes)  \
   X(32, true, 0u) X(32, false, kEpiGeneric) X(32, false, kEpiMask | kEpiColsum)                 \
   X(32, false, kEpiMask | kEpiColsum | kEpiSnake) X(32, false, kEpiMask | kEpiRes | kEpiColsum)  \
-  X(32, false, kEpiMask | kEpiRes | kEpiColsum | kEpiSnake)
+  X(32, false, kEpiMask | kEpiRes | kEpiColsum | kEpiSnake) X(32, false, kEpiMask | kEpiRes)     \
+  X(32, false, kEpiMask | kEpiRes | kEpiSnake)
 
 // `lim` = opt-in shared memory minus 1 KB; the kernels' own static shared memory comes off it too
 void tc_conv2_set_smem_limit(int lim) {

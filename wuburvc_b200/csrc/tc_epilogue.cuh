@@ -51,8 +51,10 @@ WB_DEV void store_f32x32(float* p, const float* v) {
 // A warp's 32 rows x 64 bytes leave through its 2 KB staging buffer: each lane writes its row
 // (16-byte pieces XOR-swizzled by row, conflict-free), then the warp stores 8 rows x 64 B per
 // instruction, contiguous where the rows are (512 B when a row is 64 B).  Rows >= rows_valid are
-// not stored.  g0 = address of the warp's row 0 at this column piece.
-WB_DEV void stage_put64(uint4* st, int lane, const uint32_t* w, char* g0, size_t pitch_bytes, int rows_valid) {
+// not stored.  g0 = address of the warp's row 0 at this column piece.  With `add` the pieces are
+// fp32 quadruples added to memory (one vector reduction each, resolved in L2) instead of stored.
+WB_DEV void stage_put64(uint4* st, int lane, const uint32_t* w, char* g0, size_t pitch_bytes, int rows_valid,
+                        bool add = false) {
 #pragma unroll
   for (int i = 0; i < 4; ++i)
     st[lane * 4 + (i ^ ((lane >> 1) & 3))] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
@@ -61,7 +63,14 @@ WB_DEV void stage_put64(uint4* st, int lane, const uint32_t* w, char* g0, size_t
   for (int j = 0; j < 4; ++j) {
     const int r = 8 * j + (lane >> 2), sg = lane & 3;
     const uint4 x = st[r * 4 + (sg ^ ((r >> 1) & 3))];
-    if (r < rows_valid) *reinterpret_cast<uint4*>(g0 + (size_t)r * pitch_bytes + sg * 16) = x;
+    if (r < rows_valid) {
+      char* g = g0 + (size_t)r * pitch_bytes + sg * 16;
+      if (add)
+        atomicAdd(reinterpret_cast<float4*>(g),
+                  make_float4(__uint_as_float(x.x), __uint_as_float(x.y), __uint_as_float(x.z), __uint_as_float(x.w)));
+      else
+        *reinterpret_cast<uint4*>(g) = x;
+    }
   }
   __syncwarp();
 }
@@ -80,15 +89,20 @@ WB_DEV void out_bf16x32(const RowOut& o, bf16* base, size_t off, const uint32_t*
   else store_packed16(base + off, w);
 }
 
-WB_DEV void out_f32x32(const RowOut& o, float* base, size_t off, const float* v) {
+WB_DEV void out_f32x32(const RowOut& o, float* base, size_t off, const float* v, bool add = false) {
   if (o.stage) {
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       uint32_t w[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) w[i] = __float_as_uint(v[16 * h + i]);
-      stage_put64(o.stage, o.lane, w, reinterpret_cast<char*>(base + o.off0 + 16 * h), o.pitch * 4, o.rows_valid);
+      stage_put64(o.stage, o.lane, w, reinterpret_cast<char*>(base + o.off0 + 16 * h), o.pitch * 4, o.rows_valid,
+                  add);
     }
+  } else if (add) {
+    float4* q = reinterpret_cast<float4*>(base + off);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) atomicAdd(q + i, make_float4(v[i * 4], v[i * 4 + 1], v[i * 4 + 2], v[i * 4 + 3]));
   } else {
     store_f32x32(base + off, v);
   }
@@ -135,17 +149,27 @@ struct EpiIn {
 };
 
 template <uint32_t F>
-WB_DEV void epi_load(const Epi& e, bool valid, size_t off, EpiIn& in) {
+WB_DEV void epi_load_mask(const Epi& e, bool valid, size_t off, EpiIn& in) {
   if (WB_EPI_HAS(kEpiMask, e.mask_src != nullptr) && valid) {
     const uint4* q = reinterpret_cast<const uint4*>(e.mask_src + off);
 #pragma unroll
     for (int i = 0; i < 4; ++i) in.m[i] = __ldcs(q + i);
   }
+}
+
+template <uint32_t F>
+WB_DEV void epi_load_res(const Epi& e, bool valid, size_t off, EpiIn& in) {
   if (WB_EPI_HAS(kEpiRes, e.res != nullptr) && valid) {
     const float4* q = reinterpret_cast<const float4*>(e.res + off);
 #pragma unroll
     for (int i = 0; i < 8; ++i) in.r[i] = __ldcs(q + i);
   }
+}
+
+template <uint32_t F>
+WB_DEV void epi_load(const Epi& e, bool valid, size_t off, EpiIn& in) {
+  epi_load_mask<F>(e, valid, off, in);
+  epi_load_res<F>(e, valid, off, in);
 }
 
 // Applies the epilogue to one 32-column chunk of one row (inputs from epi_load).
@@ -156,11 +180,18 @@ WB_DEV void epi_load(const Epi& e, bool valid, size_t off, EpiIn& in) {
 //   kernel, else e's global vectors offset by col)
 //   cs_acc / ap_acc: when non-null (persistent kernels), warp 0 accumulates this tile's column sums
 //   there instead of writing a per-tile partial.
+//   next / next_off: when `next`, the inputs of the row's next chunk (at next_off) are loaded into
+//   `in` as soon as this chunk has consumed them, so their latency overlaps this chunk's work.
+// Order: mask, bias, cond row, residual, scale, accumulation into out_f32, outputs, column sums
+// (of the final, accumulated value).  An accumulation whose sum nothing else in the epilogue reads
+// is a vector reduction into out_f32 (no read of the previous value on the SM).
 template <uint32_t F>
-WB_DEV void epi_finish(const Epi& e, float* v, const EpiIn& in, bool valid, size_t off, size_t part_row,
+WB_DEV void epi_finish(const Epi& e, float* v, EpiIn& in, bool valid, size_t off, size_t part_row,
                        const float* rowadd_row, const float* bias, const float* act_alpha, const float* mask_alpha,
                        int warp, int lane, float* red, float* cs_acc, float* ap_acc, int bar,
-                       bool bias16 = false, const RowOut& o = RowOut{}) {
+                       bool bias16 = false, const RowOut& o = RowOut{}, bool next = false, size_t next_off = 0) {
+  const bool has_act = WB_EPI_HAS(kEpiAct, e.act_hi != nullptr);
+  const bool has_cs = WB_EPI_HAS(kEpiColsum, e.colsum != nullptr);
   if (WB_EPI_HAS(kEpiMask, e.mask_src != nullptr)) {
     float x[32];
 #pragma unroll
@@ -172,6 +203,7 @@ WB_DEV void epi_finish(const Epi& e, float* v, const EpiIn& in, bool valid, size
         x[8 * i + 2 * j + 1] = valid ? bf16hi_f(w[j]) : 0.f;
       }
     }
+    if (next) epi_load_mask<F>(e, valid, next_off, in);
     if (WB_EPI_HAS(kEpiSnake, e.act_kind == 1)) {
       float ga[32];
 #pragma unroll
@@ -224,18 +256,9 @@ WB_DEV void epi_finish(const Epi& e, float* v, const EpiIn& in, bool valid, size
   }
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] *= e.scale;
-  if (WB_EPI_HAS(kEpiColsum, e.colsum != nullptr)) {
-    float cv[32];
-#pragma unroll
-    for (int i = 0; i < 32; ++i) cv[i] = valid ? v[i] : 0.f;
-    const float t = cta_colsum32(cv, red, warp, lane, bar);
-    if (warp == 0) {
-      if (cs_acc) *cs_acc += t;
-      else e.colsum[part_row + lane] = t;
-    }
-  }
-  if (!valid && !o.stage) return;  // (the staged path needs every lane of the warp below)
-  if (e.accumulate && valid) {  // previous value of the fp32 output (stack accumulation)
+  // accumulation: by reduction when only out_f32 receives the sum, else read + add here
+  const bool acc_red = e.accumulate && !e.out_bf16 && !e.pre_hi && !has_act && !has_cs;
+  if (e.accumulate && !acc_red && valid) {
     const float4* q = reinterpret_cast<const float4*>(e.out_f32 + off);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -246,31 +269,43 @@ WB_DEV void epi_finish(const Epi& e, float* v, const EpiIn& in, bool valid, size
       v[4 * i + 3] += a.w;
     }
   }
-  if (e.out_f32) out_f32x32(o, e.out_f32, off, v);
-  if (e.out_bf16 || e.pre_hi) {
-    uint32_t b[16];
+  if (next) epi_load_res<F>(e, valid, next_off, in);
+  if (valid || o.stage) {  // (the staged path needs every lane of the warp)
+    if (e.out_f32) out_f32x32(o, e.out_f32, off, v, acc_red);
+    if (e.out_bf16 || e.pre_hi) {
+      uint32_t b[16];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) b[i] = pack_bf16(v[2 * i], v[2 * i + 1]);
-    if (e.out_bf16) out_bf16x32(o, e.out_bf16, off, b);
-    if (e.pre_hi) out_bf16x32(o, e.pre_hi, off, b);
-  }
-  if (WB_EPI_HAS(kEpiAct, e.act_hi != nullptr)) {
-    uint32_t h[16], l[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      float a0, a1;
-      if (WB_EPI_HAS(kEpiSnake, e.act_kind == 1)) {
-        a0 = snake(v[2 * i], act_alpha[2 * i]);
-        a1 = snake(v[2 * i + 1], act_alpha[2 * i + 1]);
-      } else {
-        a0 = lrelu(v[2 * i], e.slope);
-        a1 = lrelu(v[2 * i + 1], e.slope);
-      }
-      h[i] = pack_bf16(a0, a1);
-      l[i] = pack_bf16(a0 - bf16lo_f(h[i]), a1 - bf16hi_f(h[i]));
+      for (int i = 0; i < 16; ++i) b[i] = pack_bf16(v[2 * i], v[2 * i + 1]);
+      if (e.out_bf16) out_bf16x32(o, e.out_bf16, off, b);
+      if (e.pre_hi) out_bf16x32(o, e.pre_hi, off, b);
     }
-    out_bf16x32(o, e.act_hi, off, h);
-    if (e.act_lo) out_bf16x32(o, e.act_lo, off, l);
+    if (has_act) {
+      uint32_t h[16], l[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        float a0, a1;
+        if (WB_EPI_HAS(kEpiSnake, e.act_kind == 1)) {
+          a0 = snake(v[2 * i], act_alpha[2 * i]);
+          a1 = snake(v[2 * i + 1], act_alpha[2 * i + 1]);
+        } else {
+          a0 = lrelu(v[2 * i], e.slope);
+          a1 = lrelu(v[2 * i + 1], e.slope);
+        }
+        h[i] = pack_bf16(a0, a1);
+        l[i] = pack_bf16(a0 - bf16lo_f(h[i]), a1 - bf16hi_f(h[i]));
+      }
+      out_bf16x32(o, e.act_hi, off, h);
+      if (e.act_lo) out_bf16x32(o, e.act_lo, off, l);
+    }
+  }
+  if (has_cs) {  // every lane reaches the group's named barriers; v is consumed here
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = valid ? v[i] : 0.f;
+    const float t = cta_colsum32(v, red, warp, lane, bar);
+    if (warp == 0) {
+      if (cs_acc) *cs_acc += t;
+      else e.colsum[part_row + lane] = t;
+    }
   }
 }
 
