@@ -113,10 +113,11 @@ void noise_add_act(const NoiseActArgs& a, cudaStream_t st);
 //   wt [k][C] transposed weights; wpart [noise_backward_parts][C][k]; g scratch [B*T][k]
 void noise_backward(const float* dx, const float* har, const float* wt, int B, int T, int C, int k, int stride, int pad,
                     int T_full, float* d_har, int accumulate_dhar, float* wpart, float* g, cudaStream_t st);
-int noise_backward_parts(int B, int T, int k);
+int noise_backward_parts(int B, int T, int C, int k);
 // dynamic shared memory of noise_add_act for a noise conv of k taps and the given stride
 size_t noise_act_smem(int k, int stride);
-void noise_wgrad_reduce(const float* wpart, int nparts, int C, int k, float* dW, cudaStream_t st);
+void noise_wgrad_reduce(const float* wpart, int nparts, int C, int k, float* dW, float* scratch, size_t scratch_floats,
+                        cudaStream_t st);
 
 // ---- conv_post ------------------------------------------------------------------------------
 // audio[b][t] = tanh(sum_{c,tap} a[b][t-3+tap][c] * W[c][tap]), a = hi + lo

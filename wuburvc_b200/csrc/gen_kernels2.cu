@@ -12,6 +12,20 @@ __device__ __forceinline__ float warp_sum(float v) {
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
 }
+// Warp transpose-reduction: on return lane l holds the sum over lanes of input v[l].
+__device__ __forceinline__ float warp_transpose_sum32(float* v, int lane) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    const bool upper = (lane & off) != 0;
+#pragma unroll
+    for (int i = 0; i < off; ++i) {
+      const float send = upper ? v[i] : v[i + off];
+      const float keep = upper ? v[i + off] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+    }
+  }
+  return v[0];
+}
 }  // namespace
 
 // w [C][k] -> wt [k][C]
@@ -174,10 +188,7 @@ __global__ void noise_dhar_kernel(const float* __restrict__ g, int B, int T, int
 constexpr int kNoiseTaps = 16;
 constexpr int kNwRows = 128;
 
-int noise_backward_parts(int B, int T, int k) {
-  (void)k;
-  return B * ((T + kNwRows - 1) / kNwRows);
-}
+int noise_backward_parts_rows(int B, int T) { return B * ((T + kNwRows - 1) / kNwRows); }
 
 __global__ void __launch_bounds__(256) noise_wgrad_kernel(const float* __restrict__ dx, const float* __restrict__ har,
                                                           int B, int T, int C, int k, int stride, int pad, int T_full,
@@ -260,25 +271,160 @@ __global__ void __launch_bounds__(256) noise_g_small_kernel(const float* __restr
     if (q < k) g[(size_t)row * k + q] = acc[q];
 }
 
+// ---- fused noise-conv backward: one pass over dx gives both g and the weight-gradient partials ----
+// Block = 8 warps x `rpw` consecutive rows (rows = B*T, items back to back) x one group of TP taps
+// (blockIdx.y).  Lane l holds channels [l*CPL, l*CPL + CPL) of every row it reads (C = 32*CPL).
+// A pass covers RP = 32/TP rows: v[r*TP + t] = sum over the lane's channels of dx[r][c] * wt[t][c],
+// and one transpose-reduction leaves lane l with g of (row l/TP, tap l%TP).  The same dx registers
+// feed the weight gradient acc[c][t] += dx[r][c] * har[b][j*stride - pad + tap] (lane l loads the
+// har sample of (l/TP, l%TP), shuffles broadcast it).  The warps' accumulators are summed in shared
+// memory in a fixed order into part[blockIdx.x][c][tap].
+template <int CPL, int TP>
+__global__ void __launch_bounds__(256) noise_bwd_fused_kernel(const float* __restrict__ dx,
+                                                              const float* __restrict__ wt,
+                                                              const float* __restrict__ har, int rows, int T, int k,
+                                                              int stride, int pad, int T_full, int rpw,
+                                                              float* __restrict__ g, float* __restrict__ part) {
+  constexpr int C = 32 * CPL, RP = 32 / TP;
+  __shared__ __align__(16) float ws[TP][C];
+  __shared__ float red[8][32][TP + 1];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int tap0 = blockIdx.y * TP;
+  for (int i = threadIdx.x; i < TP * C; i += blockDim.x) {
+    const int t = i / C, c = i % C;
+    ws[t][c] = (tap0 + t < k) ? wt[(size_t)(tap0 + t) * C + c] : 0.f;
+  }
+  __syncthreads();
+  float acc[CPL][TP];
+#pragma unroll
+  for (int c = 0; c < CPL; ++c)
+#pragma unroll
+    for (int t = 0; t < TP; ++t) acc[c][t] = 0.f;
+  const int my_r = lane / TP, my_t = lane % TP;
+  const int row_w = (blockIdx.x * 8 + warp) * rpw;
+  for (int r0 = row_w; r0 < row_w + rpw && r0 < rows; r0 += RP) {
+    float x[RP][CPL];
+#pragma unroll
+    for (int r = 0; r < RP; ++r) {
+      const int row = r0 + r;
+      if (row < rows) {
+        const float* src = dx + (size_t)row * C + lane * CPL;
+        if constexpr (CPL % 4 == 0) {
+#pragma unroll
+          for (int q = 0; q < CPL / 4; ++q) {
+            const float4 f = __ldcs(reinterpret_cast<const float4*>(src) + q);
+            x[r][4 * q] = f.x; x[r][4 * q + 1] = f.y; x[r][4 * q + 2] = f.z; x[r][4 * q + 3] = f.w;
+          }
+        } else if constexpr (CPL == 2) {
+          const float2 f = __ldcs(reinterpret_cast<const float2*>(src));
+          x[r][0] = f.x; x[r][1] = f.y;
+        } else {
+          x[r][0] = __ldcs(src);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) x[r][c] = 0.f;
+      }
+    }
+    // this lane's har sample: row r0 + my_r, tap tap0 + my_t
+    float h = 0.f;
+    {
+      const int row = r0 + my_r, tap = tap0 + my_t;
+      if (row < rows && tap < k) {
+        const int b = row / T, j = row - b * T;
+        const int idx = j * stride - pad + tap;
+        if (idx >= 0 && idx < T_full) h = __ldg(har + (size_t)b * T_full + idx);
+      }
+    }
+    float v[32];
+#pragma unroll
+    for (int r = 0; r < RP; ++r)
+#pragma unroll
+      for (int t = 0; t < TP; ++t) {
+        float sum = 0.f;
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) sum += x[r][c] * ws[t][lane * CPL + c];
+        v[r * TP + t] = sum;
+        const float hv = __shfl_sync(0xffffffffu, h, r * TP + t);
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) acc[c][t] += x[r][c] * hv;
+      }
+    const float gs = warp_transpose_sum32(v, lane);
+    {
+      const int row = r0 + my_r, tap = tap0 + my_t;
+      if (row < rows && tap < k) g[(size_t)row * k + tap] = gs;
+    }
+  }
+  // fixed-order block reduction of the weight gradient, one channel of every lane at a time
+#pragma unroll
+  for (int c = 0; c < CPL; ++c) {
+#pragma unroll
+    for (int t = 0; t < TP; ++t) red[warp][lane][t] = acc[c][t];
+    __syncthreads();
+    if (threadIdx.x < 32 * TP) {
+      const int l = threadIdx.x / TP, t = threadIdx.x % TP;
+      float sum = 0.f;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) sum += red[w][l][t];
+      if (tap0 + t < k) part[((size_t)blockIdx.x * C + l * CPL + c) * k + tap0 + t] = sum;
+    }
+    __syncthreads();
+  }
+}
+
+namespace {
+// taps per pass of the fused kernel (a power of two <= 8, <= k), channels per lane (0 = not covered)
+int noise_tp(int k) { return k >= 8 ? 8 : k >= 4 ? 4 : k >= 2 ? 2 : 1; }
+int noise_cpl(int C) { return (C == 32 || C == 64 || C == 128 || C == 256) ? C / 32 : 0; }
+// rows per warp: about 512 blocks over (row blocks x tap groups), a multiple of the pass height
+int noise_rpw(long long rows, int k) {
+  const int tp = noise_tp(k), rp = 32 / tp, ntg = (k + tp - 1) / tp;
+  const long long per = (rows * ntg + 8LL * 512 * rp - 1) / (8LL * 512 * rp);
+  return rp * (int)std::max(1LL, per);
+}
+}  // namespace
+
+int noise_backward_parts(int B, int T, int C, int k) {
+  if (noise_cpl(C)) {
+    const long long rows = (long long)B * T;
+    return (int)((rows + 8LL * noise_rpw(rows, k) - 1) / (8LL * noise_rpw(rows, k)));
+  }
+  return noise_backward_parts_rows(B, T);
+}
+
 void noise_backward(const float* dx, const float* har, const float* wt, int B, int T, int C, int k, int stride, int pad,
                     int T_full, float* d_har, int accumulate_dhar, float* wpart, float* g, cudaStream_t st) {
   const long long rows = (long long)B * T;
-  if (k <= 8) {
-    noise_g_small_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, st>>>(dx, wt, rows, C, k, g);
+  const int cpl = noise_cpl(C);
+  if (cpl) {
+    const int tp = noise_tp(k), rpw = noise_rpw(rows, k);
+    const dim3 grid((unsigned)noise_backward_parts(B, T, C, k), (unsigned)((k + tp - 1) / tp));
+#define WB_NB(cpl_, tp_)                                                                             \
+  if (cpl == cpl_ && tp == tp_)                                                                      \
+    noise_bwd_fused_kernel<cpl_, tp_><<<grid, 256, 0, st>>>(dx, wt, har, (int)rows, T, k, stride, pad, T_full, rpw, g, \
+                                                            wpart);
+    WB_NB(1, 1) WB_NB(1, 2) WB_NB(1, 4) WB_NB(1, 8) WB_NB(2, 1) WB_NB(2, 2) WB_NB(2, 4) WB_NB(2, 8)
+    WB_NB(4, 1) WB_NB(4, 2) WB_NB(4, 4) WB_NB(4, 8) WB_NB(8, 1) WB_NB(8, 2) WB_NB(8, 4) WB_NB(8, 8)
+#undef WB_NB
   } else {
-    const long long warps = rows * ((k + 15) / 16);
-    noise_g_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(dx, wt, rows, C, k, g);
+    if (k <= 8) {
+      noise_g_small_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, st>>>(dx, wt, rows, C, k, g);
+    } else {
+      const long long warps = rows * ((k + 15) / 16);
+      noise_g_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(dx, wt, rows, C, k, g);
+    }
+    const size_t smem = sizeof(float) * ((size_t)(kNwRows - 1) * stride + k);
+    noise_wgrad_kernel<<<dim3(C / 32, noise_backward_parts_rows(B, T)), 256, smem, st>>>(dx, har, B, T, C, k, stride,
+                                                                                         pad, T_full, wpart);
   }
   const long long n = (long long)B * T_full;
   noise_dhar_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(g, B, T, k, stride, pad, T_full, d_har,
                                                                   accumulate_dhar);
-  const size_t smem = sizeof(float) * ((size_t)(kNwRows - 1) * stride + k);
-  noise_wgrad_kernel<<<dim3(C / 32, noise_backward_parts(B, T, k)), 256, smem, st>>>(dx, har, B, T, C, k, stride, pad,
-                                                                                     T_full, wpart);
 }
 
-void noise_wgrad_reduce(const float* wpart, int nparts, int C, int k, float* dW, cudaStream_t st) {
-  col_reduce(wpart, nparts, (long long)C * k, dW, 0, st);
+void noise_wgrad_reduce(const float* wpart, int nparts, int C, int k, float* dW, float* scratch, size_t scratch_floats,
+                        cudaStream_t st) {
+  col_reduce(wpart, nparts, (long long)C * k, dW, 0, scratch, scratch_floats, st);
 }
 
 // =============================================================================================
@@ -292,19 +438,6 @@ constexpr int kPostC = 32;
 // half gives lane r the output of row r.
 constexpr int kPostWarpRows = 16;
 
-__device__ __forceinline__ float warp_colsum32_post(float* v, int lane) {
-#pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) {
-    const bool upper = (lane & off) != 0;
-#pragma unroll
-    for (int i = 0; i < off; ++i) {
-      const float send = upper ? v[i] : v[i + off];
-      const float keep = upper ? v[i + off] : v[i];
-      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
-    }
-  }
-  return v[0];
-}
 
 __global__ void __launch_bounds__(256) post_forward_kernel(const bf16* __restrict__ hi, const bf16* __restrict__ lo,
                                                            const float* __restrict__ W, int B, int T,
@@ -339,7 +472,7 @@ __global__ void __launch_bounds__(256) post_forward_kernel(const bf16* __restric
       }
       v[r] = acc;
     }
-    const float s = warp_colsum32_post(v, lane);  // lane r: row t0 + r
+    const float s = warp_transpose_sum32(v, lane);  // lane r: row t0 + r
     if (lane < kPostWarpRows && t0 + lane < T) audio[base + t0 + lane] = tanhf(s);
   }
 }

@@ -369,9 +369,10 @@ bool gen_setup(Gen& m) {
         if (!dalloc(m, &k.pp[q], n) || !dalloc(m, &k.pp_bf[q], n)) return false;
     }
     if (c.nsf) {
-      s.noise_parts = noise_backward_parts(B, s.T, s.kn);
+      s.noise_parts = noise_backward_parts(B, s.T, s.C, s.kn);
       if (!dalloc(m, &s.noise_wt, (size_t)s.C * s.kn)) return false;
       if (!dalloc(m, &s.noise_wpart, (size_t)s.noise_parts * s.C * s.kn)) return false;
+      m.noise_scratch_n = std::max(m.noise_scratch_n, (size_t)s.noise_parts * s.C * s.kn);
       if (!dalloc(m, &s.noise_g, (size_t)B * s.T * s.kn)) return false;
       // the noise kernels' shared-memory windows stay within the default 48 KB
       if (noise_act_smem(s.kn, s.sn) > 48 * 1024 || sizeof(float) * ((size_t)127 * s.sn + s.kn) > 30 * 1024) {
@@ -633,6 +634,7 @@ bool gen_setup(Gen& m) {
   }
   m.red_scratch_n = (size_t)4 << 20;
   if (!dalloc(m, &m.red_scratch, m.red_scratch_n)) return false;
+  if (m.noise_scratch_n && !dalloc(m, &m.noise_scratch, m.noise_scratch_n)) return false;
   {  // one-launch weight preparation table
     std::vector<PrepDesc> d;
     int first = 0;
@@ -822,12 +824,15 @@ bool gen_backward(Gen& m) {
         if (!run_wgrad(m, s, k.g1[cp])) return false;
       }
     }
-    // stage input gradient d_x: noise conv, ups dgrad / wgrad
+    // stage input gradient d_x: noise conv (side stream: it only reads d_x and feeds the source
+    // gradient at the end of the backward), ups dgrad / wgrad
     if (c.nsf) {
       const int nw = m.pidx("dec.noise_convs." + std::to_string(L) + ".weight");
+      if (!fork_side(m)) return false;
       noise_backward(s.d_x, m.har, s.noise_wt, B, s.T, s.C, s.kn, s.sn, s.pn, m.T, m.d_har, L < 3, s.noise_wpart,
-                     s.noise_g, st);
-      noise_wgrad_reduce(s.noise_wpart, s.noise_parts, s.C, s.kn, m.G(nw), st);
+                     s.noise_g, m.side);
+      noise_wgrad_reduce(s.noise_wpart, s.noise_parts, s.C, s.kn, m.G(nw), m.noise_scratch, m.noise_scratch_n,
+                         m.side);
     }
     CK(s.up_dg.run(st));
     if (!run_wgrad(m, s, s.up_wg)) return false;
@@ -849,6 +854,7 @@ bool gen_backward(Gen& m) {
   if (c.gin_channels)
     cond_backward(m.cs_pre, m.pre_tiles_per_item, B, c.initial_channel, m.g, c.gin_channels,
                   m.G(m.pidx("dec.cond.weight")), m.G(m.pidx("dec.cond.bias")), st);
+  if (c.nsf && !join_side(m)) return false;  // d_har is complete on the side stream
   if (c.nsf)
     nsf_backward(m.d_har, m.har, m.sw, B * m.T, m.dim, m.nsf_part, m.nsf_parts,
                  m.G(m.pidx("dec.m_source.l_linear.weight")), m.G(m.pidx("dec.m_source.l_linear.bias")), st);

@@ -136,6 +136,8 @@ struct Gen {
   int n_trans = 0, trans_blocks = 0;
   float* red_scratch = nullptr;  // two-pass deterministic reductions
   size_t red_scratch_n = 0;
+  float* noise_scratch = nullptr;  // the same for the noise-conv weight gradients (side stream)
+  size_t noise_scratch_n = 0;
 
   // CUDA graph of the resident-input step
   cudaGraphExec_t graph = nullptr;
