@@ -6,6 +6,11 @@ namespace wb {
 
 namespace {
 
+__device__ __forceinline__ float warp_sum(float v) {
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
 __device__ __forceinline__ float block_sum(float v, float* sh) {
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
@@ -59,91 +64,162 @@ __device__ __forceinline__ size_t wrow_addr(int i, int r, int rows, int cols, in
   return is_convT ? ((size_t)t * cols + c) * rows + r : ((size_t)t * rows + r) * cols + c;
 }
 
-__global__ void prep_weights_batched_kernel(const PrepDesc* __restrict__ descs, int ndesc) {
-  __shared__ float sh[32];
-  __shared__ int di;
-  if (threadIdx.x == 0) {
-    int lo = 0, hi = ndesc - 1;  // last descriptor with first <= blockIdx.x
-    while (lo < hi) {
-      const int mid = (lo + hi + 1) >> 1;
-      if (descs[mid].first <= (int)blockIdx.x) lo = mid;
-      else hi = mid - 1;
-    }
-    di = lo;
+namespace {
+// descriptor i with first_i <= block < first_{i+1} (firsts ascending); `which` 0 = norm, 1 = tile
+__device__ int prep_find(const PrepDesc* descs, int ndesc, int which) {
+  int lo = 0, hi = ndesc - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    const int f = which ? descs[mid].tile_first : descs[mid].norm_first;
+    if (f <= (int)blockIdx.x) lo = mid;
+    else hi = mid - 1;
   }
+  return lo;
+}
+}  // namespace
+
+int prep_norm_blocks(const PrepDesc& d) {
+  if (!d.g) return 0;
+  return d.is_convT ? (d.Q / 32) * d.nchunks : (d.P + 7) / 8;
+}
+
+int prep_tile_blocks(const PrepDesc& d) { return d.k * (d.P / 32) * (d.Q / (32 * d.qs)); }
+
+__global__ void __launch_bounds__(256) prep_norm_kernel(const PrepDesc* __restrict__ descs, int ndesc) {
+  __shared__ float red[8][33];
+  __shared__ int di;
+  if (threadIdx.x == 0) di = prep_find(descs, ndesc, 0);
   __syncthreads();
   const PrepDesc d = descs[di];
-  const int r = blockIdx.x - d.first;
-  const int rows = d.rows, cols = d.cols, k = d.k, is_convT = d.is_convT;
-  const int per = cols * k;
-  float scale = 1.f;
-  if (d.g) {
+  const int b = blockIdx.x - d.norm_first;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (!d.is_convT) {  // row p: every tap's contiguous Q floats
+    const int p = b * 8 + warp;
+    if (p >= d.P) return;
     float s = 0.f;
-    for (int i = threadIdx.x; i < per; i += blockDim.x) {
-      const float x = d.v[wrow_addr(i, r, rows, cols, is_convT)];
+    for (int t = 0; t < d.k; ++t) {
+      const float* row = d.v + ((size_t)t * d.P + p) * d.Q;
+#pragma unroll 4
+      for (int q = lane; q < d.Q; q += 32) {
+        const float x = row[q];
+        s += x * x;
+      }
+    }
+    s = warp_sum(s);
+    if (lane == 0) d.norm[p] = sqrtf(s);
+  } else {  // columns q0..q0+31 over one chunk of (tap, p) pairs
+    const int ncb = d.Q / 32;
+    const int cb = b % ncb, ch = b / ncb;
+    const int q = cb * 32 + lane;
+    const int i0 = ch * kPrepPairs, i1 = min(d.k * d.P, i0 + kPrepPairs);
+    float s = 0.f;
+#pragma unroll 4
+    for (int i = i0 + warp; i < i1; i += 8) {
+      const float x = d.v[(size_t)i * d.Q + q];
       s += x * x;
     }
-    s = block_sum(s, sh);
-    const float n = sqrtf(s);
-    scale = d.g[r] / n;
-    if (threadIdx.x == 0 && d.norm) d.norm[r] = n;
-  }
-  // only row-contiguous layouts here (coalesced); the transposed ones come from prep_transpose
-  for (int i = threadIdx.x; i < per; i += blockDim.x) {
-    const int t = i / cols, c = i - t * cols;
-    const float w = d.v[wrow_addr(i, r, rows, cols, is_convT)] * scale;
-    bf16 hi, lo;
-    split_bf16(w, hi, lo);
-    const size_t f = ((size_t)t * rows + r) * cols + c;  // [t][r][c]
-    if (!is_convT) {
-      d.fwd_hi[f] = hi;  // conv: r = out channel, c = in channel
-      d.fwd_lo[f] = lo;
-    } else {
-      d.dg[f] = hi;      // convT: r = in channel, c = out channel
-      d.lo_tmp[f] = lo;
+    red[warp][lane] = s;
+    __syncthreads();
+    if (warp == 0) {
+      float t = 0.f;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) t += red[w][lane];
+      d.npart[(size_t)ch * d.Q + q] = t;
     }
   }
 }
 
-// Batched bf16 [R][C] -> [C][R] transposes through 32 x 32 shared-memory tiles.
-__global__ void __launch_bounds__(256) prep_transpose_kernel(const TransDesc* __restrict__ descs, int ndesc) {
-  __shared__ unsigned short tile[32][33];
+__global__ void __launch_bounds__(256) prep_tile_kernel(const PrepDesc* __restrict__ descs, int ndesc) {
+  __shared__ float s_scale[128];
+  __shared__ unsigned short ht[128][34];  // transposed hi: [q - q0][p - p0]
   __shared__ int di;
-  if (threadIdx.x == 0 && threadIdx.y == 0) {
-    int lo = 0, hi = ndesc - 1;
-    while (lo < hi) {
-      const int mid = (lo + hi + 1) >> 1;
-      if (descs[mid].first <= (int)blockIdx.x) lo = mid;
-      else hi = mid - 1;
+  if (threadIdx.x == 0) di = prep_find(descs, ndesc, 1);
+  __syncthreads();
+  const PrepDesc d = descs[di];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int QS = d.qs, QW = 32 * QS;
+  const int nqb = d.Q / QW, npb = d.P / 32;
+  int b = blockIdx.x - d.tile_first;
+  const int qb = b % nqb;
+  b /= nqb;
+  const int pb = b % npb, t = b / npb;
+  const int p0 = pb * 32, q0 = qb * QW;
+  if (!d.is_convT) {
+    if (tid < 32) s_scale[tid] = d.g ? d.g[p0 + tid] / d.norm[p0 + tid] : 1.f;
+  } else if (tid < QW) {
+    float sc = 1.f;
+    if (d.g) {
+      float s = 0.f;
+      for (int ch = 0; ch < d.nchunks; ++ch) s += d.npart[(size_t)ch * d.Q + q0 + tid];
+      const float n = sqrtf(s);
+      sc = d.g[q0 + tid] / n;
+      if (t == 0 && pb == 0) d.norm[q0 + tid] = n;
     }
-    di = lo;
+    s_scale[tid] = sc;
   }
   __syncthreads();
-  const TransDesc d = descs[di];
-  const int b = blockIdx.x - d.first;
-  const int tc = (d.C + 31) / 32;
-  const int r0 = (b / tc) * 32, c0 = (b % tc) * 32;
-  const unsigned short* src = reinterpret_cast<const unsigned short*>(d.src);
-  unsigned short* dst = reinterpret_cast<unsigned short*>(d.dst);
-  for (int y = threadIdx.y; y < 32; y += 8) {
-    const int r = r0 + y, c = c0 + threadIdx.x;
-    if (r < d.R && c < d.C) tile[y][threadIdx.x] = src[(size_t)r * d.C + c];
+  // tap of the storage-layout output: t (conv) or the tap's place in the polyphase order (convT)
+  int ts = t;
+  if (d.is_convT) {
+    const int ph = t % d.stride;
+    ts = t / d.stride;
+    for (int q = 0; q < ph; ++q) ts += (d.k - q + d.stride - 1) / d.stride;
+  }
+  const int td = d.is_convT ? t : d.k - 1 - t;  // tap of the transposed output
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int pl = warp + 8 * j, p = p0 + pl;
+    const size_t src = ((size_t)t * d.P + p) * d.Q + q0 + lane * QS;
+    const size_t dst = ((size_t)ts * d.P + p) * d.Q + q0 + lane * QS;
+    float x[4];
+    if (QS == 4) {
+      const float4 f = *reinterpret_cast<const float4*>(d.v + src);
+      x[0] = f.x; x[1] = f.y; x[2] = f.z; x[3] = f.w;
+    } else if (QS == 2) {
+      const float2 f = *reinterpret_cast<const float2*>(d.v + src);
+      x[0] = f.x; x[1] = f.y;
+    } else {
+      x[0] = d.v[src];
+    }
+    bf16 hi[4], lo[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      if (e < QS) {
+        const float sc = d.is_convT ? s_scale[lane * QS + e] : s_scale[pl];
+        split_bf16(x[e] * sc, hi[e], lo[e]);
+        ht[lane * QS + e][pl] = __bfloat16_as_ushort(hi[e]);
+      }
+    }
+    if (QS == 4) {
+      *reinterpret_cast<uint2*>(d.fwd_hi + dst) =
+          make_uint2(__bfloat16_as_ushort(hi[0]) | ((uint32_t)__bfloat16_as_ushort(hi[1]) << 16),
+                     __bfloat16_as_ushort(hi[2]) | ((uint32_t)__bfloat16_as_ushort(hi[3]) << 16));
+      *reinterpret_cast<uint2*>(d.fwd_lo + dst) =
+          make_uint2(__bfloat16_as_ushort(lo[0]) | ((uint32_t)__bfloat16_as_ushort(lo[1]) << 16),
+                     __bfloat16_as_ushort(lo[2]) | ((uint32_t)__bfloat16_as_ushort(lo[3]) << 16));
+    } else if (QS == 2) {
+      *reinterpret_cast<uint32_t*>(d.fwd_hi + dst) =
+          __bfloat16_as_ushort(hi[0]) | ((uint32_t)__bfloat16_as_ushort(hi[1]) << 16);
+      *reinterpret_cast<uint32_t*>(d.fwd_lo + dst) =
+          __bfloat16_as_ushort(lo[0]) | ((uint32_t)__bfloat16_as_ushort(lo[1]) << 16);
+    } else {
+      d.fwd_hi[dst] = hi[0];
+      d.fwd_lo[dst] = lo[0];
+    }
   }
   __syncthreads();
-  for (int y = threadIdx.y; y < 32; y += 8) {
-    const int c = c0 + y, r = r0 + threadIdx.x;
-    if (r < d.R && c < d.C) dst[(size_t)c * d.R + r] = tile[threadIdx.x][y];
+  // transposed hi: rows q0..q0+QW-1 of dg[td] ([Q][P]), 32 p each, 16 threads x 2 values per row
+  for (int r = tid >> 4; r < QW; r += 16) {
+    const int pp = (tid & 15) * 2;
+    const uint32_t w = (uint32_t)ht[r][pp] | ((uint32_t)ht[r][pp + 1] << 16);
+    *reinterpret_cast<uint32_t*>(d.dg + ((size_t)td * d.Q + q0 + r) * d.P + p0 + pp) = w;
   }
 }
 
-int prep_transpose_blocks(int R, int C) { return ((R + 31) / 32) * ((C + 31) / 32); }
-
-void prep_transpose_batched(const TransDesc* descs, int ndesc, int total_blocks, cudaStream_t st) {
-  if (ndesc > 0 && total_blocks > 0) prep_transpose_kernel<<<total_blocks, dim3(32, 8), 0, st>>>(descs, ndesc);
-}
-
-void prep_weights_batched(const PrepDesc* descs, int ndesc, int total_rows, cudaStream_t st) {
-  prep_weights_batched_kernel<<<total_rows, 256, 0, st>>>(descs, ndesc);
+void prep_weights(const PrepDesc* descs, int ndesc, int norm_blocks, int tile_blocks, cudaStream_t st) {
+  if (ndesc <= 0) return;
+  if (norm_blocks > 0) prep_norm_kernel<<<norm_blocks, 256, 0, st>>>(descs, ndesc);
+  if (tile_blocks > 0) prep_tile_kernel<<<tile_blocks, 256, 0, st>>>(descs, ndesc);
 }
 
 __global__ void wn_backward_kernel(const float* __restrict__ dW, const float* __restrict__ v,
@@ -277,19 +353,28 @@ void pack_z(const float* z, int B, int C, int F, bf16* hi, bf16* lo, cudaStream_
   pack_z_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(z, B, C, F, hi, lo);
 }
 
-__global__ void cond_forward_kernel(const float* __restrict__ W, const float* __restrict__ bias,
-                                    const float* __restrict__ g, int B, int C, int gin, float* __restrict__ rowadd) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= B * C) return;
-  const int b = i / C, c = i % C;
-  float s = bias ? bias[c] : 0.f;
-  for (int j = 0; j < gin; ++j) s += W[(size_t)c * gin + j] * g[(size_t)b * gin + j];
-  rowadd[i] = s;
+// rowadd[b][c] = bias[c] + sum_j W[c][j] * g[b][j]: warp per output channel c (its weight row read
+// once, coalesced), every item's dot product reduced across the lanes.
+__global__ void __launch_bounds__(256) cond_forward_kernel(const float* __restrict__ W, const float* __restrict__ bias,
+                                                           const float* __restrict__ g, int B, int C, int gin,
+                                                           float* __restrict__ rowadd) {
+  const int lane = threadIdx.x & 31;
+  const int c = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (c >= C) return;
+  const float* wr = W + (size_t)c * gin;
+  const float b0 = bias ? bias[c] : 0.f;
+  for (int b = 0; b < B; ++b) {
+    const float* gb = g + (size_t)b * gin;
+    float s = 0.f;
+    for (int j = lane; j < gin; j += 32) s += wr[j] * gb[j];
+    s = warp_sum(s);
+    if (lane == 0) rowadd[(size_t)b * C + c] = b0 + s;
+  }
 }
 
 void cond_forward(const float* W, const float* bias, const float* g, int B, int C, int gin, float* rowadd,
                   cudaStream_t st) {
-  cond_forward_kernel<<<(B * C + 255) / 256, 256, 0, st>>>(W, bias, g, B, C, gin, rowadd);
+  cond_forward_kernel<<<(C + 7) / 8, 256, 0, st>>>(W, bias, g, B, C, gin, rowadd);
 }
 
 __global__ void cond_backward_kernel(const float* __restrict__ part, int tpi, int B, int C, const float* __restrict__ g,
@@ -323,8 +408,11 @@ __global__ void nsf_phase_kernel(const float* __restrict__ f0, int B, int F, int
   for (int f = 0; f < F; ++f) {
     acc[(size_t)b * F + f] = a;  // carry into frame f = fmod(sum of rad2 over frames < f, 1)
     const double rad = (double)f0[(size_t)b * F + f] / (double)sr * (double)upp;
-    const double r2 = fmod(rad + 0.5, 1.0) - 0.5;
-    a = fmod(a + r2, 1.0);
+    // fmod(x, 1) == x - trunc(x) exactly for finite x (the difference is representable)
+    const double x = rad + 0.5;
+    const double r2 = (x - trunc(x)) - 0.5;
+    const double y = a + r2;
+    a = y - trunc(y);
   }
 }
 

@@ -6,31 +6,31 @@ namespace wb {
 
 // ---- weights -------------------------------------------------------------------------------
 // Effective weight W (= g*v/||v|| under weight norm, else the raw parameter) -> bf16 GEMM layouts.
-//   conv  (param [C_out][C_in][k]):  fwd [k][C_out][C_in] hi/lo,  dgrad [k][C_in][C_out] (taps flipped)
-//   convT (param [C_in][C_out][k]):  fwd [k][C_out][C_in] hi/lo in phase order, dgrad [k][C_in][C_out]
-// `norm` receives ||v|| per dim-0 row under weight norm.
-// All weight preparations of a step in one launch: block b handles dim-0 row (b - first[i]) of
-// descriptor i, where first[i] <= b < first[i] + rows.
-// Writes only the row-contiguous layouts [k][rows][cols] (conv: fwd_hi / fwd_lo; ConvTranspose: dg
-// and lo_tmp); the transposed layouts follow from prep_transpose_batched.
+// Storage of a weight is tap-major [k][P][Q] f32 (Q fastest): conv P = C_out, Q = C_in (weight-norm
+// rows are p); ConvTranspose P = C_out, Q = C_in (weight-norm rows are q, the reference's dim 0).
+//   conv : fwd [k][C_out][C_in] hi/lo (the storage layout),   dgrad [k][C_in][C_out], taps flipped
+//   convT: fwd [k][C_out][C_in] hi/lo in polyphase tap order, dgrad [k][C_in][C_out]
+// `norm` receives ||v|| per weight-norm row.  Two launches for all weights of a step:
+//   prep_norm : norms (conv: warp per row; ConvTranspose: partial sums of squares over chunks of
+//               kPrepPairs (tap, p) pairs x 32 columns, summed in fixed order by the tile kernel)
+//   prep_tile : one tap x 32 p x 32*qs q tile per block: scaled hi/lo in the storage layout and the
+//               transposed hi through shared memory, both written coalesced.
+// P and Q must be multiples of 32.
+constexpr int kPrepPairs = 256;
 struct PrepDesc {
-  const float* v;
-  const float* g;
-  bf16 *fwd_hi, *fwd_lo, *dg, *lo_tmp;
-  float* norm;
-  int rows, cols, k, is_convT, stride, first;
+  const float* v;   // [k][P][Q]
+  const float* g;   // weight-norm gains, or null (plain weight)
+  float* norm;      // [rows] ||v|| per weight-norm row (when g)
+  float* npart;     // ConvTranspose under weight norm: [nchunks][Q] partial sums of squares
+  bf16 *fwd_hi, *fwd_lo, *dg;
+  int P, Q, k, is_convT, stride;
+  int qs;           // q columns per lane in the tile kernel (1, 2 or 4)
+  int nchunks;      // ConvTranspose norm chunks
+  int norm_first, tile_first;
 };
-void prep_weights_batched(const PrepDesc* descs, int ndesc, int total_rows, cudaStream_t st);
-
-// bf16 dst[C][R] = src[R][C] for many (src, dst) pairs in one launch; descriptor i owns blocks
-// [first_i, first_i + prep_transpose_blocks(R_i, C_i)).
-struct TransDesc {
-  const bf16* src;
-  bf16* dst;
-  int R, C, first;
-};
-int prep_transpose_blocks(int R, int C);
-void prep_transpose_batched(const TransDesc* descs, int ndesc, int total_blocks, cudaStream_t st);
+int prep_norm_blocks(const PrepDesc& d);
+int prep_tile_blocks(const PrepDesc& d);
+void prep_weights(const PrepDesc* descs, int ndesc, int norm_blocks, int tile_blocks, cudaStream_t st);
 
 // Weight-norm backward of many tensors in one launch (block = one dim-0 row of one tensor).
 struct WnDesc {

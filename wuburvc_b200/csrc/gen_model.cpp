@@ -85,7 +85,6 @@ bool make_weights(Gen& m, ConvWeights& w, const std::string& base, bool resblock
   w.stride = stride;
   const size_t n = (size_t)p.n;
   if (!dalloc(m, &w.fwd_hi, n) || !dalloc(m, &w.fwd_lo, n) || !dalloc(m, &w.dg, n)) return false;
-  if (convT && !dalloc(m, &w.lo_tmp, n)) return false;
   if (wn) {
     if (!dalloc(m, &w.norm, (size_t)w.rows) || !dalloc(m, &w.dW, n)) return false;
   } else {
@@ -635,69 +634,48 @@ bool gen_setup(Gen& m) {
   m.red_scratch_n = (size_t)4 << 20;
   if (!dalloc(m, &m.red_scratch, m.red_scratch_n)) return false;
   if (m.noise_scratch_n && !dalloc(m, &m.noise_scratch, m.noise_scratch_n)) return false;
-  {  // one-launch weight preparation table
+  {  // weight preparation table: every GEMM weight, two launches per step
     std::vector<PrepDesc> d;
-    int first = 0;
-    auto add = [&](const ConvWeights& w) {
+    int nb = 0, tb = 0;
+    auto add = [&](const ConvWeights& w) -> bool {
       PrepDesc p{};
       p.v = m.P(w.pv);
       p.g = w.pg >= 0 ? m.P(w.pg) : nullptr;
+      p.norm = w.norm;
       p.fwd_hi = w.fwd_hi;
       p.fwd_lo = w.fwd_lo;
       p.dg = w.dg;
-      p.lo_tmp = w.lo_tmp;
-      p.norm = w.norm;
-      p.rows = w.rows;
-      p.cols = w.cols;
+      p.P = w.convT ? w.cols : w.rows;
+      p.Q = w.convT ? w.rows : w.cols;
       p.k = w.k;
       p.is_convT = w.convT;
       p.stride = w.stride;
-      p.first = first;
-      first += w.rows;
+      if (p.P % 32 || p.Q % 32) {
+        fprintf(stderr, "wuburvc_b200: weight %d x %d not a multiple of 32 channels\n", p.P, p.Q);
+        return false;
+      }
+      p.qs = p.Q % 128 == 0 ? 4 : p.Q % 64 == 0 ? 2 : 1;
+      p.nchunks = (p.k * p.P + kPrepPairs - 1) / kPrepPairs;
+      if (p.g && p.is_convT && !dalloc(m, &p.npart, (size_t)p.nchunks * p.Q)) return false;
+      p.norm_first = nb;
+      p.tile_first = tb;
+      nb += prep_norm_blocks(p);
+      tb += prep_tile_blocks(p);
       d.push_back(p);
+      return true;
     };
-    add(m.wpre);
+    if (!add(m.wpre)) return false;
     for (int L = 0; L < 4; ++L) {
-      add(m.sg[L].wu);
+      if (!add(m.sg[L].wu)) return false;
       for (int j = 0; j < m.nk; ++j)
-        for (int cp = 0; cp < m.nd; ++cp) {
-          add(m.sg[L].st[j].w1[cp]);
-          add(m.sg[L].st[j].w2[cp]);
-        }
+        for (int cp = 0; cp < m.nd; ++cp)
+          if (!add(m.sg[L].st[j].w1[cp]) || !add(m.sg[L].st[j].w2[cp])) return false;
     }
     m.n_prep = (int)d.size();
-    m.prep_rows = first;
+    m.prep_norm_blocks = nb;
+    m.prep_tile_blocks = tb;
     if (!dalloc(m, &m.prep_descs, d.size())) return false;
     CK(cudaMemcpy(m.prep_descs, d.data(), d.size() * sizeof(PrepDesc), cudaMemcpyHostToDevice));
-    // transposed layouts, one [rows][cols] -> [cols][rows] per tap:
-    //   conv:  dg[k-1-t] = fwd_hi[t]^T;  ConvTranspose: fwd_hi[n(t)] = dg[t]^T, fwd_lo[n(t)] = lo_tmp[t]^T
-    //   with n(t) the tap's place in the polyphase order (phase t % stride, then t / stride)
-    std::vector<TransDesc> td;
-    int tb = 0;
-    for (const PrepDesc& p : d) {
-      const size_t plane = (size_t)p.rows * p.cols;
-      for (int t = 0; t < p.k; ++t) {
-        auto push = [&](const bf16* src, bf16* dst) {
-          TransDesc x{src, dst, p.rows, p.cols, tb};
-          tb += prep_transpose_blocks(p.rows, p.cols);
-          td.push_back(x);
-        };
-        if (!p.is_convT) {
-          push(p.fwd_hi + t * plane, p.dg + (size_t)(p.k - 1 - t) * plane);
-        } else {
-          const int ph = t % p.stride, mm = t / p.stride;
-          int n = 0;
-          for (int q = 0; q < ph; ++q) n += (p.k - q + p.stride - 1) / p.stride;
-          n += mm;
-          push(p.dg + t * plane, p.fwd_hi + (size_t)n * plane);
-          push(p.lo_tmp + t * plane, p.fwd_lo + (size_t)n * plane);
-        }
-      }
-    }
-    m.n_trans = (int)td.size();
-    m.trans_blocks = tb;
-    if (!dalloc(m, &m.trans_descs, td.size())) return false;
-    CK(cudaMemcpy(m.trans_descs, td.data(), td.size() * sizeof(TransDesc), cudaMemcpyHostToDevice));
   }
   return true;
 }
@@ -710,9 +688,8 @@ bool gen_forward(Gen& m) {
   const bool snake = c.activation == 1;
   cudaStream_t st = m.stream;
   set_reduce_scratch(m.red_scratch, m.red_scratch_n);
-  // GEMM weights for this step (weight norm + bf16 hi/lo + transposed layouts), one launch
-  prep_weights_batched(m.prep_descs, m.n_prep, m.prep_rows, st);
-  prep_transpose_batched(m.trans_descs, m.n_trans, m.trans_blocks, st);
+  // GEMM weights for this step (weight norm + bf16 hi/lo + transposed layouts)
+  prep_weights(m.prep_descs, m.n_prep, m.prep_norm_blocks, m.prep_tile_blocks, st);
   pack_z(m.z, m.B, c.in_channels, m.F, m.z_hi, m.z_lo, st);
   if (c.nsf) {
     NsfArgs a{};

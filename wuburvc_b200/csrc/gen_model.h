@@ -19,7 +19,6 @@ struct ConvWeights {
   int rows = 0, cols = 0, k = 0;  // param dims: conv [C_out][C_in][k], convT [C_in][C_out][k]
   int convT = 0, stride = 1;
   bf16 *fwd_hi = nullptr, *fwd_lo = nullptr, *dg = nullptr;
-  bf16* lo_tmp = nullptr;  // ConvTranspose: [k][C_in][C_out] lo half before the transpose into fwd_lo
   float* norm = nullptr;  // ||v|| rows (weight norm)
   float* dW = nullptr;    // gradient in param layout (grad buffer directly, or a temp under weight norm)
 };
@@ -130,10 +129,8 @@ struct Gen {
   int post_blocks = 0;
 
   StageBufs sg[4];
-  PrepDesc* prep_descs = nullptr;  // device table: every GEMM weight's preparation, one launch
-  int n_prep = 0, prep_rows = 0;
-  TransDesc* trans_descs = nullptr;  // the transposed weight layouts, one launch
-  int n_trans = 0, trans_blocks = 0;
+  PrepDesc* prep_descs = nullptr;  // device table: every GEMM weight's preparation
+  int n_prep = 0, prep_norm_blocks = 0, prep_tile_blocks = 0;
   float* red_scratch = nullptr;  // two-pass deterministic reductions
   size_t red_scratch_n = 0;
   float* noise_scratch = nullptr;  // the same for the noise-conv weight gradients (side stream)
