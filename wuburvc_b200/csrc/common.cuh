@@ -39,6 +39,12 @@ WB_DEV void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
 }
 
+// Programmatic dependent launch: let the next kernel of the stream be scheduled (its CTAs start as SMs
+// free up), and wait for the previous kernel's completion and memory before touching its outputs.
+// Both are no-ops for a kernel launched without the programmatic-serialization attribute.
+WB_DEV void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+WB_DEV void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 WB_DEV void fence_barrier_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }

@@ -634,6 +634,17 @@ bool gen_setup(Gen& m) {
   m.red_scratch_n = (size_t)4 << 20;
   if (!dalloc(m, &m.red_scratch, m.red_scratch_n)) return false;
   if (m.noise_scratch_n && !dalloc(m, &m.noise_scratch, m.noise_scratch_n)) return false;
+  // the resblock convolutions read weights and epilogue vectors that no neighbouring kernel writes
+  // (they are prepared at the start of the step): their launches overlap the previous kernel
+  for (int L = 0; L < 4; ++L)
+    for (int j = 0; j < m.nk; ++j)
+      for (int cp = 0; cp < m.nd; ++cp) {
+        StackBufs& k = m.sg[L].st[j];
+        k.f1[cp].set_pdl(true);
+        k.f2[cp].set_pdl(true);
+        k.d1[cp].set_pdl(true);
+        k.d2[cp].set_pdl(true);
+      }
   {  // weight preparation table: every GEMM weight, two launches per step
     std::vector<PrepDesc> d;
     int nb = 0, tb = 0;

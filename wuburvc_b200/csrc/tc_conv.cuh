@@ -104,6 +104,10 @@ struct TcConv2Params {
   int w_resident;           // every weight tap of the CTA's N tile is loaded once and kept
   uint32_t a_sub_bytes;     // one A (hi or lo) halo tile, 1024-aligned
   int tmem_cols;            // 2 accumulators
+  // launched with programmatic stream serialization: the prologue (barriers, TMEM, epilogue vectors,
+  // the first weight stages) overlaps the previous kernel.  Only for callers whose weights and
+  // epilogue vectors are not written by the immediately preceding kernel.
+  int pdl;
   Epi epi;
   int* err;
 };

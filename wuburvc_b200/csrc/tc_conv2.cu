@@ -57,6 +57,7 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
   uint64_t* acc_empty = acc_full + 2;  // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
 
+  griddep_launch_dependents();  // the next kernel may take SMs as this grid's CTAs finish
   if (threadIdx.x == 0) {
     for (int s = 0; s < AS; ++s) { mbar_init(&a_full[s], 1); mbar_init(&a_empty[s], 1); }
     for (int s = 0; s < WS; ++s) { mbar_init(&w_full[s], 1); mbar_init(&w_empty[s], 1); }
@@ -83,6 +84,18 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
     // ---------------- TMA producer ----------------
     bool ok = true;
     const int n0_cta = (blockIdx.x % p.n_tiles) * N;  // every tile of this CTA has this N tile
+    // weight stage u of the CTA's weight sequence (chunk u / ngroups, tap group u % ngroups) into slot s
+    auto load_w = [&](int u, int s) {
+      const int c = u / ngroups, t0 = (u % ngroups) * G, nt = min(G, ntaps - t0);
+      uint8_t* wd = w_base + (size_t)s * w_stage;
+      mbar_expect_tx_warp(&w_full[s], (uint32_t)nt * w_tap);
+      for (int j = 0; j < nt; ++j) {
+        tma_load_3d_warp(wd + j * w_tap, &maps.w_hi, &w_full[s], c * KC, n0_cta, t0 + j);
+        if (SPLIT) tma_load_3d_warp(wd + j * w_tap + w_sub, &maps.w_lo, &w_full[s], c * KC, n0_cta, t0 + j);
+      }
+    };
+    // the weights are not the previous kernel's output: they go out before the dependency wait
+    int w_pre = 0;
     if (resident) {
       mbar_expect_tx_warp(&w_full[0], (uint32_t)(nch * ntaps) * w_tap);
       for (int c = 0; c < nch; ++c)
@@ -91,7 +104,11 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
           tma_load_3d_warp(wd, &maps.w_hi, &w_full[0], c * KC, n0_cta, t);
           if (SPLIT) tma_load_3d_warp(wd + w_sub, &maps.w_lo, &w_full[0], c * KC, n0_cta, t);
         }
+    } else if (blockIdx.x < p.ntiles) {
+      w_pre = min(WS, nch * ngroups);
+      for (int u = 0; u < w_pre; ++u) load_w(u, u);
     }
+    griddep_wait();
     int sa = 0, sw = 0;
     uint32_t aph = 0, wph = 0;
     int a_uses = 0, w_uses = 0;
@@ -112,16 +129,13 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
         if (++sa == AS) { sa = 0; aph ^= 1u; }
         if (resident) continue;
         for (int g = 0; g < ngroups; ++g) {
-          const int t0 = g * G, nt = min(G, ntaps - t0);
-          if (ok && w_uses >= WS) ok = mbar_wait_warp(&w_empty[sw], wph ^ 1u, p.err, ERR_WAIT_EMPTY);
-          if (ok) {
-            uint8_t* wd = w_base + (size_t)sw * w_stage;
-            mbar_expect_tx_warp(&w_full[sw], (uint32_t)nt * w_tap);
-            for (int j = 0; j < nt; ++j) {
-              tma_load_3d_warp(wd + j * w_tap, &maps.w_hi, &w_full[sw], c * KC, n0_cta, t0 + j);
-              if (SPLIT) tma_load_3d_warp(wd + j * w_tap + w_sub, &maps.w_lo, &w_full[sw], c * KC, n0_cta, t0 + j);
-            }
+          if (w_uses < w_pre) {  // issued before the dependency wait
+            ++w_uses;
+            if (++sw == WS) { sw = 0; wph ^= 1u; }
+            continue;
           }
+          if (ok && w_uses >= WS) ok = mbar_wait_warp(&w_empty[sw], wph ^ 1u, p.err, ERR_WAIT_EMPTY);
+          if (ok) load_w(c * ngroups + g, sw);
           ++w_uses;
           if (++sw == WS) { sw = 0; wph ^= 1u; }
         }
@@ -207,6 +221,7 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
   } else {
     // ---------------- epilogue: two groups of 4 warps; group g drains TMEM accumulator g, i.e. every
     // other tile, so two tiles' epilogues run concurrently (warp w reads TMEM lane quadrant w%4) ----------------
+    griddep_wait();  // the epilogue inputs and outputs belong to the previous kernels' data
     const int qw = warp & 3, grp = warp >> 2;
     const Epi& e = p.epi;
     const int n0 = (blockIdx.x % p.n_tiles) * N;  // every tile of this CTA has this N tile
@@ -327,23 +342,34 @@ cudaError_t launch_tc_conv2(const TcConv2Maps& maps, const TcConv2Params& p, int
   const bool split = p.split != 0;
   const uint32_t f = epi_features(p.epi);
   bool done = false;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(kConv2Threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = p.pdl ? 1 : 0;
+  cudaError_t err = cudaSuccess;
 #define WB_LAUNCH(kc_, sp, f_)                                                                     \
   if (!done && kc == kc_ && split == sp && f == (f_)) {                                             \
-    tc_conv2_kernel<kc_, sp, f_><<<grid, kConv2Threads, smem, st>>>(maps, p);                      \
+    err = cudaLaunchKernelEx(&cfg, tc_conv2_kernel<kc_, sp, f_>, maps, p);                         \
     done = true;                                                                                   \
   }
   WB_CONV2_KERNELS(WB_LAUNCH)
 #undef WB_LAUNCH
   if (!done) {  // any other epilogue: the generic instantiation
     if (kc == 64) {
-      if (split) tc_conv2_kernel<64, true, kEpiGeneric><<<grid, kConv2Threads, smem, st>>>(maps, p);
-      else tc_conv2_kernel<64, false, kEpiGeneric><<<grid, kConv2Threads, smem, st>>>(maps, p);
+      if (split) err = cudaLaunchKernelEx(&cfg, tc_conv2_kernel<64, true, kEpiGeneric>, maps, p);
+      else err = cudaLaunchKernelEx(&cfg, tc_conv2_kernel<64, false, kEpiGeneric>, maps, p);
     } else {
-      if (split) tc_conv2_kernel<32, true, kEpiGeneric><<<grid, kConv2Threads, smem, st>>>(maps, p);
-      else tc_conv2_kernel<32, false, kEpiGeneric><<<grid, kConv2Threads, smem, st>>>(maps, p);
+      if (split) err = cudaLaunchKernelEx(&cfg, tc_conv2_kernel<32, true, kEpiGeneric>, maps, p);
+      else err = cudaLaunchKernelEx(&cfg, tc_conv2_kernel<32, false, kEpiGeneric>, maps, p);
     }
   }
-  return cudaGetLastError();
+  return err != cudaSuccess ? err : cudaGetLastError();
 }
 
 }  // namespace wb
