@@ -39,10 +39,11 @@ WB_DEV void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
 }
 
-// Programmatic dependent launch: let the next kernel of the stream be scheduled (its CTAs start as SMs
-// free up), and wait for the previous kernel's completion and memory before touching its outputs.
-// Both are no-ops for a kernel launched without the programmatic-serialization attribute.
-WB_DEV void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+// Programmatic dependent launch: a kernel launched with programmatic stream serialization may start
+// before its predecessor has finished (the predecessor's CTAs let it in as they exit); it waits here
+// for the predecessor's completion and memory before touching the predecessor's outputs.  A no-op for
+// a kernel launched without the attribute.  (An explicit early trigger in the predecessors measured
+// no faster and slower for the multi-wave kernels, so none is issued.)
 WB_DEV void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 WB_DEV void fence_barrier_init() {

@@ -50,7 +50,10 @@ struct ConvOp {
   // rows of the [partials][C] column-sum buffers this launch writes (one per CTA or per tile)
   int partials() const { return v2 ? 2 * c2.grid : (int)(v1.grid.x * v1.grid.z); }
   // programmatic dependent launch for the persistent kernel (see TcConv2Params::pdl)
-  void set_pdl(bool on) { c2.p.pdl = on ? 1 : 0; }
+  void set_pdl(bool on) {
+    c2.p.pdl = on ? 1 : 0;
+    v1.p.pdl = on ? 1 : 0;
+  }
   // re-points the epilogue's column-sum partial buffer
   void set_colsum(float* p) {
     v1.p.epi.colsum = p;

@@ -634,17 +634,27 @@ bool gen_setup(Gen& m) {
   m.red_scratch_n = (size_t)4 << 20;
   if (!dalloc(m, &m.red_scratch, m.red_scratch_n)) return false;
   if (m.noise_scratch_n && !dalloc(m, &m.noise_scratch, m.noise_scratch_n)) return false;
-  // the resblock convolutions read weights and epilogue vectors that no neighbouring kernel writes
-  // (they are prepared at the start of the step): their launches overlap the previous kernel
-  for (int L = 0; L < 4; ++L)
+  // Programmatic dependent launch for the tensor-core kernels of the step: each waits for its
+  // predecessor before touching activations; the persistent resblock kernels also load their weights
+  // and epilogue vectors first (prepared at the start of the step, written by no neighbouring kernel)
+  for (int L = 0; L < 4; ++L) {
+    StageBufs& s = m.sg[L];
     for (int j = 0; j < m.nk; ++j)
       for (int cp = 0; cp < m.nd; ++cp) {
-        StackBufs& k = m.sg[L].st[j];
+        StackBufs& k = s.st[j];
         k.f1[cp].set_pdl(true);
         k.f2[cp].set_pdl(true);
         k.d1[cp].set_pdl(true);
         k.d2[cp].set_pdl(true);
+        k.g1[cp].L.p.pdl = 1;
+        k.g2[cp].L.p.pdl = 1;
       }
+    s.up_fwd.p.pdl = 1;
+    s.up_dg.p.pdl = 1;
+    s.up_wg.L.p.pdl = 1;
+  }
+  m.pre_fwd.p.pdl = 1;
+  m.pre_wg.L.p.pdl = 1;
   {  // weight preparation table: every GEMM weight, two launches per step
     std::vector<PrepDesc> d;
     int nb = 0, tb = 0;

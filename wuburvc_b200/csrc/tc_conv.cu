@@ -45,6 +45,7 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  griddep_wait();  // every global read and write below follows the previous kernel
 
   // producer / MMA: converged warps, elect.sync issue, warp-uniform `ok` (no early exits)
   if (warp == 4) {
@@ -203,6 +204,7 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  griddep_wait();  // every global read and write below follows the previous kernel
 
   if (warp == 4) {
     // ---------------- TMA producer ----------------
@@ -330,6 +332,7 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  griddep_wait();  // every global read and write below follows the previous kernel
 
   if (warp == 4) {
     // ---------------- TMA producer ----------------
@@ -443,21 +446,37 @@ static void raise_smem_limits() {
 
 void tc_kernels_init() { raise_smem_limits(); }
 
+namespace {
+// launch with programmatic stream serialization when `pdl` (the kernels wait for the previous one
+// before their first global access)
+template <typename K, typename M, typename P>
+cudaError_t launch_192(K kernel, const M& maps, const P& p, dim3 grid, size_t smem, cudaStream_t st, int pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, maps, p);
+  return e != cudaSuccess ? e : cudaGetLastError();
+}
+}  // namespace
+
 cudaError_t launch_tc_conv(const TcMaps& maps, const TcConvParams& p, int kc, dim3 grid, size_t smem,
                            cudaStream_t st) {
   raise_smem_limits();
-  if (kc == 64)
-    tc_conv_kernel<64><<<grid, 192, smem, st>>>(maps, p);
-  else
-    tc_conv_kernel<32><<<grid, 192, smem, st>>>(maps, p);
-  return cudaGetLastError();
+  if (kc == 64) return launch_192(tc_conv_kernel<64>, maps, p, grid, smem, st, p.pdl);
+  return launch_192(tc_conv_kernel<32>, maps, p, grid, smem, st, p.pdl);
 }
 
 cudaError_t launch_tc_wgrad(const TcWgMaps& maps, const TcWgParams& p, dim3 grid, size_t smem, cudaStream_t st) {
   raise_smem_limits();
-  if (p.halo) tc_wgrad_halo_kernel<<<grid, 192, smem, st>>>(maps, p);
-  else tc_wgrad_kernel<<<grid, 192, smem, st>>>(maps, p);
-  return cudaGetLastError();
+  if (p.halo) return launch_192(tc_wgrad_halo_kernel, maps, p, grid, smem, st, p.pdl);
+  return launch_192(tc_wgrad_kernel, maps, p, grid, smem, st, p.pdl);
 }
 
 }  // namespace wb

@@ -69,6 +69,7 @@ struct TcConvParams {
   signed char tap_map[kMaxTapList];
   short tap_shift[kMaxTapList];
   short tap_w[kMaxTapList];
+  int pdl;             // launched with programmatic stream serialization
   Epi epi;
   int* err;
 };
@@ -148,6 +149,7 @@ struct TcWgParams {
   // (SW128 MN-major) and every tap reads it at its own row offset.
   // blockIdx.x = tap_group * oc_chunks + oc chunk.  Partial rows stay tap * c_out + oc.
   int halo, tg, ntaps, dil, pad, oc_chunks, halo_rows;
+  int pdl;             // launched with programmatic stream serialization
 };
 
 }  // namespace wb

@@ -57,7 +57,6 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
   uint64_t* acc_empty = acc_full + 2;  // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
 
-  griddep_launch_dependents();  // the next kernel may take SMs as this grid's CTAs finish
   if (threadIdx.x == 0) {
     for (int s = 0; s < AS; ++s) { mbar_init(&a_full[s], 1); mbar_init(&a_empty[s], 1); }
     for (int s = 0; s < WS; ++s) { mbar_init(&w_full[s], 1); mbar_init(&w_empty[s], 1); }
