@@ -389,48 +389,69 @@ size_t wgrad_part_floats(const WgradLaunch& L) {
   return (size_t)L.splits * L.p.n_mtiles * 128 * L.p.n_total;
 }
 
-// Halo-mode weight gradient (C_out % 128 == 0): see TcWgParams.  tg = 2 taps per CTA (at most
-// 512 / n_in accumulator columns); K blocks of 128 time rows; the halo tile of 128 channels x
-// R rows arrives as two SW128 boxes of 64 channels.
+// Halo-mode weight gradient (stride 1): see TcWgParams.  K blocks of 128 time rows.
+//   C_out % 128 == 0: tg = 2 taps per CTA (at most 512 / n_in accumulator columns); the halo tile of
+//     128 channels x R rows arrives as two SW128 boxes of 64 channels.
+//   C_out 32 / 64: pack = 128 / C_out taps per accumulator, at most 4 accumulators (and 512 / n_in
+//     columns) per CTA, the taps spread evenly over tap groups; one halo box of C_out channels
+//     (SW64 / SW128).
 static bool plan_wgrad_halo(WgradLaunch& L, const ConvGeom& g, const void* dy, const void* x, float* part, size_t cap,
                             int target_ctas, int* err) {
   TcWgParams& p = L.p;
   int n_tile = std::min(g.C_in, 256);
   while (g.C_in % n_tile) n_tile -= 16;
-  if (n_tile % 64) return false;
-  const int tg = std::min(2, 512 / n_tile);  // 2 taps per CTA: more CTAs per split, smaller partials
+  const int x_atom = n_tile % 64 == 0 ? 64 : 32;
+  if (n_tile % x_atom) return false;
+  const int pack = g.C_out % 128 == 0 ? 1 : (g.C_out == 32 || g.C_out == 64) ? 128 / g.C_out : 0;
+  if (!pack) return false;
+  int nacc;
+  if (pack == 1) {
+    nacc = std::min(2, 512 / n_tile);  // 2 taps per CTA: more CTAs per split, smaller partials
+  } else {
+    // at most 4 accumulators per CTA (more tap groups instead: smaller split-K partials), balanced
+    const int need = (g.k + pack - 1) / pack;
+    const int groups = (need + 3) / 4;
+    nacc = std::min((need + groups - 1) / groups, 512 / n_tile);
+  }
+  const int tg = nacc * pack;
   const int kr = 128;  // K block rows; the halo kernel is compiled for 128 (kHaloKR)
-  const int R = (kr + (tg - 1) * g.dil + 7) / 8 * 8;
+  // halo rows: whole 1 KB swizzle periods (8 rows of 128 B, 16 rows of 64 B)
+  const int rq = (pack == 1 || g.C_out == 64) ? 8 : 16;
+  const int R = (kr + (tg - 1) * g.dil + rq - 1) / rq * rq;
   if (R > 256) return false;
   p.halo = 1;
+  p.pack = pack;
+  p.nacc = nacc;
   p.tg = tg;
+  p.x_atom = x_atom;
   p.ntaps = g.k;
   p.dil = g.dil;
   p.pad = g.pad;
-  p.oc_chunks = g.C_out / 128;
+  p.oc_chunks = pack == 1 ? g.C_out / 128 : 1;
   p.halo_rows = R;
   p.n_in = n_tile;
   p.n_total = g.C_in;
-  p.n_atoms = n_tile / 64;
+  p.n_atoms = n_tile / x_atom;
   p.c_out = g.C_out;
   p.t_rows = g.T_in;
   p.kb_rows = kr;
   p.kb_group = 1;
   p.kblocks_per_item = (g.T_in + kr - 1) / kr;
   p.total_kblocks = g.B * p.kblocks_per_item;
-  p.n_mtiles = g.k * g.C_out / 128;  // partial rows: tap * C_out + oc
+  p.n_mtiles = (g.k * g.C_out + 127) / 128;  // partial rows: tap * C_out + oc
   const int tap_groups = (g.k + tg - 1) / tg;
   const int n_ntiles = g.C_in / n_tile;
   const int base = tap_groups * p.oc_chunks * n_ntiles;
   int splits = std::max(1, std::min(p.total_kblocks, (target_ctas + base - 1) / base));
   p.kb_per_split = (p.total_kblocks + splits - 1) / splits;
   splits = (p.total_kblocks + p.kb_per_split - 1) / p.kb_per_split;
-  const size_t stage = (size_t)128 * R * 2 + (size_t)n_tile * kr * 2;
+  const size_t a_bytes = (size_t)(pack == 1 ? 128 : g.C_out) * R * 2;
+  const size_t stage = a_bytes + (size_t)n_tile * kr * 2;
   const size_t room = kSmemBudget - 1024 - 256;
-  p.stages = (int)std::min<size_t>(3, room / stage);
+  p.stages = (int)std::min<size_t>(pack == 1 ? 3 : 4, room / stage);
   if (p.stages < 2) return false;
   L.smem = p.stages * stage + 1024 + 256;
-  p.tmem_cols = pow2_cols(tg * n_tile);
+  p.tmem_cols = pow2_cols(nacc * n_tile);
   if (p.tmem_cols > 512) return false;
   p.err = err;
   p.part = part;
@@ -439,23 +460,24 @@ static bool plan_wgrad_halo(WgradLaunch& L, const ConvGeom& g, const void* dy, c
   if ((size_t)splits * p.n_mtiles * 128 * g.C_in > cap) return false;
   L.row_tap.assign((size_t)p.n_mtiles * 128, -1);
   L.row_oc.assign((size_t)p.n_mtiles * 128, 0);
-  for (int r = 0; r < p.n_mtiles * 128; ++r) {
+  for (int r = 0; r < g.k * g.C_out; ++r) {
     L.row_tap[r] = r / g.C_out;
     L.row_oc[r] = r % g.C_out;
   }
-  // dOut halo: (C_out, T, B) with a 64-channel x R-row SW128 box (two per 128-channel chunk)
+  // dOut halo: (C_out, T, B) with a 64-channel (or, packed, C_out-channel) x R-row box
   if (!make_map_bf16_3d(&L.maps.d[0], dy, g.C_out, g.T_out, g.B, (uint64_t)g.C_out * 2,
-                        (uint64_t)g.C_out * 2 * g.T_out, 64, R, 1))
+                        (uint64_t)g.C_out * 2 * g.T_out, pack == 1 ? 64 : g.C_out, R, 1))
     return false;
   return make_map_bf16_3d(&L.maps.x, x, g.C_in, g.T_in, g.B, (uint64_t)g.C_in * 2, (uint64_t)g.C_in * 2 * g.T_in,
-                          64, kr, 1);
+                          x_atom, kr, 1);
 }
 
 bool plan_wgrad(WgradLaunch& L, const ConvGeom& g, const void* dy, const void* x, float* part, size_t cap,
                 int target_ctas, int* err) {
   memset(&L.p, 0, sizeof(L.p));
   memset(&L.maps, 0, sizeof(L.maps));
-  if (g.C_out % 128 == 0 && g.T_in == g.T_out && !getenv("WUBU_B200_WGRAD_ATOMS")) {
+  if ((g.C_out % 128 == 0 || g.C_out == 32 || g.C_out == 64) && g.T_in == g.T_out &&
+      !getenv("WUBU_B200_WGRAD_ATOMS")) {
     // a halo CTA carries tg taps' MMAs per K block: half the CTAs keep the split-K partials small
     if (plan_wgrad_halo(L, g, dy, x, part, cap, std::max(1, target_ctas / 2), err)) return true;
     memset(&L.p, 0, sizeof(L.p));

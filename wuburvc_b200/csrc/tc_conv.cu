@@ -292,21 +292,29 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 // ---------------------------------------------------------------------------------------------
-// tc_wgrad halo kernel (see TcWgParams): CTA = 128 output channels x tg taps x n_in input channels;
-// per K block of kb_rows time rows one dOut halo (two SW128 MN-major atoms of 64 channels x R rows)
-// and one activation tile (SW128 MN-major atoms of 64 channels); tap t's A operand starts
-// (tg - 1 - (t - tb)) * dil rows into the halo.
+// tc_wgrad halo kernel (see TcWgParams): per K block of kb_rows time rows ONE dOut halo (the CTA's
+// channels x R rows) and one activation tile (MN-major atoms of 64 or 32 channels).
+//   pack == 1: CTA = 128 output channels (two SW128 atoms of 64) x tg taps, one accumulator per tap;
+//     tap tb + j reads the halo from row (tg - 1 - j) * dil.
+//   pack > 1 : CTA = all C_out channels x tg = nacc * pack taps.  Accumulator j holds taps
+//     tb + j*pack .. tb + j*pack + pack - 1 in its M atoms pack-1 .. 0 (atom a at halo row
+//     (tg - pack*(j+1) + a) * dil): one MMA per K16 step covers `pack` taps.
+// Every view stays inside the halo: its last row is (tg-1)*dil + kb_rows - 1 < R.
 // ---------------------------------------------------------------------------------------------
 constexpr int kHaloKR = 128;  // time rows per K block of the halo weight gradient
 
+template <bool PACKED>
 __global__ void __launch_bounds__(192, 1)
     tc_wgrad_halo_kernel(const __grid_constant__ TcWgMaps maps, const __grid_constant__ TcWgParams p) {
+  constexpr int kMaxAcc = PACKED ? 8 : 2;  // accumulators per CTA (the planner's limits)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int pack = PACKED ? p.pack : 1, tg = p.tg;
   const int oc0 = (blockIdx.x % p.oc_chunks) * 128;
-  const int tb = (blockIdx.x / p.oc_chunks) * p.tg;  // first tap of this CTA
-  const int nt = min(p.tg, p.ntaps - tb);
+  const int tb = (blockIdx.x / p.oc_chunks) * tg;  // first tap of this CTA
+  // accumulators holding at least one real tap
+  const int nacc = min(p.nacc, (p.ntaps - tb + pack - 1) / pack);
   const int split = blockIdx.y;
   const int nbase = blockIdx.z * p.n_in;
   const int kb0 = split * p.kb_per_split;
@@ -314,8 +322,11 @@ __global__ void __launch_bounds__(192, 1)
   const int nkb = max(0, kb1 - kb0);
   const int S = p.stages;
   const int KR = kHaloKR, R = p.halo_rows, N = p.n_in;
-  const uint32_t a_bytes = 128u * (uint32_t)R * 2u;
-  const uint32_t atom_b_bytes = (uint32_t)KR * 64u * 2u;
+  // one M atom's halo row: 128 B (64 channels) or, packed, C_out * 2 B
+  const uint32_t a_row = PACKED ? (uint32_t)p.c_out * 2u : 128u;
+  const uint32_t a_bytes = (PACKED ? a_row : 256u) * (uint32_t)R;
+  const uint32_t x_row = (uint32_t)p.x_atom * 2u;
+  const uint32_t atom_b_bytes = (uint32_t)KR * x_row;
   const uint32_t b_bytes = (uint32_t)N * (uint32_t)KR * 2u;
   const uint32_t stage_bytes = a_bytes + b_bytes;
 
@@ -347,23 +358,31 @@ __global__ void __launch_bounds__(192, 1)
         const int t0 = (kb - item * p.kblocks_per_item) * KR;
         uint8_t* st = smem + (size_t)s * stage_bytes;
         mbar_expect_tx_warp(&full[s], stage_bytes);
-        // dOut rows t0 + pad - (tb + tg - 1) * dil ... : every tap's window, once (two 64-channel atoms)
-        const int hr = t0 + p.pad - (tb + p.tg - 1) * p.dil;
-        tma_load_3d_warp(st, &maps.d[0], &full[s], oc0, hr, item);
-        tma_load_3d_warp(st + a_bytes / 2, &maps.d[0], &full[s], oc0 + 64, hr, item);
+        // dOut rows t0 + pad - (tb + tg - 1) * dil ... : every tap's window, once
+        const int hr = t0 + p.pad - (tb + tg - 1) * p.dil;
+        if (!PACKED) {  // two 64-channel atoms
+          tma_load_3d_warp(st, &maps.d[0], &full[s], oc0, hr, item);
+          tma_load_3d_warp(st + a_bytes / 2, &maps.d[0], &full[s], oc0 + 64, hr, item);
+        } else {
+          tma_load_3d_warp(st, &maps.d[0], &full[s], 0, hr, item);
+        }
         for (int j = 0; j < p.n_atoms; ++j)
-          tma_load_3d_warp(st + a_bytes + j * atom_b_bytes, &maps.x, &full[s], nbase + j * 64, t0, item);
+          tma_load_3d_warp(st + a_bytes + j * atom_b_bytes, &maps.x, &full[s], nbase + j * p.x_atom, t0, item);
       }
       if (++s == S) { s = 0; ph ^= 1u; }
     }
   } else if (warp == 5) {
     // ---------------- MMA issuer ----------------
     const uint32_t idesc = make_idesc_bf16(128, N, 1, 1);
-    // A: SW128 MN-major atoms of 64 channels x R time rows (128-byte rows, next atom at LBO = R * 128 B,
-    // 8-row groups at SBO = 1024 B); the swizzle follows the absolute address, so a tap's operand is
-    // the atom started (tg - 1 - j) * dil rows in.  B: SW128 MN-major atoms of 64 channels x KR rows.
-    const uint64_t da0 = make_sdesc(smem_u32(smem), (uint32_t)R * 128u, 1024, 2);
-    const uint64_t db0 = make_sdesc(smem_u32(smem) + a_bytes, atom_b_bytes, 1024, 2);
+    // A: MN-major swizzled atoms (128-B rows: SW128, 8-row groups 1 KB apart; 64-B rows: SW64, 512 B),
+    // the next M atom at LBO (the other 64 channels, or the next tap dil rows on).  The swizzle
+    // follows the absolute address, so a view may start at any row.  B: MN-major atoms of x_atom
+    // channels x KR rows.
+    const uint32_t a_layout = a_row == 128u ? 2u : 4u, b_layout = x_row == 128u ? 2u : 4u;
+    const uint32_t a_lbo = PACKED ? (uint32_t)p.dil * a_row : (uint32_t)R * 128u;
+    const uint64_t da0 = make_sdesc(smem_u32(smem), a_lbo, a_row * 8u, a_layout);
+    const uint64_t db0 = make_sdesc(smem_u32(smem) + a_bytes, atom_b_bytes, x_row * 8u, b_layout);
+    const uint32_t a_k16 = a_row, b_k16 = x_row;  // K16 step = 16 rows, in 16-byte units
     bool ok = true;
     int s = 0;
     uint32_t ph = 0;
@@ -371,15 +390,15 @@ __global__ void __launch_bounds__(192, 1)
       if (ok) ok = mbar_wait_warp(&full[s], ph, p.err, ERR_WAIT_FULL);
       if (ok) {
         const uint32_t sb = ((uint32_t)s * stage_bytes) >> 4;
-        // straight-line issue: K blocks are kHaloKR rows, at most 4 taps
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          if (j < nt) {
-            const uint32_t toff = (uint32_t)((p.tg - 1 - j) * p.dil) * 8u;  // rows of 128 B, in 16-B units
+        for (int j = 0; j < kMaxAcc; ++j) {
+          if (j < nacc) {
+            const int row = PACKED ? (tg - pack * (j + 1)) * p.dil : (tg - 1 - j) * p.dil;
+            const uint32_t toff = (uint32_t)row * (a_row >> 4);
             const uint32_t d = tmem + (uint32_t)(j * N);
 #pragma unroll
-            for (int k = 0; k < kHaloKR / 16; ++k)  // K16 step = 16 rows = 2048 B
-              umma_f16_warp(d, da0 + sb + toff + (uint32_t)k * 128u, db0 + sb + (uint32_t)k * 128u, idesc,
+            for (int k = 0; k < kHaloKR / 16; ++k)
+              umma_f16_warp(d, da0 + sb + toff + (uint32_t)k * a_k16, db0 + sb + (uint32_t)k * b_k16, idesc,
                             (i | k) != 0);
           }
         }
@@ -389,12 +408,23 @@ __global__ void __launch_bounds__(192, 1)
     }
     if (ok) umma_commit_warp(accf);
   } else {
-    // ---------------- epilogue: 4 warps, TMEM lane quadrant = warp; one partial row block per tap ----------------
+    // ---------------- epilogue: 4 warps, TMEM lane quadrant = warp; 32 partial rows per accumulator ----------------
     const bool ok = nkb > 0 ? mbar_wait_warp(accf, 0, p.err, ERR_WAIT_ACC) : true;
     tc_fence_after();
     uint4* stage = reinterpret_cast<uint4*>(smem) + warp * 128;  // pipeline buffers are idle now
-    for (int j = 0; j < nt; ++j) {
-      const size_t row0 = (size_t)split * p.n_mtiles * 128 + (size_t)(tb + j) * p.c_out + oc0 + warp * 32;
+    for (int j = 0; j < nacc; ++j) {
+      // accumulator row m = 32 * warp + lane: tap and output channel
+      int tap, oc;
+      if (!PACKED) {
+        tap = tb + j;
+        oc = oc0 + warp * 32;
+      } else {
+        const int ap = (warp * 32) / p.c_out;
+        tap = tb + j * pack + pack - 1 - ap;
+        oc = (warp * 32) % p.c_out;
+      }
+      if (tap >= p.ntaps) continue;  // warp-uniform
+      const size_t row0 = (size_t)split * p.n_mtiles * 128 + (size_t)tap * p.c_out + oc;
       char* dst = reinterpret_cast<char*>(p.part + row0 * p.n_total + nbase);
       for (int c0 = 0; c0 < N; c0 += 32) {
         float v[32];
@@ -436,8 +466,10 @@ static void raise_smem_limits() {
   e[0] = cudaFuncSetAttribute(tc_conv_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
   e[1] = cudaFuncSetAttribute(tc_conv_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
   e[2] = cudaFuncSetAttribute(tc_wgrad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
-  const cudaError_t eh = cudaFuncSetAttribute(tc_wgrad_halo_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
-  if (eh != cudaSuccess) fprintf(stderr, "wuburvc_b200: smem limit (wgrad halo): %s\n", cudaGetErrorString(eh));
+  for (const void* k : {(const void*)tc_wgrad_halo_kernel<false>, (const void*)tc_wgrad_halo_kernel<true>}) {
+    const cudaError_t eh = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    if (eh != cudaSuccess) fprintf(stderr, "wuburvc_b200: smem limit (wgrad halo): %s\n", cudaGetErrorString(eh));
+  }
   for (int i = 0; i < 3; ++i)
     if (e[i] != cudaSuccess) fprintf(stderr, "wuburvc_b200: smem limit %d: %s\n", i, cudaGetErrorString(e[i]));
   tc_conv2_set_smem_limit(lim);
@@ -475,7 +507,8 @@ cudaError_t launch_tc_conv(const TcMaps& maps, const TcConvParams& p, int kc, di
 
 cudaError_t launch_tc_wgrad(const TcWgMaps& maps, const TcWgParams& p, dim3 grid, size_t smem, cudaStream_t st) {
   raise_smem_limits();
-  if (p.halo) return launch_192(tc_wgrad_halo_kernel, maps, p, grid, smem, st, p.pdl);
+  if (p.halo && p.pack > 1) return launch_192(tc_wgrad_halo_kernel<true>, maps, p, grid, smem, st, p.pdl);
+  if (p.halo) return launch_192(tc_wgrad_halo_kernel<false>, maps, p, grid, smem, st, p.pdl);
   return launch_192(tc_wgrad_kernel, maps, p, grid, smem, st, p.pdl);
 }
 

@@ -144,11 +144,17 @@ struct TcWgParams {
   short atom_tap[64][4];         // tap index (for the partial layout); -1 = unused atom
   float* part;                   // [split][n_mtiles*128][n_total] fp32 partials
   int* err;
-  // halo mode (C_out a multiple of 128, stride-1 conv): a CTA owns 128 output channels x `tg` taps,
-  // one TMEM accumulator per tap; the dOut halo of a K block (kb_rows + (tg-1)*dil rows) is loaded once
-  // (SW128 MN-major) and every tap reads it at its own row offset.
+  // halo mode (stride-1 conv): the dOut halo of a K block (kb_rows + (tg-1)*dil rows of the CTA's
+  // channels) is loaded once and every tap reads it at its own row offset.
+  //   pack == 1 (C_out a multiple of 128): a CTA owns 128 output channels x `tg` taps, one TMEM
+  //     accumulator per tap; the 128 channels are two SW128 MN-major atoms of 64 (LBO = halo bytes).
+  //   pack == 128 / C_out (C_out 32 or 64): the M = 128 rows of one accumulator are `pack` taps x all
+  //     C_out channels: the M atoms are the same halo started dil rows apart (LBO = dil rows), so one
+  //     MMA covers `pack` taps; `nacc` accumulators, tg = nacc * pack taps per CTA.
   // blockIdx.x = tap_group * oc_chunks + oc chunk.  Partial rows stay tap * c_out + oc.
   int halo, tg, ntaps, dil, pad, oc_chunks, halo_rows;
+  int pack, nacc;
+  int x_atom;          // channels per activation (B) atom: 64 (SW128) or 32 (SW64)
   int pdl;             // launched with programmatic stream serialization
 };
 
