@@ -37,6 +37,10 @@ CONV_CASES = [
     (1, 128, 256, 128, 11, 1),
     (2, 256, 160, 256, 3, 5),
     (1, 192, 40, 512, 7, 1),
+    # unequal channel counts and a single tap (the tap-packed weight gradient for 32 / 64 outputs)
+    (1, 64, 333, 32, 5, 2),
+    (2, 128, 190, 64, 9, 1),
+    (1, 32, 129, 64, 1, 1),
 ]
 
 
