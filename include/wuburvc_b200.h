@@ -9,6 +9,8 @@
  *                                                          + wubu_b200_conv1d_wgrad
  *       k_convt1d       src/wubu_rvc_cuda.cu:55-78      -> wubu_b200_convT
  *       tk_convt1d_bwd  src/wubu_train_cuda.cu:107-135  -> wubu_b200_convT_dgrad + wubu_b200_convT_wgrad
+ *     and the spectral loss gradient of the host trainer:
+ *       wubu_stft_loss_grad  src/wubu_train.c:318-446    -> wubu_b200_stft_loss_grad
  *
  *  2. The generator training step (wubu_b200_gen_*): forward, backward and the fused AdamW
  *     update over one flat parameter buffer, replacing wubu_train_forward_cuda /
@@ -81,6 +83,14 @@ int wubu_b200_convT_dgrad(const void* dy, const void* wd, float* dx, int B, int 
  *   Replaces the dw part of tk_convt1d_bwd (src/wubu_train_cuda.cu:107-135). */
 int wubu_b200_convT_wgrad(const void* x, const void* dy, float* dw, int B, int C_in, int T_in,
                           int C_out, int k, int stride, int pad, void* stream);
+
+/* Multi-scale STFT spectral loss (linear + log magnitude, windows 512/256/128, hop w/4) and its
+ * gradient with respect to the first signal, for B signal pairs of n samples (device fp32
+ * buffers [B][n]): loss[b] and grad[b][n].  n_scales <= 0 means 3.  Same loss and gradient as
+ * wubu_stft_loss_grad (src/wubu_train.c:318-446, called by wubu_train_step at :1156-1178), which
+ * it replaces for batches on the device; deterministic. */
+int wubu_b200_stft_loss_grad(const float* a, const float* b, int B, int n, int n_scales, float* grad,
+                             float* loss, void* stream);
 
 /* ---------------------------------------------------------------------------------------
  * 2. generator training step

@@ -18,7 +18,7 @@ import numpy as np
 from . import model
 from ._lib import LibraryMissing, check, lib
 
-__all__ = ["GenConfig", "param_table", "init_params", "Generator", "LibraryMissing", "model"]
+__all__ = ["GenConfig", "param_table", "init_params", "Generator", "LibraryMissing", "model", "stft_loss_grad"]
 
 
 class GenConfig(ctypes.Structure):
@@ -173,6 +173,28 @@ def bucket_plan(cfg: dict) -> List[Tuple[int, int]]:
         out.append((prev, int(ends[i])))
         prev = int(ends[i])
     return out
+
+
+def stft_loss_grad(a, b, n_scales: int = 3):
+    """Multi-scale STFT spectral loss (windows 512/256/128) of B signal pairs and its gradient with
+    respect to ``a`` (the reference's wubu_stft_loss_grad, src/wubu_train.c:318-446, batched on the
+    device).  ``a`` and ``b``: CUDA float32 tensors [B][n] (or [n]).  Returns (loss [B], grad)."""
+    import torch
+
+    if not (a.is_cuda and b.is_cuda) or a.shape != b.shape:
+        raise ValueError("a and b: CUDA tensors of the same shape")
+    squeeze = a.dim() == 1
+    a2 = a.reshape(1, -1) if squeeze else a
+    b2 = b.reshape(1, -1) if squeeze else b
+    a2 = a2.to(torch.float32).contiguous()
+    b2 = b2.to(torch.float32).contiguous()
+    B, n = a2.shape
+    grad = torch.empty_like(a2)
+    loss = torch.empty(B, device=a2.device, dtype=torch.float32)
+    stream = torch.cuda.current_stream(a2.device).cuda_stream
+    check(lib().wubu_b200_stft_loss_grad(a2.data_ptr(), b2.data_ptr(), B, n, n_scales, grad.data_ptr(),
+                                         loss.data_ptr(), stream), "stft_loss_grad")
+    return (loss[0], grad[0]) if squeeze else (loss, grad)
 
 
 def init_params(cfg: dict, seed: int = 0) -> np.ndarray:

@@ -8,6 +8,13 @@
 #include "conv_plan.h"
 #include "small_kernels.cuh"
 
+namespace wb {
+// stft_loss.cu
+size_t stft_scratch_floats(int B, int n, int n_scales);
+cudaError_t stft_loss_grad(const float* a, const float* b, int B, int n, int n_scales, float* grad, float* loss,
+                           float* scratch, cudaStream_t st);
+}  // namespace wb
+
 using namespace wb;
 
 namespace {
@@ -135,6 +142,24 @@ int wubu_b200_convT_wgrad(const void* x, const void* dy, float* dw, int B, int C
   if (cudaMalloc(&s.part, wgrad_part_floats(L) * sizeof(float)) != cudaSuccess) return WUBU_B200_ERR_CUDA;
   L.p.part = s.part;
   return run_wgrad(L, s, 1, C_out, k, dw, st);
+}
+
+int wubu_b200_stft_loss_grad(const float* a, const float* b, int B, int n, int n_scales, float* grad, float* loss,
+                             void* stream) {
+  if (!a || !b || !grad || !loss || B < 1 || n < 1 || B > 65535) return WUBU_B200_ERR_ARG;
+  cudaStream_t st = (cudaStream_t)stream;
+  float* scratch = nullptr;
+  if (cudaMallocAsync(&scratch, stft_scratch_floats(B, n, n_scales) * sizeof(float), st) != cudaSuccess)
+    return WUBU_B200_ERR_CUDA;
+  const cudaError_t e = stft_loss_grad(a, b, B, n, n_scales, grad, loss, scratch, st);
+  cudaFreeAsync(scratch, st);
+  if (e != cudaSuccess) return WUBU_B200_ERR_CUDA;
+  const cudaError_t s2 = cudaStreamSynchronize(st);
+  if (s2 != cudaSuccess) {
+    fprintf(stderr, "wuburvc_b200: CUDA error %s\n", cudaGetErrorString(s2));
+    return WUBU_B200_ERR_CUDA;
+  }
+  return WUBU_B200_OK;
 }
 
 }  // extern "C"
