@@ -155,6 +155,14 @@ WubuB200Gen* wubu_b200_gen_create(const WubuB200GenConfig* cfg, const WubuB200Tr
 void wubu_b200_gen_destroy(WubuB200Gen* gen);
 int wubu_b200_gen_set_params(WubuB200Gen* gen, const float* host_flat);
 int wubu_b200_gen_get_params(WubuB200Gen* gen, float* host_flat);
+/* Optimiser state for checkpoint / resume: the AdamW first and second moments as flat buffers in the
+ * same reference layout as get_params, the step count and the source-noise stream.  Replaces the
+ * host WuBuAdamW state (src/wubu_train.c:43-52) kept between wubu_adamw_step calls.  set_params
+ * restarts the optimiser, so restore with set_params first, then set_opt_state. */
+int wubu_b200_gen_get_opt_state(WubuB200Gen* gen, float* m_flat, float* v_flat, long long* step,
+                                unsigned long long* noise_stream);
+int wubu_b200_gen_set_opt_state(WubuB200Gen* gen, const float* m_flat, const float* v_flat, long long step,
+                                unsigned long long noise_stream);
 int wubu_b200_gen_get_grads(WubuB200Gen* gen, float* host_flat);
 int wubu_b200_gen_samples(const WubuB200Gen* gen); /* output samples per item */
 

@@ -99,6 +99,9 @@ _SIGS = {
     "wubu_b200_gen_set_params": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
     "wubu_b200_gen_get_params": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
     "wubu_b200_gen_get_grads": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
+    "wubu_b200_gen_get_opt_state": (ctypes.c_int, [ctypes.c_void_p] * 5),
+    "wubu_b200_gen_set_opt_state": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                                   ctypes.c_longlong, ctypes.c_ulonglong]),
     "wubu_b200_gen_samples": (ctypes.c_int, [ctypes.c_void_p]),
     "wubu_b200_gen_upload": (ctypes.c_int, [ctypes.c_void_p] * 6),
     "wubu_b200_gen_forward": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_ulonglong, ctypes.c_void_p]),
@@ -267,6 +270,22 @@ class Generator:
         out = np.empty(self.total, dtype=np.float32)
         check(L().wubu_b200_gen_get_params(self.h, _ptr(out)), "get_params")
         return out
+
+    def get_opt_state(self):
+        """AdamW moments (flat, reference layout), step count and source-noise stream."""
+        m = np.empty(self.total, dtype=np.float32)
+        v = np.empty(self.total, dtype=np.float32)
+        step, stream = ctypes.c_longlong(0), ctypes.c_ulonglong(0)
+        check(L().wubu_b200_gen_get_opt_state(self.h, _ptr(m), _ptr(v), ctypes.byref(step), ctypes.byref(stream)),
+              "get_opt_state")
+        return m, v, int(step.value), int(stream.value)
+
+    def set_opt_state(self, m: np.ndarray, v: np.ndarray, step: int, noise_stream: int = 0):
+        """Restores the optimiser (after set_params, which restarts it)."""
+        m, v = _f32(m), _f32(v)
+        assert m.size == self.total and v.size == self.total
+        check(L().wubu_b200_gen_set_opt_state(self.h, _ptr(m), _ptr(v), int(step), int(noise_stream)),
+              "set_opt_state")
 
     def get_grads(self) -> np.ndarray:
         out = np.empty(self.total, dtype=np.float32)

@@ -192,6 +192,41 @@ int wubu_b200_gen_get_params(WubuB200Gen* gen, float* host_flat) {
   return download_reference(m, m.params, host_flat);
 }
 
+int wubu_b200_gen_get_opt_state(WubuB200Gen* gen, float* m_flat, float* v_flat, long long* step,
+                                unsigned long long* noise_stream) {
+  if (!gen || !m_flat || !v_flat) return WUBU_B200_ERR_ARG;
+  Gen& m = gen->m;
+  cudaSetDevice(m.opt.device);
+  int rc = download_reference(m, m.adam_m, m_flat);
+  if (!rc) rc = download_reference(m, m.adam_v, v_flat);
+  if (rc) return rc;
+  StepState st{};
+  if (cudaMemcpy(&st, m.state, sizeof(st), cudaMemcpyDeviceToHost) != cudaSuccess) return WUBU_B200_ERR_CUDA;
+  if (step) *step = st.adam_t;
+  if (noise_stream) *noise_stream = st.noise_stream;
+  return WUBU_B200_OK;
+}
+
+int wubu_b200_gen_set_opt_state(WubuB200Gen* gen, const float* m_flat, const float* v_flat, long long step,
+                                unsigned long long noise_stream) {
+  if (!gen || !m_flat || !v_flat || step < 0 || step > 0x7fffffffLL) return WUBU_B200_ERR_ARG;
+  Gen& m = gen->m;
+  cudaSetDevice(m.opt.device);
+  const size_t bytes = sizeof(float) * (size_t)m.table.total;
+  std::vector<float> dm((size_t)m.table.total), dv(dm.size());
+  flat_to_internal(m.table, m_flat, dm.data());
+  flat_to_internal(m.table, v_flat, dv.data());
+  StepState st{};
+  st.adam_t = (int)step;
+  st.noise_stream = noise_stream;
+  // synchronous copies: the host vectors go out of scope on return
+  if (cudaStreamSynchronize(m.stream) != cudaSuccess || cudaMemcpy(m.adam_m, dm.data(), bytes, cudaMemcpyHostToDevice) ||
+      cudaMemcpy(m.adam_v, dv.data(), bytes, cudaMemcpyHostToDevice) ||
+      cudaMemcpy(m.state, &st, sizeof(st), cudaMemcpyHostToDevice))
+    return WUBU_B200_ERR_CUDA;
+  return check_err(m);
+}
+
 int wubu_b200_gen_get_grads(WubuB200Gen* gen, float* host_flat) {
   if (!gen || !host_flat) return WUBU_B200_ERR_ARG;
   Gen& m = gen->m;
