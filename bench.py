@@ -45,6 +45,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--only-device", action="store_true",
                     help="time only the device-resident steps (for profiler launch lists)")
+    ap.add_argument("--infer", action="store_true",
+                    help="forward-only long-clip inference (40 kHz, batch 1, 6000 frames = 2.4M samples, f0 "
+                         "median-filtered over 5 frames) on one GPU: prints its own JSON line and exits")
     ap.add_argument("--kernel", default=None, metavar="WHICH,STAGE",
                     help="time one convolution of the step alone (kernel_bench: which 0 f1, 1 d1, 2 g1, 3 f2, "
                          "4 d2) inside an NVTX range 'kb<which><stage>' and exit")
@@ -183,8 +186,72 @@ def run_reference(args, rank):
 TRAFFIC_BYTES = 2 * 13.898752e6
 
 
+def run_infer(args):
+    """Forward-only inference of one long clip, inputs resident (value) and through the public API
+    with the host inputs uploaded and the audio read back every call (e2e)."""
+    import ctypes
+
+    import torch
+    from wuburvc_b200 import Generator, L, model
+
+    cfg = model.config(args.config)
+    B, F = 1, (args.frames if args.frames != 32 else 6000)
+    gen = Generator(cfg, B, F, device=0)
+    z, f0, g, _ = make_inputs(cfg, B, F, seed=4321)
+    # f0 smoothed with a 5-frame median filter (voiced frames only), 20 % unvoiced
+    pad = np.pad(f0, ((0, 0), (2, 2)), mode="edge")
+    med = np.median(np.stack([pad[:, i:i + F] for i in range(5)]), axis=0).astype(np.float32)
+    f0 = np.where(f0 > 0, med, 0.0).astype(np.float32)
+    gen.upload(z, f0, g, None, None)
+    stream = torch.cuda.ExternalStream(gen.stream, device=0)
+    fwd = L().wubu_b200_gen_forward
+    for _ in range(max(3, args.warmup)):
+        check_rc(fwd(gen.h, 0, None))
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        s, e = torch.cuda.Event(True), torch.cuda.Event(True)
+        s.record(stream)
+        for i in range(args.steps):
+            check_rc(fwd(gen.h, i, None))
+        e.record(stream)
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / args.steps
+    audio = np.empty((B, gen.T), np.float32)
+    torch.cuda.synchronize()
+    s2, e2 = torch.cuda.Event(True), torch.cuda.Event(True)
+    s2.record(stream)
+    for i in range(args.steps):
+        gen.upload(z, f0, g, None, None)
+        check_rc(fwd(gen.h, i, audio.ctypes.data_as(ctypes.c_void_p)))
+    e2.record(stream)
+    torch.cuda.synchronize()
+    ms_e2e = s2.elapsed_time(e2) / args.steps
+    assert np.isfinite(audio).all()
+    secs = B * gen.T / cfg["sr"]
+    fl = 29.26e9 * (F / 32.0) * B  # algorithmic forward GFLOP per 32-frame item, scaled
+    print(json.dumps({"metric": "generator forward (inference) audio-sec/sec", "value": secs / (ms / 1e3),
+                      "unit": "audio-s/s", "n_gpus": 1, "steps": args.steps, "ms_per_step": ms,
+                      "higher_is_better": True, "dtype": "bf16 operands (bf16x3 split), fp32 accumulate",
+                      "data": "synthetic",
+                      "config": {"workload": f"40 kHz long-clip inference, batch 1, {F} frames "
+                                             f"({gen.T} samples), f0 median-filtered, 20% unvoiced"},
+                      "e2e": {"value": secs / (ms_e2e / 1e3), "unit": "audio-s/s",
+                              "h2d_bytes_per_step": int(z.nbytes + f0.nbytes + g.nbytes),
+                              "d2h_bytes_per_step": int(audio.nbytes), "ms_per_step": ms_e2e},
+                      "algorithmic_tflops": fl / (ms / 1e3) / 1e12}))
+    gen.close()
+
+
+def check_rc(rc):
+    if rc != 0:
+        raise RuntimeError(f"wuburvc_b200 call failed ({rc})")
+
+
 def main():
     args = parse()
+    if args.infer:
+        run_infer(args)
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

@@ -172,7 +172,8 @@ int wubu_b200_gen_samples(const WubuB200Gen* gen); /* output samples per item */
  *   g    [B][gin_channels]       speaker embedding (may be NULL when gin == 0)
  *   noise[B][T][harmonic_num+1]  standard-normal source noise, or NULL -> device generator
  *                                (counter-based, keyed by opt.seed and noise_stream)
- *   dldy [B][T]                  upstream gradient dL/d(audio)                            */
+ *   dldy [B][T]                  upstream gradient dL/d(audio); may be NULL for forward-only
+ *                                use (the previous upload's stays; zeros before the first)  */
 #define WUBU_B200_INPUTS_RESIDENT 1 /* use the inputs already on the device (last upload) */
 int wubu_b200_gen_upload(WubuB200Gen* gen, const float* z, const float* f0, const float* g, const float* noise,
                          const float* dldy);

@@ -110,9 +110,10 @@ int upload(Gen& m, const float* z, const float* f0, const float* g, const float*
   auto cp = [&](void* d, const void* h, size_t bytes) {
     return cudaMemcpyAsync(d, h, bytes, cudaMemcpyHostToDevice, st) == cudaSuccess;
   };
-  if (!z || !dldy) return WUBU_B200_ERR_ARG;
+  if (!z) return WUBU_B200_ERR_ARG;
   if (!cp(m.z, z, sizeof(float) * m.B * c.in_channels * m.F)) return WUBU_B200_ERR_CUDA;
-  if (!cp(m.dldy, dldy, sizeof(float) * m.B * m.T)) return WUBU_B200_ERR_CUDA;
+  // dldy may be left out for forward-only use (the previous upload's, zeros at first, stays)
+  if (dldy && !cp(m.dldy, dldy, sizeof(float) * m.B * m.T)) return WUBU_B200_ERR_CUDA;
   if (c.gin_channels) {
     if (!g) return WUBU_B200_ERR_ARG;
     if (!cp(m.g, g, sizeof(float) * m.B * c.gin_channels)) return WUBU_B200_ERR_CUDA;
