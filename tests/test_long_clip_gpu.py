@@ -1,8 +1,9 @@
 """Long-clip inference (40 kHz, batch 1, 6000 frames = 2.4M samples, forward only) checked through a
 size-independent property: with an unvoiced clip and an explicit noise input the generator is a
 local (finite receptive field) map, so the interior of the long clip's audio must equal the audio
-of a short clip cut from the same inputs.  Both runs use the same kernels with the same per-output
-reduction order; the tolerance (rel-L2 1e-6) allows for nothing but row-tile placement."""
+of a short clip cut from the same inputs.  Both runs use the same kernels; only the placement of
+an output row inside its tile or warp differs, which reorders a few fp32 sums (conv_post's
+warp transpose-reduction, for one) — measured 2.4e-6 relative, hence the rel-L2 bound of 1e-5."""
 import numpy as np
 import pytest
 
@@ -36,4 +37,4 @@ def test_long_clip_interior_equals_short_clip():
     lo, hi = margin * hop, (Fs - margin) * hop
     got = audio[0, s0 * hop + lo:s0 * hop + hi].astype(np.float64)
     want = a_short[0, lo:hi].astype(np.float64)
-    assert np.linalg.norm(got - want) <= 1e-6 * np.linalg.norm(want)
+    assert np.linalg.norm(got - want) <= 1e-5 * np.linalg.norm(want)
