@@ -88,3 +88,18 @@ def test_flops_match_survey():
     assert abs(model.train_flops_per_item(model.config("40k"), 32) / 1e9 - 87.79) < 0.01
     assert abs(model.train_flops_per_item(model.config("32k"), 40) / 1e9 - 92.27) < 0.01
     assert abs(model.train_flops_per_item(model.config("48k"), 36) / 1e9 - 118.97) < 0.01
+
+
+def test_new_entry_points_reject_bad_arguments_without_a_gpu():
+    """Argument checks come before any device call (they run here, with no GPU)."""
+    import ctypes
+
+    from wuburvc_b200 import L
+
+    h = lib()
+    assert h.wubu_b200_stft_loss_grad(None, None, 1, 100, 3, None, None, None) == -1
+    assert h.wubu_b200_stft_loss_grad(1, 1, 0, 100, 3, 1, 1, None) == -1
+    g = L()
+    assert g.wubu_b200_gen_set_opt_state(None, None, None, 0, 0) == -1
+    m = (ctypes.c_float * 4)()
+    assert g.wubu_b200_gen_get_opt_state(None, m, m, None, None) == -1
