@@ -1,6 +1,6 @@
 """Parity of the CUDA training step (through the C ABI) with the reference and the oracle.
 
-Gates (bf16 GEMM operands with fp32 accumulation):
+Gates (the target tolerances for bf16 GEMM operands with fp32 accumulation):
   forward waveform      rel-L2 <= 2e-3
   every parameter grad  rel-L2 <= 1e-2
 Compared against
