@@ -131,6 +131,12 @@ int refh_adamw(void *hp) {
 
 int refh_threads(void) { return omp_get_max_threads(); }
 
+/* The reference's own objects, for a caller that drives the reference's public entry points
+ * (e.g. wubu_train_step_cuda through a drop-in back-end) on this model. */
+void *refh_model(void *hp) { return ((RefH *)hp)->model; }
+void *refh_registry(void *hp) { return &((RefH *)hp)->reg; }
+void *refh_optimizer(void *hp) { return ((RefH *)hp)->opt; }
+
 void refh_free(void *hp) {
     RefH *h = (RefH *)hp;
     if (!h) return;

@@ -57,6 +57,9 @@ def lib():
         h.refh_adamw.argtypes = [vp]
         h.refh_threads.restype = ip
         h.refh_threads.argtypes = []
+        for f in ("refh_model", "refh_registry", "refh_optimizer"):
+            getattr(h, f).restype = vp
+            getattr(h, f).argtypes = [vp]
         h.refh_free.restype = None
         h.refh_free.argtypes = [vp]
         _lib = h

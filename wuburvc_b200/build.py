@@ -62,6 +62,24 @@ def build(verbose: bool = False, force: bool = False) -> str:
     return LIB
 
 
+SHIM_SRC = os.path.join(HERE, "shim", "wubu_train_b200.c")
+SHIM_LIB = os.path.join(HERE, "shim", "libwubu_train_b200.so")
+
+
+def build_shim(ref_src: str, ref_lib: str) -> str:
+    """The drop-in shim compiled against the reference's own headers (``ref_src``) into a shared
+    object that resolves this library and the reference's host objects (``ref_lib``) at load time
+    through relative run paths, so it travels with the repository."""
+    ref_dir = os.path.dirname(os.path.abspath(ref_lib))
+    rel_ref = os.path.relpath(ref_dir, os.path.dirname(SHIM_LIB))
+    cmd = ["gcc", "-std=gnu11", "-shared", "-fPIC", "-O2", "-I" + ref_src, "-I" + os.path.join(HERE, "..", "include"),
+           SHIM_SRC, "-o", SHIM_LIB, "-L" + HERE, "-l:libwuburvc_b200.so", "-L" + ref_dir,
+           "-l:" + os.path.basename(ref_lib), "-Wl,--no-undefined", "-Wl,-rpath,$ORIGIN/..",
+           "-Wl,-rpath,$ORIGIN/" + rel_ref]
+    subprocess.check_call(cmd)
+    return SHIM_LIB
+
+
 if __name__ == "__main__":
     build(verbose="-v" in sys.argv, force="-f" in sys.argv)
     print(LIB)
