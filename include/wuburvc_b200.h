@@ -91,6 +91,10 @@ int wubu_b200_convT_wgrad(const void* x, const void* dy, float* dw, int B, int C
  * it replaces for batches on the device; deterministic. */
 int wubu_b200_stft_loss_grad(const float* a, const float* b, int B, int n, int n_scales, float* grad,
                              float* loss, void* stream);
+/* The same on host buffers (copied to and from the current device; synchronous), the form a host
+ * trainer such as the reference's wubu_train_step(_cuda) (src/wubu_train.c:1151-1176) calls. */
+int wubu_b200_stft_loss_grad_host(const float* a, const float* b, int B, int n, int n_scales, float* grad,
+                                  float* loss);
 
 /* ---------------------------------------------------------------------------------------
  * 2. generator training step

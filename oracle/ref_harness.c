@@ -130,6 +130,9 @@ int refh_adamw(void *hp) {
 }
 
 int refh_threads(void) { return omp_get_max_threads(); }
+/* Thread count of the reference's OpenMP regions (its reductions, e.g. wubu_mse_loss, then run in a
+ * fixed order when 1). */
+void refh_set_threads(int n) { omp_set_num_threads(n); }
 
 /* The reference's own objects, for a caller that drives the reference's public entry points
  * (e.g. wubu_train_step_cuda through a drop-in back-end) on this model. */

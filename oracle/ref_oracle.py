@@ -57,6 +57,8 @@ def lib():
         h.refh_adamw.argtypes = [vp]
         h.refh_threads.restype = ip
         h.refh_threads.argtypes = []
+        h.refh_set_threads.restype = None
+        h.refh_set_threads.argtypes = [ip]
         for f in ("refh_model", "refh_registry", "refh_optimizer"):
             getattr(h, f).restype = vp
             getattr(h, f).argtypes = [vp]

@@ -21,7 +21,7 @@ def test_shim_builds_against_reference_header_and_links(tmp_path):
            "-I" + REF_SRC, "-I" + os.path.join(ROOT, "include"),
            os.path.join(ROOT, "wuburvc_b200", "shim", "wubu_train_b200.c"), "-o", str(out),
            "-L" + os.path.dirname(OUR_LIB), "-l:libwuburvc_b200.so", "-L" + os.path.dirname(REF_LIB),
-           "-l:libwubu_ref.so", "-Wl,--no-undefined"]
+           "-l:libwubu_ref.so", "-lm", "-Wl,--no-undefined"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     assert r.returncode == 0, r.stderr
     assert out.exists()

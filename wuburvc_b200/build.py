@@ -74,7 +74,7 @@ def build_shim(ref_src: str, ref_lib: str) -> str:
     rel_ref = os.path.relpath(ref_dir, os.path.dirname(SHIM_LIB))
     cmd = ["gcc", "-std=gnu11", "-shared", "-fPIC", "-O2", "-I" + ref_src, "-I" + os.path.join(HERE, "..", "include"),
            SHIM_SRC, "-o", SHIM_LIB, "-L" + HERE, "-l:libwuburvc_b200.so", "-L" + ref_dir,
-           "-l:" + os.path.basename(ref_lib), "-Wl,--no-undefined", "-Wl,-rpath,$ORIGIN/..",
+           "-l:" + os.path.basename(ref_lib), "-lm", "-Wl,--no-undefined", "-Wl,-rpath,$ORIGIN/..",
            "-Wl,-rpath,$ORIGIN/" + rel_ref]
     subprocess.check_call(cmd)
     return SHIM_LIB

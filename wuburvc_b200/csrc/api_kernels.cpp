@@ -162,4 +162,26 @@ int wubu_b200_stft_loss_grad(const float* a, const float* b, int B, int n, int n
   return WUBU_B200_OK;
 }
 
+int wubu_b200_stft_loss_grad_host(const float* a, const float* b, int B, int n, int n_scales, float* grad,
+                                  float* loss) {
+  if (!a || !b || !grad || !loss || B < 1 || n < 1 || B > 65535) return WUBU_B200_ERR_ARG;
+  const size_t bytes = sizeof(float) * (size_t)B * n;
+  float *da = nullptr, *db = nullptr, *dg = nullptr, *dl = nullptr;
+  int rc = WUBU_B200_ERR_CUDA;
+  if (cudaMalloc(&da, bytes) == cudaSuccess && cudaMalloc(&db, bytes) == cudaSuccess &&
+      cudaMalloc(&dg, bytes) == cudaSuccess && cudaMalloc(&dl, sizeof(float) * B) == cudaSuccess &&
+      cudaMemcpy(da, a, bytes, cudaMemcpyHostToDevice) == cudaSuccess &&
+      cudaMemcpy(db, b, bytes, cudaMemcpyHostToDevice) == cudaSuccess) {
+    rc = wubu_b200_stft_loss_grad(da, db, B, n, n_scales, dg, dl, nullptr);
+    if (rc == WUBU_B200_OK && (cudaMemcpy(grad, dg, bytes, cudaMemcpyDeviceToHost) != cudaSuccess ||
+                               cudaMemcpy(loss, dl, sizeof(float) * B, cudaMemcpyDeviceToHost) != cudaSuccess))
+      rc = WUBU_B200_ERR_CUDA;
+  }
+  cudaFree(da);
+  cudaFree(db);
+  cudaFree(dg);
+  cudaFree(dl);
+  return rc;
+}
+
 }  // extern "C"

@@ -1,6 +1,7 @@
 /* wubu_train_b200.c — binds src/wubu_train.h's CUDA entry points to libwuburvc_b200.so */
 #include "wubu_train.h"
 #include "wuburvc_b200.h"
+#include <math.h>
 #include <stdlib.h>
 #include <string.h>
 
@@ -60,12 +61,28 @@ int wubu_train_step_cuda(WuBuRVCModel *model, WuBuTrainRegistry *reg, WuBuAdamW 
   wubu_b200_gen_forward(c->gen, 0, audio);
   int n = n_samples < T ? n_samples : T;
   float mse = wubu_mse_loss(audio, wav, n);
-  for (int i = 0; i < T; i++) d[i] = i < n ? 2.f * (audio[i] - wav[i]) / n : 0.f;  /* + spectral term, src/wubu_train.c:1156-1193 */
+  /* the reference step's spectral term (src/wubu_train.c:1151-1176), its gradient taken on the GPU:
+   * weight WUBU_SPECTRAL_WEIGHT (default 1), rescaled to half the MSE gradient's RMS */
+  float weight = getenv("WUBU_SPECTRAL_WEIGHT") ? (float)atof(getenv("WUBU_SPECTRAL_WEIGHT")) : 1.0f;
+  float spec = 0.0f, *ds = NULL;
+  if (weight > 0.0f && n > 128 && (ds = malloc(n * sizeof(float))) != NULL) {
+    if (wubu_b200_stft_loss_grad_host(audio, wav, 1, n, 3, ds, &spec) == 0) {
+      float ss = 0.0f;
+      for (int i = 0; i < n; i++) ss += ds[i] * ds[i];
+      float rms = sqrtf(ss / (float)n);
+      float k = (rms > 1e-9f && mse > 1e-12f) ? weight * 0.5f * (2.0f / (float)n) * sqrtf(mse) / rms : 0.0f;
+      for (int i = 0; i < n; i++) ds[i] *= k;
+    } else {
+      free(ds); ds = NULL; spec = 0.0f;
+    }
+  }
+  float total = mse + spec;
+  for (int i = 0; i < T; i++) d[i] = i < n ? 2.f * (audio[i] - wav[i]) / (float)n + (ds ? ds[i] : 0.f) : 0.f;
   wubu_b200_gen_upload(c->gen, mel_in, NULL, NULL, NULL, d);
   int rc = wubu_b200_gen_backward(c->gen) || wubu_b200_gen_adamw(c->gen);
   sync_params(c, reg, &cfg, 0);             /* weights back on the host: synthesis-ready */
-  if (loss_out) *loss_out = mse;
-  model->last_loss = mse;
-  free(audio); free(d); free(zero);
-  return rc ? -1 : (mse < 0.1f ? 1 : 0);
+  if (loss_out) *loss_out = total;
+  model->last_loss = total;
+  free(audio); free(d); free(zero); free(ds);
+  return rc ? -1 : (total < 0.1f ? 1 : 0);
 }
