@@ -26,7 +26,7 @@ vp = ctypes.c_void_p
 def library_step(cfg, P, mel, wav, spectral):
     """The step through the library's API, dL/dy formed as the shim forms it (float32, in order)."""
     T = wav.shape[0]
-    gen = Generator(cfg, 1, mel.shape[1])
+    gen = Generator(cfg, 1, mel.shape[1], lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=1e-2)
     gen.set_params(flatten(cfg, P))
     gen.upload(mel[None], dldy=np.zeros((1, T), np.float32))
     audio = gen.forward()[0]

@@ -40,13 +40,19 @@ static void sync_params(TrainCacheCuda *c, WuBuTrainRegistry *reg, const WubuB20
 int wubu_train_step_cuda(WuBuRVCModel *model, WuBuTrainRegistry *reg, WuBuAdamW *opt,
                          const float *mel_in, int n_frames, const float *wav, int n_samples,
                          float *loss_out, int epoch) {
-  static TrainCacheCuda *c;              /* one context per process, like g_wcache */
+  /* One context per process, like g_wcache.  Weights and AdamW state stay on the device between
+   * calls with the same frame count and are written back to the registry after every step; a host
+   * that edits the registry's weights in between must free the context (or change n_frames) so the
+   * next call reloads them.  WuBuAdamW is opaque to this file: the hyper-parameters are the ones
+   * every reference caller creates it with (lr 1e-3, betas 0.9 / 0.999, eps 1e-8, weight decay
+   * 0.01; src/tt_train_demo.c:68, src/test_train_cuda.c:131). */
+  static TrainCacheCuda *c;
   WubuB200GenConfig cfg = decoder_config(model);
   (void)opt; (void)epoch;
   if (!c || c->frames != n_frames) {
     if (c) wubu_train_cache_free_cuda(c);
     c = wubu_train_cache_alloc_cuda();
-    WubuB200TrainOptions o = {1, n_frames, 0, 1e-3f, 0.9f, 0.999f, 1e-8f, 1e-4f, 0};
+    WubuB200TrainOptions o = {1, n_frames, 0, 1e-3f, 0.9f, 0.999f, 1e-8f, 1e-2f, 0};
     c->gen = wubu_b200_gen_create(&cfg, &o);
     c->frames = n_frames;
     c->total = wubu_b200_gen_param_total(&cfg);
