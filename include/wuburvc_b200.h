@@ -55,12 +55,14 @@ int wubu_b200_conv1d_wgrad(const void* dy, const void* x, float* dw, int B, int 
 
 /* Same result as wubu_b200_conv1d_wgrad, but allocates nothing.  No counterpart in the reference.
  *   For callers that cannot call cudaMalloc: a host whose device memory is owned entirely by its
- *   own allocator, or a real-time audio thread that must not make calls that can block and
- *   synchronise the device.  The split-K scratch is a fixed file-scope __device__ array of 16 MiB
- *   (4 Mi floats) that every GPU loading the library keeps until exit; problems whose
- *   C_out*k*C_in partial tile exceeds it are rejected with WUBU_B200_ERR_SHAPE, larger ones run
- *   with fewer splits.  The first call on a device resolves the array's device address (make it
- *   before any stream capture).  All calls share the array: calls that overlap on the GPU race. */
+ *   own allocator, or a host that forbids allocation in its processing callback (cudaMalloc /
+ *   cudaFree take the driver's locks and cudaFree may synchronise the whole device).  The split-K
+ *   scratch is a fixed file-scope __device__ array of 16 MiB (4 Mi floats) that every GPU loading
+ *   the library keeps until exit; problems whose C_out*k*C_in partial tile exceeds it (or k > 256)
+ *   are rejected with WUBU_B200_ERR_SHAPE, larger ones run with fewer splits.  The first call on a
+ *   device resolves the array's device address (make it before any stream capture).  All calls
+ *   share the array: calls that overlap on the GPU race.  The call returns once its stream has
+ *   finished the work (it reads back the kernels' error word). */
 int wubu_b200_conv1d_wgrad_noalloc(const void* dy, const void* x, float* dw, int B, int C_in, int T, int C_out,
                                    int k, int dil, int pad, void* stream);
 

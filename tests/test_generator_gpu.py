@@ -15,6 +15,7 @@ import pytest
 import torch
 
 from oracle import generator_ref as G
+from oracle import ref_oracle
 from wuburvc_b200 import Generator, flatten, model, unflatten
 
 pytestmark = pytest.mark.gpu
@@ -25,7 +26,7 @@ GRAD_TOL = 1e-2
 
 
 def rel(a, b):
-    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    a, b = np.asarray(a, np.float64).reshape(-1), np.asarray(b, np.float64).reshape(-1)
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-300))
 
 
@@ -73,9 +74,27 @@ def test_decoder_matches_reference_c_trainer(tag):
     grads = unflatten(cfg, gen.get_grads())
     worst = 0.0
     for i, n in enumerate(names):
-        e = abs(np.linalg.norm(grads[n]) - d["gnorm"][i]) / d["gnorm"][i]
+        g = grads[n].reshape(-1).astype(np.float64)
+        gn = d["gnorm"][i]
+        e = abs(np.linalg.norm(g) - gn) / gn
         worst = max(worst, e)
+        # direction, not only the norm: the reference's sampled entries and its element sum.  A
+        # gradient within rel-L2 GRAD_TOL differs from the reference by at most GRAD_TOL*||g|| in
+        # every entry and by at most GRAD_TOL*||g||*sqrt(n) in the sum (Cauchy-Schwarz)
+        sl = slice(d["offs"][i], d["offs"][i + 1])
+        idx, gv = d["idx"][sl], d["gval"][sl].astype(np.float64)
+        assert np.abs(g[idx] - gv).max() <= GRAD_TOL * gn, n
+        assert abs(g.sum() - d["gsum"][i]) <= GRAD_TOL * gn * np.sqrt(g.size), n
     assert worst <= GRAD_TOL
+    # every tensor by rel-L2 against the reference trainer run live (it travels, built in oracle/_ref)
+    if ref_oracle.available():
+        ref = ref_oracle.RefTrainer(P, cfg["upsample_rates"], cfg["upsample_kernels"])
+        ref.forward(z[0])
+        ref.backward(dldy[0])
+        live = ref.grads()
+        ref.close()
+        bad = {n: rel(grads[n], live[n]) for n in names if rel(grads[n], live[n]) > GRAD_TOL}
+        assert not bad, bad
     # one AdamW step on the device against the AdamW restatement (itself pinned to the
     # reference's wubu_adamw_step by test_oracle_adamw_matches_reference) on the same gradients
     gflat = gen.get_grads()

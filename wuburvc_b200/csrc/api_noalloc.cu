@@ -2,10 +2,12 @@
 //
 // wubu_b200_conv1d_wgrad allocates its split-K partial buffer and error word with cudaMalloc on
 // every call.  Some callers cannot do that: a host whose device memory is entirely owned by its own
-// allocator (a framework's caching allocator that has reserved the HBM), or a real-time audio host
-// whose processing thread must not make calls that may block and synchronise the device.  For them
-// this variant keeps its scratch in a file-scope __device__ array of fixed size, present on every
-// GPU that loads the library until the process exits.
+// allocator (a framework's caching allocator that has reserved the HBM), or a host that forbids
+// allocation inside its processing callback, because cudaMalloc / cudaFree take the driver's locks
+// and cudaFree may synchronise the whole device.  For them this variant keeps its scratch in a
+// file-scope __device__ array of fixed size, present on every GPU that loads the library until the
+// process exits.  The call still waits for its own stream to finish (it reads back the kernels'
+// error word before returning).
 #include <mutex>
 
 #include "../../include/wuburvc_b200.h"
@@ -47,19 +49,30 @@ float* scratch_address(int* rc) {
   return g_dev_scratch[dev];
 }
 
-// dw[oc][ic][tap] = sum over splits of part[split][tap * C_out + oc][ic] (fixed order)
+// dw[oc][ic][tap] = sum over splits of part[split][tap * C_out + oc][ic] (fixed order).  A block owns
+// one output channel and 32 input channels: it reads each tap's 32 partials as one coalesced row
+// (ic fastest, as the weight-gradient kernel wrote them), sums the splits, and writes the
+// transposed [ic][tap] tile to dw as one contiguous run through shared memory.
+constexpr int kReduceIc = 32;
+constexpr int kReduceMaxTaps = 256;
+
 __global__ void noalloc_wgrad_reduce_kernel(const float* __restrict__ part, int splits, long long ld, int c_out,
                                             int c_in, int k, float* __restrict__ dw) {
-  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  const long long n = (long long)c_out * c_in * k;
-  if (i >= n) return;
-  const int tap = (int)(i % k);
-  const long long oi = i / k;
-  const int ic = (int)(oi % c_in), oc = (int)(oi / c_in);
-  const long long src = ((long long)tap * c_out + oc) * c_in + ic;
-  float s = 0.f;
-  for (int sp = 0; sp < splits; ++sp) s += part[(long long)sp * ld + src];
-  dw[i] = s;
+  extern __shared__ float tile[];  // [kReduceIc][k]
+  const int oc = blockIdx.y;
+  const int ic0 = blockIdx.x * kReduceIc;
+  const int nic = min(kReduceIc, c_in - ic0);
+  for (int idx = threadIdx.x; idx < k * kReduceIc; idx += blockDim.x) {
+    const int tap = idx / kReduceIc, icl = idx % kReduceIc;
+    if (icl >= nic) continue;
+    const long long src = ((long long)tap * c_out + oc) * c_in + ic0 + icl;
+    float s = 0.f;
+    for (int sp = 0; sp < splits; ++sp) s += part[(long long)sp * ld + src];
+    tile[icl * k + tap] = s;
+  }
+  __syncthreads();
+  float* out = dw + ((long long)oc * c_in + ic0) * k;
+  for (int j = threadIdx.x; j < nic * k; j += blockDim.x) out[j] = tile[j];
 }
 
 }  // namespace
@@ -70,7 +83,8 @@ using namespace wb;
 
 extern "C" int wubu_b200_conv1d_wgrad_noalloc(const void* dy, const void* x, float* dw, int B, int C_in, int T,
                                               int C_out, int k, int dil, int pad, void* stream) {
-  if (!dy || !x || !dw || B < 1 || T < 1 || k < 1) return WUBU_B200_ERR_ARG;
+  if (!dy || !x || !dw || B < 1 || T < 1 || k < 1 || C_in < 1 || C_out < 1) return WUBU_B200_ERR_ARG;
+  if (k > kReduceMaxTaps || C_out > 65535) return WUBU_B200_ERR_SHAPE;
   int rc = WUBU_B200_OK;
   float* base = scratch_address(&rc);
   if (!base) return rc;
@@ -97,9 +111,9 @@ extern "C" int wubu_b200_conv1d_wgrad_noalloc(const void* dy, const void* x, flo
   // the error word must start at zero; the partials are fully overwritten by every call
   if (cudaMemsetAsync(err, 0, sizeof(int), st) != cudaSuccess) return WUBU_B200_ERR_CUDA;
   if (L.run(st) != cudaSuccess) return WUBU_B200_ERR_CUDA;
-  const long long n = (long long)C_out * C_in * k;
-  noalloc_wgrad_reduce_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(part, L.splits, (long long)per_split, C_out,
-                                                                          C_in, k, dw);
+  const dim3 rgrid((unsigned)((C_in + kReduceIc - 1) / kReduceIc), (unsigned)C_out);
+  noalloc_wgrad_reduce_kernel<<<rgrid, 128, (size_t)kReduceIc * k * sizeof(float), st>>>(
+      part, L.splits, (long long)per_split, C_out, C_in, k, dw);
   if (cudaGetLastError() != cudaSuccess) return WUBU_B200_ERR_CUDA;
   int h = 0;
   if (cudaMemcpyAsync(&h, err, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess) return WUBU_B200_ERR_CUDA;
