@@ -33,14 +33,19 @@ extern "C" {
 #define WUBU_B200_ERR_TIMEOUT (-4) /* a kernel's bounded wait expired; the context stays usable */
 #define WUBU_B200_ERR_COMM (-5)
 #define WUBU_B200_ERR_NOMEM (-6)
+#define WUBU_B200_ERR_RANGE (-7) /* a forward GEMM operand reached 65504, the limit of its fp16 split */
 
 /* ---------------------------------------------------------------------------------------
  * 1. convolution primitives (device pointers, `stream` = cudaStream_t or NULL)
  * ------------------------------------------------------------------------------------- */
 
 /* Conv1d, stride 1: out[b,t,o] = bias[o] + sum_{tap,i} x[b, t-pad+dil*tap, i] * w[tap,o,i]
- *   x_hi/x_lo [B][T][C_in] bf16, w_hi/w_lo [k][C_out][C_in] bf16, out [B][T_out][C_out] f32,
- *   T_out = T + 2*pad - dil*(k-1).  split=1: bf16x3 (hi*hi + lo*hi + hi*lo), else hi only.
+ *   x_hi/x_lo [B][T][C_in], w_hi/w_lo [k][C_out][C_in], out [B][T_out][C_out] f32,
+ *   T_out = T + 2*pad - dil*(k-1).
+ *   split=1: fp32-accurate forward.  Each operand is an fp16 pair, value = hi + lo / 2048
+ *            (hi = fp16(x), lo = fp16((x - hi) * 2048)); |x| must stay below 65504.  The product
+ *            is hi*hi + (hi*lo + lo*hi) / 2048.
+ *   split=0: x_hi and w_hi are bf16, the lo pointers are ignored (one bf16 product).
  *   Replaces k_conv1d (src/wubu_rvc_cuda.cu:36-53) and conv1d_fwd (src/wubu_train.c:461-486). */
 int wubu_b200_conv1d(const void* x_hi, const void* x_lo, const void* w_hi, const void* w_lo,
                      const float* bias, float* out, int B, int C_in, int T, int C_out, int k, int dil,
@@ -67,7 +72,8 @@ int wubu_b200_conv1d_wgrad_noalloc(const void* dy, const void* x, float* dw, int
                                    int k, int dil, int pad, void* stream);
 
 /* ConvTranspose1d (polyphase): out[b, i*s-pad+tap, o] += x[b,i,c] * W[c][o][tap]
- *   x [B][T_in][C_in] bf16; wp [k][C_out][C_in] bf16 = W taps in phase order
+ *   x [B][T_in][C_in]; wp [k][C_out][C_in] = W taps in phase order (operand pairs as for
+ *   wubu_b200_conv1d: fp16 hi + lo/2048 when split=1, bf16 hi alone when split=0)
  *   (phase r = 0..s-1, taps r, r+s, r+2s, ...), transposed; out [B][T_in*s][C_out] f32.
  *   Requires k - 2*pad == s.  Replaces k_convt1d (src/wubu_rvc_cuda.cu:55-78), convt1d_fwd
  *   (src/wubu_train.c:533-562). */
@@ -188,7 +194,14 @@ int wubu_b200_gen_backward(WubuB200Gen* gen);
 int wubu_b200_gen_adamw(WubuB200Gen* gen);
 /* One full step (upload unless RESIDENT, forward, backward, gradient all-reduce when a
  * communicator is attached, AdamW).  audio_out (host, may be NULL) receives the forward output.
- * The step is captured once into a CUDA graph and replayed. */
+ * The step is captured once into a CUDA graph and replayed.
+ *
+ * Forward GEMM operands are fp16 hi + fp16 lo/2048 pairs (fp32-accurate) while every operand stays
+ * below 65504.  When one reaches it, the step's update is skipped on the device (on every rank under
+ * data parallelism), the context switches for good to bf16 hi + bf16 lo pairs (range-safe, ~2^-17
+ * relative) and train_step / forward recompute the step, so the caller sees no error.  The
+ * asynchronous step cannot: wubu_b200_gen_sync then returns WUBU_B200_ERR_RANGE once (the steps
+ * enqueued since the overflow left the parameters unchanged) and later steps use the bf16 pairs. */
 int wubu_b200_gen_train_step(WubuB200Gen* gen, const float* z, const float* f0, const float* g, const float* noise,
                              const float* dldy, float* audio_out, unsigned long long noise_stream, int flags);
 /* Enqueue one resident-input step without synchronising (for device-side timing). */

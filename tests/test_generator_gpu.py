@@ -185,3 +185,56 @@ def test_training_reduces_mse():
         gen.adamw()
     assert losses[-1] < losses[0]
     gen.close()
+
+
+def test_operand_beyond_fp16_range_falls_back_to_bf16_pairs():
+    """Forward GEMM operands are fp16 hi + lo/2048 pairs, which cannot hold 65504 or more.  When an
+    operand reaches it the step's update is skipped on the device, the context switches for good to
+    bf16 hi + lo pairs and the call recomputes the step: the caller sees a normal result, and the
+    update is applied exactly once (same parameters as a context that was already on bf16 pairs).
+    The asynchronous step reports the skip once through sync and leaves the parameters unchanged."""
+    cfg = model.decoder_only("40k")
+    B, F = 1, 4
+    P = flatten(cfg, G.init_params_ref(cfg, 1))
+    z = G.counter_normal(2, 1, B * 192 * F).reshape(B, 192, F).astype(np.float32)
+    bad = z.copy()
+    bad[0, 5, 2] = 1e5
+    T = F * model.hop(cfg)
+    dldy = G.counter_normal(2, 2, B * T).reshape(B, T).astype(np.float32)
+
+    d = Generator(cfg, B, F)
+    d.set_params(P)
+    d.upload(z)
+    want = d.forward()
+    d.upload(bad, dldy=dldy)
+    assert np.isfinite(d.forward()).all()  # recomputed on bf16 pairs
+    d.upload(z)
+    assert rel(d.forward(), want) < 1e-4  # bf16 pairs: ~2^-17 per operand
+    d.close()
+
+    a = Generator(cfg, B, F)  # the step overflows, is skipped, switched and recomputed
+    a.set_params(P)
+    a.train_step(bad, dldy=dldy)
+    pa = a.get_params()
+    a.close()
+
+    b = Generator(cfg, B, F)  # switched by its first forward, then one step
+    b.set_params(P)
+    b.upload(bad, dldy=dldy)
+    b.forward()
+    b.set_params(P)
+    b.train_step(bad, dldy=dldy)
+    assert np.array_equal(b.get_params(), pa)
+    b.close()
+
+    c = Generator(cfg, B, F)
+    c.set_params(P)
+    c.upload(bad, dldy=dldy)
+    c.step_async(0)
+    with pytest.raises(RuntimeError, match="code -7"):
+        c.sync()
+    assert np.array_equal(c.get_params(), P)  # the overflowing step changed nothing
+    c.step_async(0)
+    c.sync()
+    assert np.array_equal(c.get_params(), pa)
+    c.close()

@@ -103,3 +103,22 @@ def test_new_entry_points_reject_bad_arguments_without_a_gpu():
     assert g.wubu_b200_gen_set_opt_state(None, None, None, 0, 0) == -1
     m = (ctypes.c_float * 4)()
     assert g.wubu_b200_gen_get_opt_state(None, m, m, None, None) == -1
+
+
+def test_primitives_reject_bad_arguments_before_touching_the_device():
+    """Null operands and non-positive sizes return WUBU_B200_ERR_ARG (-1) before any CUDA call, so
+    this runs without a GPU.  (A null operand would otherwise become a tensor map at address 0.)"""
+    import ctypes
+
+    h = lib()
+    buf = ctypes.create_string_buffer(64)
+    p = ctypes.cast(buf, ctypes.c_void_p)
+    # split mode needs the lo halves
+    assert h.wubu_b200_conv1d(p, None, p, None, None, p, 1, 32, 16, 32, 3, 1, 1, 1, None) == -1
+    assert h.wubu_b200_conv1d(None, None, p, None, None, p, 1, 32, 16, 32, 3, 1, 1, 0, None) == -1
+    assert h.wubu_b200_conv1d(p, None, p, None, None, p, 0, 32, 16, 32, 3, 1, 1, 0, None) == -1
+    assert h.wubu_b200_conv1d_wgrad(p, None, p, 1, 32, 16, 32, 3, 1, 1, None) == -1
+    assert h.wubu_b200_conv1d_wgrad_noalloc(p, p, None, 1, 32, 16, 32, 3, 1, 1, None) == -1
+    assert h.wubu_b200_convT(p, p, p, None, None, p, 1, 64, 8, 32, 4, 2, 1, 1, None) == -1
+    assert h.wubu_b200_convT_dgrad(p, p, p, 1, 64, 8, 32, 0, 2, 1, None) == -1
+    assert h.wubu_b200_convT_wgrad(p, None, p, 1, 64, 8, 32, 4, 2, 1, None) == -1

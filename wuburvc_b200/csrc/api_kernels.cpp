@@ -39,8 +39,8 @@ int finish(cudaStream_t st, int* derr) {
   int h = 0;
   cudaMemcpy(&h, derr, sizeof(int), cudaMemcpyDeviceToHost);
   if (h) {
-    fprintf(stderr, "wuburvc_b200: kernel reported error %d (wait timeout)\n", h);
-    return WUBU_B200_ERR_TIMEOUT;
+    fprintf(stderr, "wuburvc_b200: kernel reported error %d\n", h);
+    return h == ERR_RANGE ? WUBU_B200_ERR_RANGE : WUBU_B200_ERR_TIMEOUT;
   }
   return WUBU_B200_OK;
 }
@@ -49,6 +49,10 @@ bool launched(cudaError_t e) {
   if (e != cudaSuccess) fprintf(stderr, "wuburvc_b200: launch failed: %s\n", cudaGetErrorString(e));
   return e == cudaSuccess;
 }
+
+// Positive sizes and the pointers a launch dereferences (a null operand would become a tensor map at
+// address 0, which the kernel would then read).
+bool dims_ok(int B, int a, int b, int c, int k) { return B > 0 && a > 0 && b > 0 && c > 0 && k > 0; }
 
 Epi plain_epi(const float* bias, float* out) {
   Epi e{};
@@ -77,6 +81,9 @@ extern "C" {
 int wubu_b200_conv1d(const void* x_hi, const void* x_lo, const void* w_hi, const void* w_lo, const float* bias,
                      float* out, int B, int C_in, int T, int C_out, int k, int dil, int pad, int split,
                      void* stream) {
+  if (!x_hi || !w_hi || !out || (split && (!x_lo || !w_lo)) || !dims_ok(B, C_in, T, C_out, k) || dil < 1 ||
+      pad < 0 || T + 2 * pad - dil * (k - 1) < 1)
+    return WUBU_B200_ERR_ARG;
   cudaStream_t st = (cudaStream_t)stream;
   Scratch s;
   if (cudaMalloc(&s.err, sizeof(int)) != cudaSuccess) return WUBU_B200_ERR_CUDA;
@@ -90,6 +97,8 @@ int wubu_b200_conv1d(const void* x_hi, const void* x_lo, const void* w_hi, const
 
 int wubu_b200_conv1d_wgrad(const void* dy, const void* x, float* dw, int B, int C_in, int T, int C_out, int k,
                            int dil, int pad, void* stream) {
+  if (!dy || !x || !dw || !dims_ok(B, C_in, T, C_out, k) || dil < 1 || pad < 0 || T + 2 * pad - dil * (k - 1) < 1)
+    return WUBU_B200_ERR_ARG;
   cudaStream_t st = (cudaStream_t)stream;
   Scratch s;
   if (cudaMalloc(&s.err, sizeof(int)) != cudaSuccess) return WUBU_B200_ERR_CUDA;
@@ -105,6 +114,9 @@ int wubu_b200_conv1d_wgrad(const void* dy, const void* x, float* dw, int B, int 
 int wubu_b200_convT(const void* x_hi, const void* x_lo, const void* wp_hi, const void* wp_lo, const float* bias,
                     float* out, int B, int C_in, int T_in, int C_out, int k, int stride, int pad, int split,
                     void* stream) {
+  if (!x_hi || !wp_hi || !out || (split && (!x_lo || !wp_lo)) || !dims_ok(B, C_in, T_in, C_out, k) || stride < 1 ||
+      pad < 0)
+    return WUBU_B200_ERR_ARG;
   cudaStream_t st = (cudaStream_t)stream;
   Scratch s;
   if (cudaMalloc(&s.err, sizeof(int)) != cudaSuccess) return WUBU_B200_ERR_CUDA;
@@ -119,6 +131,7 @@ int wubu_b200_convT(const void* x_hi, const void* x_lo, const void* wp_hi, const
 
 int wubu_b200_convT_dgrad(const void* dy, const void* wd, float* dx, int B, int C_in, int T_in, int C_out, int k,
                           int stride, int pad, void* stream) {
+  if (!dy || !wd || !dx || !dims_ok(B, C_in, T_in, C_out, k) || stride < 1 || pad < 0) return WUBU_B200_ERR_ARG;
   cudaStream_t st = (cudaStream_t)stream;
   Scratch s;
   if (cudaMalloc(&s.err, sizeof(int)) != cudaSuccess) return WUBU_B200_ERR_CUDA;
@@ -132,6 +145,7 @@ int wubu_b200_convT_dgrad(const void* dy, const void* wd, float* dx, int B, int 
 
 int wubu_b200_convT_wgrad(const void* x, const void* dy, float* dw, int B, int C_in, int T_in, int C_out, int k,
                           int stride, int pad, void* stream) {
+  if (!x || !dy || !dw || !dims_ok(B, C_in, T_in, C_out, k) || stride < 1 || pad < 0) return WUBU_B200_ERR_ARG;
   cudaStream_t st = (cudaStream_t)stream;
   Scratch s;
   if (cudaMalloc(&s.err, sizeof(int)) != cudaSuccess) return WUBU_B200_ERR_CUDA;

@@ -96,7 +96,13 @@ static std::vector<std::pair<long long, long long>> plan_buckets(const ParamTabl
   return b;
 }
 
-static std::vector<std::pair<long long, long long>> make_buckets(const Gen& m) { return plan_buckets(m.table); }
+// The context's buckets: the last one also carries the range-flag slot after the gradients (4 floats,
+// keeping the bucket a multiple of 16 bytes), so every rank learns whether any rank's forward overflowed.
+static std::vector<std::pair<long long, long long>> make_buckets(const Gen& m) {
+  auto b = plan_buckets(m.table);
+  b.back().second = m.table.total + 4;
+  return b;
+}
 
 }  // namespace wb
 
@@ -123,6 +129,7 @@ int comm_bucket_ready(Gen& m, int b, cudaStream_t producer) {
   Comm* c = m.comm;
   if (!c || c->world <= 1) return 0;
   NcclApi& api = nccl();
+  if (b + 1 == (int)c->buckets.size()) range_flag(m.err, m.grads + m.table.total, producer);
   if (cudaEventRecord(c->ready[b], producer) != cudaSuccess) return WUBU_B200_ERR_CUDA;
   if (cudaStreamWaitEvent(c->cs, c->ready[b], 0) != cudaSuccess) return WUBU_B200_ERR_CUDA;
   const auto& r = c->buckets[b];

@@ -2,6 +2,7 @@
 #pragma once
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <stdio.h>
@@ -11,6 +12,18 @@
 namespace wb {
 
 typedef __nv_bfloat16 bf16;
+typedef __half f16;
+
+// Forward GEMM operands are fp32 values split into an fp16 high part and an fp16 low part scaled by
+// 2^11: x = hi + lo / 2^11 to ~2^-22 relative (11 significant bits each; the scale keeps the low
+// part out of fp16's subnormal range for |x| >= 2^-14, and |lo| <= |x| so it cannot overflow where
+// hi does not).  Products hi*hi + (hi*lo + lo*hi) / 2^11 are then fp32-accurate; the two sums land
+// in separate accumulators and the epilogue applies the 1/2^11.  Values must stay below 65504
+// (fp16's largest); producers report larger ones (ERR_RANGE) and the context then falls back to
+// bf16 hi + bf16 lo pairs (range-safe, ~2^-17 relative).
+constexpr float kLoScale = 2048.f;
+constexpr float kLoUnscale = 1.f / 2048.f;
+constexpr float kF16Max = 65504.f;
 
 // Error codes written by kernels into the context's device error word.
 enum : int {
@@ -19,6 +32,7 @@ enum : int {
   ERR_WAIT_EMPTY = 2,     // producer gave up waiting for a free stage
   ERR_WAIT_ACC = 3,       // epilogue gave up waiting for the accumulator
   ERR_BAD_SHAPE = 4,
+  ERR_RANGE = 5,          // a forward operand exceeded the fp16 range of the operand split
 };
 
 // Time after which a bounded mbarrier wait gives up and the kernel reports a timeout (ns of
@@ -245,17 +259,21 @@ WB_DEV uint64_t make_sdesc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_byte
   return d;
 }
 
-// Instruction descriptor for kind::f16 with bf16 A/B and f32 accumulation.
-WB_DEV uint32_t make_idesc_bf16(int M, int N, int a_mn_major, int b_mn_major) {
+// Instruction descriptor for kind::f16 with f32 accumulation; A and B are both bf16 (bf16 = 1) or
+// both fp16 (bf16 = 0).
+WB_DEV uint32_t make_idesc(int M, int N, int a_mn_major, int b_mn_major, int bf16) {
   uint32_t d = 0;
-  d |= 1u << 4;                 // D format f32
-  d |= 1u << 7;                 // A format bf16
-  d |= 1u << 10;                // B format bf16
+  d |= 1u << 4;                          // D format f32
+  d |= (uint32_t)(bf16 ? 1 : 0) << 7;    // A format: 0 f16, 1 bf16
+  d |= (uint32_t)(bf16 ? 1 : 0) << 10;   // B format
   d |= (uint32_t)(a_mn_major & 1) << 15;
   d |= (uint32_t)(b_mn_major & 1) << 16;
   d |= (uint32_t)((N >> 3) & 0x3F) << 17;
   d |= (uint32_t)((M >> 4) & 0x1F) << 24;
   return d;
+}
+WB_DEV uint32_t make_idesc_bf16(int M, int N, int a_mn_major, int b_mn_major) {
+  return make_idesc(M, N, a_mn_major, b_mn_major, 1);
 }
 
 // ---- misc -------------------------------------------------------------------
@@ -270,6 +288,32 @@ WB_DEV float snake(float x, float a) {
 WB_DEV void split_bf16(float x, bf16& hi, bf16& lo) {
   hi = __float2bfloat16_rn(x);
   lo = __float2bfloat16_rn(x - __bfloat162float(hi));
+}
+
+// the forward operand split (see kLoScale): x = hi + lo / 2^11
+WB_DEV void split_f16(float x, f16& hi, f16& lo) {
+  hi = __float2half_rn(x);
+  lo = __float2half_rn((x - __half2float(hi)) * kLoScale);
+}
+WB_DEV float join_f16(f16 hi, f16 lo) { return __half2float(hi) + __half2float(lo) * kLoUnscale; }
+
+// A forward operand stored as 16-bit words in either format: fp16 hi / scaled lo (fmt_bf16 = 0) or
+// the range-safe bf16 hi / lo a context falls back to after a range error (fmt_bf16 = 1).
+WB_DEV void split_op(float x, int fmt_bf16, f16& hi, f16& lo) {
+  if (fmt_bf16) {
+    bf16 h, l;
+    split_bf16(x, h, l);
+    hi = __ushort_as_half(__bfloat16_as_ushort(h));
+    lo = __ushort_as_half(__bfloat16_as_ushort(l));
+  } else {
+    split_f16(x, hi, lo);
+  }
+}
+WB_DEV float join_op(f16 hi, f16 lo, int fmt_bf16) {
+  if (fmt_bf16)
+    return __bfloat162float(__ushort_as_bfloat16(__half_as_ushort(hi))) +
+           __bfloat162float(__ushort_as_bfloat16(__half_as_ushort(lo)));
+  return join_f16(hi, lo);
 }
 
 }  // namespace wb

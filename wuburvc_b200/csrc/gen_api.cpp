@@ -11,6 +11,7 @@ bool gen_forward(Gen& m);
 bool gen_backward(Gen& m);
 bool gen_adamw(Gen& m, float grad_scale, int bump_noise);
 void gen_free(Gen& m);
+bool gen_set_operand_format(Gen& m, int bf16);
 int comm_attach(Gen& m, int rank, int world, const void* id128);
 int comm_unique_id(void* out128);
 int comm_world(Gen& m);
@@ -33,11 +34,25 @@ int check_err(Gen& m) {
   int h = 0;
   if (cudaMemcpy(&h, m.err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return WUBU_B200_ERR_CUDA;
   if (h) {
-    fprintf(stderr, "wuburvc_b200: a kernel's bounded wait expired (code %d)\n", h);
     cudaMemset(m.err, 0, sizeof(int));
+    if (h == ERR_RANGE) {
+      fprintf(stderr, "wuburvc_b200: a forward operand (activation, weight or z) reached 65504, the limit of "
+                      "the fp16 operand split\n");
+      return WUBU_B200_ERR_RANGE;
+    }
+    fprintf(stderr, "wuburvc_b200: a kernel's bounded wait expired (code %d)\n", h);
     return WUBU_B200_ERR_TIMEOUT;
   }
   return WUBU_B200_OK;
+}
+
+// After a range error (a forward operand reached the fp16 limit of the operand split; the step's
+// update was skipped on the device) the context switches to the bf16 pair format for good.  Returns
+// true when the caller should recompute the step.
+bool range_fallback(Gen& m, int rc) {
+  if (rc != WUBU_B200_ERR_RANGE || m.op_bf16) return false;
+  fprintf(stderr, "wuburvc_b200: switching this context's forward operands to the bf16 pair format\n");
+  return gen_set_operand_format(m, 1);
 }
 
 // whole flat buffers between the reference tensor layouts and the device storage layouts
@@ -247,12 +262,16 @@ int wubu_b200_gen_forward(WubuB200Gen* gen, unsigned long long noise_stream, flo
   if (!gen) return WUBU_B200_ERR_ARG;
   Gen& m = gen->m;
   cudaSetDevice(m.opt.device);
-  if (set_noise_stream(m, noise_stream)) return WUBU_B200_ERR_CUDA;
-  if (!gen_forward(m)) return WUBU_B200_ERR_CUDA;
-  if (audio_out && cudaMemcpyAsync(audio_out, m.audio, sizeof(float) * m.B * m.T, cudaMemcpyDeviceToHost, m.stream) !=
-                       cudaSuccess)
-    return WUBU_B200_ERR_CUDA;
-  return check_err(m);
+  for (int attempt = 0;; ++attempt) {
+    if (set_noise_stream(m, noise_stream)) return WUBU_B200_ERR_CUDA;
+    if (!gen_forward(m)) return WUBU_B200_ERR_CUDA;
+    if (audio_out &&
+        cudaMemcpyAsync(audio_out, m.audio, sizeof(float) * m.B * m.T, cudaMemcpyDeviceToHost, m.stream) != cudaSuccess)
+      return WUBU_B200_ERR_CUDA;
+    const int rc = check_err(m);
+    if (attempt == 0 && range_fallback(m, rc)) continue;
+    return rc;
+  }
 }
 
 int wubu_b200_gen_backward(WubuB200Gen* gen) {
@@ -278,13 +297,18 @@ int wubu_b200_gen_train_step(WubuB200Gen* gen, const float* z, const float* f0, 
     const int rc = upload(m, z, f0, g, noise, dldy);
     if (rc) return rc;
   }
-  if (set_noise_stream(m, noise_stream)) return WUBU_B200_ERR_CUDA;
-  const int rc = run_step_graph(m);
-  if (rc) return rc;
-  if (audio_out && cudaMemcpyAsync(audio_out, m.audio, sizeof(float) * m.B * m.T, cudaMemcpyDeviceToHost, m.stream) !=
-                       cudaSuccess)
-    return WUBU_B200_ERR_CUDA;
-  return check_err(m);
+  for (int attempt = 0;; ++attempt) {
+    if (set_noise_stream(m, noise_stream)) return WUBU_B200_ERR_CUDA;
+    const int rc = run_step_graph(m);
+    if (rc) return rc;
+    if (audio_out &&
+        cudaMemcpyAsync(audio_out, m.audio, sizeof(float) * m.B * m.T, cudaMemcpyDeviceToHost, m.stream) != cudaSuccess)
+      return WUBU_B200_ERR_CUDA;
+    const int rc2 = check_err(m);
+    // the overflowing step changed nothing (its update was skipped on every rank): recompute it
+    if (attempt == 0 && range_fallback(m, rc2)) continue;
+    return rc2;
+  }
 }
 
 int wubu_b200_gen_train_step_async(WubuB200Gen* gen, unsigned long long noise_stream) {
@@ -298,7 +322,9 @@ int wubu_b200_gen_train_step_async(WubuB200Gen* gen, unsigned long long noise_st
 int wubu_b200_gen_sync(WubuB200Gen* gen) {
   if (!gen) return WUBU_B200_ERR_ARG;
   cudaSetDevice(gen->m.opt.device);
-  return check_err(gen->m);
+  const int rc = check_err(gen->m);
+  range_fallback(gen->m, rc);  // the skipped steps are reported; later steps use the bf16 format
+  return rc;
 }
 
 int wubu_b200_gen_graph_kernels(WubuB200Gen* gen) {

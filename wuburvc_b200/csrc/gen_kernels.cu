@@ -131,7 +131,7 @@ __global__ void __launch_bounds__(256) prep_norm_kernel(const PrepDesc* __restri
 
 __global__ void __launch_bounds__(256) prep_tile_kernel(const PrepDesc* __restrict__ descs, int ndesc) {
   __shared__ float s_scale[128];
-  __shared__ unsigned short ht[128][34];  // transposed hi: [q - q0][p - p0]
+  __shared__ unsigned short ht[128][34];  // transposed bf16 weight: [q - q0][p - p0]
   __shared__ int di;
   if (threadIdx.x == 0) di = prep_find(descs, ndesc, 1);
   __syncthreads();
@@ -181,34 +181,38 @@ __global__ void __launch_bounds__(256) prep_tile_kernel(const PrepDesc* __restri
     } else {
       x[0] = d.v[src];
     }
-    bf16 hi[4], lo[4];
+    f16 hi[4], lo[4];
+    bool big = false;
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       if (e < QS) {
         const float sc = d.is_convT ? s_scale[lane * QS + e] : s_scale[pl];
-        split_bf16(x[e] * sc, hi[e], lo[e]);
-        ht[lane * QS + e][pl] = __bfloat16_as_ushort(hi[e]);
+        const float w = x[e] * sc;
+        split_op(w, d.fmt_bf16, hi[e], lo[e]);
+        big |= !d.fmt_bf16 && !(fabsf(w) < kF16Max);
+        ht[lane * QS + e][pl] = __bfloat16_as_ushort(__float2bfloat16_rn(w));
       }
     }
+    if (big && d.range_err) atomicCAS(d.range_err, 0, ERR_RANGE);
     if (QS == 4) {
       *reinterpret_cast<uint2*>(d.fwd_hi + dst) =
-          make_uint2(__bfloat16_as_ushort(hi[0]) | ((uint32_t)__bfloat16_as_ushort(hi[1]) << 16),
-                     __bfloat16_as_ushort(hi[2]) | ((uint32_t)__bfloat16_as_ushort(hi[3]) << 16));
+          make_uint2(__half_as_ushort(hi[0]) | ((uint32_t)__half_as_ushort(hi[1]) << 16),
+                     __half_as_ushort(hi[2]) | ((uint32_t)__half_as_ushort(hi[3]) << 16));
       *reinterpret_cast<uint2*>(d.fwd_lo + dst) =
-          make_uint2(__bfloat16_as_ushort(lo[0]) | ((uint32_t)__bfloat16_as_ushort(lo[1]) << 16),
-                     __bfloat16_as_ushort(lo[2]) | ((uint32_t)__bfloat16_as_ushort(lo[3]) << 16));
+          make_uint2(__half_as_ushort(lo[0]) | ((uint32_t)__half_as_ushort(lo[1]) << 16),
+                     __half_as_ushort(lo[2]) | ((uint32_t)__half_as_ushort(lo[3]) << 16));
     } else if (QS == 2) {
       *reinterpret_cast<uint32_t*>(d.fwd_hi + dst) =
-          __bfloat16_as_ushort(hi[0]) | ((uint32_t)__bfloat16_as_ushort(hi[1]) << 16);
+          __half_as_ushort(hi[0]) | ((uint32_t)__half_as_ushort(hi[1]) << 16);
       *reinterpret_cast<uint32_t*>(d.fwd_lo + dst) =
-          __bfloat16_as_ushort(lo[0]) | ((uint32_t)__bfloat16_as_ushort(lo[1]) << 16);
+          __half_as_ushort(lo[0]) | ((uint32_t)__half_as_ushort(lo[1]) << 16);
     } else {
       d.fwd_hi[dst] = hi[0];
       d.fwd_lo[dst] = lo[0];
     }
   }
   __syncthreads();
-  // transposed hi: rows q0..q0+QW-1 of dg[td] ([Q][P]), 32 p each, 16 threads x 2 values per row
+  // transposed bf16: rows q0..q0+QW-1 of dg[td] ([Q][P]), 32 p each, 16 threads x 2 values per row
   for (int r = tid >> 4; r < QW; r += 16) {
     const int pp = (tid & 15) * 2;
     const uint32_t w = (uint32_t)ht[r][pp] | ((uint32_t)ht[r][pp + 1] << 16);
@@ -286,16 +290,34 @@ void wn_backward_batched(const WnDesc* descs, int ndesc, int total_rows, cudaStr
 }
 
 // Step state lives on the device so a captured step graph advances it by itself.
-__global__ void step_bump_kernel(StepState* s, int bump_noise) {
+WB_DEV bool skip_step(const int* err, const float* skip_flag) {
+  return (err && *err == ERR_RANGE) || (skip_flag && *skip_flag > 0.f);
+}
+
+__global__ void step_bump_kernel(StepState* s, int bump_noise, const int* err, const float* skip_flag) {
+  if (skip_step(err, skip_flag)) return;
   s->adam_t += 1;
   if (bump_noise) s->noise_stream += 1;
 }
 
-void step_bump(StepState* s, int bump_noise, cudaStream_t st) { step_bump_kernel<<<1, 1, 0, st>>>(s, bump_noise); }
+void step_bump(StepState* s, int bump_noise, const int* err, const float* skip_flag, cudaStream_t st) {
+  step_bump_kernel<<<1, 1, 0, st>>>(s, bump_noise, err, skip_flag);
+}
+
+__global__ void range_flag_kernel(const int* err, float* flag) { *flag = (*err == ERR_RANGE) ? 1.f : 0.f; }
+
+void range_flag(const int* err, float* flag, cudaStream_t st) { range_flag_kernel<<<1, 1, 0, st>>>(err, flag); }
 
 __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
                              float* __restrict__ v, long long n, float lr, float b1, float b2, float eps, float wd,
-                             const StepState* __restrict__ state, float grad_scale) {
+                             const StepState* __restrict__ state, float grad_scale, int* err,
+                             const float* skip_flag) {
+  // a step whose forward overflowed the operand format (here or, under data parallelism, on another
+  // rank) is skipped whole; the host recomputes it
+  if (skip_step(err, skip_flag)) {
+    if (blockIdx.x == 0 && threadIdx.x == 0 && err) atomicCAS(err, 0, ERR_RANGE);
+    return;
+  }
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   const long long n4 = n >> 2;
   // bias corrections of src/wubu_train.c:97-103 (clamped, and applied twice like the reference)
@@ -328,29 +350,33 @@ __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g,
 }
 
 void adamw(float* p, const float* g, float* m, float* v, long long n, float lr, float b1, float b2, float eps, float wd,
-           const StepState* state, float grad_scale, cudaStream_t st) {
+           const StepState* state, float grad_scale, int* err, const float* skip_flag, cudaStream_t st) {
   // n is a multiple of 4 (flat buffer segments are 64-float aligned)
   const long long n4 = n >> 2;
-  adamw_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(p, g, m, v, n, lr, b1, b2, eps, wd, state, grad_scale);
+  adamw_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(p, g, m, v, n, lr, b1, b2, eps, wd, state, grad_scale,
+                                                             err, skip_flag);
 }
 
 // =============================================================================================
 // inputs / cond
 // =============================================================================================
-__global__ void pack_z_kernel(const float* __restrict__ z, int B, int C, int F, bf16* __restrict__ hi,
-                              bf16* __restrict__ lo) {
+__global__ void pack_z_kernel(const float* __restrict__ z, int B, int C, int F, f16* __restrict__ hi,
+                              f16* __restrict__ lo, bf16* __restrict__ zb, int* range_err, int fmt_bf16) {
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (long long)B * C * F) return;
   const int c = (int)(i % C);
   const long long bf = i / C;
   const int f = (int)(bf % F), b = (int)(bf / F);
   const float x = z[((size_t)b * C + c) * F + f];
-  split_bf16(x, hi[i], lo[i]);
+  split_op(x, fmt_bf16, hi[i], lo[i]);
+  zb[i] = __float2bfloat16_rn(x);
+  if (!fmt_bf16 && !(fabsf(x) < kF16Max) && range_err) atomicCAS(range_err, 0, ERR_RANGE);
 }
 
-void pack_z(const float* z, int B, int C, int F, bf16* hi, bf16* lo, cudaStream_t st) {
+void pack_z(const float* z, int B, int C, int F, f16* hi, f16* lo, bf16* zb, int* range_err, int fmt_bf16,
+            cudaStream_t st) {
   const long long n = (long long)B * C * F;
-  pack_z_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(z, B, C, F, hi, lo);
+  pack_z_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(z, B, C, F, hi, lo, zb, range_err, fmt_bf16);
 }
 
 // rowadd[b][c] = bias[c] + sum_j W[c][j] * g[b][j]: warp per output channel c (its weight row read

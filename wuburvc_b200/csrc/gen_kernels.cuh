@@ -5,7 +5,8 @@
 namespace wb {
 
 // ---- weights -------------------------------------------------------------------------------
-// Effective weight W (= g*v/||v|| under weight norm, else the raw parameter) -> bf16 GEMM layouts.
+// Effective weight W (= g*v/||v|| under weight norm, else the raw parameter) -> GEMM layouts: the
+// forward's operand pair (fp16 hi + scaled lo, or bf16 hi + lo) and the input gradient's bf16.
 // Storage of a weight is tap-major [k][P][Q] f32 (Q fastest): conv P = C_out, Q = C_in (weight-norm
 // rows are p); ConvTranspose P = C_out, Q = C_in (weight-norm rows are q, the reference's dim 0).
 //   conv : fwd [k][C_out][C_in] hi/lo (the storage layout),   dgrad [k][C_in][C_out], taps flipped
@@ -13,8 +14,8 @@ namespace wb {
 // `norm` receives ||v|| per weight-norm row.  Two launches for all weights of a step:
 //   prep_norm : norms (conv: warp per row; ConvTranspose: partial sums of squares over chunks of
 //               kPrepPairs (tap, p) pairs x 32 columns, summed in fixed order by the tile kernel)
-//   prep_tile : one tap x 32 p x 32*qs q tile per block: scaled hi/lo in the storage layout and the
-//               transposed hi through shared memory, both written coalesced.
+//   prep_tile : one tap x 32 p x 32*qs q tile per block: the scaled operand pair in the storage
+//               layout and the transposed bf16 through shared memory, both written coalesced.
 // P and Q must be multiples of 32.
 constexpr int kPrepPairs = 256;
 struct PrepDesc {
@@ -22,7 +23,10 @@ struct PrepDesc {
   const float* g;   // weight-norm gains, or null (plain weight)
   float* norm;      // [rows] ||v|| per weight-norm row (when g)
   float* npart;     // ConvTranspose under weight norm: [nchunks][Q] partial sums of squares
-  bf16 *fwd_hi, *fwd_lo, *dg;
+  f16 *fwd_hi, *fwd_lo;  // forward operand pair (fp16 hi + fp16 lo * 2^11, or the bf16 pair)
+  bf16* dg;               // input-gradient operand (bf16)
+  int* range_err;         // set to ERR_RANGE if |W| >= 65504
+  int fmt_bf16;           // forward pair as bf16 hi + bf16 lo (the range-safe fallback format)
   int P, Q, k, is_convT, stride;
   int qs;           // q columns per lane in the tile kernel (1, 2 or 4)
   int nchunks;      // ConvTranspose norm chunks
@@ -52,16 +56,24 @@ struct StepState {
   int adam_t;                       // AdamW step count
   int pad;
 };
-void step_bump(StepState* s, int bump_noise, cudaStream_t st);
+// Both skip a step whose forward reported a range error (err == ERR_RANGE), or, under data
+// parallelism, on which any rank did (skip_flag > 0: the ranks' flags summed by the all-reduce); the
+// step then leaves the parameters, moments and counters as they were, to be recomputed.  adamw also
+// raises ERR_RANGE on this rank when only another rank overflowed, so every rank's host sees it.
+void step_bump(StepState* s, int bump_noise, const int* err, const float* skip_flag, cudaStream_t st);
 
 // AdamW over a flat buffer, restating the reference update (bias correction applied twice).
 // Gradients are multiplied by grad_scale first (1/world under data parallelism).
 void adamw(float* p, const float* g, float* m, float* v, long long n, float lr, float b1, float b2, float eps,
-           float wd, const StepState* state, float grad_scale, cudaStream_t st);
+           float wd, const StepState* state, float grad_scale, int* err, const float* skip_flag, cudaStream_t st);
+// flag = (err == ERR_RANGE) as a float, for the data-parallel all-reduce
+void range_flag(const int* err, float* flag, cudaStream_t st);
 
 // ---- inputs --------------------------------------------------------------------------------
-// z [B][C][F] f32 -> [B][F][C] bf16 hi/lo
-void pack_z(const float* z, int B, int C, int F, bf16* hi, bf16* lo, cudaStream_t st);
+// z [B][C][F] f32 -> [B][F][C] operand pair (fp16 hi / scaled lo, or the bf16 pair) and a bf16 copy
+// (the conv_pre weight gradient's operand)
+void pack_z(const float* z, int B, int C, int F, f16* hi, f16* lo, bf16* zb, int* range_err, int fmt_bf16,
+            cudaStream_t st);
 
 // cond(g): rowadd[b][c] = bias[c] + sum_i W[c][i] g[b][i]
 void cond_forward(const float* W, const float* bias, const float* g, int B, int C, int gin, float* rowadd,
@@ -103,9 +115,12 @@ struct NoiseActArgs {
   float slope;
   int n_act;              // snake: one activation per stack (alpha differs); lrelu: 1
   const float* alpha[3];
-  bf16* act_hi[3];
-  bf16* act_lo[3];
+  f16* act_hi[3];         // activation: forward operand pair (fp16 hi + fp16 lo * 2^11) ...
+  f16* act_lo[3];
+  bf16* act_bf[3];        // ... and its bf16 copy (weight-gradient operand, LeakyReLU masks)
   bf16* pre;              // bf16 copy of x (snake masks)
+  int* range_err;         // set to ERR_RANGE if |activation| >= 65504
+  int fmt_bf16;           // operand pair as bf16 hi + lo (fallback format)
 };
 void noise_add_act(const NoiseActArgs& a, cudaStream_t st);
 
@@ -120,17 +135,18 @@ void noise_wgrad_reduce(const float* wpart, int nparts, int C, int k, float* dW,
                         cudaStream_t st);
 
 // ---- conv_post ------------------------------------------------------------------------------
-// audio[b][t] = tanh(sum_{c,tap} a[b][t-3+tap][c] * W[c][tap]), a = hi + lo
-void post_forward(const bf16* a_hi, const bf16* a_lo, const float* W, int B, int T, int C, int k, float* audio,
-                  cudaStream_t st);
+// audio[b][t] = tanh(sum_{c,tap} a[b][t-3+tap][c] * W[c][tap]), a = the operand pair (hi, lo)
+void post_forward(const f16* a_hi, const f16* a_lo, int fmt_bf16, const float* W, int B, int T, int C, int k,
+                  float* audio, cudaStream_t st);
 // d_pre = dy*(1-y^2); d_a = conv_post^T(d_pre); d_stage = d_a * act'(stage) * scale -> f32 + bf16
 // partials: colsum of d_stage (64-row blocks), dW_post, snake d(alpha)
 struct PostBwdArgs {
   const float* dy;        // [B][T]
   const float* audio;     // [B][T]
   const float* W;         // [C][k]
-  const bf16* a_hi;       // [B][T][C] activation (wgrad operand, with lo)
-  const bf16* a_lo;
+  const f16* a_hi;        // [B][T][C] activation (wgrad operand): the operand pair
+  const f16* a_lo;
+  int fmt_bf16;           // pair format of a_hi / a_lo
   const bf16* mask_src;   // activated (lrelu sign) or pre-activation (snake)
   const float* alpha;     // snake alpha [C]
   int act_kind;

@@ -99,10 +99,12 @@ __global__ void __launch_bounds__(256) noise_add_act_kernel(NoiseActArgs a) {
     if (a.pre) a.pre[i] = __float2bfloat16_rn(x[r]);
     for (int q = 0; q < a.n_act; ++q) {
       const float y = act_fwd2(x[r], a.act_kind, a.slope, al[q]);
-      bf16 hi, lo;
-      split_bf16(y, hi, lo);
+      f16 hi, lo;
+      split_op(y, a.fmt_bf16, hi, lo);
       a.act_hi[q][i] = hi;
       a.act_lo[q][i] = lo;
+      a.act_bf[q][i] = __float2bfloat16_rn(y);
+      if (!a.fmt_bf16 && !(fabsf(y) < kF16Max) && a.range_err) atomicCAS(a.range_err, 0, ERR_RANGE);
     }
   }
 }
@@ -439,8 +441,8 @@ constexpr int kPostC = 32;
 constexpr int kPostWarpRows = 16;
 
 
-__global__ void __launch_bounds__(256) post_forward_kernel(const bf16* __restrict__ hi, const bf16* __restrict__ lo,
-                                                           const float* __restrict__ W, int B, int T,
+__global__ void __launch_bounds__(256) post_forward_kernel(const f16* __restrict__ hi, const f16* __restrict__ lo,
+                                                           int fmt_bf16, const float* __restrict__ W, int B, int T,
                                                            float* __restrict__ audio) {
   const int lane = threadIdx.x & 31;
   constexpr int pad = kPostK / 2, win = kPostWarpRows + kPostK - 1;
@@ -459,7 +461,7 @@ __global__ void __launch_bounds__(256) post_forward_kernel(const bf16* __restric
       x[i] = 0.f;
       if (r >= 0 && r < T) {
         const size_t off = (base + r) * kPostC + lane;
-        x[i] = __bfloat162float(hi[off]) + __bfloat162float(lo[off]);
+        x[i] = join_op(hi[off], lo[off], fmt_bf16);
       }
     }
     float v[32];
@@ -477,11 +479,11 @@ __global__ void __launch_bounds__(256) post_forward_kernel(const bf16* __restric
   }
 }
 
-void post_forward(const bf16* a_hi, const bf16* a_lo, const float* W, int B, int T, int C, int k, float* audio,
-                  cudaStream_t st) {
+void post_forward(const f16* a_hi, const f16* a_lo, int fmt_bf16, const float* W, int B, int T, int C, int k,
+                  float* audio, cudaStream_t st) {
   (void)C;
   (void)k;  // 32 x 7 (checked at setup)
-  post_forward_kernel<<<148 * 8, 256, 0, st>>>(a_hi, a_lo, W, B, T, audio);
+  post_forward_kernel<<<148 * 8, 256, 0, st>>>(a_hi, a_lo, fmt_bf16, W, B, T, audio);
 }
 
 constexpr int kPostRows = 64;
@@ -522,7 +524,7 @@ __global__ void __launch_bounds__(256) post_backward_kernel(PostBwdArgs a) {
     xin8[r] = xm8[r] = 0.f;
     if (row < nrows) {
       const size_t off = (size_t)row * kPostC + c;
-      xin8[r] = __bfloat162float(a.a_hi[off]) + __bfloat162float(a.a_lo[off]);
+      xin8[r] = join_op(a.a_hi[off], a.a_lo[off], a.fmt_bf16);
       xm8[r] = __bfloat162float(a.mask_src[off]);
     }
   }

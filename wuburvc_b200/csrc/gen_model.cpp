@@ -2,8 +2,10 @@
 // backward, AdamW, CUDA-graph capture.
 //
 // Data layout in HBM: every activation is channels-last [B][T][C].  Residual streams (pair inputs,
-// stage sums, their gradients) are fp32; GEMM operands are bf16 — forward operands as hi/lo pairs
-// (bf16x3 products), backward operands single bf16.  Parameters, gradients and AdamW moments live
+// stage sums, their gradients) are fp32.  Forward GEMM operands are fp16 hi + fp16 lo*2^11 pairs
+// (three products, fp32-accurate; bf16 pairs after a range error); every activation also keeps a
+// bf16 copy, the weight gradient's operand and the LeakyReLU mask source; backward operands are
+// single bf16.  Parameters, gradients and AdamW moments live
 // in flat fp32 buffers laid out by the parameter table.
 #include "gen_model.h"
 
@@ -17,6 +19,7 @@ namespace wb {
 
 // comm.cpp (no-ops without a communicator)
 int comm_bucket_ready(Gen& m, int bucket, cudaStream_t producer);
+int comm_world(Gen& m);
 int comm_join(Gen& m);
 void comm_destroy(Gen& m);
 
@@ -266,12 +269,16 @@ bool gen_setup(Gen& m) {
 
   m.table = build_param_table(c);
   const size_t P = (size_t)m.table.total;
-  if (!dalloc(m, &m.params, P) || !dalloc(m, &m.grads, P) || !dalloc(m, &m.adam_m, P) || !dalloc(m, &m.adam_v, P))
+  // the gradient buffer carries one more slot after the parameters: the data-parallel range flag
+  // (summed over ranks in the last all-reduce bucket)
+  if (!dalloc(m, &m.params, P) || !dalloc(m, &m.grads, P + 64) || !dalloc(m, &m.adam_m, P) ||
+      !dalloc(m, &m.adam_v, P))
     return false;
 
   // ---- inputs ----
   if (!dalloc(m, &m.z, (size_t)B * c.in_channels * m.F) || !dalloc(m, &m.dldy, (size_t)B * m.T)) return false;
-  if (!dalloc(m, &m.z_hi, (size_t)B * m.F * c.in_channels) || !dalloc(m, &m.z_lo, (size_t)B * m.F * c.in_channels))
+  if (!dalloc(m, &m.z_hi, (size_t)B * m.F * c.in_channels) || !dalloc(m, &m.z_lo, (size_t)B * m.F * c.in_channels) ||
+      !dalloc(m, &m.z_bf, (size_t)B * m.F * c.in_channels))
     return false;
   if (c.gin_channels && !dalloc(m, &m.g, (size_t)B * c.gin_channels)) return false;
   if (c.nsf) {
@@ -325,20 +332,23 @@ bool gen_setup(Gen& m) {
 
   // ---- activations ----
   const size_t n_pre = (size_t)B * m.F * C0;
-  if (!dalloc(m, &m.pre_hi, n_pre) || !dalloc(m, &m.pre_lo, n_pre) || !dalloc(m, &m.d_pre_bf, n_pre)) return false;
+  if (!dalloc(m, &m.pre_hi, n_pre) || !dalloc(m, &m.pre_lo, n_pre) || !dalloc(m, &m.pre_bf, n_pre) ||
+      !dalloc(m, &m.d_pre_bf, n_pre))
+    return false;
   if (snake && !dalloc(m, &m.pre_pre, n_pre)) return false;
   if (c.gin_channels && !dalloc(m, &m.rowadd, (size_t)B * C0)) return false;
   if (!dalloc(m, &m.audio, (size_t)B * m.T)) return false;
   for (int L = 0; L < 4; ++L) {
     StageBufs& s = m.sg[L];
     const size_t n = (size_t)s.rows * s.C;
-    if (!dalloc(m, &s.x_in, n) || !dalloc(m, &s.sout, n) || !dalloc(m, &s.sa_hi, n) || !dalloc(m, &s.sa_lo, n))
+    if (!dalloc(m, &s.x_in, n) || !dalloc(m, &s.sout, n) || !dalloc(m, &s.sa_hi, n) || !dalloc(m, &s.sa_lo, n) ||
+        !dalloc(m, &s.sa_bf, n))
       return false;
     if (!dalloc(m, &s.d_s, n) || !dalloc(m, &s.d_s_bf, n) || !dalloc(m, &s.d_x, n) || !dalloc(m, &s.d_x_bf, n))
       return false;
     const int nxa = snake ? m.nk : 1;
     for (int q = 0; q < nxa; ++q)
-      if (!dalloc(m, &s.xa_hi[q], n) || !dalloc(m, &s.xa_lo[q], n)) return false;
+      if (!dalloc(m, &s.xa_hi[q], n) || !dalloc(m, &s.xa_lo[q], n) || !dalloc(m, &s.xa_bf[q], n)) return false;
     if (snake && (!dalloc(m, &s.x_pre, n) || !dalloc(m, &s.s_pre, n))) return false;
     const int tiles = B * ((s.T + 127) / 128);
     for (int j = 0; j < m.nk; ++j) {
@@ -347,13 +357,16 @@ bool gen_setup(Gen& m) {
       k.p[0] = s.x_in;
       k.a1_hi[0] = s.xa_hi[snake ? j : 0];
       k.a1_lo[0] = s.xa_lo[snake ? j : 0];
+      k.a1_bf[0] = s.xa_bf[snake ? j : 0];
       k.a1_pre[0] = s.x_pre;
       for (int cp = 0; cp < m.nd; ++cp) {
         if (cp > 0) {
-          if (!dalloc(m, &k.p[cp], n) || !dalloc(m, &k.a1_hi[cp], n) || !dalloc(m, &k.a1_lo[cp], n)) return false;
+          if (!dalloc(m, &k.p[cp], n) || !dalloc(m, &k.a1_hi[cp], n) || !dalloc(m, &k.a1_lo[cp], n) ||
+              !dalloc(m, &k.a1_bf[cp], n))
+            return false;
           if (snake && !dalloc(m, &k.a1_pre[cp], n)) return false;
         }
-        if (!dalloc(m, &k.a2_hi[cp], n) || !dalloc(m, &k.a2_lo[cp], n)) return false;
+        if (!dalloc(m, &k.a2_hi[cp], n) || !dalloc(m, &k.a2_lo[cp], n) || !dalloc(m, &k.a2_bf[cp], n)) return false;
         if (snake && !dalloc(m, &k.a2_pre[cp], n)) return false;
         // column-sum partials: one row per tile (general kernel) or per CTA of the persistent kernel,
         // which may split N in two and writes two rows (epilogue groups) per CTA: at most 4 * tiles rows
@@ -389,6 +402,8 @@ bool gen_setup(Gen& m) {
     e.rowadd = m.rowadd;
     e.act_hi = m.pre_hi;
     e.act_lo = m.pre_lo;
+    e.act_bf = m.pre_bf;
+    e.range_err = m.err;
     e.act_kind = c.activation;
     e.act_alpha = alpha_ptr(m, "dec.ups_act.0.alpha");
     e.pre_hi = m.pre_pre;
@@ -399,8 +414,8 @@ bool gen_setup(Gen& m) {
     StageBufs& s = m.sg[L];
     const bool last = L == 3;
     const int Tin = (L == 0) ? m.F : m.sg[L - 1].T;
-    const bf16* in_hi = (L == 0) ? m.pre_hi : m.sg[L - 1].sa_hi;
-    const bf16* in_lo = (L == 0) ? m.pre_lo : m.sg[L - 1].sa_lo;
+    const f16* in_hi = (L == 0) ? m.pre_hi : m.sg[L - 1].sa_hi;
+    const f16* in_lo = (L == 0) ? m.pre_lo : m.sg[L - 1].sa_lo;
     {  // ups forward
       Epi e = epi0(c.lrelu_slope);
       e.bias = m.P(s.wu.pb);
@@ -421,6 +436,8 @@ bool gen_setup(Gen& m) {
           e.bias = m.P(k.w1[cp].pb);
           e.act_hi = k.a2_hi[cp];
           e.act_lo = k.a2_lo[cp];
+          e.act_bf = k.a2_bf[cp];
+          e.range_err = m.err;
           e.act_kind = c.activation;
           e.act_alpha = alpha_ptr(m, "dec.resblocks." + R + ".alpha2." + P);
           e.pre_hi = k.a2_pre[cp];
@@ -437,6 +454,8 @@ bool gen_setup(Gen& m) {
             e.out_f32 = k.p[cp + 1];
             e.act_hi = k.a1_hi[cp + 1];
             e.act_lo = k.a1_lo[cp + 1];
+            e.act_bf = k.a1_bf[cp + 1];
+            e.range_err = m.err;
             e.act_alpha = alpha_ptr(m, "dec.resblocks." + R + ".alpha1." + std::to_string(cp + 1));
             e.pre_hi = k.a1_pre[cp + 1];
           } else {
@@ -446,6 +465,8 @@ bool gen_setup(Gen& m) {
             if (j == m.nk - 1) {
               e.act_hi = s.sa_hi;
               e.act_lo = s.sa_lo;
+              e.act_bf = s.sa_bf;
+              e.range_err = m.err;
               e.pre_hi = s.s_pre;
               e.slope = last ? c.final_slope : c.lrelu_slope;
               e.act_alpha = alpha_ptr(m, last ? "dec.post_act.alpha" : "dec.ups_act." + std::to_string(L + 1) + ".alpha");
@@ -483,7 +504,7 @@ bool gen_setup(Gen& m) {
         {  // conv2 dgrad -> d_c1 (mask of conv1's activation)
           Epi e = epi0(c.lrelu_slope);
           e.act_kind = c.activation;
-          e.mask_src = snake ? k.a2_pre[cp] : k.a2_hi[cp];
+          e.mask_src = snake ? k.a2_pre[cp] : k.a2_bf[cp];
           e.mask_alpha = alpha_ptr(m, "dec.resblocks." + R + ".alpha2." + P);
           e.alpha_part = k.ap2[cp];
           e.out_bf16 = k.d_c1;
@@ -494,13 +515,13 @@ bool gen_setup(Gen& m) {
         }
         {  // conv2 wgrad
           ConvGeom g{B, s.T, s.T, s.C, s.C, kk, 1, (kk - 1) / 2};
-          if (!plan_wgrad(k.g2[cp].L, g, dp_out_b, k.a2_hi[cp], nullptr, ~size_t(0), kWgradCtas, m.err)) return false;
+          if (!plan_wgrad(k.g2[cp].L, g, dp_out_b, k.a2_bf[cp], nullptr, ~size_t(0), kWgradCtas, m.err)) return false;
           if (!make_wgrad_job(m, k.g2[cp], 0, s.C, kk, k.w2[cp])) return false;
         }
         {  // conv1 dgrad -> gradient wrt the pair input
           Epi e = epi0(c.lrelu_slope);
           e.act_kind = c.activation;
-          e.mask_src = snake ? k.a1_pre[cp] : k.a1_hi[cp];
+          e.mask_src = snake ? k.a1_pre[cp] : k.a1_bf[cp];
           e.mask_alpha = alpha_ptr(m, "dec.resblocks." + R + ".alpha1." + P);
           e.alpha_part = k.ap1[cp];
           e.res = (cp == m.nd - 1) ? s.d_s : k.pp[cp % 2];
@@ -519,7 +540,7 @@ bool gen_setup(Gen& m) {
         }
         {  // conv1 wgrad
           ConvGeom g{B, s.T, s.T, s.C, s.C, kk, dil, dil * (kk - 1) / 2};
-          if (!plan_wgrad(k.g1[cp].L, g, k.d_c1, k.a1_hi[cp], nullptr, ~size_t(0), kWgradCtas, m.err)) return false;
+          if (!plan_wgrad(k.g1[cp].L, g, k.d_c1, k.a1_bf[cp], nullptr, ~size_t(0), kWgradCtas, m.err)) return false;
           if (!make_wgrad_job(m, k.g1[cp], 0, s.C, kk, k.w1[cp])) return false;
         }
       }
@@ -536,7 +557,7 @@ bool gen_setup(Gen& m) {
       e.alpha_part = s.ap_up;
       if (L > 0) {
         StageBufs& pv = m.sg[L - 1];
-        e.mask_src = snake ? pv.s_pre : pv.sa_hi;
+        e.mask_src = snake ? pv.s_pre : pv.sa_bf;
         e.scale = 1.f / (float)m.nk;
         e.out_f32 = pv.d_s;
         e.out_bf16 = pv.d_s_bf;
@@ -544,7 +565,7 @@ bool gen_setup(Gen& m) {
         pv.cs_ds_tiles = tiles;
         e.colsum = pv.cs_ds;
       } else {
-        e.mask_src = snake ? m.pre_pre : m.pre_hi;
+        e.mask_src = snake ? m.pre_pre : m.pre_bf;
         e.out_bf16 = m.d_pre_bf;
         if (!dalloc(m, &m.cs_pre, (size_t)tiles * C0)) return false;
         m.cs_pre_tiles = tiles;
@@ -552,7 +573,7 @@ bool gen_setup(Gen& m) {
         e.colsum = m.cs_pre;
       }
       if (!plan_convT_dgrad(s.up_dg, B, Tin, s.Cin, s.C, s.ku, s.su, s.pu, s.d_x_bf, s.wu.dg, e, m.err)) return false;
-      const bf16* xin = (L == 0) ? m.pre_hi : m.sg[L - 1].sa_hi;
+      const bf16* xin = (L == 0) ? m.pre_bf : m.sg[L - 1].sa_bf;
       if (!plan_convT_wgrad(s.up_wg.L, B, Tin, s.Cin, s.C, s.ku, s.su, s.pu, xin, s.d_x_bf, nullptr, ~size_t(0),
                             kWgradCtas, m.err))
         return false;
@@ -561,7 +582,7 @@ bool gen_setup(Gen& m) {
   }
   {  // conv_pre wgrad
     ConvGeom g{B, m.F, m.F, c.in_channels, C0, 7, 1, 3};
-    if (!plan_wgrad(m.pre_wg.L, g, m.d_pre_bf, m.z_hi, nullptr, ~size_t(0), kWgradCtas, m.err)) return false;
+    if (!plan_wgrad(m.pre_wg.L, g, m.d_pre_bf, m.z_bf, nullptr, ~size_t(0), kWgradCtas, m.err)) return false;
     if (!make_wgrad_job(m, m.pre_wg, 0, C0, 7, m.wpre)) return false;
   }
   // ---- batched per-stage reductions ----
@@ -665,6 +686,7 @@ bool gen_setup(Gen& m) {
       p.norm = w.norm;
       p.fwd_hi = w.fwd_hi;
       p.fwd_lo = w.fwd_lo;
+      p.range_err = m.err;
       p.dg = w.dg;
       p.P = w.convT ? w.cols : w.rows;
       p.Q = w.convT ? w.rows : w.cols;
@@ -697,7 +719,39 @@ bool gen_setup(Gen& m) {
     m.prep_tile_blocks = tb;
     if (!dalloc(m, &m.prep_descs, d.size())) return false;
     CK(cudaMemcpy(m.prep_descs, d.data(), d.size() * sizeof(PrepDesc), cudaMemcpyHostToDevice));
+    m.prep_host = d;
   }
+  return true;
+}
+
+// Forward operand format of every producer and forward GEMM (see Gen::op_bf16).  The step graph is
+// released: the next step captures it again with the new format.
+bool gen_set_operand_format(Gen& m, int bf16) {
+  m.op_bf16 = bf16 ? 1 : 0;
+  auto conv = [&](TcConvParams& p) {
+    p.split_bf16 = m.op_bf16;
+    p.epi.act_bf16pair = m.op_bf16;
+  };
+  auto conv2 = [&](TcConv2Params& p) {
+    p.split_bf16 = m.op_bf16;
+    p.epi.act_bf16pair = m.op_bf16;
+  };
+  conv(m.pre_fwd.p);
+  for (int L = 0; L < 4; ++L) {
+    StageBufs& s = m.sg[L];
+    conv(s.up_fwd.p);
+    for (int j = 0; j < m.nk; ++j)
+      for (int cp = 0; cp < m.nd; ++cp)
+        for (ConvOp* op : {&s.st[j].f1[cp], &s.st[j].f2[cp]}) {
+          conv(op->v1.p);
+          conv2(op->c2.p);
+        }
+  }
+  for (auto& d : m.prep_host) d.fmt_bf16 = m.op_bf16;
+  CK(cudaStreamSynchronize(m.stream));
+  CK(cudaMemcpy(m.prep_descs, m.prep_host.data(), m.prep_host.size() * sizeof(PrepDesc), cudaMemcpyHostToDevice));
+  if (m.graph) cudaGraphExecDestroy(m.graph);
+  m.graph = nullptr;
   return true;
 }
 
@@ -711,7 +765,7 @@ bool gen_forward(Gen& m) {
   set_reduce_scratch(m.red_scratch, m.red_scratch_n);
   // GEMM weights for this step (weight norm + bf16 hi/lo + transposed layouts)
   prep_weights(m.prep_descs, m.n_prep, m.prep_norm_blocks, m.prep_tile_blocks, st);
-  pack_z(m.z, m.B, c.in_channels, m.F, m.z_hi, m.z_lo, st);
+  pack_z(m.z, m.B, c.in_channels, m.F, m.z_hi, m.z_lo, m.z_bf, m.err, m.op_bf16, st);
   if (c.nsf) {
     NsfArgs a{};
     a.f0 = m.f0;
@@ -761,8 +815,11 @@ bool gen_forward(Gen& m) {
       na.alpha[q] = snake ? alpha_ptr(m, "dec.resblocks." + std::to_string(L * m.nk + q) + ".alpha1.0") : nullptr;
       na.act_hi[q] = s.xa_hi[q];
       na.act_lo[q] = s.xa_lo[q];
+      na.act_bf[q] = s.xa_bf[q];
     }
     na.pre = s.x_pre;
+    na.range_err = m.err;
+    na.fmt_bf16 = m.op_bf16;
     noise_add_act(na, st);
     for (int j = 0; j < m.nk; ++j)
       for (int cp = 0; cp < m.nd; ++cp) {
@@ -770,7 +827,7 @@ bool gen_forward(Gen& m) {
         CK(s.st[j].f2[cp].run(st));
       }
   }
-  post_forward(m.sg[3].sa_hi, m.sg[3].sa_lo, m.P(m.pidx("dec.conv_post.weight")), m.B, m.T, m.sg[3].C, 7, m.audio,
+  post_forward(m.sg[3].sa_hi, m.sg[3].sa_lo, m.op_bf16, m.P(m.pidx("dec.conv_post.weight")), m.B, m.T, m.sg[3].C, 7, m.audio,
                st);
   return true;
 }
@@ -793,7 +850,8 @@ bool gen_backward(Gen& m) {
     a.W = m.P(m.pidx("dec.conv_post.weight"));
     a.a_hi = s3.sa_hi;
     a.a_lo = s3.sa_lo;
-    a.mask_src = snake ? s3.s_pre : s3.sa_hi;
+    a.fmt_bf16 = m.op_bf16;
+    a.mask_src = snake ? s3.s_pre : s3.sa_bf;
     a.alpha = alpha_ptr(m, "dec.post_act.alpha");
     a.act_kind = c.activation;
     a.slope = c.final_slope;
@@ -861,9 +919,11 @@ bool gen_backward(Gen& m) {
 }
 
 bool gen_adamw(Gen& m, float grad_scale, int bump_noise) {
-  step_bump(m.state, bump_noise, m.stream);
+  // under data parallelism the ranks' range flags arrive summed in the slot after the gradients
+  const float* flag = comm_world(m) > 1 ? m.grads + m.table.total : nullptr;
+  step_bump(m.state, bump_noise, m.err, flag, m.stream);
   adamw(m.params, m.grads, m.adam_m, m.adam_v, m.table.total, m.opt.lr, m.opt.beta1, m.opt.beta2, m.opt.eps,
-        m.opt.weight_decay, m.state, grad_scale, m.stream);
+        m.opt.weight_decay, m.state, grad_scale, m.err, flag, m.stream);
   return cudaGetLastError() == cudaSuccess;
 }
 

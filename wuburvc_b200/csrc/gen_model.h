@@ -18,7 +18,8 @@ struct ConvWeights {
   int pv = -1, pg = -1, pb = -1;  // param indices (v or W, g, bias)
   int rows = 0, cols = 0, k = 0;  // param dims: conv [C_out][C_in][k], convT [C_in][C_out][k]
   int convT = 0, stride = 1;
-  bf16 *fwd_hi = nullptr, *fwd_lo = nullptr, *dg = nullptr;
+  f16 *fwd_hi = nullptr, *fwd_lo = nullptr;  // forward operand pair (see Gen::op_bf16)
+  bf16* dg = nullptr;                         // input-gradient operand
   float* norm = nullptr;  // ||v|| rows (weight norm)
   float* dW = nullptr;    // gradient in param layout (grad buffer directly, or a temp under weight norm)
 };
@@ -43,9 +44,13 @@ struct WgradBatch {
 
 struct StackBufs {
   // forward (index = pair)
-  bf16 *a1_hi[3] = {}, *a1_lo[3] = {}, *a1_pre[3] = {};  // activation of the pair input
+  // activations: forward operand pair (see Gen::op_bf16), bf16 copy (weight-gradient operand and
+  // LeakyReLU mask), bf16 pre-activation (Snake masks)
+  f16 *a1_hi[3] = {}, *a1_lo[3] = {};                    // activation of the pair input
+  bf16 *a1_bf[3] = {}, *a1_pre[3] = {};
   float* p[3] = {};                                      // pair input (p[0] aliases the stage input)
-  bf16 *a2_hi[3] = {}, *a2_lo[3] = {}, *a2_pre[3] = {};  // activation of conv1's output
+  f16 *a2_hi[3] = {}, *a2_lo[3] = {};                    // activation of conv1's output
+  bf16 *a2_bf[3] = {}, *a2_pre[3] = {};
   // backward
   bf16* d_c1 = nullptr;
   float* pp[2] = {};
@@ -61,9 +66,11 @@ struct StageBufs {
   int T = 0, C = 0, Cin = 0, rows = 0, ku = 0, su = 0, pu = 0;
   int kn = 0, sn = 0, pn = 0;
   float* x_in = nullptr;
-  bf16 *xa_hi[3] = {}, *xa_lo[3] = {}, *x_pre = nullptr;
+  f16 *xa_hi[3] = {}, *xa_lo[3] = {};
+  bf16 *xa_bf[3] = {}, *x_pre = nullptr;
   float* sout = nullptr;
-  bf16 *sa_hi = nullptr, *sa_lo = nullptr, *s_pre = nullptr;
+  f16 *sa_hi = nullptr, *sa_lo = nullptr;
+  bf16 *sa_bf = nullptr, *s_pre = nullptr;
   float* d_s = nullptr;
   bf16* d_s_bf = nullptr;
   float* d_x = nullptr;
@@ -109,7 +116,8 @@ struct Gen {
   // inputs
   float *z = nullptr, *f0 = nullptr, *g = nullptr, *noise = nullptr, *dldy = nullptr;
   bool has_noise_input = false;
-  bf16 *z_hi = nullptr, *z_lo = nullptr;
+  f16 *z_hi = nullptr, *z_lo = nullptr;
+  bf16* z_bf = nullptr;
   // source
   float *har = nullptr, *sw = nullptr, *d_har = nullptr, *nsf_part = nullptr;
   double* nsf_acc = nullptr;
@@ -117,7 +125,8 @@ struct Gen {
   // conv_pre / cond
   ConvWeights wpre;
   float* rowadd = nullptr;
-  bf16 *pre_hi = nullptr, *pre_lo = nullptr, *pre_pre = nullptr;
+  f16 *pre_hi = nullptr, *pre_lo = nullptr;
+  bf16 *pre_bf = nullptr, *pre_pre = nullptr;
   bf16* d_pre_bf = nullptr;
   float* cs_pre = nullptr;
   int cs_pre_tiles = 0, pre_tiles_per_item = 0;
@@ -130,6 +139,10 @@ struct Gen {
 
   StageBufs sg[4];
   PrepDesc* prep_descs = nullptr;  // device table: every GEMM weight's preparation
+  std::vector<PrepDesc> prep_host; // host copy (re-uploaded when the operand format changes)
+  // forward operand format: 0 = fp16 hi + fp16 lo*2^11 (fp32-accurate, |x| < 65504); 1 = bf16 hi +
+  // bf16 lo (range-safe, ~2^-17), the format a context switches to for good after a range error
+  int op_bf16 = 0;
   int n_prep = 0, prep_norm_blocks = 0, prep_tile_blocks = 0;
   float* red_scratch = nullptr;  // two-pass deterministic reductions
   size_t red_scratch_n = 0;

@@ -77,10 +77,11 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else if (warp == 5) {
     // ---------------- MMA issuer ----------------
-    // bf16x3 as A_hi x [W_hi | W_lo] (2N wide: the tiles are adjacent rows) + A_lo x W_hi into the
-    // upper N columns; the epilogue adds the halves
-    const uint32_t idesc = make_idesc_bf16(128, N, 0, 0);
-    const uint32_t idesc2 = make_idesc_bf16(128, 2 * N, 0, 0);
+    // the split product as A_hi x [W_hi | W_lo] (2N wide: the tiles are adjacent rows) + A_lo x W_hi
+    // into the upper N columns; the epilogue adds the halves (the upper one unscaled)
+    const int fmt_bf16 = p.split ? p.split_bf16 : 1;
+    const uint32_t idesc = make_idesc(128, N, 0, 0, fmt_bf16);
+    const uint32_t idesc2 = make_idesc(128, 2 * N, 0, 0, fmt_bf16);
     constexpr uint32_t layout = (KC == 64) ? 2u : 4u;        // 128B / 64B swizzle
     constexpr uint32_t sbo = (KC == 64) ? 1024u : 512u;       // 8 rows x row bytes
     const uint64_t d0 = make_sdesc(smem_u32(smem), 16, sbo, layout);
@@ -126,11 +127,12 @@ __global__ void __launch_bounds__(192, 1)
       float v[32];
       if (ok) {
         tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
-        if (p.split) {  // [0, N) holds hi*hi, [N, 2N) hi*lo + lo*hi
+        if (p.split) {  // [0, N) holds hi*hi, [N, 2N) hi*lo + lo*hi (scaled by 2^11 in the fp16 format)
           float u[32];
           tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(N + c0), u);
+          const float ls = p.split_bf16 ? 1.f : kLoUnscale;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] += u[i];
+          for (int i = 0; i < 32; ++i) v[i] += u[i] * ls;
         }
       } else
 #pragma unroll

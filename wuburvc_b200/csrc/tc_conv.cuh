@@ -8,8 +8,8 @@
 //               Conv1d forward, the Conv1d input-gradient (flipped taps, transposed weights), the
 //               polyphase ConvTranspose1d forward (one phase per blockIdx.z) and the ConvTranspose1d
 //               input-gradient (one strided A view per tap residue).  In split mode the A and W
-//               operands are bf16 hi/lo pairs and three MMAs (hi*hi + lo*hi + hi*lo) give an
-//               fp32-accurate product.
+//               operands are hi/lo pairs (fp16 hi + fp16 lo*2^11 for the forward, or bf16 hi + bf16
+//               lo) and three products (hi*hi + lo*hi + hi*lo) give an fp32-accurate result.
 //  * tc_wgrad : dW[tap, o, i] = sum_{b,t} dOut[b, t - shift_tap, o] * A[b, t, i], split over time
 //               (K) across CTAs with deterministic fp32 partials.  Both operands are MN-major in
 //               shared memory; several taps are packed into one 128-row M tile when C_out < 128.
@@ -34,8 +34,12 @@ struct Epi {
   const float* res;         // [B][T][n_total] fp32 residual added after the mask
   float* out_f32;           // [B][T][n_total]
   bf16* out_bf16;           // [B][T][n_total]
-  bf16* act_hi;             // [B][T][n_total] activation of the result, bf16 hi part
-  bf16* act_lo;             //                                       ... lo part
+  f16* act_hi;              // [B][T][n_total] activation of the result, fp16 hi part (forward operand)
+  f16* act_lo;              //                   ... its fp16 lo part scaled by 2^11 (with act_hi)
+  bf16* act_bf;             //                   ... bf16 copy (weight-gradient operand, LeakyReLU masks)
+  int* range_err;           // error word: set to ERR_RANGE if |activation| >= 65504
+  int act_bf16pair;         // write act_hi / act_lo as a bf16 hi + bf16 lo pair instead (the
+                            // range-safe operand format a context falls back to after ERR_RANGE)
   const float* act_alpha;   // [n_total] snake alpha of the activation
   bf16* pre_hi;             // [B][T][n_total] bf16 copy of the result (snake pre-activation)
   float* colsum;            // [tiles][n_total] column-sum partials (bias gradients)
@@ -57,7 +61,8 @@ struct TcConvParams {
   int n_tile;          // GEMM N per CTA (multiple of 16, <= 256)
   int n_total;         // channel pitch of every [B][T][C] output
   int n_chunks;        // C_in / KC
-  int split;           // bf16x3 forward
+  int split;           // operands as hi/lo pairs, three products (fp32-accurate)
+  int split_bf16;      // split pair format: 0 = fp16 hi + fp16 lo*2^11 (forward), 1 = bf16 hi + bf16 lo
   int lo_base;
   int stages;
   int kgroup;          // (tap, chunk) steps per pipeline stage
@@ -96,6 +101,7 @@ struct TcConv2Params {
   int n_total;              // C_out: output channel pitch
   int n_chunks;             // C_in / KC
   int split;
+  int split_bf16;           // split pair format (as TcConvParams::split_bf16)
   int ntaps;
   int dil;                  // tap t reads halo rows t*dil .. t*dil+127
   int halo_start;           // row offset of the halo tile relative to the tile's first output row

@@ -142,12 +142,14 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
     }
   } else if (warp == kMmaWarp) {
     // ---------------- MMA issuer ----------------
-    // bf16x3 as two MMAs per K16 step: A_hi x [W_hi | W_lo] (N = 2N: the tap's hi and lo weight tiles
-    // are adjacent rows in shared memory) into accumulator columns [0, 2N), then A_lo x W_hi added to
-    // columns [N, 2N); the epilogue sums the two halves.  Fewer operand reads from shared memory than
+    // The split product as two MMAs per K16 step: A_hi x [W_hi | W_lo] (N = 2N: the tap's hi and lo
+    // weight tiles are adjacent rows in shared memory) into accumulator columns [0, 2N), then A_lo x
+    // W_hi added to columns [N, 2N); the epilogue sums the two halves (the second one unscaled).  Fewer operand reads from shared memory than
     // three N-wide MMAs, and a wider (more efficient) first MMA.
-    const uint32_t idesc = make_idesc_bf16(128, N, 0, 0);
-    const uint32_t idesc2 = make_idesc_bf16(128, 2 * N, 0, 0);
+    // split pairs: fp16 hi / scaled lo (forward) or bf16 hi / lo; single operands are bf16
+    const int fmt_bf16 = SPLIT ? p.split_bf16 : 1;
+    const uint32_t idesc = make_idesc(128, N, 0, 0, fmt_bf16);
+    const uint32_t idesc2 = make_idesc(128, 2 * N, 0, 0, fmt_bf16);
     constexpr uint32_t wlayout = (KC == 64) ? 2u : 4u;
     constexpr uint32_t wsbo = (KC == 64) ? 1024u : 512u;
     // A: the halo tile in the swizzled K-major layout TMA writes (rows of KC channels, 8-row swizzle
@@ -172,7 +174,7 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
         if (ok) ok = mbar_wait_warp(&a_full[sa], aph, p.err, ERR_WAIT_FULL);
         const uint64_t dah = da0 + (uint64_t)((sa * a_stage) >> 4);
         const uint64_t dal = dah + (uint64_t)(a_sub >> 4);
-        // one tap: KC/16 K16 steps, 3 MMAs each under the bf16x3 split
+        // one tap: KC/16 K16 steps, 2 MMAs each under the split (3 products)
         auto issue_tap = [&](uint32_t w_off, int t, uint32_t acc0) {
           const uint64_t dwh = dw0 + (uint64_t)(w_off >> 4);
           const uint64_t dwl = dwh + (uint64_t)(w_sub >> 4);
@@ -255,11 +257,12 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
         if (ok) {
           const uint32_t ta = tmem + (uint32_t)(buf * N * nA) + ((uint32_t)(qw * 32) << 16) + (uint32_t)c0;
           tmem_ld32(ta, v);
-          if (SPLIT) {  // [0, N) holds hi*hi, [N, 2N) hi*lo + lo*hi: their sum is the bf16x3 product
+          if (SPLIT) {  // [0, N) holds hi*hi, [N, 2N) hi*lo + lo*hi (scaled by 2^11 in the fp16 format)
             float u[32];
             tmem_ld32(ta + (uint32_t)N, u);
+            const float ls = p.split_bf16 ? 1.f : kLoUnscale;
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] += u[i];
+            for (int i = 0; i < 32; ++i) v[i] += u[i] * ls;
           }
         } else
 #pragma unroll
@@ -298,7 +301,7 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
   }
 }
 
-// Instantiated (KC, SPLIT, epilogue feature set) combinations: the forward (bf16x3) and input-gradient
+// Instantiated (KC, SPLIT, epilogue feature set) combinations: the forward (split) and input-gradient
 // epilogues of the resblock convolutions (with and without column sums), plus a generic kernel for
 // any other epilogue.
 #define WB_CONV2_KERNELS(X)                                                                     \

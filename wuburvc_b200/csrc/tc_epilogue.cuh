@@ -3,7 +3,8 @@
 // Four epilogue warps own TMEM lanes 0..127 (one output row per thread).  Per 32-column chunk the
 // accumulator row is combined with: activation-derivative mask (LeakyReLU sign or Snake), bias,
 // cond(g) row-broadcast, fp32 residual, scale, column-sum partials (bias gradients), accumulation
-// into an fp32 sum, and written as fp32 / bf16 / activated bf16 hi+lo pairs.
+// into an fp32 sum, and written as fp32 / bf16 / the activation as a GEMM operand pair with a bf16
+// copy.
 #pragma once
 #include "tc_conv.cuh"
 
@@ -31,6 +32,16 @@ WB_DEV float bf16hi_f(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 // two floats -> packed bf16x2 (round to nearest even), one conversion instruction
 WB_DEV uint32_t pack_bf16(float a, float b) {
   const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  uint32_t u;
+  memcpy(&u, &h, sizeof(u));
+  return u;
+}
+
+// fp16 pairs the same way (the forward operand split)
+WB_DEV float f16lo_f(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w & 0xffffu))); }
+WB_DEV float f16hi_f(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w >> 16))); }
+WB_DEV uint32_t pack_f16(float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
   uint32_t u;
   memcpy(&u, &h, sizeof(u));
   return u;
@@ -128,7 +139,7 @@ enum : uint32_t {
   kEpiSnake = 2u,    // Snake (else LeakyReLU) for the mask and the activation
   kEpiRes = 4u,      // fp32 residual
   kEpiColsum = 8u,   // column-sum partials of the result (bias gradient)
-  kEpiAct = 16u,     // activated bf16 hi/lo output
+  kEpiAct = 16u,     // activation output: operand pair (fp16 hi + lo * 2^11, or bf16 hi + lo) + bf16 copy
   kEpiGeneric = 1u << 31,
 };
 
@@ -280,7 +291,11 @@ WB_DEV void epi_finish(const Epi& e, float* v, EpiIn& in, bool valid, size_t off
       if (e.pre_hi) out_bf16x32(o, e.pre_hi, off, b);
     }
     if (has_act) {
-      uint32_t h[16], l[16];
+      // the activation as the next forward GEMM's operand pair (fp16 hi, fp16 lo * 2^11; or the
+      // bf16 pair of the fallback format) and as a bf16 copy (the weight gradient's operand and the
+      // LeakyReLU mask source)
+      uint32_t h[16], l[16], bw[16];
+      bool big = false;
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         float a0, a1;
@@ -291,11 +306,20 @@ WB_DEV void epi_finish(const Epi& e, float* v, EpiIn& in, bool valid, size_t off
           a0 = lrelu(v[2 * i], e.slope);
           a1 = lrelu(v[2 * i + 1], e.slope);
         }
-        h[i] = pack_bf16(a0, a1);
-        l[i] = pack_bf16(a0 - bf16lo_f(h[i]), a1 - bf16hi_f(h[i]));
+        bw[i] = pack_bf16(a0, a1);
+        if (e.act_bf16pair) {
+          h[i] = bw[i];
+          l[i] = pack_bf16(a0 - bf16lo_f(h[i]), a1 - bf16hi_f(h[i]));
+        } else {
+          big |= !(fabsf(a0) < kF16Max) || !(fabsf(a1) < kF16Max);
+          h[i] = pack_f16(a0, a1);
+          l[i] = pack_f16((a0 - f16lo_f(h[i])) * kLoScale, (a1 - f16hi_f(h[i])) * kLoScale);
+        }
       }
-      out_bf16x32(o, e.act_hi, off, h);
-      if (e.act_lo) out_bf16x32(o, e.act_lo, off, l);
+      if (big && valid && e.range_err) atomicCAS(e.range_err, 0, ERR_RANGE);
+      out_bf16x32(o, reinterpret_cast<bf16*>(e.act_hi), off, h);
+      if (e.act_lo) out_bf16x32(o, reinterpret_cast<bf16*>(e.act_lo), off, l);
+      if (e.act_bf) out_bf16x32(o, e.act_bf, off, bw);
     }
   }
   if (has_cs) {  // every lane reaches the group's named barriers; v is consumed here
