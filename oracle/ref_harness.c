@@ -129,6 +129,21 @@ int refh_adamw(void *hp) {
     return 0;
 }
 
+/* Copies a flat buffer in registry order into the registry's gradients (for applying the
+ * reference's own AdamW to gradients computed elsewhere).  Returns the number of floats read. */
+long refh_reg_set_grads(void *hp, const float *in) {
+  RefH *h = (RefH *)hp;
+  long off = 0;
+  for (int i = 0; i < h->reg.count; i++) {
+    memcpy(h->reg.params[i].grad, in + off, (size_t)h->reg.params[i].n * sizeof(float));
+    off += h->reg.params[i].n;
+  }
+  return off;
+}
+
+/* Model config field the reference's inference generator reads (src/wubu_rvc_real.c:1420). */
+void refh_set_sample_rate(void *hp, int sr) { ((RefH *)hp)->model->sample_rate = sr; }
+
 int refh_threads(void) { return omp_get_max_threads(); }
 /* Thread count of the reference's OpenMP regions (its reductions, e.g. wubu_mse_loss, then run in a
  * fixed order when 1). */

@@ -8,7 +8,8 @@ compiled unmodified, and feeds it an in-memory model.
 
 The reference trainer has no batch dimension, no harmonic source, no cond(g) and no noise convs
 (``src/wubu_train_cuda.cu:8-10``); it trains de-normalised weights named like its registry
-(``src/wubu_train.c:131-210``).
+(``src/wubu_train.c:131-210``).  Tensors outside the registry (cond, l_linear, noise convs) may be
+added to the model too: the reference's inference generator and the drop-in shim read them by name.
 """
 from __future__ import annotations
 
@@ -55,6 +56,10 @@ def lib():
         h.refh_backward.argtypes = [vp, vp, vp]
         h.refh_adamw.restype = ip
         h.refh_adamw.argtypes = [vp]
+        h.refh_reg_set_grads.restype = ctypes.c_long
+        h.refh_reg_set_grads.argtypes = [vp, vp]
+        h.refh_set_sample_rate.restype = None
+        h.refh_set_sample_rate.argtypes = [vp, ip]
         h.refh_threads.restype = ip
         h.refh_threads.argtypes = []
         h.refh_set_threads.restype = None
@@ -80,9 +85,11 @@ class RefTrainer:
     dec.conv_post.weight); rates / kernels: upsampling config."""
 
     def __init__(self, params: Dict[str, np.ndarray], rates, kernels, lr=1e-3, betas=(0.9, 0.999), eps=1e-8,
-                 wd=1e-4):
+                 wd=1e-4, sample_rate=0):
         L = lib()
-        self.h = L.refh_create(256)
+        self.h = L.refh_create(320)
+        if sample_rate:
+            L.refh_set_sample_rate(self.h, sample_rate)
         self._keep = []
         for name, a in params.items():
             a = np.ascontiguousarray(a, dtype=np.float32)
@@ -144,6 +151,11 @@ class RefTrainer:
 
     def adamw(self):
         lib().refh_adamw(self.h)
+
+    def set_grads(self, named: Dict[str, np.ndarray]):
+        """Registry gradients from named arrays (e.g. computed by the CUDA library)."""
+        flat = np.concatenate([np.ascontiguousarray(named[n], dtype=np.float32).reshape(-1) for n in self.names])
+        lib().refh_reg_set_grads(self.h, _p(flat))
 
     @staticmethod
     def threads() -> int:

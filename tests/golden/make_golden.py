@@ -13,7 +13,7 @@ the reference tree exists; the fixtures are committed and travel, the reference 
 
 Inputs and weights come from the counter generator (seeded), so every consumer can rebuild them.
 
-  python tests/golden/make_golden.py      (needs /root/reference and oracle/_ref built)
+  python tests/golden/make_golden.py      (needs the reference tree -- WUBU_REFERENCE -- and oracle/_ref)
 """
 import os
 import sys
@@ -28,7 +28,9 @@ from oracle import generator_ref as G  # noqa: E402
 from oracle import ref_oracle  # noqa: E402
 from wuburvc_b200 import model  # noqa: E402
 
-REF = "/root/reference"
+from oracle.refpath import reference_root  # noqa: E402
+
+REF = reference_root()
 N_SAMPLES = 24
 ADAM = dict(lr=1e-3, betas=(0.9, 0.999), eps=1e-8, wd=1e-4)
 
@@ -110,6 +112,8 @@ def sinegen_fixture():
 
 
 if __name__ == "__main__":
+    if REF is None:
+        raise SystemExit("reference tree not found: set WUBU_REFERENCE")
     if not ref_oracle.available():
         raise SystemExit("build oracle/_ref first: make -C oracle")
     decoder_fixture("40k", model.decoder_only("40k"), F=8)
