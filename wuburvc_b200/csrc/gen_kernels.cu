@@ -427,17 +427,55 @@ void cond_backward(const float* tile_part, int tiles_per_item, int B, int C, con
 // =============================================================================================
 // harmonic source (SineGen + l_linear + tanh)
 // =============================================================================================
-__global__ void nsf_phase_kernel(const float* __restrict__ f0, int B, int F, int upp, float sr, double* acc) {
-  const int b = blockIdx.x * blockDim.x + threadIdx.x;
-  if (b >= B) return;
-  double a = 0.0;
-  for (int f = 0; f < F; ++f) {
-    acc[(size_t)b * F + f] = a;  // carry into frame f = fmod(sum of rad2 over frames < f, 1)
-    const double rad = (double)f0[(size_t)b * F + f] / (double)sr * (double)upp;
-    // fmod(x, 1) == x - trunc(x) exactly for finite x (the difference is representable)
-    const double x = rad + 0.5;
-    const double r2 = (x - trunc(x)) - 0.5;
-    const double y = a + r2;
+// Phase carried into each frame: acc[b][f] = sum over frames g < f of r2(g) (mod 1), r2(g) =
+// fmod(f0[g]/sr*upp + 0.5, 1) - 0.5, the cumulative carry of SineGen (models.py:313-316; the
+// reference's serial loop at src/wubu_rvc_real.c:1471-1489).  Only the value mod 1 matters (the source
+// takes sin(2*pi*phase)), so the carry is a parallel prefix sum in fp64 wrapped to (-1, 1): one block
+// per item, each thread sums a contiguous run of frames, a block-wide exclusive scan gives every run
+// its starting carry, and each thread re-walks its run from there.  Over 6000 frames |sum| <= 3000,
+// so the unwrapped fp64 partial sums keep ~1e-12 absolute accuracy; the order is fixed
+// (deterministic).
+WB_DEV double nsf_r2(float f0, float sr, int upp) {
+  // fmod(x, 1) == x - trunc(x) exactly for finite x (the difference is representable)
+  const double x = (double)f0 / (double)sr * (double)upp + 0.5;
+  return (x - trunc(x)) - 0.5;
+}
+
+constexpr int kPhaseThreads = 256;
+
+__global__ void __launch_bounds__(kPhaseThreads) nsf_phase_kernel(const float* __restrict__ f0, int F, int upp,
+                                                                  float sr, double* __restrict__ acc) {
+  __shared__ double warp_tot[kPhaseThreads / 32];
+  const int b = blockIdx.x, j = threadIdx.x, lane = j & 31, warp = j >> 5;
+  const int per = (F + kPhaseThreads - 1) / kPhaseThreads;
+  const int f_begin = min(F, j * per), f_end = min(F, f_begin + per);
+  const float* fb = f0 + (size_t)b * F;
+  double loc = 0.0;
+  for (int f = f_begin; f < f_end; ++f) loc += nsf_r2(fb[f], sr, upp);
+  // inclusive scan within the warp, then over the warps' totals
+  double inc = loc;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const double v = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += v;
+  }
+  if (lane == 31) warp_tot[warp] = inc;
+  __syncthreads();
+  if (warp == 0) {
+    double t = lane < kPhaseThreads / 32 ? warp_tot[lane] : 0.0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const double v = __shfl_up_sync(0xffffffffu, t, o);
+      if (lane >= o) t += v;
+    }
+    if (lane < kPhaseThreads / 32) warp_tot[lane] = t;  // inclusive over warps
+  }
+  __syncthreads();
+  const double base = (inc - loc) + (warp > 0 ? warp_tot[warp - 1] : 0.0);  // exclusive prefix
+  double a = base - trunc(base);
+  for (int f = f_begin; f < f_end; ++f) {
+    acc[(size_t)b * F + f] = a;
+    const double y = a + nsf_r2(fb[f], sr, upp);
     a = y - trunc(y);
   }
 }
@@ -475,7 +513,7 @@ __global__ void nsf_sample_kernel(NsfArgs a) {
 }
 
 void nsf_forward(const NsfArgs& a, cudaStream_t st) {
-  nsf_phase_kernel<<<(a.B + 63) / 64, 64, 0, st>>>(a.f0, a.B, a.F, a.upp, a.sr, a.acc);
+  nsf_phase_kernel<<<a.B, kPhaseThreads, 0, st>>>(a.f0, a.F, a.upp, a.sr, a.acc);
   const long long n = (long long)a.B * a.F * a.upp;
   nsf_sample_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(a);
 }
