@@ -104,6 +104,18 @@ int wubu_b200_stft_loss_grad(const float* a, const float* b, int B, int n, int n
 int wubu_b200_stft_loss_grad_host(const float* a, const float* b, int B, int n, int n_scales, float* grad,
                                   float* loss);
 
+/* Bounded waits.  Every wait of the library's tensor-core kernels on a pipeline barrier gives up
+ * after a limit (default 2 s, far above any legitimate wait); the kernel then records an error,
+ * lets its own copies and MMAs in flight finish (each drain again bounded), frees its TMEM and
+ * returns, and the call reports WUBU_B200_ERR_TIMEOUT with the context still usable.  No
+ * counterpart in the reference (its kernels have no barrier waits).
+ * set_wait_limit_ns sets the limit (ns) for the launch plans built afterwards (contexts created,
+ * primitive calls made); 0 restores the default.  wait_selftest makes one warp wait on a barrier
+ * that nothing arrives on, for limit_ns (0 < limit_ns <= 10 s): it returns WUBU_B200_ERR_TIMEOUT
+ * when the wait ran out as designed. */
+int wubu_b200_set_wait_limit_ns(unsigned long long ns);
+int wubu_b200_wait_selftest(unsigned long long limit_ns, void* stream);
+
 /* ---------------------------------------------------------------------------------------
  * 2. generator training step
  * ------------------------------------------------------------------------------------- */

@@ -26,6 +26,8 @@ SIGNATURES = {
     "wubu_b200_convT_wgrad": (c_int, [c_void_p, c_void_p, c_void_p] + [c_int] * 7 + [c_void_p]),
     "wubu_b200_stft_loss_grad": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]),
     "wubu_b200_stft_loss_grad_host": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
+    "wubu_b200_set_wait_limit_ns": (c_int, [ctypes.c_ulonglong]),
+    "wubu_b200_wait_selftest": (c_int, [ctypes.c_ulonglong, c_void_p]),
 }
 
 

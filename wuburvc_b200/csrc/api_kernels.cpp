@@ -19,6 +19,19 @@ using namespace wb;
 
 namespace {
 
+// One warp waits, with the kernels' bounded wait, on a barrier that nothing arrives on: the wait runs
+// out after limit_ns by design and records ERR_WAIT_FULL.  Nothing is in flight, so the kernel simply
+// returns.
+__global__ void wait_probe_kernel(int* err, unsigned long long limit_ns) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  mbar_wait_warp(&bar, 0, err, ERR_WAIT_FULL, limit_ns);
+}
+
 struct Scratch {
   int* err = nullptr;
   float* part = nullptr;
@@ -196,6 +209,22 @@ int wubu_b200_stft_loss_grad_host(const float* a, const float* b, int B, int n, 
   cudaFree(dg);
   cudaFree(dl);
   return rc;
+}
+
+int wubu_b200_set_wait_limit_ns(unsigned long long ns) {
+  set_wait_limit_ns(ns);
+  return WUBU_B200_OK;
+}
+
+int wubu_b200_wait_selftest(unsigned long long limit_ns, void* stream) {
+  if (limit_ns == 0 || limit_ns > 10000000000ull) return WUBU_B200_ERR_ARG;
+  cudaStream_t st = (cudaStream_t)stream;
+  Scratch s;
+  if (cudaMalloc(&s.err, sizeof(int)) != cudaSuccess) return WUBU_B200_ERR_CUDA;
+  if (cudaMemsetAsync(s.err, 0, sizeof(int), st) != cudaSuccess) return WUBU_B200_ERR_CUDA;
+  wait_probe_kernel<<<1, 32, 0, st>>>(s.err, limit_ns);
+  if (!launched(cudaGetLastError())) return WUBU_B200_ERR_CUDA;
+  return finish(st, s.err);
 }
 
 }  // extern "C"

@@ -35,8 +35,10 @@ enum : int {
   ERR_RANGE = 5,          // a forward operand exceeded the fp16 range of the operand split
 };
 
-// Time after which a bounded mbarrier wait gives up and the kernel reports a timeout (ns of
+// Default time after which a bounded mbarrier wait gives up and the kernel reports a timeout (ns of
 // %globaltimer; far above any legitimate wait, short enough that a broken pipeline ends quickly).
+// The kernels take the limit from their launch parameters (wait_ns), set by the planner from
+// wubu_b200_set_wait_limit_ns.
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
 
 WB_DEV unsigned long long global_ns() {
@@ -184,7 +186,8 @@ WB_DEV void tma_load_4d_warp(void* dst, const CUtensorMap* map, uint64_t* bar, i
 // Bounded wait by a converged warp; every lane gets the same verdict.  The spin loop lives inside one
 // asm block so the compiler sees no divergent control flow around the issuing code (a C++ loop here
 // makes it treat descriptors as per-lane values and every tcgen05.mma pays for uniformising them).
-WB_DEV bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* err, int code) {
+WB_DEV bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* err, int code,
+                           unsigned long long limit_ns = kWaitLimitNs) {
   uint32_t done;
   asm volatile(
       "{\n\t.reg .pred p, q;\n\t.reg .u64 t0, t1;\n\t"
@@ -201,12 +204,29 @@ WB_DEV bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* err, int code) {
       "WB_WAIT_DONE:\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(done)
-      : "r"(smem_u32(bar)), "r"(parity), "l"(kWaitLimitNs)
+      : "r"(smem_u32(bar)), "r"(parity), "l"(limit_ns)
       : "memory");
   const bool ok = __all_sync(0xffffffffu, done != 0);
   if (!ok && err && (threadIdx.x & 31) == 0) atomicCAS(err, 0, code);
   return ok;
 }
+
+// The producer's record of its fills: bit s of `issued` = pipeline slot s (< 32) received a TMA fill,
+// bit s of `parity` = the phase parity of its last one.  Before the kernel ends the producer waits
+// (bounded) for the last fill of every slot, so that even after another warp gave up on a timed-out
+// wait no copy lands in shared memory once the CTA has exited.  In a normal run those phases have
+// long completed and the drain costs one poll per slot.
+struct FillTrack {
+  uint32_t issued = 0, parity = 0;
+  WB_DEV void fill(int s, uint32_t ph) {
+    issued |= 1u << s;
+    parity = (parity & ~(1u << s)) | ((ph & 1u) << s);
+  }
+  WB_DEV void drain(uint64_t* full, int* err, unsigned long long limit_ns) const {
+    for (int s = 0; s < 32; ++s)
+      if ((issued >> s) & 1u) mbar_wait_warp(&full[s], (parity >> s) & 1u, err, ERR_WAIT_FULL, limit_ns);
+  }
+};
 
 // Non-blocking test by a converged warp: has the phase with this parity completed?  (One
 // mbarrier.test_wait; lets the MMA warp look at the next stage while it issues the current one.)

@@ -4,12 +4,20 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
 
 namespace wb {
+
+namespace {
+std::atomic<unsigned long long> g_wait_limit_ns{kWaitLimitNs};
+}  // namespace
+
+unsigned long long wait_limit_ns() { return g_wait_limit_ns.load(); }
+void set_wait_limit_ns(unsigned long long ns) { g_wait_limit_ns.store(ns ? ns : kWaitLimitNs); }
 
 namespace {
 
@@ -100,6 +108,7 @@ static bool finish_fwd(ConvLaunch& L, int B, int c_in, int n_total, int split, i
   p.tmem_cols = pow2_cols(n_tile * (split ? 2 : 1));  // 2n columns under the two-MMA bf16x3 split
   p.tiles_per_item = (p.m_rows + 127) / 128;
   p.err = err;
+  p.wait_ns = wait_limit_ns();
   L.grid = dim3(B * p.tiles_per_item, n_total / n_tile, nphase);
   return true;
 }
@@ -171,6 +180,7 @@ bool plan_conv2(Conv2Launch& L, const ConvGeom& g, const void* x_hi, const void*
   p.split = split;
   p.epi = epi;
   p.err = err;
+  p.wait_ns = wait_limit_ns();
   const int nA = split ? 2 : 1;
   // weights: resident (every chunk and tap of the CTA's N tile loaded once) when they fit beside two
   // A stages, else a ring of stages holding w_group taps each.  The wider channel chunk is preferred:
@@ -370,6 +380,7 @@ static bool finish_wgrad(WgradLaunch& L, int B, int T_rows, int C_in, int C_out,
   L.smem = p.stages * p.kb_group * kb + 1024 + 256;
   p.tmem_cols = pow2_cols(n_tile);
   p.err = err;
+  p.wait_ns = wait_limit_ns();
   p.part = part;
   L.splits = splits;
   L.grid = dim3(p.n_mtiles, splits, n_ntiles);
@@ -454,6 +465,7 @@ static bool plan_wgrad_halo(WgradLaunch& L, const ConvGeom& g, const void* dy, c
   p.tmem_cols = pow2_cols(nacc * n_tile);
   if (p.tmem_cols > 512) return false;
   p.err = err;
+  p.wait_ns = wait_limit_ns();
   p.part = part;
   L.splits = splits;
   L.grid = dim3(tap_groups * p.oc_chunks, splits, n_ntiles);

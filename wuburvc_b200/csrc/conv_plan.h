@@ -10,6 +10,9 @@
 namespace wb {
 
 void tc_kernels_init();  // raises the kernels' shared-memory limit (call before graph capture)
+// Bounded-wait limit (ns) written into every plan built afterwards (default kWaitLimitNs; 0 restores it).
+unsigned long long wait_limit_ns();
+void set_wait_limit_ns(unsigned long long ns);
 cudaError_t launch_tc_conv(const TcMaps& maps, const TcConvParams& p, int kc, dim3 grid, size_t smem,
                            cudaStream_t st);
 cudaError_t launch_tc_wgrad(const TcWgMaps& maps, const TcWgParams& p, dim3 grid, size_t smem,

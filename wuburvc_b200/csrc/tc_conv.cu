@@ -34,11 +34,13 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * stage_bytes);
   uint64_t* empty = full + S;
   uint64_t* accf = empty + S;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accf + 1);
+  uint64_t* mma_done = accf + 1;  // every MMA of the CTA complete (drained before TMEM is freed)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
     mbar_init(accf, 1);
+    mbar_init(mma_done, 1);
     fence_barrier_init();
   }
   if (warp == 5) tmem_alloc(tmem_slot, (uint32_t)p.tmem_cols);
@@ -51,13 +53,15 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 4) {
     // ---------------- TMA producer ----------------
     bool ok = true;
+    FillTrack fill;
     int s = 0;
     uint32_t ph = 0;
     for (int g = 0; g < ngroups; ++g) {
-      if (ok && g >= S) ok = mbar_wait_warp(&empty[s], ph ^ 1u, p.err, ERR_WAIT_EMPTY);
+      if (ok && g >= S) ok = mbar_wait_warp(&empty[s], ph ^ 1u, p.err, ERR_WAIT_EMPTY, p.wait_ns);
       if (ok) {
         const int ks0 = g * G, nk = min(G, ksteps - ks0);
         uint8_t* st = smem + (size_t)s * stage_bytes;
+        fill.fill(s, ph);
         mbar_expect_tx_warp(&full[s], (uint32_t)nk * step_bytes);
         for (int i = 0; i < nk; ++i) {
           const int ks = ks0 + i;
@@ -75,6 +79,7 @@ __global__ void __launch_bounds__(192, 1)
       }
       if (++s == S) { s = 0; ph ^= 1u; }
     }
+    fill.drain(full, p.err, p.wait_ns);  // no copy of this CTA may land after it exits
   } else if (warp == 5) {
     // ---------------- MMA issuer ----------------
     // the split product as A_hi x [W_hi | W_lo] (2N wide: the tiles are adjacent rows) + A_lo x W_hi
@@ -89,7 +94,7 @@ __global__ void __launch_bounds__(192, 1)
     int s = 0;
     uint32_t ph = 0;
     for (int g = 0; g < ngroups; ++g) {
-      if (ok) ok = mbar_wait_warp(&full[s], ph, p.err, ERR_WAIT_FULL);
+      if (ok) ok = mbar_wait_warp(&full[s], ph, p.err, ERR_WAIT_FULL, p.wait_ns);
       if (ok) {
         const int nk = min(G, ksteps - g * G);
         for (int i = 0; i < nk; ++i) {
@@ -113,9 +118,12 @@ __global__ void __launch_bounds__(192, 1)
       if (++s == S) { s = 0; ph ^= 1u; }
     }
     if (ok) umma_commit_warp(accf);
+    // every MMA this warp issued has completed before TMEM is released (also after a timed-out wait)
+    umma_commit_warp(mma_done);
+    mbar_wait_warp(mma_done, 0, p.err, ERR_WAIT_ACC, p.wait_ns);
   } else {
     // ---------------- epilogue (warps 0..3 <-> TMEM lanes 0..127) ----------------
-    const bool ok = mbar_wait_warp(accf, 0, p.err, ERR_WAIT_ACC);
+    const bool ok = mbar_wait_warp(accf, 0, p.err, ERR_WAIT_ACC, p.wait_ns);
     tc_fence_after();
     const int q = q0 + warp * 32 + lane;
     const int orow = q * p.out_stride + p.out_off[phase];
@@ -182,7 +190,8 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * stage_bytes);
   uint64_t* empty = full + S;
   uint64_t* accf = empty + S;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accf + 1);
+  uint64_t* mma_done = accf + 1;  // every MMA of the CTA complete (drained before TMEM is freed)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
 
   // this M tile's atoms (dOut view, row shift, first channel), hoisted out of the parameter tables
   int a_map[4], a_shift[4], a_oc0[4];
@@ -200,6 +209,7 @@ __global__ void __launch_bounds__(192, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
     mbar_init(accf, 1);
+    mbar_init(mma_done, 1);
     fence_barrier_init();
   }
   if (warp == 5) tmem_alloc(tmem_slot, (uint32_t)p.tmem_cols);
@@ -211,13 +221,15 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 4) {
     // ---------------- TMA producer ----------------
     bool ok = true;
+    FillTrack fill;
     int s = 0;
     uint32_t ph = 0;
     for (int g = 0; g < ngroups; ++g) {
-      if (ok && g >= S) ok = mbar_wait_warp(&empty[s], ph ^ 1u, p.err, ERR_WAIT_EMPTY);
+      if (ok && g >= S) ok = mbar_wait_warp(&empty[s], ph ^ 1u, p.err, ERR_WAIT_EMPTY, p.wait_ns);
       if (ok) {
         const int kbg = kb0 + g * G, nk = min(G, kb1 - kbg);
         uint8_t* st = smem + (size_t)s * stage_bytes;
+        fill.fill(s, ph);
         mbar_expect_tx_warp(&full[s], (uint32_t)nk * kb_load);
         for (int i = 0; i < nk; ++i) {
           const int kb = kbg + i;
@@ -234,6 +246,7 @@ __global__ void __launch_bounds__(192, 1)
       }
       if (++s == S) { s = 0; ph ^= 1u; }
     }
+    fill.drain(full, p.err, p.wait_ns);  // no copy of this CTA may land after it exits
   } else if (warp == 5) {
     // ---------------- MMA issuer ----------------
     const uint32_t idesc = make_idesc_bf16(128, p.n_in, 1, 1);
@@ -247,7 +260,7 @@ __global__ void __launch_bounds__(192, 1)
     int s = 0;
     uint32_t ph = 0;
     for (int g = 0; g < ngroups; ++g) {
-      if (ok) ok = mbar_wait_warp(&full[s], ph, p.err, ERR_WAIT_FULL);
+      if (ok) ok = mbar_wait_warp(&full[s], ph, p.err, ERR_WAIT_FULL, p.wait_ns);
       if (ok) {
         const int nk = min(G, kb1 - (kb0 + g * G));
         const uint32_t sbase = ((uint32_t)s * stage_bytes) >> 4;
@@ -261,9 +274,12 @@ __global__ void __launch_bounds__(192, 1)
       if (++s == S) { s = 0; ph ^= 1u; }
     }
     if (ok) umma_commit_warp(accf);
+    // every MMA this warp issued has completed before TMEM is released (also after a timed-out wait)
+    umma_commit_warp(mma_done);
+    mbar_wait_warp(mma_done, 0, p.err, ERR_WAIT_ACC, p.wait_ns);
   } else {
     // ---------------- epilogue: 4 warps, TMEM lane quadrant = warp ----------------
-    bool ok = nkb > 0 ? mbar_wait_warp(accf, 0, p.err, ERR_WAIT_ACC) : true;
+    bool ok = nkb > 0 ? mbar_wait_warp(accf, 0, p.err, ERR_WAIT_ACC, p.wait_ns) : true;
     tc_fence_after();
     // the pipeline buffers are idle once the accumulator is complete: 2 KB staging per warp
     uint4* stage = reinterpret_cast<uint4*>(smem) + warp * 128;
@@ -335,10 +351,12 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * stage_bytes);
   uint64_t* empty = full + S;
   uint64_t* accf = empty + S;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accf + 1);
+  uint64_t* mma_done = accf + 1;  // every MMA of the CTA complete (drained before TMEM is freed)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
     mbar_init(accf, 1);
+    mbar_init(mma_done, 1);
     fence_barrier_init();
   }
   if (warp == 5) tmem_alloc(tmem_slot, (uint32_t)p.tmem_cols);
@@ -350,15 +368,17 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 4) {
     // ---------------- TMA producer ----------------
     bool ok = true;
+    FillTrack fill;
     int s = 0;
     uint32_t ph = 0;
     for (int i = 0; i < nkb; ++i) {
-      if (ok && i >= S) ok = mbar_wait_warp(&empty[s], ph ^ 1u, p.err, ERR_WAIT_EMPTY);
+      if (ok && i >= S) ok = mbar_wait_warp(&empty[s], ph ^ 1u, p.err, ERR_WAIT_EMPTY, p.wait_ns);
       if (ok) {
         const int kb = kb0 + i;
         const int item = kb / p.kblocks_per_item;
         const int t0 = (kb - item * p.kblocks_per_item) * KR;
         uint8_t* st = smem + (size_t)s * stage_bytes;
+        fill.fill(s, ph);
         mbar_expect_tx_warp(&full[s], stage_bytes);
         // dOut rows t0 + pad - (tb + tg - 1) * dil ... : every tap's window, once
         const int hr = t0 + p.pad - (tb + tg - 1) * p.dil;
@@ -373,6 +393,7 @@ __global__ void __launch_bounds__(192, 1)
       }
       if (++s == S) { s = 0; ph ^= 1u; }
     }
+    fill.drain(full, p.err, p.wait_ns);  // no copy of this CTA may land after it exits
   } else if (warp == 5) {
     // ---------------- MMA issuer ----------------
     const uint32_t idesc = make_idesc_bf16(128, N, 1, 1);
@@ -389,7 +410,7 @@ __global__ void __launch_bounds__(192, 1)
     int s = 0;
     uint32_t ph = 0;
     for (int i = 0; i < nkb; ++i) {
-      if (ok) ok = mbar_wait_warp(&full[s], ph, p.err, ERR_WAIT_FULL);
+      if (ok) ok = mbar_wait_warp(&full[s], ph, p.err, ERR_WAIT_FULL, p.wait_ns);
       if (ok) {
         const uint32_t sb = ((uint32_t)s * stage_bytes) >> 4;
 #pragma unroll
@@ -409,9 +430,12 @@ __global__ void __launch_bounds__(192, 1)
       if (++s == S) { s = 0; ph ^= 1u; }
     }
     if (ok) umma_commit_warp(accf);
+    // every MMA this warp issued has completed before TMEM is released (also after a timed-out wait)
+    umma_commit_warp(mma_done);
+    mbar_wait_warp(mma_done, 0, p.err, ERR_WAIT_ACC, p.wait_ns);
   } else {
     // ---------------- epilogue: 4 warps, TMEM lane quadrant = warp; 32 partial rows per accumulator ----------------
-    const bool ok = nkb > 0 ? mbar_wait_warp(accf, 0, p.err, ERR_WAIT_ACC) : true;
+    const bool ok = nkb > 0 ? mbar_wait_warp(accf, 0, p.err, ERR_WAIT_ACC, p.wait_ns) : true;
     tc_fence_after();
     uint4* stage = reinterpret_cast<uint4*>(smem) + warp * 128;  // pipeline buffers are idle now
     for (int j = 0; j < nacc; ++j) {

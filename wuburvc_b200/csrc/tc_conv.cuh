@@ -75,6 +75,7 @@ struct TcConvParams {
   short tap_shift[kMaxTapList];
   short tap_w[kMaxTapList];
   int pdl;             // launched with programmatic stream serialization
+  unsigned long long wait_ns;  // bounded-wait limit
   Epi epi;
   int* err;
 };
@@ -115,6 +116,7 @@ struct TcConv2Params {
   // the first weight stages) overlaps the previous kernel.  Only for callers whose weights and
   // epilogue vectors are not written by the immediately preceding kernel.
   int pdl;
+  unsigned long long wait_ns;  // bounded-wait limit
   Epi epi;
   int* err;
 };
@@ -162,6 +164,7 @@ struct TcWgParams {
   int pack, nacc;
   int x_atom;          // channels per activation (B) atom: 64 (SW128) or 32 (SW64)
   int pdl;             // launched with programmatic stream serialization
+  unsigned long long wait_ns;  // bounded-wait limit
 };
 
 }  // namespace wb

@@ -55,12 +55,14 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
   uint64_t* w_empty = w_full + WS;
   uint64_t* acc_full = w_empty + WS;   // [2]
   uint64_t* acc_empty = acc_full + 2;  // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* mma_done = acc_empty + 2;  // every MMA of the CTA complete (drained before TMEM is freed)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < AS; ++s) { mbar_init(&a_full[s], 1); mbar_init(&a_empty[s], 1); }
     for (int s = 0; s < WS; ++s) { mbar_init(&w_full[s], 1); mbar_init(&w_empty[s], 1); }
     for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], 1); }
+    mbar_init(mma_done, 1);
     fence_barrier_init();
   }
   if (warp == kMmaWarp) tmem_alloc(tmem_slot, (uint32_t)p.tmem_cols);
@@ -82,11 +84,14 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
   if (warp == kProducerWarp) {
     // ---------------- TMA producer ----------------
     bool ok = true;
+    FillTrack fa, fw;
     const int n0_cta = (blockIdx.x % p.n_tiles) * N;  // every tile of this CTA has this N tile
-    // weight stage u of the CTA's weight sequence (chunk u / ngroups, tap group u % ngroups) into slot s
-    auto load_w = [&](int u, int s) {
+    // weight stage u of the CTA's weight sequence (chunk u / ngroups, tap group u % ngroups) into slot s,
+    // the slot's phase parity ph
+    auto load_w = [&](int u, int s, uint32_t ph) {
       const int c = u / ngroups, t0 = (u % ngroups) * G, nt = min(G, ntaps - t0);
       uint8_t* wd = w_base + (size_t)s * w_stage;
+      fw.fill(s, ph);
       mbar_expect_tx_warp(&w_full[s], (uint32_t)nt * w_tap);
       for (int j = 0; j < nt; ++j) {
         tma_load_3d_warp(wd + j * w_tap, &maps.w_hi, &w_full[s], c * KC, n0_cta, t0 + j);
@@ -97,6 +102,7 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
     int w_pre = 0;
     if (resident) {
       mbar_expect_tx_warp(&w_full[0], (uint32_t)(nch * ntaps) * w_tap);
+      fw.fill(0, 0);
       for (int c = 0; c < nch; ++c)
         for (int t = 0; t < ntaps; ++t) {
           uint8_t* wd = w_base + (size_t)(c * ntaps + t) * w_tap;
@@ -105,7 +111,7 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
         }
     } else if (blockIdx.x < p.ntiles) {
       w_pre = min(WS, nch * ngroups);
-      for (int u = 0; u < w_pre; ++u) load_w(u, u);
+      for (int u = 0; u < w_pre; ++u) load_w(u, u, 0);
     }
     griddep_wait();
     int sa = 0, sw = 0;
@@ -116,10 +122,11 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
       const int item = mtile / p.tiles_per_item;
       const int q0 = (mtile - item * p.tiles_per_item) * 128;
       for (int c = 0; c < nch; ++c) {
-        if (ok && a_uses >= AS) ok = mbar_wait_warp(&a_empty[sa], aph ^ 1u, p.err, ERR_WAIT_EMPTY);
+        if (ok && a_uses >= AS) ok = mbar_wait_warp(&a_empty[sa], aph ^ 1u, p.err, ERR_WAIT_EMPTY, p.wait_ns);
         if (ok) {
           // one swizzled box per operand: R rows of KC channels
           uint8_t* ad = a_base + (size_t)sa * a_stage;
+          fa.fill(sa, aph);
           mbar_expect_tx_warp(&a_full[sa], nA * (uint32_t)p.halo_rows * KC * 2u);
           tma_load_3d_warp(ad, &maps.a_hi, &a_full[sa], c * KC, q0 + p.halo_start, item);
           if (SPLIT) tma_load_3d_warp(ad + a_sub, &maps.a_lo, &a_full[sa], c * KC, q0 + p.halo_start, item);
@@ -133,13 +140,16 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
             if (++sw == WS) { sw = 0; wph ^= 1u; }
             continue;
           }
-          if (ok && w_uses >= WS) ok = mbar_wait_warp(&w_empty[sw], wph ^ 1u, p.err, ERR_WAIT_EMPTY);
-          if (ok) load_w(c * ngroups + g, sw);
+          if (ok && w_uses >= WS) ok = mbar_wait_warp(&w_empty[sw], wph ^ 1u, p.err, ERR_WAIT_EMPTY, p.wait_ns);
+          if (ok) load_w(c * ngroups + g, sw, wph);
           ++w_uses;
           if (++sw == WS) { sw = 0; wph ^= 1u; }
         }
       }
     }
+    // no copy of this CTA may land after it exits
+    fa.drain(a_full, p.err, p.wait_ns);
+    fw.drain(w_full, p.err, p.wait_ns);
   } else if (warp == kMmaWarp) {
     // ---------------- MMA issuer ----------------
     // The split product as two MMAs per K16 step: A_hi x [W_hi | W_lo] (N = 2N: the tap's hi and lo
@@ -161,17 +171,17 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
     const uint32_t tap_step = (uint32_t)dil * (KC * 2u / 16u);  // 16-byte units per tap (dil rows)
     const uint32_t k_step_a = 2u;                                 // K16 step = 32 bytes along the row
     bool ok = true;
-    if (resident) ok = mbar_wait_warp(&w_full[0], 0, p.err, ERR_WAIT_FULL);
+    if (resident) ok = mbar_wait_warp(&w_full[0], 0, p.err, ERR_WAIT_FULL, p.wait_ns);
     int sa = 0, sw = 0, t_it = 0;
     uint32_t aph = 0, wph = 0;
     bool w_ready = false;  // weight stage sw known complete (polled ahead)
     for (int tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x, ++t_it) {
       const int buf = t_it & 1;
-      if (ok && t_it >= 2) ok = mbar_wait_warp(&acc_empty[buf], ((t_it >> 1) & 1) ^ 1, p.err, ERR_WAIT_ACC);
+      if (ok && t_it >= 2) ok = mbar_wait_warp(&acc_empty[buf], ((t_it >> 1) & 1) ^ 1, p.err, ERR_WAIT_ACC, p.wait_ns);
       tc_fence_after();
       const uint32_t d = tmem + (uint32_t)(buf * N * nA);  // nA = 2: accumulator of 2N columns
       for (int c = 0; c < nch; ++c) {
-        if (ok) ok = mbar_wait_warp(&a_full[sa], aph, p.err, ERR_WAIT_FULL);
+        if (ok) ok = mbar_wait_warp(&a_full[sa], aph, p.err, ERR_WAIT_FULL, p.wait_ns);
         const uint64_t dah = da0 + (uint64_t)((sa * a_stage) >> 4);
         const uint64_t dal = dah + (uint64_t)(a_sub >> 4);
         // one tap: KC/16 K16 steps, 2 MMAs each under the split (3 products)
@@ -199,7 +209,7 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
         } else {
           for (int g = 0; g < ngroups; ++g) {
             const int t0 = g * G, nt = min(G, ntaps - t0);
-            if (ok && !w_ready) ok = mbar_wait_warp(&w_full[sw], wph, p.err, ERR_WAIT_FULL);
+            if (ok && !w_ready) ok = mbar_wait_warp(&w_full[sw], wph, p.err, ERR_WAIT_FULL, p.wait_ns);
             // look at the next weight stage now, so its (usually complete) wait is off the issue path
             int sw2 = sw + 1;
             uint32_t ph2 = wph;
@@ -219,6 +229,9 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
       }
       if (ok) umma_commit_warp(&acc_full[buf]);
     }
+    // every MMA this warp issued has completed before TMEM is released (also after a timed-out wait)
+    umma_commit_warp(mma_done);
+    mbar_wait_warp(mma_done, 0, p.err, ERR_WAIT_ACC, p.wait_ns);
   } else {
     // ---------------- epilogue: two groups of 4 warps; group g drains TMEM accumulator g, i.e. every
     // other tile, so two tiles' epilogues run concurrently (warp w reads TMEM lane quadrant w%4) ----------------
@@ -249,7 +262,7 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
       // the first chunk's inputs are in flight while the accumulator is still being computed
       EpiIn in;
       epi_load<F>(e, valid, row_off, in);
-      if (ok) ok = mbar_wait_warp(&acc_full[buf], (t_it >> 1) & 1, p.err, ERR_WAIT_ACC);
+      if (ok) ok = mbar_wait_warp(&acc_full[buf], (t_it >> 1) & 1, p.err, ERR_WAIT_ACC, p.wait_ns);
       tc_fence_after();
 #pragma unroll 1
       for (int c0 = 0; c0 < N; c0 += 32) {
