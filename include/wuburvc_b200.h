@@ -239,6 +239,11 @@ int wubu_b200_gen_kernel_bench(WubuB200Gen* gen, int which, int stage, int iters
  * over ranks in buckets on a communication stream while the backward runs, then scaled 1/world. */
 int wubu_b200_nccl_unique_id(void* out128);
 int wubu_b200_gen_attach_comm(WubuB200Gen* gen, int rank, int world, const void* id128);
+/* A step's collectives must finish within `ms` (default 60000) of the call that waits for them
+ * (train_step, sync, ...).  Past it, or on an NCCL error, the communicator is aborted (ending the
+ * collectives that wait on a lost peer), the call returns WUBU_B200_ERR_COMM and the context runs no
+ * further step.  Needs an attached communicator. */
+int wubu_b200_gen_set_comm_timeout_ms(WubuB200Gen* gen, int ms);
 
 #ifdef __cplusplus
 }

@@ -116,6 +116,7 @@ _SIGS = {
                                                   ctypes.c_void_p, ctypes.c_void_p]),
     "wubu_b200_nccl_unique_id": (ctypes.c_int, [ctypes.c_void_p]),
     "wubu_b200_gen_attach_comm": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
+    "wubu_b200_gen_set_comm_timeout_ms": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
 }
 
 INPUTS_RESIDENT = 1
@@ -350,3 +351,7 @@ class Generator:
     def attach_comm(self, rank: int, world: int, uid: bytes):
         buf = ctypes.create_string_buffer(uid, 128)
         check(L().wubu_b200_gen_attach_comm(self.h, rank, world, buf), "attach_comm")
+
+    def set_comm_timeout(self, seconds: float):
+        """Deadline for a step's collectives; past it the communicator is aborted (WUBU_B200_ERR_COMM)."""
+        check(L().wubu_b200_gen_set_comm_timeout_ms(self.h, max(1, int(seconds * 1000))), "set_comm_timeout")

@@ -6,6 +6,10 @@
 // backward.  AdamW waits for the last bucket and applies the 1/world scaling.
 #include <dlfcn.h>
 
+#include <sched.h>
+#include <unistd.h>
+
+#include <chrono>
 #include <cstdio>
 #include <cstring>
 #include <vector>
@@ -21,7 +25,7 @@ typedef struct ncclComm* ncclComm_t;
 typedef struct {
   char internal[128];
 } ncclUniqueId;
-typedef enum { ncclSuccess = 0 } ncclResult_t;
+typedef enum { ncclSuccess = 0, ncclInProgress = 7 } ncclResult_t;
 enum { ncclFloat32 = 7 };
 enum { ncclSum = 0 };
 
@@ -32,6 +36,7 @@ struct NcclApi {
   int (*AllReduce)(const void*, void*, size_t, int, int, ncclComm_t, cudaStream_t) = nullptr;
   int (*CommDestroy)(ncclComm_t) = nullptr;
   int (*CommAbort)(ncclComm_t) = nullptr;
+  int (*CommGetAsyncError)(ncclComm_t, int*) = nullptr;
   const char* (*GetErrorString)(int) = nullptr;
   bool ok = false;
 };
@@ -55,6 +60,7 @@ NcclApi& nccl() {
   api.AllReduce = (int (*)(const void*, void*, size_t, int, int, ncclComm_t, cudaStream_t))dlsym(api.h, "ncclAllReduce");
   api.CommDestroy = (int (*)(ncclComm_t))dlsym(api.h, "ncclCommDestroy");
   api.CommAbort = (int (*)(ncclComm_t))dlsym(api.h, "ncclCommAbort");
+  api.CommGetAsyncError = (int (*)(ncclComm_t, int*))dlsym(api.h, "ncclCommGetAsyncError");
   api.GetErrorString = (const char* (*)(int))dlsym(api.h, "ncclGetErrorString");
   api.ok = api.GetUniqueId && api.CommInitRank && api.AllReduce && api.CommDestroy;
   return api;
@@ -69,6 +75,8 @@ struct Comm {
   cudaEvent_t done = nullptr;
   std::vector<cudaEvent_t> ready;           // one per bucket, recorded on the main stream
   std::vector<std::pair<long long, long long>> buckets;  // [off, end) in floats
+  int timeout_ms = 60000;  // a step's collectives must finish within this (comm_sync)
+  bool aborted = false;    // the communicator was aborted: the context runs no further step
 };
 
 // Bucket boundaries: end of conv_post + stage 3, stage 2, stage 1, stage 0, and the rest.
@@ -128,6 +136,7 @@ int comm_bucket_count(Gen& m) { return m.comm ? (int)m.comm->buckets.size() : 0;
 int comm_bucket_ready(Gen& m, int b, cudaStream_t producer) {
   Comm* c = m.comm;
   if (!c || c->world <= 1) return 0;
+  if (c->aborted) return WUBU_B200_ERR_COMM;
   NcclApi& api = nccl();
   if (b + 1 == (int)c->buckets.size()) range_flag(m.err, m.grads + m.table.total, producer);
   if (cudaEventRecord(c->ready[b], producer) != cudaSuccess) return WUBU_B200_ERR_CUDA;
@@ -153,6 +162,48 @@ int comm_join(Gen& m) {
 }
 
 int comm_world(Gen& m) { return m.comm ? m.comm->world : 1; }
+
+bool comm_aborted(Gen& m) { return m.comm && m.comm->aborted; }
+
+int comm_set_timeout(Gen& m, int ms) {
+  if (!m.comm || ms <= 0) return WUBU_B200_ERR_ARG;
+  m.comm->timeout_ms = ms;
+  return 0;
+}
+
+// Waits for the model stream of a context with a communicator.  The stream and the communicator's
+// asynchronous error are polled; past the deadline (a peer that hangs or left mid-step) or on an
+// NCCL error, the communicator is aborted, which ends the collectives waiting on the peer, and the
+// call reports WUBU_B200_ERR_COMM.  The context then runs no further step (its captured step holds
+// the aborted communicator).
+int comm_sync(Gen& m) {
+  Comm* c = m.comm;
+  NcclApi& api = nccl();
+  const auto t0 = std::chrono::steady_clock::now();
+  auto fail = [&](const char* why) {
+    fprintf(stderr, "wuburvc_b200: %s: aborting the communicator\n", why);
+    if (api.CommAbort && c->comm) api.CommAbort(c->comm);
+    c->comm = nullptr;
+    c->aborted = true;
+    cudaStreamSynchronize(m.stream);  // the aborted collectives have ended
+    cudaGetLastError();
+    return WUBU_B200_ERR_COMM;
+  };
+  for (long long spins = 0;; ++spins) {
+    const cudaError_t q = cudaStreamQuery(m.stream);
+    if (q == cudaSuccess) return 0;
+    if (q != cudaErrorNotReady) return WUBU_B200_ERR_CUDA;
+    if (api.CommGetAsyncError && c->comm) {
+      int ae = ncclSuccess;
+      if (api.CommGetAsyncError(c->comm, &ae) == ncclSuccess && ae != ncclSuccess && ae != ncclInProgress)
+        return fail(api.GetErrorString ? api.GetErrorString(ae) : "NCCL asynchronous error");
+    }
+    const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0);
+    if (ms.count() > c->timeout_ms) return fail("the step's collectives did not finish within the comm timeout");
+    if (spins < 20000) sched_yield();
+    else usleep(50);
+  }
+}
 
 int comm_allreduce_grads(Gen& m) {
   for (int b = 0; b < comm_bucket_count(m); ++b) {

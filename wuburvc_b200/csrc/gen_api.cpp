@@ -15,6 +15,9 @@ bool gen_set_operand_format(Gen& m, int bf16);
 int comm_attach(Gen& m, int rank, int world, const void* id128);
 int comm_unique_id(void* out128);
 int comm_world(Gen& m);
+int comm_sync(Gen& m);
+bool comm_aborted(Gen& m);
+int comm_set_timeout(Gen& m, int ms);
 }  // namespace wb
 
 using namespace wb;
@@ -26,6 +29,10 @@ struct WubuB200Gen {
 namespace {
 
 int check_err(Gen& m) {
+  if (comm_world(m) > 1) {  // data parallel: bounded wait on the collectives (comm.cpp)
+    const int rc = comm_sync(m);
+    if (rc) return rc;
+  }
   cudaError_t e = cudaStreamSynchronize(m.stream);
   if (e != cudaSuccess) {
     fprintf(stderr, "wuburvc_b200: CUDA error: %s\n", cudaGetErrorString(e));
@@ -89,6 +96,7 @@ bool enqueue_step(Gen& m) {
 }
 
 int run_step_graph(Gen& m) {
+  if (comm_aborted(m)) return WUBU_B200_ERR_COMM;
   if (!m.graph) {
     cudaGraph_t g = nullptr;
     if (cudaStreamBeginCapture(m.stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) return WUBU_B200_ERR_CUDA;
@@ -372,6 +380,11 @@ int wubu_b200_gen_kernel_bench(WubuB200Gen* gen, int which, int stage, int iters
 int wubu_b200_nccl_unique_id(void* out128) {
   if (!out128) return WUBU_B200_ERR_ARG;
   return comm_unique_id(out128);
+}
+
+int wubu_b200_gen_set_comm_timeout_ms(WubuB200Gen* gen, int ms) {
+  if (!gen) return WUBU_B200_ERR_ARG;
+  return comm_set_timeout(gen->m, ms);
 }
 
 int wubu_b200_gen_attach_comm(WubuB200Gen* gen, int rank, int world, const void* id128) {
