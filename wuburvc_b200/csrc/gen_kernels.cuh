@@ -117,7 +117,7 @@ struct NoiseActArgs {
   const float* alpha[3];
   f16* act_hi[3];         // activation: forward operand pair (fp16 hi + fp16 lo * 2^11) ...
   f16* act_lo[3];
-  bf16* act_bf[3];        // ... and an optional bf16 copy
+  bf16* act_bf[3];        // ... and its bf16 copy (weight-gradient operand, LeakyReLU masks)
   bf16* pre;              // bf16 copy of x (snake masks)
   int* range_err;         // set to ERR_RANGE if |activation| >= 65504
   int fmt_bf16;           // operand pair as bf16 hi + lo (fallback format)

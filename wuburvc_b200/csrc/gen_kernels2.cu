@@ -103,7 +103,7 @@ __global__ void __launch_bounds__(256) noise_add_act_kernel(NoiseActArgs a) {
       split_op(y, a.fmt_bf16, hi, lo);
       a.act_hi[q][i] = hi;
       a.act_lo[q][i] = lo;
-      if (a.act_bf[q]) a.act_bf[q][i] = __float2bfloat16_rn(y);
+      a.act_bf[q][i] = __float2bfloat16_rn(y);
       if (!a.fmt_bf16 && !(fabsf(y) < kF16Max) && a.range_err) atomicCAS(a.range_err, 0, ERR_RANGE);
     }
   }

@@ -3,10 +3,9 @@
 //
 // Data layout in HBM: every activation is channels-last [B][T][C].  Residual streams (pair inputs,
 // stage sums, their gradients) are fp32.  Forward GEMM operands are fp16 hi + fp16 lo*2^11 pairs
-// (three products, fp32-accurate; bf16 pairs after a range error).  The high part of a resblock
-// activation is also its weight gradient's operand (converted to bf16 in shared memory) and its
-// LeakyReLU mask source; the stage outputs and z keep a bf16 copy for the other weight gradients.
-// Backward operands are single bf16.  Parameters, gradients and AdamW moments live
+// (three products, fp32-accurate; bf16 pairs after a range error); every activation also keeps a
+// bf16 copy, the weight gradient's operand and the LeakyReLU mask source; backward operands are
+// single bf16.  Parameters, gradients and AdamW moments live
 // in flat fp32 buffers laid out by the parameter table.
 #include "gen_model.h"
 
@@ -51,22 +50,6 @@ bool dalloc(Gen& m, T** p, size_t n) {
   cudaMemset(q, 0, n * sizeof(T));
   m.allocs.push_back(q);
   *p = static_cast<T*>(q);
-  return true;
-}
-
-// The LeakyReLU mask of a resblock activation is read from its forward operand's high part: fp16 and
-// bf16 keep the sign and zero in the same bit positions, so reading the fp16 bits as bf16 gives the
-// right sign (a positive value below 3e-8 rounds to +0 and takes the negative slope: kink noise).
-const bf16* as_mask(const f16* hi) { return reinterpret_cast<const bf16*>(hi); }
-
-// The resblock weight gradients read their activation operand as the fp16 high part, converted to
-// bf16 in shared memory by the halo kernel (the only weight-gradient kernel that converts).
-bool set_x_f16(WgradLaunch& L) {
-  if (!L.p.halo) {
-    fprintf(stderr, "wuburvc_b200: a resblock weight gradient did not plan on the halo kernel\n");
-    return false;
-  }
-  L.p.x_f16 = 1;
   return true;
 }
 
@@ -365,7 +348,7 @@ bool gen_setup(Gen& m) {
       return false;
     const int nxa = snake ? m.nk : 1;
     for (int q = 0; q < nxa; ++q)
-      if (!dalloc(m, &s.xa_hi[q], n) || !dalloc(m, &s.xa_lo[q], n)) return false;
+      if (!dalloc(m, &s.xa_hi[q], n) || !dalloc(m, &s.xa_lo[q], n) || !dalloc(m, &s.xa_bf[q], n)) return false;
     if (snake && (!dalloc(m, &s.x_pre, n) || !dalloc(m, &s.s_pre, n))) return false;
     const int tiles = B * ((s.T + 127) / 128);
     for (int j = 0; j < m.nk; ++j) {
@@ -374,13 +357,16 @@ bool gen_setup(Gen& m) {
       k.p[0] = s.x_in;
       k.a1_hi[0] = s.xa_hi[snake ? j : 0];
       k.a1_lo[0] = s.xa_lo[snake ? j : 0];
+      k.a1_bf[0] = s.xa_bf[snake ? j : 0];
       k.a1_pre[0] = s.x_pre;
       for (int cp = 0; cp < m.nd; ++cp) {
         if (cp > 0) {
-          if (!dalloc(m, &k.p[cp], n) || !dalloc(m, &k.a1_hi[cp], n) || !dalloc(m, &k.a1_lo[cp], n)) return false;
+          if (!dalloc(m, &k.p[cp], n) || !dalloc(m, &k.a1_hi[cp], n) || !dalloc(m, &k.a1_lo[cp], n) ||
+              !dalloc(m, &k.a1_bf[cp], n))
+            return false;
           if (snake && !dalloc(m, &k.a1_pre[cp], n)) return false;
         }
-        if (!dalloc(m, &k.a2_hi[cp], n) || !dalloc(m, &k.a2_lo[cp], n)) return false;
+        if (!dalloc(m, &k.a2_hi[cp], n) || !dalloc(m, &k.a2_lo[cp], n) || !dalloc(m, &k.a2_bf[cp], n)) return false;
         if (snake && !dalloc(m, &k.a2_pre[cp], n)) return false;
         // column-sum partials: one row per tile (general kernel) or per CTA of the persistent kernel,
         // which may split N in two and writes two rows (epilogue groups) per CTA: at most 4 * tiles rows
@@ -450,6 +436,7 @@ bool gen_setup(Gen& m) {
           e.bias = m.P(k.w1[cp].pb);
           e.act_hi = k.a2_hi[cp];
           e.act_lo = k.a2_lo[cp];
+          e.act_bf = k.a2_bf[cp];
           e.range_err = m.err;
           e.act_kind = c.activation;
           e.act_alpha = alpha_ptr(m, "dec.resblocks." + R + ".alpha2." + P);
@@ -467,6 +454,7 @@ bool gen_setup(Gen& m) {
             e.out_f32 = k.p[cp + 1];
             e.act_hi = k.a1_hi[cp + 1];
             e.act_lo = k.a1_lo[cp + 1];
+            e.act_bf = k.a1_bf[cp + 1];
             e.range_err = m.err;
             e.act_alpha = alpha_ptr(m, "dec.resblocks." + R + ".alpha1." + std::to_string(cp + 1));
             e.pre_hi = k.a1_pre[cp + 1];
@@ -516,7 +504,7 @@ bool gen_setup(Gen& m) {
         {  // conv2 dgrad -> d_c1 (mask of conv1's activation)
           Epi e = epi0(c.lrelu_slope);
           e.act_kind = c.activation;
-          e.mask_src = snake ? k.a2_pre[cp] : as_mask(k.a2_hi[cp]);
+          e.mask_src = snake ? k.a2_pre[cp] : k.a2_bf[cp];
           e.mask_alpha = alpha_ptr(m, "dec.resblocks." + R + ".alpha2." + P);
           e.alpha_part = k.ap2[cp];
           e.out_bf16 = k.d_c1;
@@ -527,15 +515,13 @@ bool gen_setup(Gen& m) {
         }
         {  // conv2 wgrad
           ConvGeom g{B, s.T, s.T, s.C, s.C, kk, 1, (kk - 1) / 2};
-          if (!plan_wgrad(k.g2[cp].L, g, dp_out_b, k.a2_hi[cp], nullptr, ~size_t(0), kWgradCtas, m.err) ||
-              !set_x_f16(k.g2[cp].L))
-            return false;
+          if (!plan_wgrad(k.g2[cp].L, g, dp_out_b, k.a2_bf[cp], nullptr, ~size_t(0), kWgradCtas, m.err)) return false;
           if (!make_wgrad_job(m, k.g2[cp], 0, s.C, kk, k.w2[cp])) return false;
         }
         {  // conv1 dgrad -> gradient wrt the pair input
           Epi e = epi0(c.lrelu_slope);
           e.act_kind = c.activation;
-          e.mask_src = snake ? k.a1_pre[cp] : as_mask(k.a1_hi[cp]);
+          e.mask_src = snake ? k.a1_pre[cp] : k.a1_bf[cp];
           e.mask_alpha = alpha_ptr(m, "dec.resblocks." + R + ".alpha1." + P);
           e.alpha_part = k.ap1[cp];
           e.res = (cp == m.nd - 1) ? s.d_s : k.pp[cp % 2];
@@ -554,9 +540,7 @@ bool gen_setup(Gen& m) {
         }
         {  // conv1 wgrad
           ConvGeom g{B, s.T, s.T, s.C, s.C, kk, dil, dil * (kk - 1) / 2};
-          if (!plan_wgrad(k.g1[cp].L, g, k.d_c1, k.a1_hi[cp], nullptr, ~size_t(0), kWgradCtas, m.err) ||
-              !set_x_f16(k.g1[cp].L))
-            return false;
+          if (!plan_wgrad(k.g1[cp].L, g, k.d_c1, k.a1_bf[cp], nullptr, ~size_t(0), kWgradCtas, m.err)) return false;
           if (!make_wgrad_job(m, k.g1[cp], 0, s.C, kk, k.w1[cp])) return false;
         }
       }
@@ -763,12 +747,6 @@ bool gen_set_operand_format(Gen& m, int bf16) {
           conv2(op->c2.p);
         }
   }
-  for (int L = 0; L < 4; ++L)
-    for (int j = 0; j < m.nk; ++j)
-      for (int cp = 0; cp < m.nd; ++cp) {
-        m.sg[L].st[j].g1[cp].L.p.x_f16 = !m.op_bf16;
-        m.sg[L].st[j].g2[cp].L.p.x_f16 = !m.op_bf16;
-      }
   for (auto& d : m.prep_host) d.fmt_bf16 = m.op_bf16;
   CK(cudaStreamSynchronize(m.stream));
   CK(cudaMemcpy(m.prep_descs, m.prep_host.data(), m.prep_host.size() * sizeof(PrepDesc), cudaMemcpyHostToDevice));
@@ -837,6 +815,7 @@ bool gen_forward(Gen& m) {
       na.alpha[q] = snake ? alpha_ptr(m, "dec.resblocks." + std::to_string(L * m.nk + q) + ".alpha1.0") : nullptr;
       na.act_hi[q] = s.xa_hi[q];
       na.act_lo[q] = s.xa_lo[q];
+      na.act_bf[q] = s.xa_bf[q];
     }
     na.pre = s.x_pre;
     na.range_err = m.err;

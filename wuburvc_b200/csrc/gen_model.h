@@ -44,13 +44,13 @@ struct WgradBatch {
 
 struct StackBufs {
   // forward (index = pair)
-  // activations: forward operand pair (see Gen::op_bf16; the high part is also the weight gradient's
-  // operand and the LeakyReLU mask source), bf16 pre-activation (Snake masks)
+  // activations: forward operand pair (see Gen::op_bf16), bf16 copy (weight-gradient operand and
+  // LeakyReLU mask), bf16 pre-activation (Snake masks)
   f16 *a1_hi[3] = {}, *a1_lo[3] = {};                    // activation of the pair input
-  bf16* a1_pre[3] = {};
+  bf16 *a1_bf[3] = {}, *a1_pre[3] = {};
   float* p[3] = {};                                      // pair input (p[0] aliases the stage input)
   f16 *a2_hi[3] = {}, *a2_lo[3] = {};                    // activation of conv1's output
-  bf16* a2_pre[3] = {};
+  bf16 *a2_bf[3] = {}, *a2_pre[3] = {};
   // backward
   bf16* d_c1 = nullptr;
   float* pp[2] = {};
@@ -67,10 +67,10 @@ struct StageBufs {
   int kn = 0, sn = 0, pn = 0;
   float* x_in = nullptr;
   f16 *xa_hi[3] = {}, *xa_lo[3] = {};
-  bf16* x_pre = nullptr;
+  bf16 *xa_bf[3] = {}, *x_pre = nullptr;
   float* sout = nullptr;
   f16 *sa_hi = nullptr, *sa_lo = nullptr;
-  bf16 *sa_bf = nullptr, *s_pre = nullptr;  // sa_bf: bf16 copy (ConvTranspose weight gradient, masks)
+  bf16 *sa_bf = nullptr, *s_pre = nullptr;
   float* d_s = nullptr;
   bf16* d_s_bf = nullptr;
   float* d_x = nullptr;

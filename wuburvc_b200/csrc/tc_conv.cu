@@ -352,11 +352,9 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* empty = full + S;
   uint64_t* accf = empty + S;
   uint64_t* mma_done = accf + 1;  // every MMA of the CTA complete (drained before TMEM is freed)
-  uint64_t* conv = mma_done + 1;  // [S] stage s's activation tile converted to bf16 (x_f16)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(conv + S);
-  const bool x_f16 = p.x_f16 != 0;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); mbar_init(&conv[s], 4); }
+    for (int s = 0; s < S; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
     mbar_init(accf, 1);
     mbar_init(mma_done, 1);
     fence_barrier_init();
@@ -412,8 +410,7 @@ __global__ void __launch_bounds__(192, 1)
     int s = 0;
     uint32_t ph = 0;
     for (int i = 0; i < nkb; ++i) {
-      // with an fp16 activation operand the stage is ready once the epilogue warps converted it
-      if (ok) ok = mbar_wait_warp(x_f16 ? &conv[s] : &full[s], ph, p.err, ERR_WAIT_FULL, p.wait_ns);
+      if (ok) ok = mbar_wait_warp(&full[s], ph, p.err, ERR_WAIT_FULL, p.wait_ns);
       if (ok) {
         const uint32_t sb = ((uint32_t)s * stage_bytes) >> 4;
 #pragma unroll
@@ -437,37 +434,6 @@ __global__ void __launch_bounds__(192, 1)
     umma_commit_warp(mma_done);
     mbar_wait_warp(mma_done, 0, p.err, ERR_WAIT_ACC, p.wait_ns);
   } else {
-    if (x_f16) {
-      // ---------------- fp16 -> bf16 of each stage's activation tile, in place (element-wise, so
-      // the swizzled layout does not matter); the generic-proxy stores are fenced for the tensor
-      // core's async proxy before the warp's arrival on conv[s] ----------------
-      bool cok = true;
-      int s = 0;
-      uint32_t ph = 0;
-      const int nvec = (int)(b_bytes / 16u);
-      for (int i = 0; i < nkb; ++i) {
-        if (cok) cok = mbar_wait_warp(&full[s], ph, p.err, ERR_WAIT_FULL, p.wait_ns);
-        if (cok) {
-          uint4* xv = reinterpret_cast<uint4*>(smem + (size_t)s * stage_bytes + a_bytes);
-          for (int v = threadIdx.x; v < nvec; v += 128) {
-            uint4 q = xv[v];
-            uint32_t* w = &q.x;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float lo = __half2float(__ushort_as_half((unsigned short)(w[e] & 0xffffu)));
-              const float hi = __half2float(__ushort_as_half((unsigned short)(w[e] >> 16)));
-              const __nv_bfloat162 b = __floats2bfloat162_rn(lo, hi);
-              memcpy(&w[e], &b, sizeof(uint32_t));
-            }
-            xv[v] = q;
-          }
-          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-          __syncwarp();
-          if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&conv[s])) : "memory");
-        }
-        if (++s == S) { s = 0; ph ^= 1u; }
-      }
-    }
     // ---------------- epilogue: 4 warps, TMEM lane quadrant = warp; 32 partial rows per accumulator ----------------
     const bool ok = nkb > 0 ? mbar_wait_warp(accf, 0, p.err, ERR_WAIT_ACC, p.wait_ns) : true;
     tc_fence_after();

@@ -163,9 +163,6 @@ struct TcWgParams {
   int halo, tg, ntaps, dil, pad, oc_chunks, halo_rows;
   int pack, nacc;
   int x_atom;          // channels per activation (B) atom: 64 (SW128) or 32 (SW64)
-  int x_f16;           // halo mode: the activation operand is stored as fp16 (the forward operand's
-                       // high part); the epilogue warps convert each stage's tile to bf16 in shared
-                       // memory before the MMAs read it
   int pdl;             // launched with programmatic stream serialization
   unsigned long long wait_ns;  // bounded-wait limit
 };
