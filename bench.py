@@ -44,6 +44,8 @@ def parse():
     ap.add_argument("--config", default="40k")
     ap.add_argument("--batch", type=int, default=16)
     ap.add_argument("--frames", type=int, default=32)
+    ap.add_argument("--dtype", default="bf16", choices=["bf16", "fp32"],
+                    help="backward GEMM arithmetic: bf16 operands, or fp32 (bf16 hi + lo pairs, three products)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--only-device", action="store_true",
                     help="time only the device-resident steps (for profiler launch lists)")
@@ -271,7 +273,7 @@ def main():
     cfg = model.config(args.config)
     B, F = args.batch, args.frames
     # learning rate of RVC's own generator training (configs/v2/*.json "learning_rate": 1e-4)
-    gen = Generator(cfg, B, F, device=local, lr=LR)
+    gen = Generator(cfg, B, F, device=local, lr=LR, precision=args.dtype)
     # Each timed phase starts from the initial parameters (which also restarts AdamW): AdamW on a
     # constant synthetic dL/dy drifts every weight the same way, and a few dozen steps later the
     # activations leave the fp16 range of the forward operands; the library would then switch the
@@ -376,15 +378,19 @@ def main():
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16+fp16", "data": "synthetic",
+            "vs_baseline": None, "dtype": "bf16+fp16" if args.dtype == "bf16" else "fp32 (bf16x3 backward, fp16x3 forward)",
+            "data": "synthetic",
             "config": {"workload": f"{args.config} NSF-HiFiGAN generator train step (fwd + bwd + AdamW), "
                                    f"batch {B}/GPU, {F} frames = {T} samples per item",
                        "global_batch": B * world, "frames": F, "samples_per_item": T,
                        "parallelism": f"dp{world}",
-                       "dtype": "forward GEMMs on fp16 operand pairs (fp32-accurate), backward GEMMs on bf16, "
-                                "fp32 accumulation and fp32 residual streams",
+                       "dtype": "forward GEMMs on fp16 operand pairs (fp32-accurate), backward GEMMs on "
+                                + ("bf16" if args.dtype == "bf16" else "bf16 hi + lo pairs (3 products, fp32 precision)")
+                                + ", fp32 accumulation and fp32 residual streams",
                        "gemm": "tcgen05 kind::f16, fp32 accumulate; forward fp16 hi + lo/2048 pairs (3 products), "
-                               "backward bf16",
+                               "backward " + ("bf16" if args.dtype == "bf16" else
+                                              "bf16 pairs: input gradients 2 MMAs (3 products), weight "
+                                              "gradients 3 launches"),
                        "l2": "working set of several GB per step is larger than L2; no flush",
                        "adamw_lr": LR, "params": "reset to their init before each timed phase"},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,

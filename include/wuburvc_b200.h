@@ -145,12 +145,21 @@ typedef struct WubuB200GenConfig {
   int nsf;                    /* 1: harmonic source + noise convs */
 } WubuB200GenConfig;
 
+/* Arithmetic of the backward GEMMs (WubuB200TrainOptions.precision).  The forward GEMMs take fp16
+ * hi + scaled-lo operand pairs (three products, fp32-accurate) in both modes.
+ *   BF16: input- and weight-gradient GEMMs on single bf16 operands with fp32 accumulation.
+ *   FP32: every backward GEMM operand is a bf16 hi + bf16 lo pair (x = hi + lo to ~2^-17) and three
+ *         products are taken (hi*hi + hi*lo + lo*hi): the fp32-accurate mode of the reference's fp32
+ *         conv loops (src/wubu_train.c:461-601), at about three times the backward's tensor work. */
+enum { WUBU_B200_PRECISION_BF16 = 0, WUBU_B200_PRECISION_FP32 = 1 };
+
 typedef struct WubuB200TrainOptions {
   int batch;                  /* items per step on this GPU */
   int frames;                 /* frames per item */
   int device;                 /* CUDA device ordinal */
   float lr, beta1, beta2, eps, weight_decay;  /* AdamW, src/wubu_train.c:57-73 */
   unsigned long long seed;    /* source-noise generator seed */
+  int precision;              /* WUBU_B200_PRECISION_BF16 (0, default) or _FP32 */
 } WubuB200TrainOptions;
 
 typedef struct WubuB200Gen WubuB200Gen; /* opaque */

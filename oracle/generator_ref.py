@@ -173,10 +173,10 @@ def snake(x, alpha):
     return x + torch.sin(a * x) ** 2 / a
 
 
-def act(x, cfg, alpha=None, slope=LRELU):
+def act(x, cfg, alpha=None, slope=None):
     if cfg["activation"] == "snake":
         return snake(x, alpha)
-    return F.leaky_relu(x, slope)
+    return F.leaky_relu(x, cfg.get("lrelu_slope", LRELU) if slope is None else slope)
 
 
 def wn(g, v):

@@ -84,7 +84,10 @@ class TrainOptions(ctypes.Structure):
         ("eps", ctypes.c_float),
         ("weight_decay", ctypes.c_float),
         ("seed", ctypes.c_ulonglong),
+        ("precision", ctypes.c_int),
     ]
+
+PRECISIONS = {"bf16": 0, "fp32": 1}
 
 
 _SIGS = {
@@ -234,14 +237,21 @@ class Generator:
     """One training context on one GPU (``batch`` items of ``frames`` frames)."""
 
     def __init__(self, cfg: dict, batch: int, frames: int, device: int = 0, lr: float = 1e-3,
-                 betas=(0.9, 0.999), eps: float = 1e-8, weight_decay: float = 1e-4, seed: int = 0):
+                 betas=(0.9, 0.999), eps: float = 1e-8, weight_decay: float = 1e-4, seed: int = 0,
+                 precision: str = "bf16"):
+        """precision: "bf16" (backward GEMMs on bf16 operands) or "fp32" (bf16 hi + lo pairs, three
+        products: fp32-accurate gradients at about three times the backward's tensor work)."""
+        if precision not in PRECISIONS:
+            raise ValueError(f"precision must be one of {sorted(PRECISIONS)}")
         self.cfg = dict(cfg)
         self.B, self.F = batch, frames
+        self.precision = precision
         self._c = GenConfig.from_dict(cfg)
         o = TrainOptions()
         o.batch, o.frames, o.device = batch, frames, device
         o.lr, o.beta1, o.beta2, o.eps, o.weight_decay = lr, betas[0], betas[1], eps, weight_decay
         o.seed = seed
+        o.precision = PRECISIONS[precision]
         self._o = o
         self.h = L().wubu_b200_gen_create(ctypes.byref(self._c), ctypes.byref(o))
         if not self.h:

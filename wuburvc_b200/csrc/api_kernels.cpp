@@ -150,7 +150,7 @@ int wubu_b200_convT_dgrad(const void* dy, const void* wd, float* dx, int B, int 
   if (cudaMalloc(&s.err, sizeof(int)) != cudaSuccess) return WUBU_B200_ERR_CUDA;
   cudaMemsetAsync(s.err, 0, sizeof(int), st);
   ConvLaunch L;
-  if (!plan_convT_dgrad(L, B, T_in, C_in, C_out, k, stride, pad, dy, wd, plain_epi(nullptr, dx), s.err))
+  if (!plan_convT_dgrad(L, B, T_in, C_in, C_out, k, stride, pad, dy, wd, nullptr, nullptr, plain_epi(nullptr, dx), s.err))
     return WUBU_B200_ERR_SHAPE;
   if (!launched(L.run(st))) return WUBU_B200_ERR_CUDA;
   return finish(st, s.err);

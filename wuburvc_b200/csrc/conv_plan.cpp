@@ -286,11 +286,12 @@ bool plan_convT(ConvLaunch& L, int B, int T_in, int C_in, int C_out, int k, int 
 static int floordiv(int a, int b) { return (a >= 0) ? a / b : -((-a + b - 1) / b); }
 
 bool plan_convT_dgrad(ConvLaunch& L, int B, int T_in, int C_in, int C_out, int k, int s, int pad, const void* dy,
-                      const void* wd, const Epi& epi, int* err) {
+                      const void* wd, const void* dy_lo, const void* wd_lo, const Epi& epi, int* err) {
   memset(&L.p, 0, sizeof(L.p));
   memset(&L.maps, 0, sizeof(L.maps));
   TcConvParams& p = L.p;
-  if (s > kMaxMaps || k > kMaxTapList) return false;
+  const int split = (dy_lo && wd_lo) ? 1 : 0;
+  if ((split ? 2 * s : s) > kMaxMapsA || k > kMaxTapList) return false;
   const int T_out = T_in * s;
   p.m_rows = T_in;
   p.t_out = T_in;
@@ -305,22 +306,26 @@ bool plan_convT_dgrad(ConvLaunch& L, int B, int T_in, int C_in, int C_out, int k
     p.tap_shift[t] = (short)floordiv(d, s);
     p.tap_w[t] = (short)t;
   }
-  p.lo_base = 0;
+  p.lo_base = s;  // lo views (split) after the s hi views
   p.epi = epi;
-  int n_tile = std::min(C_in, 256);
+  const int n_tile = fwd_n_tile(C_in, split);
   int kc, stages, kgroup;
   size_t smem;
-  pick_fwd_tiling(C_out, n_tile, 0, kc, stages, kgroup, smem);
-  for (int r = 0; r < s; ++r) {
-    const uint64_t rows = (uint64_t)(T_out - r + s - 1) / s;
-    const char* base = static_cast<const char*>(dy) + (size_t)r * C_out * 2;
-    if (!make_map_bf16_3d(&L.maps.a[r], base, C_out, rows, B, (uint64_t)s * C_out * 2, (uint64_t)T_out * C_out * 2,
-                          kc, 128, 1))
-      return false;
-  }
+  pick_fwd_tiling(C_out, n_tile, split, kc, stages, kgroup, smem);
+  for (int h = 0; h <= split; ++h)
+    for (int r = 0; r < s; ++r) {
+      const uint64_t rows = (uint64_t)(T_out - r + s - 1) / s;
+      const char* base = static_cast<const char*>(h ? dy_lo : dy) + (size_t)r * C_out * 2;
+      if (!make_map_bf16_3d(&L.maps.a[h * s + r], base, C_out, rows, B, (uint64_t)s * C_out * 2,
+                            (uint64_t)T_out * C_out * 2, kc, 128, 1))
+        return false;
+    }
   const uint64_t wr = (uint64_t)C_out * 2, wt = wr * C_in;
   if (!make_map_bf16_3d(&L.maps.w_hi, wd, C_out, C_in, k, wr, wt, kc, n_tile, 1)) return false;
-  return finish_fwd(L, B, C_out, C_in, 0, 1, err);
+  if (split && !make_map_bf16_3d(&L.maps.w_lo, wd_lo, C_out, C_in, k, wr, wt, kc, n_tile, 1)) return false;
+  if (!finish_fwd(L, B, C_out, C_in, split, 1, err)) return false;
+  p.split_bf16 = 1;  // gradient pairs are bf16 hi + bf16 lo
+  return true;
 }
 
 // ------------------------------------------------------------------------------------------------

@@ -101,9 +101,11 @@ bool plan_convT(ConvLaunch& L, int B, int T_in, int C_in, int C_out, int k, int 
                 const Epi& epi, int* err);
 
 // ConvTranspose1d input-gradient: dx[b,i,ci] = sum_tap sum_co dy[b, i*s - pad + tap, co] * W[ci][co][tap]
-//   dy [B][T_out][C_out] bf16; wd [k][C_in][C_out] bf16 (tap-major, K-major in C_out).
+//   dy [B][T_out][C_out] bf16; wd [k][C_in][C_out] bf16 (tap-major, K-major in C_out).  With dy_lo and
+//   wd_lo (their bf16 lo companions) the operands are bf16 pairs and three products are taken.
 bool plan_convT_dgrad(ConvLaunch& L, int B, int T_in, int C_in, int C_out, int k, int s, int pad,
-                      const void* dy, const void* wd, const Epi& epi, int* err);
+                      const void* dy, const void* wd, const void* dy_lo, const void* wd_lo, const Epi& epi,
+                      int* err);
 
 // Conv1d weight gradient: dW[co][ci][tap] = sum_{b,t} dy[b,t,co] * x[b, t - pad + dil*tap, ci]
 bool plan_wgrad(WgradLaunch& L, const ConvGeom& g, const void* dy, const void* x, float* part,

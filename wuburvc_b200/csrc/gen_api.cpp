@@ -161,6 +161,7 @@ extern "C" {
 
 WubuB200Gen* wubu_b200_gen_create(const WubuB200GenConfig* cfg, const WubuB200TrainOptions* opt) {
   if (!cfg || !opt || !config_valid(*cfg) || opt->batch < 1 || opt->frames < 1) return nullptr;
+  if (opt->precision != WUBU_B200_PRECISION_BF16 && opt->precision != WUBU_B200_PRECISION_FP32) return nullptr;
   int ndev = 0;
   if (cudaGetDeviceCount(&ndev) != cudaSuccess || opt->device < 0 || opt->device >= ndev) {
     fprintf(stderr, "wuburvc_b200: no CUDA device %d\n", opt ? opt->device : -1);

@@ -132,6 +132,7 @@ __global__ void __launch_bounds__(256) prep_norm_kernel(const PrepDesc* __restri
 __global__ void __launch_bounds__(256) prep_tile_kernel(const PrepDesc* __restrict__ descs, int ndesc) {
   __shared__ float s_scale[128];
   __shared__ unsigned short ht[128][34];  // transposed bf16 weight: [q - q0][p - p0]
+  __shared__ unsigned short lt[128][34];  // its lo companion (fp32 precision)
   __shared__ int di;
   if (threadIdx.x == 0) di = prep_find(descs, ndesc, 1);
   __syncthreads();
@@ -190,7 +191,9 @@ __global__ void __launch_bounds__(256) prep_tile_kernel(const PrepDesc* __restri
         const float w = x[e] * sc;
         split_op(w, d.fmt_bf16, hi[e], lo[e]);
         big |= !d.fmt_bf16 && !(fabsf(w) < kF16Max);
-        ht[lane * QS + e][pl] = __bfloat16_as_ushort(__float2bfloat16_rn(w));
+        const bf16 wb16 = __float2bfloat16_rn(w);
+        ht[lane * QS + e][pl] = __bfloat16_as_ushort(wb16);
+        lt[lane * QS + e][pl] = __bfloat16_as_ushort(__float2bfloat16_rn(w - __bfloat162float(wb16)));
       }
     }
     if (big && d.range_err) atomicCAS(d.range_err, 0, ERR_RANGE);
@@ -217,6 +220,9 @@ __global__ void __launch_bounds__(256) prep_tile_kernel(const PrepDesc* __restri
     const int pp = (tid & 15) * 2;
     const uint32_t w = (uint32_t)ht[r][pp] | ((uint32_t)ht[r][pp + 1] << 16);
     *reinterpret_cast<uint32_t*>(d.dg + ((size_t)td * d.Q + q0 + r) * d.P + p0 + pp) = w;
+    if (d.dg_lo)
+      *reinterpret_cast<uint32_t*>(d.dg_lo + ((size_t)td * d.Q + q0 + r) * d.P + p0 + pp) =
+          (uint32_t)lt[r][pp] | ((uint32_t)lt[r][pp + 1] << 16);
   }
 }
 
@@ -361,7 +367,8 @@ void adamw(float* p, const float* g, float* m, float* v, long long n, float lr, 
 // inputs / cond
 // =============================================================================================
 __global__ void pack_z_kernel(const float* __restrict__ z, int B, int C, int F, f16* __restrict__ hi,
-                              f16* __restrict__ lo, bf16* __restrict__ zb, int* range_err, int fmt_bf16) {
+                              f16* __restrict__ lo, bf16* __restrict__ zb, bf16* __restrict__ zb_lo, int* range_err,
+                              int fmt_bf16) {
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (long long)B * C * F) return;
   const int c = (int)(i % C);
@@ -369,14 +376,16 @@ __global__ void pack_z_kernel(const float* __restrict__ z, int B, int C, int F, 
   const int f = (int)(bf % F), b = (int)(bf / F);
   const float x = z[((size_t)b * C + c) * F + f];
   split_op(x, fmt_bf16, hi[i], lo[i]);
-  zb[i] = __float2bfloat16_rn(x);
+  const bf16 xb = __float2bfloat16_rn(x);
+  zb[i] = xb;
+  if (zb_lo) zb_lo[i] = __float2bfloat16_rn(x - __bfloat162float(xb));
   if (!fmt_bf16 && !(fabsf(x) < kF16Max) && range_err) atomicCAS(range_err, 0, ERR_RANGE);
 }
 
-void pack_z(const float* z, int B, int C, int F, f16* hi, f16* lo, bf16* zb, int* range_err, int fmt_bf16,
-            cudaStream_t st) {
+void pack_z(const float* z, int B, int C, int F, f16* hi, f16* lo, bf16* zb, bf16* zb_lo, int* range_err,
+            int fmt_bf16, cudaStream_t st) {
   const long long n = (long long)B * C * F;
-  pack_z_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(z, B, C, F, hi, lo, zb, range_err, fmt_bf16);
+  pack_z_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(z, B, C, F, hi, lo, zb, zb_lo, range_err, fmt_bf16);
 }
 
 // rowadd[b][c] = bias[c] + sum_j W[c][j] * g[b][j]: warp per output channel c (its weight row read

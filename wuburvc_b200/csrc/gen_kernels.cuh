@@ -25,6 +25,7 @@ struct PrepDesc {
   float* npart;     // ConvTranspose under weight norm: [nchunks][Q] partial sums of squares
   f16 *fwd_hi, *fwd_lo;  // forward operand pair (fp16 hi + fp16 lo * 2^11, or the bf16 pair)
   bf16* dg;               // input-gradient operand (bf16)
+  bf16* dg_lo;            // its lo companion (fp32 precision), or null
   int* range_err;         // set to ERR_RANGE if |W| >= 65504
   int fmt_bf16;           // forward pair as bf16 hi + bf16 lo (the range-safe fallback format)
   int P, Q, k, is_convT, stride;
@@ -71,9 +72,9 @@ void range_flag(const int* err, float* flag, cudaStream_t st);
 
 // ---- inputs --------------------------------------------------------------------------------
 // z [B][C][F] f32 -> [B][F][C] operand pair (fp16 hi / scaled lo, or the bf16 pair) and a bf16 copy
-// (the conv_pre weight gradient's operand)
-void pack_z(const float* z, int B, int C, int F, f16* hi, f16* lo, bf16* zb, int* range_err, int fmt_bf16,
-            cudaStream_t st);
+// (the conv_pre weight gradient's operand) with, when zb_lo is given, its lo companion (fp32 precision)
+void pack_z(const float* z, int B, int C, int F, f16* hi, f16* lo, bf16* zb, bf16* zb_lo, int* range_err,
+            int fmt_bf16, cudaStream_t st);
 
 // cond(g): rowadd[b][c] = bias[c] + sum_i W[c][i] g[b][i]
 void cond_forward(const float* W, const float* bias, const float* g, int B, int C, int gin, float* rowadd,
@@ -118,7 +119,9 @@ struct NoiseActArgs {
   f16* act_hi[3];         // activation: forward operand pair (fp16 hi + fp16 lo * 2^11) ...
   f16* act_lo[3];
   bf16* act_bf[3];        // ... and its bf16 copy (weight-gradient operand, LeakyReLU masks)
+  bf16* act_bflo[3];      // lo companions of act_bf (fp32 precision), or null
   bf16* pre;              // bf16 copy of x (snake masks)
+  bf16* pre_lo;           // its lo companion (fp32 precision), or null
   int* range_err;         // set to ERR_RANGE if |activation| >= 65504
   int fmt_bf16;           // operand pair as bf16 hi + lo (fallback format)
 };
@@ -148,12 +151,14 @@ struct PostBwdArgs {
   const f16* a_lo;
   int fmt_bf16;           // pair format of a_hi / a_lo
   const bf16* mask_src;   // activated (lrelu sign) or pre-activation (snake)
+  const bf16* mask_lo;    // lo companion of a Snake mask source (fp32 precision), or null
   const float* alpha;     // snake alpha [C]
   int act_kind;
   float slope, scale;
   int B, T, C, k;
   float* d_stage;         // [B][T][C] f32
   bf16* d_stage_bf;       // [B][T][C]
+  bf16* d_stage_bf_lo;    // its lo companion (fp32 precision), or null
   float* colsum_part;     // [nblk][C]
   float* w_part;          // [nblk][C*k]
   float* alpha_part;      // [nblk][C]

@@ -96,14 +96,20 @@ __global__ void __launch_bounds__(256) noise_add_act_kernel(NoiseActArgs a) {
   for (int r = 0; r < kNaRowsPerWarp; ++r) {
     if (r >= nr) break;
     const size_t i = ((size_t)b * a.T + jw + r) * a.C + c;
-    if (a.pre) a.pre[i] = __float2bfloat16_rn(x[r]);
+    if (a.pre) {
+      const bf16 h = __float2bfloat16_rn(x[r]);
+      a.pre[i] = h;
+      if (a.pre_lo) a.pre_lo[i] = __float2bfloat16_rn(x[r] - __bfloat162float(h));
+    }
     for (int q = 0; q < a.n_act; ++q) {
       const float y = act_fwd2(x[r], a.act_kind, a.slope, al[q]);
       f16 hi, lo;
       split_op(y, a.fmt_bf16, hi, lo);
       a.act_hi[q][i] = hi;
       a.act_lo[q][i] = lo;
-      a.act_bf[q][i] = __float2bfloat16_rn(y);
+      const bf16 yb = __float2bfloat16_rn(y);
+      a.act_bf[q][i] = yb;
+      if (a.act_bflo[q]) a.act_bflo[q][i] = __float2bfloat16_rn(y - __bfloat162float(yb));
       if (!a.fmt_bf16 && !(fabsf(y) < kF16Max) && a.range_err) atomicCAS(a.range_err, 0, ERR_RANGE);
     }
   }
@@ -526,6 +532,7 @@ __global__ void __launch_bounds__(256) post_backward_kernel(PostBwdArgs a) {
       const size_t off = (size_t)row * kPostC + c;
       xin8[r] = join_op(a.a_hi[off], a.a_lo[off], a.fmt_bf16);
       xm8[r] = __bfloat162float(a.mask_src[off]);
+      if (a.mask_lo) xm8[r] += __bfloat162float(a.mask_lo[off]);
     }
   }
 #pragma unroll
@@ -571,7 +578,9 @@ __global__ void __launch_bounds__(256) post_backward_kernel(PostBwdArgs a) {
     }
     const float ds = da * deriv * a.scale;
     a.d_stage[off] = ds;
-    a.d_stage_bf[off] = __float2bfloat16_rn(ds);
+    const bf16 dsb = __float2bfloat16_rn(ds);
+    a.d_stage_bf[off] = dsb;
+    if (a.d_stage_bf_lo) a.d_stage_bf_lo[off] = __float2bfloat16_rn(ds - __bfloat162float(dsb));
     cs += ds;
   }
   red[warp][c] = cs;

@@ -4,9 +4,11 @@
 // Data layout in HBM: every activation is channels-last [B][T][C].  Residual streams (pair inputs,
 // stage sums, their gradients) are fp32.  Forward GEMM operands are fp16 hi + fp16 lo*2^11 pairs
 // (three products, fp32-accurate; bf16 pairs after a range error); every activation also keeps a
-// bf16 copy, the weight gradient's operand and the LeakyReLU mask source; backward operands are
-// single bf16.  Parameters, gradients and AdamW moments live
-// in flat fp32 buffers laid out by the parameter table.
+// bf16 copy, the weight gradient's operand and the LeakyReLU mask source.  Backward operands are
+// single bf16, or under fp32 precision bf16 hi + lo pairs: every bf16 operand tensor then has a lo
+// companion written by its producer, the input gradients take three products in one kernel and the
+// weight gradients three launches summed by one reduction.  Parameters, gradients and AdamW moments
+// live in flat fp32 buffers laid out by the parameter table.
 #include "gen_model.h"
 
 #include <cmath>
@@ -88,6 +90,7 @@ bool make_weights(Gen& m, ConvWeights& w, const std::string& base, bool resblock
   w.stride = stride;
   const size_t n = (size_t)p.n;
   if (!dalloc(m, &w.fwd_hi, n) || !dalloc(m, &w.fwd_lo, n) || !dalloc(m, &w.dg, n)) return false;
+  if (m.fp32 && !dalloc(m, &w.dg_lo, n)) return false;
   if (wn) {
     if (!dalloc(m, &w.norm, (size_t)w.rows) || !dalloc(m, &w.dW, n)) return false;
   } else {
@@ -108,9 +111,41 @@ bool make_wgrad_job(Gen& m, WgradJob& j, int layout, int c_out, int k, const Con
     if (j.L.row_tap[r] >= 0) seen[(size_t)j.L.row_oc[r] * k + j.L.row_tap[r]] = 1;
   for (char x : seen)
     if (!x) return false;
-  if (!dalloc(m, &j.part, wgrad_part_floats(j.L))) return false;
+  const size_t one = wgrad_part_floats(j.L);
+  if (!dalloc(m, &j.part, one * j.nl)) return false;
   j.L.p.part = j.part;
+  for (int i = 0; i + 1 < j.nl; ++i) {
+    if (j.lo[i].splits != j.L.splits || j.lo[i].p.n_mtiles != j.L.p.n_mtiles || j.lo[i].p.n_total != j.L.p.n_total)
+      return false;
+    j.lo[i].p.part = j.part + one * (i + 1);
+  }
   return true;
+}
+
+size_t job_part_floats(const WgradJob& j) { return wgrad_part_floats(j.L) * j.nl; }
+
+// Input-gradient GEMM: single bf16 operands, or under fp32 precision bf16 hi + lo pairs (three products).
+bool plan_dgrad(Gen& m, ConvOp& op, const ConvGeom& g, const bf16* dy, const bf16* dy_lo, const ConvWeights& w,
+                const Epi& e) {
+  if (m.fp32 && (!dy_lo || !w.dg_lo)) return false;
+  if (!plan_conv_any(op, g, dy, m.fp32 ? dy_lo : nullptr, w.dg, m.fp32 ? w.dg_lo : nullptr, m.fp32, e, m.err))
+    return false;
+  op.v1.p.split_bf16 = 1;  // gradient pairs are bf16 hi + bf16 lo (no effect without the split)
+  op.c2.p.split_bf16 = 1;
+  return true;
+}
+
+// Weight-gradient GEMM of a Conv1d: one launch, or under fp32 precision three (dy_hi x x_hi, dy_hi x
+// x_lo, dy_lo x x_hi) whose split-K partials one reduction sums.
+bool plan_wgrad_job(Gen& m, WgradJob& j, const ConvGeom& g, const bf16* dy, const bf16* dy_lo, const bf16* x,
+                    const bf16* x_lo, const ConvWeights& w) {
+  j.nl = m.fp32 ? 3 : 1;
+  if (m.fp32 && (!dy_lo || !x_lo)) return false;
+  if (!plan_wgrad(j.L, g, dy, x, nullptr, ~size_t(0), kWgradCtas, m.err)) return false;
+  if (m.fp32 && (!plan_wgrad(j.lo[0], g, dy, x_lo, nullptr, ~size_t(0), kWgradCtas, m.err) ||
+                 !plan_wgrad(j.lo[1], g, dy_lo, x, nullptr, ~size_t(0), kWgradCtas, m.err)))
+    return false;
+  return make_wgrad_job(m, j, 0, g.C_out, g.k, w);
 }
 
 // The split-K reduction of a weight gradient: partial rows are (tap * C_out + oc) x C_in, so the first
@@ -123,7 +158,7 @@ ReduceDesc wgrad_desc(Gen& m, const WgradJob& j) {
   d.out = w.pg >= 0 ? w.dW : m.G(w.pv);
   d.ld = (long long)j.L.p.n_mtiles * 128 * j.L.p.n_total;
   d.n = (long long)j.k * j.c_out * j.L.p.n_total;
-  d.nparts = j.L.splits;
+  d.nparts = j.L.splits * j.nl;  // the fp32-precision launches' partials follow L's
   return d;
 }
 
@@ -220,8 +255,14 @@ bool join_side(Gen& m) {
   return true;
 }
 
-bool run_wgrad(Gen& m, StageBufs& s, const WgradJob& j) {
+bool run_wgrad_launches(Gen& m, const WgradJob& j) {
   CK(j.L.run(m.stream));
+  for (int i = 0; i + 1 < j.nl; ++i) CK(j.lo[i].run(m.stream));
+  return true;
+}
+
+bool run_wgrad(Gen& m, StageBufs& s, const WgradJob& j) {
+  if (!run_wgrad_launches(m, j)) return false;
   if (j.flush >= 0) {  // the group's reductions overlap the next convolutions
     const WgradBatch& b = s.wg_batches[j.flush];
     if (!fork_side(m)) return false;
@@ -233,7 +274,7 @@ bool run_wgrad(Gen& m, StageBufs& s, const WgradJob& j) {
 
 // conv_pre's weight gradient (kernel + reduction + weight norm; a handful of launches, once per step)
 bool run_pre_wgrad(Gen& m) {
-  CK(m.pre_wg.L.run(m.stream));
+  if (!run_wgrad_launches(m, m.pre_wg)) return false;
   const ReduceDesc d = wgrad_desc(m, m.pre_wg);
   col_reduce_ld(d.part, d.nparts, d.n, d.ld, d.out, 0, m.stream);
   const ConvWeights& w = m.wpre;
@@ -260,6 +301,9 @@ bool gen_setup(Gen& m) {
   m.dim = c.harmonic_num + 1;
   const bool snake = c.activation == 1;
   const int B = m.B;
+  m.fp32 = m.opt.precision == WUBU_B200_PRECISION_FP32;
+  // a bf16 lo companion, allocated under fp32 precision only (left null otherwise)
+  auto lo_alloc = [&](bf16** p, size_t n) { return !m.fp32 || dalloc(m, p, n); };
   CK(cudaSetDevice(m.opt.device));
   CK(cudaStreamCreateWithFlags(&m.stream, cudaStreamNonBlocking));
   CK(cudaStreamCreateWithFlags(&m.side, cudaStreamNonBlocking));
@@ -278,7 +322,7 @@ bool gen_setup(Gen& m) {
   // ---- inputs ----
   if (!dalloc(m, &m.z, (size_t)B * c.in_channels * m.F) || !dalloc(m, &m.dldy, (size_t)B * m.T)) return false;
   if (!dalloc(m, &m.z_hi, (size_t)B * m.F * c.in_channels) || !dalloc(m, &m.z_lo, (size_t)B * m.F * c.in_channels) ||
-      !dalloc(m, &m.z_bf, (size_t)B * m.F * c.in_channels))
+      !dalloc(m, &m.z_bf, (size_t)B * m.F * c.in_channels) || !lo_alloc(&m.z_bflo, (size_t)B * m.F * c.in_channels))
     return false;
   if (c.gin_channels && !dalloc(m, &m.g, (size_t)B * c.gin_channels)) return false;
   if (c.nsf) {
@@ -336,6 +380,8 @@ bool gen_setup(Gen& m) {
       !dalloc(m, &m.d_pre_bf, n_pre))
     return false;
   if (snake && !dalloc(m, &m.pre_pre, n_pre)) return false;
+  if (!lo_alloc(&m.pre_bflo, n_pre) || !lo_alloc(&m.d_pre_bflo, n_pre) || (snake && !lo_alloc(&m.pre_prelo, n_pre)))
+    return false;
   if (c.gin_channels && !dalloc(m, &m.rowadd, (size_t)B * C0)) return false;
   if (!dalloc(m, &m.audio, (size_t)B * m.T)) return false;
   for (int L = 0; L < 4; ++L) {
@@ -346,10 +392,14 @@ bool gen_setup(Gen& m) {
       return false;
     if (!dalloc(m, &s.d_s, n) || !dalloc(m, &s.d_s_bf, n) || !dalloc(m, &s.d_x, n) || !dalloc(m, &s.d_x_bf, n))
       return false;
+    if (!lo_alloc(&s.sa_bflo, n) || !lo_alloc(&s.d_s_bflo, n) || !lo_alloc(&s.d_x_bflo, n)) return false;
     const int nxa = snake ? m.nk : 1;
     for (int q = 0; q < nxa; ++q)
-      if (!dalloc(m, &s.xa_hi[q], n) || !dalloc(m, &s.xa_lo[q], n) || !dalloc(m, &s.xa_bf[q], n)) return false;
+      if (!dalloc(m, &s.xa_hi[q], n) || !dalloc(m, &s.xa_lo[q], n) || !dalloc(m, &s.xa_bf[q], n) ||
+          !lo_alloc(&s.xa_bflo[q], n))
+        return false;
     if (snake && (!dalloc(m, &s.x_pre, n) || !dalloc(m, &s.s_pre, n))) return false;
+    if (snake && (!lo_alloc(&s.x_prelo, n) || !lo_alloc(&s.s_prelo, n))) return false;
     const int tiles = B * ((s.T + 127) / 128);
     for (int j = 0; j < m.nk; ++j) {
       StackBufs& k = s.st[j];
@@ -359,15 +409,19 @@ bool gen_setup(Gen& m) {
       k.a1_lo[0] = s.xa_lo[snake ? j : 0];
       k.a1_bf[0] = s.xa_bf[snake ? j : 0];
       k.a1_pre[0] = s.x_pre;
+      k.a1_bflo[0] = s.xa_bflo[snake ? j : 0];
+      k.a1_prelo[0] = s.x_prelo;
       for (int cp = 0; cp < m.nd; ++cp) {
         if (cp > 0) {
           if (!dalloc(m, &k.p[cp], n) || !dalloc(m, &k.a1_hi[cp], n) || !dalloc(m, &k.a1_lo[cp], n) ||
-              !dalloc(m, &k.a1_bf[cp], n))
+              !dalloc(m, &k.a1_bf[cp], n) || !lo_alloc(&k.a1_bflo[cp], n))
             return false;
-          if (snake && !dalloc(m, &k.a1_pre[cp], n)) return false;
+          if (snake && (!dalloc(m, &k.a1_pre[cp], n) || !lo_alloc(&k.a1_prelo[cp], n))) return false;
         }
-        if (!dalloc(m, &k.a2_hi[cp], n) || !dalloc(m, &k.a2_lo[cp], n) || !dalloc(m, &k.a2_bf[cp], n)) return false;
-        if (snake && !dalloc(m, &k.a2_pre[cp], n)) return false;
+        if (!dalloc(m, &k.a2_hi[cp], n) || !dalloc(m, &k.a2_lo[cp], n) || !dalloc(m, &k.a2_bf[cp], n) ||
+            !lo_alloc(&k.a2_bflo[cp], n))
+          return false;
+        if (snake && (!dalloc(m, &k.a2_pre[cp], n) || !lo_alloc(&k.a2_prelo[cp], n))) return false;
         // column-sum partials: one row per tile (general kernel) or per CTA of the persistent kernel,
         // which may split N in two and writes two rows (epilogue groups) per CTA: at most 4 * tiles rows
         if (!dalloc(m, &k.cs_dc1[cp], (size_t)4 * tiles * s.C) || !dalloc(m, &k.cs_dp[cp], (size_t)4 * tiles * s.C))
@@ -376,9 +430,9 @@ bool gen_setup(Gen& m) {
             (!dalloc(m, &k.ap1[cp], (size_t)4 * tiles * s.C) || !dalloc(m, &k.ap2[cp], (size_t)4 * tiles * s.C)))
           return false;
       }
-      if (!dalloc(m, &k.d_c1, n)) return false;
+      if (!dalloc(m, &k.d_c1, n) || !lo_alloc(&k.d_c1_lo, n)) return false;
       for (int q = 0; q < 2; ++q)
-        if (!dalloc(m, &k.pp[q], n) || !dalloc(m, &k.pp_bf[q], n)) return false;
+        if (!dalloc(m, &k.pp[q], n) || !dalloc(m, &k.pp_bf[q], n) || !lo_alloc(&k.pp_bflo[q], n)) return false;
     }
     if (c.nsf) {
       s.noise_parts = noise_backward_parts(B, s.T, s.C, s.kn);
@@ -403,10 +457,12 @@ bool gen_setup(Gen& m) {
     e.act_hi = m.pre_hi;
     e.act_lo = m.pre_lo;
     e.act_bf = m.pre_bf;
+    e.act_bflo = m.pre_bflo;
     e.range_err = m.err;
     e.act_kind = c.activation;
     e.act_alpha = alpha_ptr(m, "dec.ups_act.0.alpha");
     e.pre_hi = m.pre_pre;
+    e.pre_lo = m.pre_prelo;
     ConvGeom g{B, m.F, m.F, c.in_channels, C0, 7, 1, 3};
     if (!plan_conv(m.pre_fwd, g, m.z_hi, m.z_lo, m.wpre.fwd_hi, m.wpre.fwd_lo, 1, e, m.err)) return false;
   }
@@ -437,10 +493,12 @@ bool gen_setup(Gen& m) {
           e.act_hi = k.a2_hi[cp];
           e.act_lo = k.a2_lo[cp];
           e.act_bf = k.a2_bf[cp];
+          e.act_bflo = k.a2_bflo[cp];
           e.range_err = m.err;
           e.act_kind = c.activation;
           e.act_alpha = alpha_ptr(m, "dec.resblocks." + R + ".alpha2." + P);
           e.pre_hi = k.a2_pre[cp];
+          e.pre_lo = k.a2_prelo[cp];
           ConvGeom g{B, s.T, s.T, s.C, s.C, kk, dil, dil * (kk - 1) / 2};
           if (!plan_conv_any(k.f1[cp], g, k.a1_hi[cp], k.a1_lo[cp], k.w1[cp].fwd_hi, k.w1[cp].fwd_lo, 1, e, m.err))
             return false;
@@ -455,9 +513,11 @@ bool gen_setup(Gen& m) {
             e.act_hi = k.a1_hi[cp + 1];
             e.act_lo = k.a1_lo[cp + 1];
             e.act_bf = k.a1_bf[cp + 1];
+            e.act_bflo = k.a1_bflo[cp + 1];
             e.range_err = m.err;
             e.act_alpha = alpha_ptr(m, "dec.resblocks." + R + ".alpha1." + std::to_string(cp + 1));
             e.pre_hi = k.a1_pre[cp + 1];
+            e.pre_lo = k.a1_prelo[cp + 1];
           } else {
             e.scale = 1.f / (float)m.nk;
             e.out_f32 = s.sout;
@@ -466,8 +526,10 @@ bool gen_setup(Gen& m) {
               e.act_hi = s.sa_hi;
               e.act_lo = s.sa_lo;
               e.act_bf = s.sa_bf;
+              e.act_bflo = s.sa_bflo;
               e.range_err = m.err;
               e.pre_hi = s.s_pre;
+              e.pre_lo = s.s_prelo;
               e.slope = last ? c.final_slope : c.lrelu_slope;
               e.act_alpha = alpha_ptr(m, last ? "dec.post_act.alpha" : "dec.ups_act." + std::to_string(L + 1) + ".alpha");
             }
@@ -500,28 +562,32 @@ bool gen_setup(Gen& m) {
         const std::string P = std::to_string(cp);
         const float* dp_out_f = (cp == m.nd - 1) ? s.d_s : k.pp[cp % 2];
         const bf16* dp_out_b = (cp == m.nd - 1) ? s.d_s_bf : k.pp_bf[cp % 2];
+        const bf16* dp_out_lo = (cp == m.nd - 1) ? s.d_s_bflo : k.pp_bflo[cp % 2];
         (void)dp_out_f;
         {  // conv2 dgrad -> d_c1 (mask of conv1's activation)
           Epi e = epi0(c.lrelu_slope);
           e.act_kind = c.activation;
           e.mask_src = snake ? k.a2_pre[cp] : k.a2_bf[cp];
+          e.mask_lo = snake ? k.a2_prelo[cp] : nullptr;
           e.mask_alpha = alpha_ptr(m, "dec.resblocks." + R + ".alpha2." + P);
           e.alpha_part = k.ap2[cp];
           e.out_bf16 = k.d_c1;
+          e.out_bf16_lo = k.d_c1_lo;
           e.colsum = k.cs_dc1[cp];
           ConvGeom g{B, s.T, s.T, s.C, s.C, kk, 1, (kk - 1) / 2};
-          if (!plan_conv_any(k.d2[cp], g, dp_out_b, nullptr, k.w2[cp].dg, nullptr, 0, e, m.err)) return false;
+          if (!plan_dgrad(m, k.d2[cp], g, dp_out_b, dp_out_lo, k.w2[cp], e)) return false;
           if (k.d2[cp].partials() > 4 * k.tiles) return false;  // partial buffers hold 4 * tiles rows
         }
         {  // conv2 wgrad
           ConvGeom g{B, s.T, s.T, s.C, s.C, kk, 1, (kk - 1) / 2};
-          if (!plan_wgrad(k.g2[cp].L, g, dp_out_b, k.a2_bf[cp], nullptr, ~size_t(0), kWgradCtas, m.err)) return false;
-          if (!make_wgrad_job(m, k.g2[cp], 0, s.C, kk, k.w2[cp])) return false;
+          if (!plan_wgrad_job(m, k.g2[cp], g, dp_out_b, dp_out_lo, k.a2_bf[cp], k.a2_bflo[cp], k.w2[cp]))
+            return false;
         }
         {  // conv1 dgrad -> gradient wrt the pair input
           Epi e = epi0(c.lrelu_slope);
           e.act_kind = c.activation;
           e.mask_src = snake ? k.a1_pre[cp] : k.a1_bf[cp];
+          e.mask_lo = snake ? k.a1_prelo[cp] : nullptr;
           e.mask_alpha = alpha_ptr(m, "dec.resblocks." + R + ".alpha1." + P);
           e.alpha_part = k.ap1[cp];
           e.res = (cp == m.nd - 1) ? s.d_s : k.pp[cp % 2];
@@ -529,19 +595,20 @@ bool gen_setup(Gen& m) {
           if (cp > 0) {
             e.out_f32 = k.pp[(cp - 1) % 2];
             e.out_bf16 = k.pp_bf[(cp - 1) % 2];
+            e.out_bf16_lo = k.pp_bflo[(cp - 1) % 2];
           } else {
             e.out_f32 = s.d_x;
             e.accumulate = j > 0;
             e.out_bf16 = (j == m.nk - 1) ? s.d_x_bf : nullptr;
+            e.out_bf16_lo = (j == m.nk - 1) ? s.d_x_bflo : nullptr;
           }
           ConvGeom g{B, s.T, s.T, s.C, s.C, kk, dil, dil * (kk - 1) / 2};
-          if (!plan_conv_any(k.d1[cp], g, k.d_c1, nullptr, k.w1[cp].dg, nullptr, 0, e, m.err)) return false;
+          if (!plan_dgrad(m, k.d1[cp], g, k.d_c1, k.d_c1_lo, k.w1[cp], e)) return false;
           if (k.d1[cp].partials() > 4 * k.tiles) return false;
         }
         {  // conv1 wgrad
           ConvGeom g{B, s.T, s.T, s.C, s.C, kk, dil, dil * (kk - 1) / 2};
-          if (!plan_wgrad(k.g1[cp].L, g, k.d_c1, k.a1_bf[cp], nullptr, ~size_t(0), kWgradCtas, m.err)) return false;
-          if (!make_wgrad_job(m, k.g1[cp], 0, s.C, kk, k.w1[cp])) return false;
+          if (!plan_wgrad_job(m, k.g1[cp], g, k.d_c1, k.d_c1_lo, k.a1_bf[cp], k.a1_bflo[cp], k.w1[cp])) return false;
         }
       }
     }
@@ -558,32 +625,45 @@ bool gen_setup(Gen& m) {
       if (L > 0) {
         StageBufs& pv = m.sg[L - 1];
         e.mask_src = snake ? pv.s_pre : pv.sa_bf;
+        e.mask_lo = snake ? pv.s_prelo : nullptr;
         e.scale = 1.f / (float)m.nk;
         e.out_f32 = pv.d_s;
         e.out_bf16 = pv.d_s_bf;
+        e.out_bf16_lo = pv.d_s_bflo;
         if (!dalloc(m, &pv.cs_ds, (size_t)tiles * pv.C)) return false;
         pv.cs_ds_tiles = tiles;
         e.colsum = pv.cs_ds;
       } else {
         e.mask_src = snake ? m.pre_pre : m.pre_bf;
+        e.mask_lo = snake ? m.pre_prelo : nullptr;
         e.out_bf16 = m.d_pre_bf;
+        e.out_bf16_lo = m.d_pre_bflo;
         if (!dalloc(m, &m.cs_pre, (size_t)tiles * C0)) return false;
         m.cs_pre_tiles = tiles;
         m.pre_tiles_per_item = (Tin + 127) / 128;
         e.colsum = m.cs_pre;
       }
-      if (!plan_convT_dgrad(s.up_dg, B, Tin, s.Cin, s.C, s.ku, s.su, s.pu, s.d_x_bf, s.wu.dg, e, m.err)) return false;
+      if (!plan_convT_dgrad(s.up_dg, B, Tin, s.Cin, s.C, s.ku, s.su, s.pu, s.d_x_bf, s.wu.dg,
+                            m.fp32 ? s.d_x_bflo : nullptr, m.fp32 ? s.wu.dg_lo : nullptr, e, m.err))
+        return false;
       const bf16* xin = (L == 0) ? m.pre_bf : m.sg[L - 1].sa_bf;
-      if (!plan_convT_wgrad(s.up_wg.L, B, Tin, s.Cin, s.C, s.ku, s.su, s.pu, xin, s.d_x_bf, nullptr, ~size_t(0),
+      const bf16* xin_lo = (L == 0) ? m.pre_bflo : m.sg[L - 1].sa_bflo;
+      WgradJob& j = s.up_wg;
+      j.nl = m.fp32 ? 3 : 1;
+      if (!plan_convT_wgrad(j.L, B, Tin, s.Cin, s.C, s.ku, s.su, s.pu, xin, s.d_x_bf, nullptr, ~size_t(0),
                             kWgradCtas, m.err))
         return false;
-      if (!make_wgrad_job(m, s.up_wg, 1, s.C, s.ku, s.wu)) return false;
+      if (m.fp32 && (!plan_convT_wgrad(j.lo[0], B, Tin, s.Cin, s.C, s.ku, s.su, s.pu, xin_lo, s.d_x_bf, nullptr,
+                                       ~size_t(0), kWgradCtas, m.err) ||
+                     !plan_convT_wgrad(j.lo[1], B, Tin, s.Cin, s.C, s.ku, s.su, s.pu, xin, s.d_x_bflo, nullptr,
+                                       ~size_t(0), kWgradCtas, m.err)))
+        return false;
+      if (!make_wgrad_job(m, j, 1, s.C, s.ku, s.wu)) return false;
     }
   }
   {  // conv_pre wgrad
     ConvGeom g{B, m.F, m.F, c.in_channels, C0, 7, 1, 3};
-    if (!plan_wgrad(m.pre_wg.L, g, m.d_pre_bf, m.z_bf, nullptr, ~size_t(0), kWgradCtas, m.err)) return false;
-    if (!make_wgrad_job(m, m.pre_wg, 0, C0, 7, m.wpre)) return false;
+    if (!plan_wgrad_job(m, m.pre_wg, g, m.d_pre_bf, m.d_pre_bflo, m.z_bf, m.z_bflo, m.wpre)) return false;
   }
   // ---- batched per-stage reductions ----
   for (int L = 0; L < 4; ++L) {
@@ -612,8 +692,8 @@ bool gen_setup(Gen& m) {
         WgradJob& jb = *jobs[i];
         wg.push_back(wgrad_desc(m, jb));
         if (jb.w->pg >= 0) wn.push_back(wn_desc(m, *jb.w));
-        bytes += wgrad_part_floats(jb.L) * sizeof(float);
-        const size_t next = i + 1 < jobs.size() ? wgrad_part_floats(jobs[i + 1]->L) * sizeof(float) : 0;
+        bytes += job_part_floats(jb) * sizeof(float);
+        const size_t next = i + 1 < jobs.size() ? job_part_floats(*jobs[i + 1]) * sizeof(float) : 0;
         if (i + 1 == jobs.size() || bytes + next > kWgBatchBytes) {
           WgradBatch bt;
           if (!upload_reduce_table(m, wg, &bt.wg_d, &bt.wg_n, &bt.wg_blocks) ||
@@ -667,15 +747,19 @@ bool gen_setup(Gen& m) {
         k.f2[cp].set_pdl(true);
         k.d1[cp].set_pdl(true);
         k.d2[cp].set_pdl(true);
-        k.g1[cp].L.p.pdl = 1;
-        k.g2[cp].L.p.pdl = 1;
+        for (WgradJob* wj : {&k.g1[cp], &k.g2[cp]}) {
+          wj->L.p.pdl = 1;
+          wj->lo[0].p.pdl = wj->lo[1].p.pdl = 1;
+        }
       }
     s.up_fwd.p.pdl = 1;
     s.up_dg.p.pdl = 1;
     s.up_wg.L.p.pdl = 1;
+    s.up_wg.lo[0].p.pdl = s.up_wg.lo[1].p.pdl = 1;
   }
   m.pre_fwd.p.pdl = 1;
   m.pre_wg.L.p.pdl = 1;
+  m.pre_wg.lo[0].p.pdl = m.pre_wg.lo[1].p.pdl = 1;
   {  // weight preparation table: every GEMM weight, two launches per step
     std::vector<PrepDesc> d;
     int nb = 0, tb = 0;
@@ -688,6 +772,7 @@ bool gen_setup(Gen& m) {
       p.fwd_lo = w.fwd_lo;
       p.range_err = m.err;
       p.dg = w.dg;
+      p.dg_lo = w.dg_lo;
       p.P = w.convT ? w.cols : w.rows;
       p.Q = w.convT ? w.rows : w.cols;
       p.k = w.k;
@@ -765,7 +850,7 @@ bool gen_forward(Gen& m) {
   set_reduce_scratch(m.red_scratch, m.red_scratch_n);
   // GEMM weights for this step (weight norm + bf16 hi/lo + transposed layouts)
   prep_weights(m.prep_descs, m.n_prep, m.prep_norm_blocks, m.prep_tile_blocks, st);
-  pack_z(m.z, m.B, c.in_channels, m.F, m.z_hi, m.z_lo, m.z_bf, m.err, m.op_bf16, st);
+  pack_z(m.z, m.B, c.in_channels, m.F, m.z_hi, m.z_lo, m.z_bf, m.z_bflo, m.err, m.op_bf16, st);
   if (c.nsf) {
     NsfArgs a{};
     a.f0 = m.f0;
@@ -816,8 +901,10 @@ bool gen_forward(Gen& m) {
       na.act_hi[q] = s.xa_hi[q];
       na.act_lo[q] = s.xa_lo[q];
       na.act_bf[q] = s.xa_bf[q];
+      na.act_bflo[q] = s.xa_bflo[q];
     }
     na.pre = s.x_pre;
+    na.pre_lo = s.x_prelo;
     na.range_err = m.err;
     na.fmt_bf16 = m.op_bf16;
     noise_add_act(na, st);
@@ -852,6 +939,7 @@ bool gen_backward(Gen& m) {
     a.a_lo = s3.sa_lo;
     a.fmt_bf16 = m.op_bf16;
     a.mask_src = snake ? s3.s_pre : s3.sa_bf;
+    a.mask_lo = snake ? s3.s_prelo : nullptr;
     a.alpha = alpha_ptr(m, "dec.post_act.alpha");
     a.act_kind = c.activation;
     a.slope = c.final_slope;
@@ -862,6 +950,7 @@ bool gen_backward(Gen& m) {
     a.k = 7;
     a.d_stage = s3.d_s;
     a.d_stage_bf = s3.d_s_bf;
+    a.d_stage_bf_lo = s3.d_s_bflo;
     a.colsum_part = m.post_cs;
     a.w_part = m.post_wpart;
     a.alpha_part = m.post_ap;

@@ -20,12 +20,16 @@ struct ConvWeights {
   int convT = 0, stride = 1;
   f16 *fwd_hi = nullptr, *fwd_lo = nullptr;  // forward operand pair (see Gen::op_bf16)
   bf16* dg = nullptr;                         // input-gradient operand
+  bf16* dg_lo = nullptr;                      // its lo companion (fp32 precision)
   float* norm = nullptr;  // ||v|| rows (weight norm)
   float* dW = nullptr;    // gradient in param layout (grad buffer directly, or a temp under weight norm)
 };
 
 struct WgradJob {
   WgradLaunch L;
+  // fp32 precision: the products dy_hi x x_lo and dy_lo x x_hi, same plan, their partials after L's
+  WgradLaunch lo[2];
+  int nl = 1;  // launches (1, or 3 under fp32 precision)
   float* part = nullptr;  // this job's split-K partials (reduced later in a batched launch)
   int flush = -1;         // WgradBatch of the stage to launch after this job's kernel (-1: none)
   const ConvWeights* w = nullptr;
@@ -51,10 +55,14 @@ struct StackBufs {
   float* p[3] = {};                                      // pair input (p[0] aliases the stage input)
   f16 *a2_hi[3] = {}, *a2_lo[3] = {};                    // activation of conv1's output
   bf16 *a2_bf[3] = {}, *a2_pre[3] = {};
+  // fp32 precision: bf16 lo companions of the bf16 tensors (null otherwise)
+  bf16 *a1_bflo[3] = {}, *a1_prelo[3] = {}, *a2_bflo[3] = {}, *a2_prelo[3] = {};
   // backward
   bf16* d_c1 = nullptr;
+  bf16* d_c1_lo = nullptr;
   float* pp[2] = {};
   bf16* pp_bf[2] = {};
+  bf16* pp_bflo[2] = {};
   float *cs_dc1[3] = {}, *cs_dp[3] = {}, *ap1[3] = {}, *ap2[3] = {};
   int tiles = 0;
   ConvWeights w1[3], w2[3];
@@ -75,6 +83,9 @@ struct StageBufs {
   bf16* d_s_bf = nullptr;
   float* d_x = nullptr;
   bf16* d_x_bf = nullptr;
+  // fp32 precision: bf16 lo companions (null otherwise)
+  bf16 *xa_bflo[3] = {}, *x_prelo = nullptr, *sa_bflo = nullptr, *s_prelo = nullptr;
+  bf16 *d_s_bflo = nullptr, *d_x_bflo = nullptr;
   float* cs_ds = nullptr;  // colsum partials of d_s (from its producer)
   int cs_ds_tiles = 0;
   float* ap_up = nullptr;  // snake alpha partials of the activation feeding ups L (from up_dg)
@@ -118,6 +129,7 @@ struct Gen {
   bool has_noise_input = false;
   f16 *z_hi = nullptr, *z_lo = nullptr;
   bf16* z_bf = nullptr;
+  bf16* z_bflo = nullptr;  // fp32 precision
   // source
   float *har = nullptr, *sw = nullptr, *d_har = nullptr, *nsf_part = nullptr;
   double* nsf_acc = nullptr;
@@ -128,6 +140,7 @@ struct Gen {
   f16 *pre_hi = nullptr, *pre_lo = nullptr;
   bf16 *pre_bf = nullptr, *pre_pre = nullptr;
   bf16* d_pre_bf = nullptr;
+  bf16 *pre_bflo = nullptr, *pre_prelo = nullptr, *d_pre_bflo = nullptr;  // fp32 precision
   float* cs_pre = nullptr;
   int cs_pre_tiles = 0, pre_tiles_per_item = 0;
   ConvLaunch pre_fwd;
@@ -143,6 +156,8 @@ struct Gen {
   // forward operand format: 0 = fp16 hi + fp16 lo*2^11 (fp32-accurate, |x| < 65504); 1 = bf16 hi +
   // bf16 lo (range-safe, ~2^-17), the format a context switches to for good after a range error
   int op_bf16 = 0;
+  // backward GEMM operands as bf16 hi + lo pairs (opt.precision == WUBU_B200_PRECISION_FP32)
+  int fp32 = 0;
   int n_prep = 0, prep_norm_blocks = 0, prep_tile_blocks = 0;
   float* red_scratch = nullptr;  // two-pass deterministic reductions
   size_t red_scratch_n = 0;

@@ -18,7 +18,8 @@
 
 namespace wb {
 
-constexpr int kMaxMaps = 14;
+constexpr int kMaxMaps = 14;   // dOut views of the weight-gradient kernel (one per ConvTranspose residue)
+constexpr int kMaxMapsA = 24;  // A views of the conv kernel: hi and lo per ConvTranspose residue (stride <= 12)
 constexpr int kMaxTapList = 48;
 constexpr int kMaxPhases = 12;
 
@@ -47,10 +48,15 @@ struct Epi {
   float slope;              // lrelu slope (activation and mask)
   int accumulate;           // out_f32 += result
   int act_kind;             // 0 lrelu, 1 snake
+  // fp32 precision: bf16 lo companions (value = hi + lo, ~2^-17 relative) of the bf16 tensors above
+  bf16* out_bf16_lo;        // of out_bf16 (the next input-gradient GEMM's A operand pair)
+  bf16* act_bflo;           // of act_bf (the weight gradient's activation operand pair)
+  bf16* pre_lo;             // of pre_hi (Snake pre-activation)
+  const bf16* mask_lo;      // of mask_src (the Snake derivative from the pair; LeakyReLU needs the sign only)
 };
 
 struct TcMaps {
-  CUtensorMap a[kMaxMaps];  // A operand maps; lo maps at a[lo_base + i]
+  CUtensorMap a[kMaxMapsA];  // A operand maps; lo maps at a[lo_base + i]
   CUtensorMap w_hi;
   CUtensorMap w_lo;
 };

@@ -140,14 +140,16 @@ enum : uint32_t {
   kEpiRes = 4u,      // fp32 residual
   kEpiColsum = 8u,   // column-sum partials of the result (bias gradient)
   kEpiAct = 16u,     // activation output: operand pair (fp16 hi + lo * 2^11, or bf16 hi + lo) + bf16 copy
+  kEpiLo = 32u,      // fp32 precision: bf16 lo companions of the bf16 outputs and of the Snake mask source
   kEpiGeneric = 1u << 31,
 };
 
 // The feature set of an epilogue, as the kernels' template argument expects it.
 inline uint32_t epi_features(const Epi& e) {
   const bool snake = e.act_kind == 1 && (e.mask_src || e.act_hi);
+  const bool lo = e.out_bf16_lo || e.act_bflo || e.pre_lo || e.mask_lo;
   return (e.mask_src ? kEpiMask : 0u) | (snake ? kEpiSnake : 0u) | (e.res ? kEpiRes : 0u) |
-         (e.colsum ? kEpiColsum : 0u) | (e.act_hi ? kEpiAct : 0u);
+         (e.colsum ? kEpiColsum : 0u) | (e.act_hi ? kEpiAct : 0u) | (lo ? kEpiLo : 0u);
 }
 
 #define WB_EPI_HAS(bit, runtime) ((F & kEpiGeneric) ? (runtime) : ((F & (bit)) != 0))
@@ -156,6 +158,7 @@ inline uint32_t epi_features(const Epi& e) {
 // accumulator is ready) so their memory latency overlaps the wait.
 struct EpiIn {
   uint4 m[4];   // mask source (bf16)
+  uint4 ml[4];  // its lo companion (fp32-precision Snake masks)
   float4 r[8];  // residual
 };
 
@@ -165,6 +168,11 @@ WB_DEV void epi_load_mask(const Epi& e, bool valid, size_t off, EpiIn& in) {
     const uint4* q = reinterpret_cast<const uint4*>(e.mask_src + off);
 #pragma unroll
     for (int i = 0; i < 4; ++i) in.m[i] = __ldcs(q + i);
+    if (WB_EPI_HAS(kEpiLo, e.mask_lo != nullptr) && e.mask_lo) {
+      const uint4* ql = reinterpret_cast<const uint4*>(e.mask_lo + off);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) in.ml[i] = __ldcs(ql + i);
+    }
   }
 }
 
@@ -212,6 +220,17 @@ WB_DEV void epi_finish(const Epi& e, float* v, EpiIn& in, bool valid, size_t off
       for (int j = 0; j < 4; ++j) {
         x[8 * i + 2 * j] = valid ? bf16lo_f(w[j]) : 0.f;
         x[8 * i + 2 * j + 1] = valid ? bf16hi_f(w[j]) : 0.f;
+      }
+    }
+    if (WB_EPI_HAS(kEpiLo, e.mask_lo != nullptr) && e.mask_lo && valid) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t w[4] = {in.ml[i].x, in.ml[i].y, in.ml[i].z, in.ml[i].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          x[8 * i + 2 * j] += bf16lo_f(w[j]);
+          x[8 * i + 2 * j + 1] += bf16hi_f(w[j]);
+        }
       }
     }
     if (next) epi_load_mask<F>(e, valid, next_off, in);
@@ -289,12 +308,20 @@ WB_DEV void epi_finish(const Epi& e, float* v, EpiIn& in, bool valid, size_t off
       for (int i = 0; i < 16; ++i) b[i] = pack_bf16(v[2 * i], v[2 * i + 1]);
       if (e.out_bf16) out_bf16x32(o, e.out_bf16, off, b);
       if (e.pre_hi) out_bf16x32(o, e.pre_hi, off, b);
+      if (WB_EPI_HAS(kEpiLo, e.out_bf16_lo || e.pre_lo) && (e.out_bf16_lo || e.pre_lo)) {
+        // lo companions: v - bf16(v), exact in fp32, rounded to bf16
+#pragma unroll
+        for (int i = 0; i < 16; ++i) b[i] = pack_bf16(v[2 * i] - bf16lo_f(b[i]), v[2 * i + 1] - bf16hi_f(b[i]));
+        if (e.out_bf16_lo) out_bf16x32(o, e.out_bf16_lo, off, b);
+        if (e.pre_lo) out_bf16x32(o, e.pre_lo, off, b);
+      }
     }
     if (has_act) {
       // the activation as the next forward GEMM's operand pair (fp16 hi, fp16 lo * 2^11; or the
       // bf16 pair of the fallback format) and as a bf16 copy (the weight gradient's operand and the
       // LeakyReLU mask source)
-      uint32_t h[16], l[16], bw[16];
+      uint32_t h[16], l[16], bw[16], bl[16];
+      const bool has_bflo = WB_EPI_HAS(kEpiLo, e.act_bflo != nullptr) && e.act_bflo;
       bool big = false;
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
@@ -307,6 +334,7 @@ WB_DEV void epi_finish(const Epi& e, float* v, EpiIn& in, bool valid, size_t off
           a1 = lrelu(v[2 * i + 1], e.slope);
         }
         bw[i] = pack_bf16(a0, a1);
+        if (has_bflo) bl[i] = pack_bf16(a0 - bf16lo_f(bw[i]), a1 - bf16hi_f(bw[i]));
         if (e.act_bf16pair) {
           h[i] = bw[i];
           l[i] = pack_bf16(a0 - bf16lo_f(h[i]), a1 - bf16hi_f(h[i]));
@@ -320,6 +348,7 @@ WB_DEV void epi_finish(const Epi& e, float* v, EpiIn& in, bool valid, size_t off
       out_bf16x32(o, reinterpret_cast<bf16*>(e.act_hi), off, h);
       if (e.act_lo) out_bf16x32(o, reinterpret_cast<bf16*>(e.act_lo), off, l);
       if (e.act_bf) out_bf16x32(o, e.act_bf, off, bw);
+      if (has_bflo) out_bf16x32(o, e.act_bflo, off, bl);
     }
   }
   if (has_cs) {  // every lane reaches the group's named barriers; v is consumed here
