@@ -54,7 +54,7 @@ def parse():
                          "median-filtered over 5 frames) on one GPU: prints its own JSON line and exits")
     ap.add_argument("--kernel", default=None, metavar="WHICH,STAGE",
                     help="time one convolution of the step alone (kernel_bench: which 0 f1, 1 d1, 2 g1, 3 f2, "
-                         "4 d2) inside an NVTX range 'kb<which><stage>' and exit")
+                         "4 d2, 5 ups forward, 6 ups input gradient, 7 ups weight gradient, 8 conv_pre, 9 g2) inside an NVTX range 'kb<which><stage>' and exit")
     return ap.parse_args()
 
 

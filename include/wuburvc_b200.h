@@ -237,9 +237,12 @@ int wubu_b200_gen_graph_kernels(WubuB200Gen* gen);
 
 /* Times `iters` back-to-back launches of one convolution of the step with CUDA events on the
  * model stream.  which: 0 = forward conv1 of the first dilation pair of the largest-k stack of
- * stage `stage` (bf16x3), 1 = its input-gradient conv, 2 = its weight gradient, 3 = the pair's
- * forward conv2 (residual epilogue), 4 = conv2's input-gradient conv.  Returns the mean launch time (ms) and
- * the algorithmic FLOPs of one launch (2*MACs of the convolution, not counting split terms). */
+ * stage `stage` (fp16 operand pairs), 1 = its input-gradient conv, 2 = its weight gradient, 3 = the
+ * pair's forward conv2 (residual epilogue), 4 = conv2's input-gradient conv, 5 = the stage's
+ * ConvTranspose forward, 6 = its input gradient, 7 = its weight gradient, 8 = conv_pre's forward
+ * (stage ignored), 9 = conv2's weight gradient.  Under fp32 precision a weight gradient times its
+ * first launch (one of three).  Returns the mean launch time (ms) and the algorithmic FLOPs of one
+ * launch (2*MACs of the convolution, not counting split terms). */
 int wubu_b200_gen_kernel_bench(WubuB200Gen* gen, int which, int stage, int iters, float* ms_per_launch,
                                double* flops_per_launch);
 

@@ -343,7 +343,7 @@ int wubu_b200_gen_graph_kernels(WubuB200Gen* gen) {
 
 int wubu_b200_gen_kernel_bench(WubuB200Gen* gen, int which, int stage, int iters, float* ms_per_launch,
                                double* flops_per_launch) {
-  if (!gen || stage < 0 || stage > 3 || iters < 1 || which < 0 || which > 4) return WUBU_B200_ERR_ARG;
+  if (!gen || stage < 0 || stage > 3 || iters < 1 || which < 0 || which > 9) return WUBU_B200_ERR_ARG;
   Gen& m = gen->m;
   cudaSetDevice(m.opt.device);
   StageBufs& s = m.sg[stage];
@@ -351,13 +351,25 @@ int wubu_b200_gen_kernel_bench(WubuB200Gen* gen, int which, int stage, int iters
   for (int q = 1; q < m.nk; ++q)
     if (m.cfg.resblock_kernels[q] > m.cfg.resblock_kernels[j]) j = q;
   StackBufs& k = s.st[j];
-  const double flops = 2.0 * s.rows * (double)s.C * s.C * m.cfg.resblock_kernels[j];
+  // algorithmic FLOPs: resblock convs 2 rows C^2 k; ConvTranspose 2 rows_out C Cin k/s (each output
+  // sample meets k/s taps); conv_pre 2 B F C0 C_in 7
+  double flops = 2.0 * s.rows * (double)s.C * s.C * m.cfg.resblock_kernels[j];
+  if (which >= 5 && which <= 7) flops = 2.0 * s.rows * (double)s.C * s.Cin * s.ku / s.su;
+  if (which == 8) flops = 2.0 * m.B * m.F * (double)m.cfg.initial_channel * m.cfg.in_channels * 7;
+  if (which == 9) flops = 2.0 * s.rows * (double)s.C * s.C * m.cfg.resblock_kernels[j];
   auto launch = [&]() -> bool {
-    if (which == 0) return k.f1[0].run(m.stream) == cudaSuccess;
-    if (which == 1) return k.d1[0].run(m.stream) == cudaSuccess;
-    if (which == 3) return k.f2[0].run(m.stream) == cudaSuccess;
-    if (which == 4) return k.d2[0].run(m.stream) == cudaSuccess;
-    return k.g1[0].L.run(m.stream) == cudaSuccess;
+    switch (which) {
+      case 0: return k.f1[0].run(m.stream) == cudaSuccess;
+      case 1: return k.d1[0].run(m.stream) == cudaSuccess;
+      case 2: return k.g1[0].L.run(m.stream) == cudaSuccess;
+      case 3: return k.f2[0].run(m.stream) == cudaSuccess;
+      case 4: return k.d2[0].run(m.stream) == cudaSuccess;
+      case 5: return s.up_fwd.run(m.stream) == cudaSuccess;
+      case 6: return s.up_dg.run(m.stream) == cudaSuccess;
+      case 7: return s.up_wg.L.run(m.stream) == cudaSuccess;
+      case 8: return m.pre_fwd.run(m.stream) == cudaSuccess;
+      default: return k.g2[0].L.run(m.stream) == cudaSuccess;
+    }
   };
   for (int i = 0; i < 2; ++i)
     if (!launch()) return WUBU_B200_ERR_CUDA;

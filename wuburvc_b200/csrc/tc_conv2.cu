@@ -61,7 +61,9 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < AS; ++s) { mbar_init(&a_full[s], 1); mbar_init(&a_empty[s], 1); }
     for (int s = 0; s < WS; ++s) { mbar_init(&w_full[s], 1); mbar_init(&w_empty[s], 1); }
-    for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], 1); }
+    // an accumulator is free again once every epilogue group that reads it has arrived (see below)
+    const uint32_t acc_readers = N >= 64 ? 2u : 1u;
+    for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], acc_readers); }
     mbar_init(mma_done, 1);
     fence_barrier_init();
   }
@@ -233,8 +235,10 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
     umma_commit_warp(mma_done);
     mbar_wait_warp(mma_done, 0, p.err, ERR_WAIT_ACC, p.wait_ns);
   } else {
-    // ---------------- epilogue: two groups of 4 warps; group g drains TMEM accumulator g, i.e. every
-    // other tile, so two tiles' epilogues run concurrently (warp w reads TMEM lane quadrant w%4) ----------------
+    // ---------------- epilogue: two groups of 4 warps (warp w reads TMEM lane quadrant w%4).  With
+    // N >= 64 both groups drain every tile, group g the column half g, so a tile's epilogue takes half
+    // the time and the last one (which no MMA work hides) ends sooner; with N = 32 (one 32-column
+    // chunk) group g drains every other tile, so two tiles' epilogues run concurrently ----------------
     griddep_wait();  // the epilogue inputs and outputs belong to the previous kernels' data
     const int qw = warp & 3, grp = warp >> 2;
     const Epi& e = p.epi;
@@ -242,10 +246,13 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
     const float* bias = e.bias ? s_bias : nullptr;
     const float* aal = e.act_alpha ? s_aalpha : nullptr;
     const float* mal = e.mask_alpha ? s_malpha : nullptr;
-    int t_it = grp;
+    const bool halves = N >= 64;
+    const int c_beg = halves ? grp * (N / 2) : 0, c_end = halves ? c_beg + N / 2 : N;
+    int t_it = halves ? 0 : grp;
     bool ok = true;
-    for (int tile = blockIdx.x + grp * gridDim.x; tile < p.ntiles; tile += 2 * gridDim.x, t_it += 2) {
-      const int buf = grp;
+    for (int tile = blockIdx.x + (halves ? 0 : grp * (int)gridDim.x); tile < p.ntiles;
+         tile += (halves ? 1 : 2) * gridDim.x, t_it += halves ? 1 : 2) {
+      const int buf = t_it & 1;
       const int mtile = tile / p.n_tiles;
       const int item = mtile / p.tiles_per_item;
       const int q = (mtile - item * p.tiles_per_item) * 128 + qw * 32 + lane;
@@ -255,17 +262,17 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
       const int wrow0 = (mtile - item * p.tiles_per_item) * 128 + qw * 32;  // warp's first output row
       RowOut o;
       o.stage = s_stage[warp];
-      o.off0 = ((size_t)item * p.t_rows + wrow0) * p.n_total + n0;
+      o.off0 = ((size_t)item * p.t_rows + wrow0) * p.n_total + n0 + c_beg;
       o.pitch = (size_t)p.n_total;
       o.rows_valid = ok ? max(0, min(32, p.t_rows - wrow0)) : 0;
       o.lane = lane;
       // the first chunk's inputs are in flight while the accumulator is still being computed
       EpiIn in;
-      epi_load<F>(e, valid, row_off, in);
+      epi_load<F>(e, valid, row_off + c_beg, in);
       if (ok) ok = mbar_wait_warp(&acc_full[buf], (t_it >> 1) & 1, p.err, ERR_WAIT_ACC, p.wait_ns);
       tc_fence_after();
 #pragma unroll 1
-      for (int c0 = 0; c0 < N; c0 += 32) {
+      for (int c0 = c_beg; c0 < c_end; c0 += 32) {
         float v[32];
         if (ok) {
           const uint32_t ta = tmem + (uint32_t)(buf * N * nA) + ((uint32_t)(qw * 32) << 16) + (uint32_t)c0;
@@ -284,7 +291,7 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
         float cs = 0.f, ap = 0.f;
         epi_finish<F>(e, v, in, valid && ok, row_off + c0, 0, ra ? ra + c0 : nullptr, bias ? bias + c0 : nullptr,
                    aal ? aal + c0 : nullptr, mal ? mal + c0 : nullptr, qw, lane, red[grp], &cs, &ap, 1 + grp, true,
-                   o, c0 + 32 < N, row_off + c0 + 32);
+                   o, c0 + 32 < c_end, row_off + c0 + 32);
         o.off0 += 32;
         if (qw == 0) {  // column sums accumulate over the group's tiles (warp 0 holds this tile's)
           s_csum[grp][c0 + lane] += cs;
@@ -296,7 +303,8 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
       if (qw == 0 && lane == 0) mbar_arrive(&acc_empty[buf]);
     }
     if (qw == 0) {
-      // one partial row per group (2 per CTA): its sums in this CTA's N tile, zeros elsewhere
+      // one partial row per group (2 per CTA): its sums in this CTA's N tile (its column half, or
+      // every column of its tiles), zeros elsewhere
       const size_t prow = (size_t)(2 * blockIdx.x + grp) * p.n_total;
       for (int c = 0; c < p.n_total; c += 32) {
         const int rel = c - n0;
