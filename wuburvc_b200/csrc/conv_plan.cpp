@@ -373,7 +373,8 @@ static bool finish_wgrad(WgradLaunch& L, int B, int T_rows, int C_in, int C_out,
   p.total_kblocks = B * p.kblocks_per_item;
   const int n_ntiles = C_in / n_tile;
   const int base = p.n_mtiles * n_ntiles;
-  int splits = std::max(1, std::min(p.total_kblocks, (target_ctas + base - 1) / base));
+  // at most target_ctas CTAs (whole waves; rounding up would start a nearly empty extra wave)
+  int splits = std::max(1, std::min(p.total_kblocks, target_ctas / base));
   p.kb_per_split = (p.total_kblocks + splits - 1) / splits;
   splits = (p.total_kblocks + p.kb_per_split - 1) / p.kb_per_split;
   // stages of kb_group 64-row blocks: about three stages, each as many blocks as fit
@@ -458,7 +459,9 @@ static bool plan_wgrad_halo(WgradLaunch& L, const ConvGeom& g, const void* dy, c
   const int tap_groups = (g.k + tg - 1) / tg;
   const int n_ntiles = g.C_in / n_tile;
   const int base = tap_groups * p.oc_chunks * n_ntiles;
-  int splits = std::max(1, std::min(p.total_kblocks, (target_ctas + base - 1) / base));
+  // at most target_ctas CTAs: the kernel holds one CTA per SM at 128+ channels, so a grid just above
+  // the SM count (6 x 25 = 150) would run a second wave of two CTAs
+  int splits = std::max(1, std::min(p.total_kblocks, target_ctas / base));
   p.kb_per_split = (p.total_kblocks + splits - 1) / splits;
   splits = (p.total_kblocks + p.kb_per_split - 1) / p.kb_per_split;
   const size_t a_bytes = (size_t)(pack == 1 ? 128 : g.C_out) * R * 2;
