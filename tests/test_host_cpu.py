@@ -122,3 +122,24 @@ def test_primitives_reject_bad_arguments_before_touching_the_device():
     assert h.wubu_b200_convT(p, p, p, None, None, p, 1, 64, 8, 32, 4, 2, 1, 1, None) == -1
     assert h.wubu_b200_convT_dgrad(p, p, p, 1, 64, 8, 32, 0, 2, 1, None) == -1
     assert h.wubu_b200_convT_wgrad(p, None, p, 1, 64, 8, 32, 4, 2, 1, None) == -1
+
+
+def test_precision_option_is_checked_before_any_device_call():
+    """The options struct carries the precision enum at the end (the header's layout), and both the
+    Python constructor and wubu_b200_gen_create refuse an unknown value without touching a device."""
+    import ctypes
+
+    import pytest
+
+    from wuburvc_b200 import PRECISIONS, GenConfig, Generator, L, TrainOptions
+
+    assert PRECISIONS == {"bf16": 0, "fp32": 1}
+    assert [f[0] for f in TrainOptions._fields_][-1] == "precision"
+    hdr = open(os.path.join(ROOT, "include", "wuburvc_b200.h")).read()
+    assert "WUBU_B200_PRECISION_BF16 = 0" in hdr and "WUBU_B200_PRECISION_FP32 = 1" in hdr
+    with pytest.raises(ValueError):
+        Generator(model.config("40k"), 1, 4, precision="tf32")
+    c = GenConfig.from_dict(model.config("40k"))
+    o = TrainOptions()
+    o.batch, o.frames, o.precision = 1, 4, 7
+    assert not L().wubu_b200_gen_create(ctypes.byref(c), ctypes.byref(o))
