@@ -42,8 +42,10 @@ int pow2_cols(int n) {
 
 constexpr size_t kSmemBudget = 220 * 1024;
 // the persistent conv keeps ~24 KB of static shared memory (epilogue vectors, column sums, the
-// epilogue warps' store staging)
-constexpr size_t kSmemBudget2 = 202 * 1024;  // dynamic <= budget - 512, plus 24 KB static <= 227 KB
+// epilogue warps' store staging).  Its dynamic budget leaves ~7 KB of the SM's 228 KB free: one
+// block of the side stream's reductions (4 KB + the 1 KB per-block reserve) then runs beside it
+// instead of waiting for an SM between launches (measured 1.6 % faster on the step than 202 KB).
+constexpr size_t kSmemBudget2 = 196 * 1024;
 
 }  // namespace
 

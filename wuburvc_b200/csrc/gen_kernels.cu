@@ -193,7 +193,7 @@ __global__ void __launch_bounds__(256) prep_tile_kernel(const PrepDesc* __restri
         big |= !d.fmt_bf16 && !(fabsf(w) < kF16Max);
         const bf16 wb16 = __float2bfloat16_rn(w);
         ht[lane * QS + e][pl] = __bfloat16_as_ushort(wb16);
-        lt[lane * QS + e][pl] = __bfloat16_as_ushort(__float2bfloat16_rn(w - __bfloat162float(wb16)));
+        if (d.dg_lo) lt[lane * QS + e][pl] = __bfloat16_as_ushort(__float2bfloat16_rn(w - __bfloat162float(wb16)));
       }
     }
     if (big && d.range_err) atomicCAS(d.range_err, 0, ERR_RANGE);
