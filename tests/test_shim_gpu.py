@@ -55,8 +55,8 @@ def rel(a, b):
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-300))
 
 
-def library_grads(cfg, P, mel, dldy):
-    gen = Generator(cfg, 1, mel.shape[1])
+def library_grads(cfg, P, mel, dldy, precision="bf16"):
+    gen = Generator(cfg, 1, mel.shape[1], precision=precision)
     gen.set_params(flatten(cfg, P))
     gen.upload(mel[None], dldy=dldy[None])
     audio = gen.forward()[0]
@@ -67,14 +67,20 @@ def library_grads(cfg, P, mel, dldy):
 
 
 @needs_shim
-def test_forward_and_backward_through_the_shim_equal_the_library():
+@pytest.mark.parametrize("precision", ["bf16", "fp32"])
+def test_forward_and_backward_through_the_shim_equal_the_library(precision, monkeypatch):
+    """Also in the fp32 mode, which the shim takes from WUBU_B200_PRECISION."""
+    if precision == "fp32":
+        monkeypatch.setenv("WUBU_B200_PRECISION", "fp32")
+    else:
+        monkeypatch.delenv("WUBU_B200_PRECISION", raising=False)
     cfg = model.decoder_only("40k")
     F = 8
     T = F * model.hop(cfg)
     P = G.init_params_ref(cfg, 7)
     mel = G.counter_normal(21, 1, 192 * F).reshape(192, F).astype(np.float32)
     dldy = G.counter_normal(21, 2, T).astype(np.float32)
-    want_audio, want = library_grads(cfg, P, mel, dldy)
+    want_audio, want = library_grads(cfg, P, mel, dldy, precision)
     ref = ref_oracle.RefTrainer(P, cfg["upsample_rates"], cfg["upsample_kernels"])
     R = ref_oracle.lib()
     s = shim_lib()

@@ -18,6 +18,8 @@
  *     reference makes at src/wubu_train_cuda.cu:861), sets model->last_loss / last_epoch, and
  *     returns 1 if the loss is below 0.1, 0 otherwise, -1 on error;
  *   - -1 and a message on stderr for every failure, NULL arguments included.
+ * WUBU_B200_PRECISION=fp32 in the environment runs the library's fp32 mode (the reference's entry
+ * points have no dtype argument).
  * The spectral gradient runs on the GPU (wubu_b200_stft_loss_grad_host, the same loss and gradient
  * as the reference's wubu_stft_loss_grad).  One generator context per TrainCacheCuda (the step keeps
  * its own, re-created when the frame count changes).  Not thread-safe, like the reference, except
@@ -43,6 +45,7 @@ struct TrainCacheCuda {
   float *zeros;      /* zero source noise (inference without noise injection) */
   int n_out;
   int have_forward;
+  int precision;                   /* WUBU_B200_PRECISION_* of the context */
   const WuBuRVCModel *model;       /* inference cache: the model whose weights are on the device ... */
   unsigned long long fingerprint;  /* ... and a fingerprint of them */
 };
@@ -158,8 +161,17 @@ static int gather_params(TrainCacheCuda *c, const WuBuRVCModel *m, int copy, uns
 }
 
 /* (re)creates the cache's generator for this config and frame count */
+/* The reference's entry points carry no arithmetic type: WUBU_B200_PRECISION=fp32 selects the
+ * library's fp32 mode (bf16 hi + lo backward operands), anything else the default bf16 mode. */
+static int shim_precision(void) {
+  const char *p = getenv("WUBU_B200_PRECISION");
+  return (p && strcmp(p, "fp32") == 0) ? WUBU_B200_PRECISION_FP32 : WUBU_B200_PRECISION_BF16;
+}
+
 static int ensure_gen(TrainCacheCuda *c, const WubuB200GenConfig *cfg, int frames) {
-  if (c->gen && c->frames == frames && memcmp(&c->cfg, cfg, sizeof *cfg) == 0) return 0;
+  const int precision = shim_precision();
+  if (c->gen && c->frames == frames && c->precision == precision && memcmp(&c->cfg, cfg, sizeof *cfg) == 0)
+    return 0;
   wubu_b200_gen_destroy(c->gen);
   free(c->flat);
   free(c->audio);
@@ -177,6 +189,7 @@ static int ensure_gen(TrainCacheCuda *c, const WubuB200GenConfig *cfg, int frame
   o.beta1 = 0.9f;
   o.beta2 = 0.999f;
   o.eps = 1e-8f;
+  o.precision = precision;
   c->gen = wubu_b200_gen_create(cfg, &o);
   if (!c->gen) return fail("wubu_b200_gen_create failed (no sm_100 GPU, unsupported shape or out of memory)");
   c->cfg = *cfg;
@@ -191,6 +204,7 @@ static int ensure_gen(TrainCacheCuda *c, const WubuB200GenConfig *cfg, int frame
   }
   c->n_out = T;
   c->frames = frames;
+  c->precision = precision;
   return 0;
 }
 
