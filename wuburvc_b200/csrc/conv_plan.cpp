@@ -46,6 +46,7 @@ constexpr size_t kSmemBudget = 220 * 1024;
 // block of the side stream's reductions (4 KB + the 1 KB per-block reserve) then runs beside it
 // instead of waiting for an SM between launches (measured 1.6 % faster on the step than 202 KB).
 constexpr size_t kSmemBudget2 = 196 * 1024;
+constexpr int kMaxHaloStages = 6;  // halo ring depth of the persistent conv (barriers: 512 B reserved)
 
 }  // namespace
 
@@ -219,7 +220,19 @@ bool plan_conv2(Conv2Launch& L, const ConvGeom& g, const void* x_hi, const void*
   }
   if (best.score < 0) return false;
   const int kc = best.kc;
-  p.a_stages = 2;
+  // 32 input channels: every tile is one halo load and little MMA work, so resident weights leave
+  // the rest of the budget to a deeper halo ring that keeps the MMAs from waiting on TMA latency
+  // (measured faster at 32 channels; at 64 the deeper ring costs the input gradients more than it
+  // gives, as it leaves the side stream's reductions no room on the SM)
+  int a_stages = 2;
+  if (best.resident && g.C_in <= 32) {
+    const size_t a_stage = (size_t)nA * best.a_sub;
+    while (a_stages < kMaxHaloStages && best.smem + a_stage <= kSmemBudget2 - 512) {
+      best.smem += a_stage;
+      ++a_stages;
+    }
+  }
+  p.a_stages = a_stages;
   p.w_resident = best.resident;
   p.w_group = best.G;
   p.w_stages = best.WS;
