@@ -201,6 +201,7 @@ def run_infer(args):
     cfg = model.config(args.config)
     B, F = 1, (args.frames if args.frames != 32 else 6000)
     gen = Generator(cfg, B, F, device=0)
+    gen.set_forward_only(True)  # inference: nothing the backward would read is written
     z, f0, g, _ = make_inputs(cfg, B, F, seed=4321)
     # f0 smoothed with a 5-frame median filter (voiced frames only), 20 % unvoiced
     pad = np.pad(f0, ((0, 0), (2, 2)), mode="edge")

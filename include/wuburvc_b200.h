@@ -211,6 +211,12 @@ int wubu_b200_gen_samples(const WubuB200Gen* gen); /* output samples per item */
 int wubu_b200_gen_upload(WubuB200Gen* gen, const float* z, const float* f0, const float* g, const float* noise,
                          const float* dldy);
 int wubu_b200_gen_forward(WubuB200Gen* gen, unsigned long long noise_stream, float* audio_out);
+/* Forward-only (inference) mode, on = 1 / off = 0: the forward stops writing the tensors that only
+ * the backward reads (the activations' bf16 copies, Snake pre-activations, z's bf16 copy and the
+ * input-gradient weight layout); the waveform is bit-identical.  While it is on, backward, AdamW and
+ * the training steps return WUBU_B200_ERR_ARG.  The reference's CUDA inference
+ * (wubu_generator_nsf_cuda, src/wubu_rvc_cuda.cu:280) runs in this mode. */
+int wubu_b200_gen_set_forward_only(WubuB200Gen* gen, int on);
 int wubu_b200_gen_backward(WubuB200Gen* gen);
 int wubu_b200_gen_adamw(WubuB200Gen* gen);
 /* One full step (upload unless RESIDENT, forward, backward, gradient all-reduce when a

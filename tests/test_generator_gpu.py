@@ -238,3 +238,38 @@ def test_operand_beyond_fp16_range_falls_back_to_bf16_pairs():
     c.sync()
     assert np.array_equal(c.get_params(), pa)
     c.close()
+
+
+@pytest.mark.parametrize("tag", ["40k", "48k_snake"])
+def test_forward_only_mode_gives_the_same_waveform_and_refuses_training(tag):
+    """Inference mode skips the backward-only tensors: the waveform is bit-identical, backward and
+    the training steps are refused while it is on, and after it is switched off a step equals a
+    fresh context's step."""
+    cfg = model.config(tag)
+    B, F = 2, 8
+    T = F * model.hop(cfg)
+    P = flatten(cfg, G.init_params_ref(cfg, 9))
+    z = G.counter_normal(12, 1, B * 192 * F).reshape(B, 192, F).astype(np.float32)
+    g = G.counter_normal(12, 2, B * 256).reshape(B, 256).astype(np.float32)
+    f0 = np.full((B, F), 180.0, np.float32)
+    dldy = G.counter_normal(12, 3, B * T).reshape(B, T).astype(np.float32)
+    ref = Generator(cfg, B, F)
+    ref.set_params(P)
+    ref.upload(z, f0, g, None, dldy)
+    want = ref.forward(noise_stream=4)
+    ref.train_step(z, f0, g, None, dldy, noise_stream=5)
+    want_params = ref.get_params()
+    ref.close()
+    gen = Generator(cfg, B, F)
+    gen.set_params(P)
+    gen.set_forward_only(True)
+    gen.upload(z, f0, g, None, dldy)
+    assert np.array_equal(gen.forward(noise_stream=4), want)
+    with pytest.raises(RuntimeError):
+        gen.backward()
+    with pytest.raises(RuntimeError):
+        gen.train_step(z, f0, g, None, dldy, noise_stream=5)
+    gen.set_forward_only(False)
+    gen.train_step(z, f0, g, None, dldy, noise_stream=5)
+    assert np.array_equal(gen.get_params(), want_params)
+    gen.close()

@@ -108,6 +108,7 @@ _SIGS = {
     "wubu_b200_gen_samples": (ctypes.c_int, [ctypes.c_void_p]),
     "wubu_b200_gen_upload": (ctypes.c_int, [ctypes.c_void_p] * 6),
     "wubu_b200_gen_forward": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_ulonglong, ctypes.c_void_p]),
+    "wubu_b200_gen_set_forward_only": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
     "wubu_b200_gen_backward": (ctypes.c_int, [ctypes.c_void_p]),
     "wubu_b200_gen_adamw": (ctypes.c_int, [ctypes.c_void_p]),
     "wubu_b200_gen_train_step": (ctypes.c_int, [ctypes.c_void_p] * 7 + [ctypes.c_ulonglong, ctypes.c_int]),
@@ -312,6 +313,11 @@ class Generator:
         out = np.empty((self.B, self.T), dtype=np.float32)
         check(L().wubu_b200_gen_forward(self.h, noise_stream, _ptr(out)), "forward")
         return out
+
+    def set_forward_only(self, on: bool = True):
+        """Inference mode: the forward skips what only the backward reads (same waveform); backward
+        and training steps raise while it is on."""
+        check(L().wubu_b200_gen_set_forward_only(self.h, 1 if on else 0), "set_forward_only")
 
     def backward(self):
         check(L().wubu_b200_gen_backward(self.h), "backward")

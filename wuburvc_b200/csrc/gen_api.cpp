@@ -12,6 +12,7 @@ bool gen_backward(Gen& m);
 bool gen_adamw(Gen& m, float grad_scale, int bump_noise);
 void gen_free(Gen& m);
 bool gen_set_operand_format(Gen& m, int bf16);
+bool gen_set_forward_only(Gen& m, int on);
 int comm_attach(Gen& m, int rank, int world, const void* id128);
 int comm_unique_id(void* out128);
 int comm_world(Gen& m);
@@ -283,15 +284,21 @@ int wubu_b200_gen_forward(WubuB200Gen* gen, unsigned long long noise_stream, flo
   }
 }
 
-int wubu_b200_gen_backward(WubuB200Gen* gen) {
+int wubu_b200_gen_set_forward_only(WubuB200Gen* gen, int on) {
   if (!gen) return WUBU_B200_ERR_ARG;
+  cudaSetDevice(gen->m.opt.device);
+  return gen_set_forward_only(gen->m, on) ? 0 : WUBU_B200_ERR_CUDA;
+}
+
+int wubu_b200_gen_backward(WubuB200Gen* gen) {
+  if (!gen || gen->m.forward_only) return WUBU_B200_ERR_ARG;
   cudaSetDevice(gen->m.opt.device);
   if (!gen_backward(gen->m)) return WUBU_B200_ERR_CUDA;
   return check_err(gen->m);
 }
 
 int wubu_b200_gen_adamw(WubuB200Gen* gen) {
-  if (!gen) return WUBU_B200_ERR_ARG;
+  if (!gen || gen->m.forward_only) return WUBU_B200_ERR_ARG;
   cudaSetDevice(gen->m.opt.device);
   if (!gen_adamw(gen->m, 1.f / (float)comm_world(gen->m), 0)) return WUBU_B200_ERR_CUDA;
   return check_err(gen->m);
@@ -299,7 +306,7 @@ int wubu_b200_gen_adamw(WubuB200Gen* gen) {
 
 int wubu_b200_gen_train_step(WubuB200Gen* gen, const float* z, const float* f0, const float* g, const float* noise,
                              const float* dldy, float* audio_out, unsigned long long noise_stream, int flags) {
-  if (!gen) return WUBU_B200_ERR_ARG;
+  if (!gen || gen->m.forward_only) return WUBU_B200_ERR_ARG;
   Gen& m = gen->m;
   cudaSetDevice(m.opt.device);
   if (!(flags & WUBU_B200_INPUTS_RESIDENT)) {
@@ -321,7 +328,7 @@ int wubu_b200_gen_train_step(WubuB200Gen* gen, const float* z, const float* f0, 
 }
 
 int wubu_b200_gen_train_step_async(WubuB200Gen* gen, unsigned long long noise_stream) {
-  if (!gen) return WUBU_B200_ERR_ARG;
+  if (!gen || gen->m.forward_only) return WUBU_B200_ERR_ARG;
   Gen& m = gen->m;
   cudaSetDevice(m.opt.device);
   if (set_noise_stream(m, noise_stream)) return WUBU_B200_ERR_CUDA;

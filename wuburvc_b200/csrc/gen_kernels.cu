@@ -216,6 +216,8 @@ __global__ void __launch_bounds__(256) prep_tile_kernel(const PrepDesc* __restri
   }
   __syncthreads();
   // transposed bf16: rows q0..q0+QW-1 of dg[td] ([Q][P]), 32 p each, 16 threads x 2 values per row
+  // (none in a forward-only context)
+  if (!d.dg) return;
   for (int r = tid >> 4; r < QW; r += 16) {
     const int pp = (tid & 15) * 2;
     const uint32_t w = (uint32_t)ht[r][pp] | ((uint32_t)ht[r][pp + 1] << 16);
@@ -377,7 +379,7 @@ __global__ void pack_z_kernel(const float* __restrict__ z, int B, int C, int F, 
   const float x = z[((size_t)b * C + c) * F + f];
   split_op(x, fmt_bf16, hi[i], lo[i]);
   const bf16 xb = __float2bfloat16_rn(x);
-  zb[i] = xb;
+  if (zb) zb[i] = xb;
   if (zb_lo) zb_lo[i] = __float2bfloat16_rn(x - __bfloat162float(xb));
   if (!fmt_bf16 && !(fabsf(x) < kF16Max) && range_err) atomicCAS(range_err, 0, ERR_RANGE);
 }

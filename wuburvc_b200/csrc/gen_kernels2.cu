@@ -108,7 +108,7 @@ __global__ void __launch_bounds__(256) noise_add_act_kernel(NoiseActArgs a) {
       a.act_hi[q][i] = hi;
       a.act_lo[q][i] = lo;
       const bf16 yb = __float2bfloat16_rn(y);
-      a.act_bf[q][i] = yb;
+      if (a.act_bf[q]) a.act_bf[q][i] = yb;
       if (a.act_bflo[q]) a.act_bflo[q][i] = __float2bfloat16_rn(y - __bfloat162float(yb));
       if (!a.fmt_bf16 && !(fabsf(y) < kF16Max) && a.range_err) atomicCAS(a.range_err, 0, ERR_RANGE);
     }

@@ -790,6 +790,7 @@ bool gen_setup(Gen& m) {
       nb += prep_norm_blocks(p);
       tb += prep_tile_blocks(p);
       d.push_back(p);
+      m.all_weights.push_back(&w);
       return true;
     };
     if (!add(m.wpre)) return false;
@@ -840,6 +841,46 @@ bool gen_set_operand_format(Gen& m, int bf16) {
   return true;
 }
 
+// Forward-only mode (see Gen::forward_only): the forward plans and the weight preparation stop (or
+// resume) writing the tensors only the backward reads.  The step graph is released.
+bool gen_set_forward_only(Gen& m, int on) {
+  m.forward_only = on ? 1 : 0;
+  auto act = [&](Epi& e, bf16* bf, bf16* bflo, bf16* pre, bf16* prelo) {
+    e.act_bf = on ? nullptr : bf;
+    e.act_bflo = on ? nullptr : bflo;
+    e.pre_hi = on ? nullptr : pre;
+    e.pre_lo = on ? nullptr : prelo;
+  };
+  auto both = [&](ConvOp& op, bf16* bf, bf16* bflo, bf16* pre, bf16* prelo) {
+    act(op.v1.p.epi, bf, bflo, pre, prelo);
+    act(op.c2.p.epi, bf, bflo, pre, prelo);
+  };
+  act(m.pre_fwd.p.epi, m.pre_bf, m.pre_bflo, m.pre_pre, m.pre_prelo);
+  for (int L = 0; L < 4; ++L) {
+    StageBufs& s = m.sg[L];
+    for (int j = 0; j < m.nk; ++j) {
+      StackBufs& k = s.st[j];
+      for (int cp = 0; cp < m.nd; ++cp) {
+        both(k.f1[cp], k.a2_bf[cp], k.a2_bflo[cp], k.a2_pre[cp], k.a2_prelo[cp]);
+        if (cp + 1 < m.nd)
+          both(k.f2[cp], k.a1_bf[cp + 1], k.a1_bflo[cp + 1], k.a1_pre[cp + 1], k.a1_prelo[cp + 1]);
+        else if (j == m.nk - 1)
+          both(k.f2[cp], s.sa_bf, s.sa_bflo, s.s_pre, s.s_prelo);
+      }
+    }
+  }
+  CK(cudaStreamSynchronize(m.stream));
+  if (m.prep_host.size() != m.all_weights.size()) return false;
+  for (size_t i = 0; i < m.prep_host.size(); ++i) {
+    m.prep_host[i].dg = on ? nullptr : m.all_weights[i]->dg;
+    m.prep_host[i].dg_lo = on ? nullptr : m.all_weights[i]->dg_lo;
+  }
+  CK(cudaMemcpy(m.prep_descs, m.prep_host.data(), m.prep_host.size() * sizeof(PrepDesc), cudaMemcpyHostToDevice));
+  if (m.graph) cudaGraphExecDestroy(m.graph);
+  m.graph = nullptr;
+  return true;
+}
+
 // =============================================================================================
 // forward
 // =============================================================================================
@@ -850,7 +891,8 @@ bool gen_forward(Gen& m) {
   set_reduce_scratch(m.red_scratch, m.red_scratch_n);
   // GEMM weights for this step (weight norm + bf16 hi/lo + transposed layouts)
   prep_weights(m.prep_descs, m.n_prep, m.prep_norm_blocks, m.prep_tile_blocks, st);
-  pack_z(m.z, m.B, c.in_channels, m.F, m.z_hi, m.z_lo, m.z_bf, m.z_bflo, m.err, m.op_bf16, st);
+  pack_z(m.z, m.B, c.in_channels, m.F, m.z_hi, m.z_lo, m.forward_only ? nullptr : m.z_bf,
+         m.forward_only ? nullptr : m.z_bflo, m.err, m.op_bf16, st);
   if (c.nsf) {
     NsfArgs a{};
     a.f0 = m.f0;
@@ -900,11 +942,11 @@ bool gen_forward(Gen& m) {
       na.alpha[q] = snake ? alpha_ptr(m, "dec.resblocks." + std::to_string(L * m.nk + q) + ".alpha1.0") : nullptr;
       na.act_hi[q] = s.xa_hi[q];
       na.act_lo[q] = s.xa_lo[q];
-      na.act_bf[q] = s.xa_bf[q];
-      na.act_bflo[q] = s.xa_bflo[q];
+      na.act_bf[q] = m.forward_only ? nullptr : s.xa_bf[q];
+      na.act_bflo[q] = m.forward_only ? nullptr : s.xa_bflo[q];
     }
-    na.pre = s.x_pre;
-    na.pre_lo = s.x_prelo;
+    na.pre = m.forward_only ? nullptr : s.x_pre;
+    na.pre_lo = m.forward_only ? nullptr : s.x_prelo;
     na.range_err = m.err;
     na.fmt_bf16 = m.op_bf16;
     noise_add_act(na, st);

@@ -153,11 +153,15 @@ struct Gen {
   StageBufs sg[4];
   PrepDesc* prep_descs = nullptr;  // device table: every GEMM weight's preparation
   std::vector<PrepDesc> prep_host; // host copy (re-uploaded when the operand format changes)
+  std::vector<const ConvWeights*> all_weights;  // the weights of prep_host, in its order
   // forward operand format: 0 = fp16 hi + fp16 lo*2^11 (fp32-accurate, |x| < 65504); 1 = bf16 hi +
   // bf16 lo (range-safe, ~2^-17), the format a context switches to for good after a range error
   int op_bf16 = 0;
   // backward GEMM operands as bf16 hi + lo pairs (opt.precision == WUBU_B200_PRECISION_FP32)
   int fp32 = 0;
+  // forward-only (inference): the forward skips what only the backward reads (bf16 activation copies,
+  // Snake pre-activations, z's bf16 copy, the input-gradient weight layout); no backward runs
+  int forward_only = 0;
   int n_prep = 0, prep_norm_blocks = 0, prep_tile_blocks = 0;
   float* red_scratch = nullptr;  // two-pass deterministic reductions
   size_t red_scratch_n = 0;

@@ -46,6 +46,7 @@ struct TrainCacheCuda {
   int n_out;
   int have_forward;
   int precision;                   /* WUBU_B200_PRECISION_* of the context */
+  int forward_only;                /* the context runs inference only (wubu_generator_nsf_cuda) */
   const WuBuRVCModel *model;       /* inference cache: the model whose weights are on the device ... */
   unsigned long long fingerprint;  /* ... and a fingerprint of them */
 };
@@ -180,6 +181,7 @@ static int ensure_gen(TrainCacheCuda *c, const WubuB200GenConfig *cfg, int frame
   c->flat = c->audio = c->zeros = NULL;
   c->frames = 0;
   c->have_forward = 0;
+  c->forward_only = 0;
   c->model = NULL;
   WubuB200TrainOptions o;
   memset(&o, 0, sizeof o);
@@ -369,6 +371,13 @@ int wubu_generator_nsf_cuda(WuBuRVCModel *model, const float *z, int nF, int int
     goto out;
   }
   if (ensure_gen(ctx, &cfg, nF) != 0) goto out;
+  if (!ctx->forward_only) {  /* inference: nothing the backward would read is written */
+    if (wubu_b200_gen_set_forward_only(ctx->gen, 1) != 0) {
+      fail("generator: forward-only mode failed");
+      goto out;
+    }
+    ctx->forward_only = 1;
+  }
   if (ctx->n_out > max_samples) {
     fail("generator: max_samples is smaller than the output");
     goto out;
