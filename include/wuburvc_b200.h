@@ -211,11 +211,15 @@ int wubu_b200_gen_samples(const WubuB200Gen* gen); /* output samples per item */
 int wubu_b200_gen_upload(WubuB200Gen* gen, const float* z, const float* f0, const float* g, const float* noise,
                          const float* dldy);
 int wubu_b200_gen_forward(WubuB200Gen* gen, unsigned long long noise_stream, float* audio_out);
-/* Forward-only (inference) mode, on = 1 / off = 0: the forward stops writing the tensors that only
- * the backward reads (the activations' bf16 copies, Snake pre-activations, z's bf16 copy and the
- * input-gradient weight layout); the waveform is bit-identical.  While it is on, backward, AdamW and
- * the training steps return WUBU_B200_ERR_ARG.  The reference's CUDA inference
- * (wubu_generator_nsf_cuda, src/wubu_rvc_cuda.cu:280) runs in this mode. */
+/* Forward-only (inference) mode.  on = 1: the forward stops writing the tensors that only the
+ * backward reads (the activations' bf16 copies, Snake pre-activations, z's bf16 copy and the
+ * input-gradient weight layout); the waveform is bit-identical to the training forward's.
+ * on = 2: in addition every forward GEMM takes single fp16 operands (one product per K step instead
+ * of the fp16 pair's three; forward rel-L2 about 4e-4 against fp64, inside the 2e-3 forward gate);
+ * after a range error the context returns to the exact pairs.  on = 0: training.  While on != 0,
+ * backward, AdamW and the training steps return WUBU_B200_ERR_ARG.  The reference's CUDA inference
+ * (wubu_generator_nsf_cuda, src/wubu_rvc_cuda.cu:280) runs in mode 1 (2 with
+ * WUBU_B200_INFERENCE=fast in the environment). */
 int wubu_b200_gen_set_forward_only(WubuB200Gen* gen, int on);
 int wubu_b200_gen_backward(WubuB200Gen* gen);
 int wubu_b200_gen_adamw(WubuB200Gen* gen);

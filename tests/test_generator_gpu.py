@@ -273,3 +273,33 @@ def test_forward_only_mode_gives_the_same_waveform_and_refuses_training(tag):
     gen.train_step(z, f0, g, None, dldy, noise_stream=5)
     assert np.array_equal(gen.get_params(), want_params)
     gen.close()
+
+
+@pytest.mark.parametrize("tag,B,F", [("40k", 2, 32), ("48k_snake", 1, 36), ("32k", 2, 40)])
+def test_fast_inference_forward_matches_oracle(tag, B, F):
+    """Fast inference (single fp16 GEMM operands, forward-only): the waveform within the 2e-3 forward
+    gate of the fp64 oracle (the exact pairs reach ~1e-6), and the exact forward-only mode unchanged."""
+    cfg = model.config(tag)
+    z, f0, g, dldy = nsf_inputs(cfg, B, F)
+    T = F * model.hop(cfg)
+    dim = cfg["harmonic_num"] + 1
+    stream = 9
+    noise = G.counter_normal(0, stream, B * T * dim).reshape(B, T, dim)
+    rand_ini = G.counter_rand_ini(0, stream, dim)
+    P = G.init_params_ref(cfg, 2)
+    gen = Generator(cfg, B, F, seed=0)
+    gen.set_params(flatten(cfg, P))
+    gen.upload(z, f0, g, noise.astype(np.float32), None)
+    gen.set_forward_only(True)
+    exact = gen.forward(noise_stream=stream)
+    gen.set_forward_only(True, fast=True)
+    fast = gen.forward(noise_stream=stream)
+    gen.set_forward_only(True)
+    again = gen.forward(noise_stream=stream)
+    gen.close()
+    a64, _ = G.train_grads(P, cfg, z, f0, g[:, :, None], noise, rand_ini, np.zeros((B, 1, T)))
+    e_fast, e_exact = rel(fast, a64[:, 0, :]), rel(exact, a64[:, 0, :])
+    print(f"\n[fast inference {tag}] forward rel-L2 fast {e_fast:.2e}, exact {e_exact:.2e}")
+    assert e_fast <= FWD_TOL
+    assert e_exact <= 1e-5
+    assert np.array_equal(again, exact)

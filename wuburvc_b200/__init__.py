@@ -314,10 +314,11 @@ class Generator:
         check(L().wubu_b200_gen_forward(self.h, noise_stream, _ptr(out)), "forward")
         return out
 
-    def set_forward_only(self, on: bool = True):
-        """Inference mode: the forward skips what only the backward reads (same waveform); backward
-        and training steps raise while it is on."""
-        check(L().wubu_b200_gen_set_forward_only(self.h, 1 if on else 0), "set_forward_only")
+    def set_forward_only(self, on: bool = True, fast: bool = False):
+        """Inference mode: the forward skips what only the backward reads (same waveform); with
+        fast, single fp16 GEMM operands (forward rel-L2 ~4e-4 against fp64).  Backward and training
+        steps raise while it is on."""
+        check(L().wubu_b200_gen_set_forward_only(self.h, (2 if fast else 1) if on else 0), "set_forward_only")
 
     def backward(self):
         check(L().wubu_b200_gen_backward(self.h), "backward")

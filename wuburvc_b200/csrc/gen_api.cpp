@@ -285,7 +285,7 @@ int wubu_b200_gen_forward(WubuB200Gen* gen, unsigned long long noise_stream, flo
 }
 
 int wubu_b200_gen_set_forward_only(WubuB200Gen* gen, int on) {
-  if (!gen) return WUBU_B200_ERR_ARG;
+  if (!gen || on < 0 || on > 2) return WUBU_B200_ERR_ARG;
   cudaSetDevice(gen->m.opt.device);
   return gen_set_forward_only(gen->m, on) ? 0 : WUBU_B200_ERR_CUDA;
 }

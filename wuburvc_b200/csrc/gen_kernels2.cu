@@ -467,7 +467,7 @@ __global__ void __launch_bounds__(256) post_forward_kernel(const f16* __restrict
       x[i] = 0.f;
       if (r >= 0 && r < T) {
         const size_t off = (base + r) * kPostC + lane;
-        x[i] = join_op(hi[off], lo[off], fmt_bf16);
+        x[i] = lo ? join_op(hi[off], lo[off], fmt_bf16) : __half2float(hi[off]);  // no lo: fast inference
       }
     }
     float v[32];

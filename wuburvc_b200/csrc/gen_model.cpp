@@ -814,6 +814,7 @@ bool gen_setup(Gen& m) {
 // released: the next step captures it again with the new format.
 bool gen_set_operand_format(Gen& m, int bf16) {
   m.op_bf16 = bf16 ? 1 : 0;
+  if (m.op_bf16) m.fast = 0;  // single fp16 operands have the same range limit: back to the pairs
   auto conv = [&](TcConvParams& p) {
     p.split_bf16 = m.op_bf16;
     p.epi.act_bf16pair = m.op_bf16;
@@ -841,8 +842,61 @@ bool gen_set_operand_format(Gen& m, int bf16) {
   return true;
 }
 
+namespace {
+// The fast-inference forward plans: the regular forward's epilogues (in their forward-only form) on
+// single fp16 operands, the operand's hi half alone (the lo half is neither read nor written).
+bool plan_fast(Gen& m) {
+  const WubuB200GenConfig& c = m.cfg;
+  const int B = m.B, C0 = c.initial_channel;
+  auto single = [](TcConvParams& p) { p.single_f16 = 1; };
+  {
+    Epi e = m.pre_fwd.p.epi;
+    e.act_lo = nullptr;
+    ConvGeom g{B, m.F, m.F, c.in_channels, C0, 7, 1, 3};
+    if (!plan_conv(m.pre_fast, g, m.z_hi, nullptr, m.wpre.fwd_hi, nullptr, 0, e, m.err)) return false;
+    single(m.pre_fast.p);
+    m.pre_fast.p.pdl = 1;
+  }
+  for (int L = 0; L < 4; ++L) {
+    StageBufs& s = m.sg[L];
+    const int Tin = (L == 0) ? m.F : m.sg[L - 1].T;
+    const f16* in_hi = (L == 0) ? m.pre_hi : m.sg[L - 1].sa_hi;
+    Epi eu = s.up_fwd.p.epi;
+    if (!plan_convT(s.up_fast, B, Tin, s.Cin, s.C, s.ku, s.su, s.pu, in_hi, nullptr, s.wu.fwd_hi, nullptr, 0, eu,
+                    m.err))
+      return false;
+    single(s.up_fast.p);
+    s.up_fast.p.pdl = 1;
+    for (int j = 0; j < m.nk; ++j) {
+      StackBufs& k = s.st[j];
+      const int kk = c.resblock_kernels[j];
+      for (int cp = 0; cp < m.nd; ++cp) {
+        const int dil = c.resblock_dilations[j][cp];
+        for (int which = 0; which < 2; ++which) {
+          ConvOp& src = which ? k.f2[cp] : k.f1[cp];
+          ConvOp& dst = which ? k.f2f[cp] : k.f1f[cp];
+          Epi e = src.v2 ? src.c2.p.epi : src.v1.p.epi;
+          e.act_lo = nullptr;
+          const ConvGeom g = which ? ConvGeom{B, s.T, s.T, s.C, s.C, kk, 1, (kk - 1) / 2}
+                                   : ConvGeom{B, s.T, s.T, s.C, s.C, kk, dil, dil * (kk - 1) / 2};
+          const f16* x = which ? k.a2_hi[cp] : k.a1_hi[cp];
+          const ConvWeights& w = which ? k.w2[cp] : k.w1[cp];
+          if (!plan_conv_any(dst, g, x, nullptr, w.fwd_hi, nullptr, 0, e, m.err)) return false;
+          single(dst.v1.p);
+          dst.c2.p.single_f16 = 1;
+          dst.set_pdl(true);
+        }
+      }
+    }
+  }
+  m.fast_planned = true;
+  return true;
+}
+}  // namespace
+
 // Forward-only mode (see Gen::forward_only): the forward plans and the weight preparation stop (or
-// resume) writing the tensors only the backward reads.  The step graph is released.
+// resume) writing the tensors only the backward reads; on = 2 also selects the fast-inference plans.
+// The step graph is released.
 bool gen_set_forward_only(Gen& m, int on) {
   m.forward_only = on ? 1 : 0;
   auto act = [&](Epi& e, bf16* bf, bf16* bflo, bf16* pre, bf16* prelo) {
@@ -878,6 +932,13 @@ bool gen_set_forward_only(Gen& m, int on) {
   CK(cudaMemcpy(m.prep_descs, m.prep_host.data(), m.prep_host.size() * sizeof(PrepDesc), cudaMemcpyHostToDevice));
   if (m.graph) cudaGraphExecDestroy(m.graph);
   m.graph = nullptr;
+  // the fast plans copy the forward-only epilogues above; a context whose operands fell back to bf16
+  // pairs after a range error stays on those
+  m.fast = 0;
+  if (on == 2 && !m.op_bf16) {
+    if (!m.fast_planned && !plan_fast(m)) return false;
+    m.fast = 1;
+  }
   return true;
 }
 
@@ -916,10 +977,10 @@ bool gen_forward(Gen& m) {
   if (c.gin_channels)
     cond_forward(m.P(m.pidx("dec.cond.weight")), m.P(m.pidx("dec.cond.bias")), m.g, m.B, c.initial_channel,
                  c.gin_channels, m.rowadd, st);
-  CK(m.pre_fwd.run(st));
+  CK((m.fast ? m.pre_fast : m.pre_fwd).run(st));
   for (int L = 0; L < 4; ++L) {
     StageBufs& s = m.sg[L];
-    CK(s.up_fwd.run(st));
+    CK((m.fast ? s.up_fast : s.up_fwd).run(st));
     NoiseActArgs na{};
     na.x = s.x_in;
     na.har = c.nsf ? m.har : nullptr;
@@ -952,11 +1013,11 @@ bool gen_forward(Gen& m) {
     noise_add_act(na, st);
     for (int j = 0; j < m.nk; ++j)
       for (int cp = 0; cp < m.nd; ++cp) {
-        CK(s.st[j].f1[cp].run(st));
-        CK(s.st[j].f2[cp].run(st));
+        CK((m.fast ? s.st[j].f1f[cp] : s.st[j].f1[cp]).run(st));
+        CK((m.fast ? s.st[j].f2f[cp] : s.st[j].f2[cp]).run(st));
       }
   }
-  post_forward(m.sg[3].sa_hi, m.sg[3].sa_lo, m.op_bf16, m.P(m.pidx("dec.conv_post.weight")), m.B, m.T, m.sg[3].C, 7, m.audio,
+  post_forward(m.sg[3].sa_hi, m.fast ? nullptr : m.sg[3].sa_lo, m.op_bf16, m.P(m.pidx("dec.conv_post.weight")), m.B, m.T, m.sg[3].C, 7, m.audio,
                st);
   return true;
 }

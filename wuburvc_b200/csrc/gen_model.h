@@ -67,6 +67,7 @@ struct StackBufs {
   int tiles = 0;
   ConvWeights w1[3], w2[3];
   ConvOp f1[3], f2[3], d2[3], d1[3];
+  ConvOp f1f[3], f2f[3];  // fast inference: single fp16 operands (planned on first use)
   WgradJob g1[3], g2[3];
 };
 
@@ -96,6 +97,7 @@ struct StageBufs {
   int noise_parts = 0;
   ConvWeights wu;
   ConvLaunch up_fwd, up_dg;
+  ConvLaunch up_fast;  // fast inference
   WgradJob up_wg;
   StackBufs st[3];
   float* cs_dx = nullptr;  // the stacks' cs_dp[0] partial slots, contiguous (ups / noise-conv bias)
@@ -144,6 +146,7 @@ struct Gen {
   float* cs_pre = nullptr;
   int cs_pre_tiles = 0, pre_tiles_per_item = 0;
   ConvLaunch pre_fwd;
+  ConvLaunch pre_fast;  // fast inference
   WgradJob pre_wg;
   // conv_post
   float* audio = nullptr;
@@ -162,6 +165,10 @@ struct Gen {
   // forward-only (inference): the forward skips what only the backward reads (bf16 activation copies,
   // Snake pre-activations, z's bf16 copy, the input-gradient weight layout); no backward runs
   int forward_only = 0;
+  // fast inference (forward-only): single fp16 operands, one product per K step (forward rel-L2 ~4e-4
+  // against fp64); left for the exact pairs after a range error
+  int fast = 0;
+  bool fast_planned = false;
   int n_prep = 0, prep_norm_blocks = 0, prep_tile_blocks = 0;
   float* red_scratch = nullptr;  // two-pass deterministic reductions
   size_t red_scratch_n = 0;

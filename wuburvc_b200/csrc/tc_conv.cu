@@ -84,7 +84,7 @@ __global__ void __launch_bounds__(192, 1)
     // ---------------- MMA issuer ----------------
     // the split product as A_hi x [W_hi | W_lo] (2N wide: the tiles are adjacent rows) + A_lo x W_hi
     // into the upper N columns; the epilogue adds the halves (the upper one unscaled)
-    const int fmt_bf16 = p.split ? p.split_bf16 : 1;
+    const int fmt_bf16 = p.split ? p.split_bf16 : (p.single_f16 ? 0 : 1);
     const uint32_t idesc = make_idesc(128, N, 0, 0, fmt_bf16);
     const uint32_t idesc2 = make_idesc(128, 2 * N, 0, 0, fmt_bf16);
     constexpr uint32_t layout = (KC == 64) ? 2u : 4u;        // 128B / 64B swizzle

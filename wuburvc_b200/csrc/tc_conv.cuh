@@ -69,6 +69,7 @@ struct TcConvParams {
   int n_chunks;        // C_in / KC
   int split;           // operands as hi/lo pairs, three products (fp32-accurate)
   int split_bf16;      // split pair format: 0 = fp16 hi + fp16 lo*2^11 (forward), 1 = bf16 hi + bf16 lo
+  int single_f16;      // without the split: the single operands are fp16 (fast inference), else bf16
   int lo_base;
   int stages;
   int kgroup;          // (tap, chunk) steps per pipeline stage
@@ -109,6 +110,7 @@ struct TcConv2Params {
   int n_chunks;             // C_in / KC
   int split;
   int split_bf16;           // split pair format (as TcConvParams::split_bf16)
+  int single_f16;           // as TcConvParams::single_f16
   int ntaps;
   int dil;                  // tap t reads halo rows t*dil .. t*dil+127
   int halo_start;           // row offset of the halo tile relative to the tile's first output row

@@ -159,7 +159,7 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
     // W_hi added to columns [N, 2N); the epilogue sums the two halves (the second one unscaled).  Fewer operand reads from shared memory than
     // three N-wide MMAs, and a wider (more efficient) first MMA.
     // split pairs: fp16 hi / scaled lo (forward) or bf16 hi / lo; single operands are bf16
-    const int fmt_bf16 = SPLIT ? p.split_bf16 : 1;
+    const int fmt_bf16 = SPLIT ? p.split_bf16 : (p.single_f16 ? 0 : 1);
     const uint32_t idesc = make_idesc(128, N, 0, 0, fmt_bf16);
     const uint32_t idesc2 = make_idesc(128, 2 * N, 0, 0, fmt_bf16);
     constexpr uint32_t wlayout = (KC == 64) ? 2u : 4u;
@@ -322,22 +322,24 @@ __global__ void __launch_bounds__(kConv2Threads, 1)
   }
 }
 
-// Instantiated (KC, SPLIT, epilogue feature set) combinations: the forward (split) and input-gradient
-// epilogues of the resblock convolutions (with and without column sums), plus a generic kernel for
-// any other epilogue.
+// Instantiated (KC, SPLIT, epilogue feature set) combinations: the forward (split), the fast-inference
+// forward (single fp16 operands) and input-gradient epilogues of the resblock convolutions (with and
+// without column sums), plus a generic kernel for any other epilogue.
 #define WB_CONV2_KERNELS(X)                                                                     \
   X(64, true, kEpiGeneric) X(64, true, kEpiAct) X(64, true, kEpiAct | kEpiSnake)                 \
   X(64, true, kEpiRes | kEpiAct) X(64, true, kEpiRes | kEpiAct | kEpiSnake) X(64, true, kEpiRes)  \
   X(64, true, 0u) X(64, false, kEpiGeneric) X(64, false, kEpiMask | kEpiColsum)                 \
   X(64, false, kEpiMask | kEpiColsum | kEpiSnake) X(64, false, kEpiMask | kEpiRes | kEpiColsum)  \
   X(64, false, kEpiMask | kEpiRes | kEpiColsum | kEpiSnake) X(64, false, kEpiMask | kEpiRes)     \
-  X(64, false, kEpiMask | kEpiRes | kEpiSnake)                                                   \
+  X(64, false, kEpiMask | kEpiRes | kEpiSnake) X(64, false, kEpiAct) X(64, false, kEpiRes | kEpiAct) \
+  X(64, false, kEpiAct | kEpiSnake) X(64, false, kEpiRes | kEpiAct | kEpiSnake) X(64, false, kEpiRes) \
   X(32, true, kEpiGeneric) X(32, true, kEpiAct) X(32, true, kEpiAct | kEpiSnake)                 \
   X(32, true, kEpiRes | kEpiAct) X(32, true, kEpiRes | kEpiAct | kEpiSnake) X(32, true, kEpiRes)  \
   X(32, true, 0u) X(32, false, kEpiGeneric) X(32, false, kEpiMask | kEpiColsum)                 \
   X(32, false, kEpiMask | kEpiColsum | kEpiSnake) X(32, false, kEpiMask | kEpiRes | kEpiColsum)  \
   X(32, false, kEpiMask | kEpiRes | kEpiColsum | kEpiSnake) X(32, false, kEpiMask | kEpiRes)     \
-  X(32, false, kEpiMask | kEpiRes | kEpiSnake)
+  X(32, false, kEpiMask | kEpiRes | kEpiSnake) X(32, false, kEpiAct) X(32, false, kEpiRes | kEpiAct) \
+  X(32, false, kEpiAct | kEpiSnake) X(32, false, kEpiRes | kEpiAct | kEpiSnake) X(32, false, kEpiRes)
 
 // `lim` = opt-in shared memory minus 1 KB; the kernels' own static shared memory comes off it too
 void tc_conv2_set_smem_limit(int lim) {

@@ -372,7 +372,8 @@ int wubu_generator_nsf_cuda(WuBuRVCModel *model, const float *z, int nF, int int
   }
   if (ensure_gen(ctx, &cfg, nF) != 0) goto out;
   if (!ctx->forward_only) {  /* inference: nothing the backward would read is written */
-    if (wubu_b200_gen_set_forward_only(ctx->gen, 1) != 0) {
+    const char *mode = getenv("WUBU_B200_INFERENCE");  /* "fast": single fp16 GEMM operands */
+    if (wubu_b200_gen_set_forward_only(ctx->gen, (mode && strcmp(mode, "fast") == 0) ? 2 : 1) != 0) {
       fail("generator: forward-only mode failed");
       goto out;
     }
