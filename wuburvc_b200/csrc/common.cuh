@@ -299,9 +299,23 @@ WB_DEV uint32_t make_idesc_bf16(int M, int N, int a_mn_major, int b_mn_major) {
 // ---- misc -------------------------------------------------------------------
 WB_DEV float lrelu(float x, float s) { return x > 0.f ? x : s * x; }
 
+// Snake(alpha) = x + sin^2(alpha x) / alpha, with the SFU sine and a fast divide (absolute error of
+// the sine ~1e-6 for the activations' range, far below the bf16 and fp32-mode gradient gates)
 WB_DEV float snake(float x, float a) {
-  float s = sinf(a * x);
-  return x + s * s / a;
+  const float s = __sinf(a * x);
+  return x + __fdividef(s * s, a);
+}
+// Snake's derivative 1 + sin(2 alpha x) and its alpha derivative
+// x sin(2 alpha x) / alpha - sin^2(alpha x) / alpha^2, from one accurate sine / cosine pair: summed
+// over every row of a channel, the alpha gradient's terms cancel, and the SFU sine's absolute error
+// (fine for the forward) would dominate the sum
+WB_DEV void snake_grads(float x, float a, float& dx, float& da) {
+  float sn, cs;
+  sincosf(a * x, &sn, &cs);
+  const float s2 = 2.f * sn * cs;
+  const float ia = __fdividef(1.f, a);
+  dx = 1.f + s2;
+  da = (x * s2 - sn * sn * ia) * ia;
 }
 
 // split an fp32 value into bf16 hi + bf16 lo (hi + lo == x to ~2^-17 relative)

@@ -567,12 +567,9 @@ __global__ void __launch_bounds__(256) post_backward_kernel(PostBwdArgs a) {
     const float x = xm8[r];
     float deriv;
     if (a.act_kind == 1) {
-      const float al = a.alpha[c];
-      float sn, csn;
-      sincosf(al * x, &sn, &csn);
-      const float s2 = 2.f * sn * csn;
-      as += da * (x * s2 / al - sn * sn / (al * al));
-      deriv = 1.f + s2;
+      float dal;
+      snake_grads(x, a.alpha[c], deriv, dal);
+      as += da * dal;
     } else {
       deriv = x > 0.f ? 1.f : a.slope;
     }

@@ -238,12 +238,10 @@ WB_DEV void epi_finish(const Epi& e, float* v, EpiIn& in, bool valid, size_t off
       float ga[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        const float a = mask_alpha[i];
-        float sn, cs;
-        sincosf(a * x[i], &sn, &cs);
-        const float s2 = 2.f * sn * cs;  // sin(2 a x)
-        ga[i] = valid ? v[i] * (x[i] * s2 / a - sn * sn / (a * a)) : 0.f;
-        v[i] *= 1.f + s2;
+        float dx, da;
+        snake_grads(x[i], mask_alpha[i], dx, da);
+        ga[i] = valid ? v[i] * da : 0.f;
+        v[i] *= dx;
       }
       if (e.alpha_part) {
         const float t = cta_colsum32(ga, red, warp, lane, bar);
