@@ -306,12 +306,23 @@ WB_DEV float snake(float x, float a) {
   return x + __fdividef(s * s, a);
 }
 // Snake's derivative 1 + sin(2 alpha x) and its alpha derivative
-// x sin(2 alpha x) / alpha - sin^2(alpha x) / alpha^2, from one accurate sine / cosine pair: summed
-// over every row of a channel, the alpha gradient's terms cancel, and the SFU sine's absolute error
-// (fine for the forward) would dominate the sum
+// x sin(2 alpha x) / alpha - sin^2(alpha x) / alpha^2 (a difference of two ~x^2 terms for small
+// arguments), from one sine / cosine pair accurate in RELATIVE terms down to small arguments
 WB_DEV void snake_grads(float x, float a, float& dx, float& da) {
+  // |alpha x| < 1/4: Taylor series (relative error below 1e-9; the SFU's absolute error would swamp
+  // sin^2 of small arguments).  Else Cody-Waite reduction of the argument to [-pi, pi] (2 pi as a
+  // float plus its rounding remainder, two FMAs) and the SFU pair, accurate on that interval.
+  const float y = a * x, y2 = y * y;
+  const float ts = y * (1.f - y2 * (1.f / 6.f - y2 * (1.f / 120.f - y2 * (1.f / 5040.f))));
+  const float tc = 1.f - y2 * (0.5f - y2 * (1.f / 24.f - y2 * (1.f / 720.f)));
+  const float k = rintf(y * 0.15915494309189535f);
+  float r = fmaf(-k, 6.28318548202514648f, y);
+  r = fmaf(-k, -1.7484556000744487e-07f, r);
   float sn, cs;
-  sincosf(a * x, &sn, &cs);
+  __sincosf(r, &sn, &cs);
+  const bool small = fabsf(y) < 0.25f;
+  sn = small ? ts : sn;
+  cs = small ? tc : cs;
   const float s2 = 2.f * sn * cs;
   const float ia = __fdividef(1.f, a);
   dx = 1.f + s2;
