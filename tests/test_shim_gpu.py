@@ -165,13 +165,19 @@ def test_reference_ab_program_passes_on_the_shim():
 
 
 @needs_shim
-@pytest.mark.parametrize("use_snake", [0, 1])
-def test_generator_nsf_cuda_equals_library_and_matches_oracle(use_snake):
+@pytest.mark.parametrize("use_snake,fast", [(0, False), (1, False), (0, True), (1, True)])
+def test_generator_nsf_cuda_equals_library_and_matches_oracle(use_snake, fast, monkeypatch):
     """wubu_generator_nsf_cuda (src/wubu_rvc_real.h:95) on a reference model holding the full NSF
     generator as RVC checkpoints do: one-harmonic source (l_linear 1 x 1), cond(g), noise convs,
     de-normalised weights.  Without noise injection the source is deterministic, so the result must
-    equal the library's own forward of the same generator and match the fp64 oracle."""
+    equal the library's own forward of the same generator (in the same inference mode) and match
+    the fp64 oracle; WUBU_B200_INFERENCE=fast selects the single-fp16 mode."""
     import torch
+
+    if fast:
+        monkeypatch.setenv("WUBU_B200_INFERENCE", "fast")
+    else:
+        monkeypatch.delenv("WUBU_B200_INFERENCE", raising=False)
 
     cfg = model.config("40k", harmonic_num=0, weight_norm=False,
                        activation="snake" if use_snake else "lrelu")
@@ -191,6 +197,7 @@ def test_generator_nsf_cuda_equals_library_and_matches_oracle(use_snake):
     ref.close()
     gen = Generator(cfg, 1, F)
     gen.set_params(flatten(cfg, P))
+    gen.set_forward_only(True, fast=fast)
     gen.upload(z[None], f0[None], g[None], np.zeros((1, T, 1), np.float32), None)
     want = gen.forward()[0]
     gen.close()

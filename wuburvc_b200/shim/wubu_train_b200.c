@@ -46,7 +46,8 @@ struct TrainCacheCuda {
   int n_out;
   int have_forward;
   int precision;                   /* WUBU_B200_PRECISION_* of the context */
-  int forward_only;                /* the context runs inference only (wubu_generator_nsf_cuda) */
+  int forward_only;                /* inference mode of the context (wubu_generator_nsf_cuda): 0 none,
+                                    * 1 exact, 2 fast (single fp16 operands) */
   const WuBuRVCModel *model;       /* inference cache: the model whose weights are on the device ... */
   unsigned long long fingerprint;  /* ... and a fingerprint of them */
 };
@@ -371,13 +372,17 @@ int wubu_generator_nsf_cuda(WuBuRVCModel *model, const float *z, int nF, int int
     goto out;
   }
   if (ensure_gen(ctx, &cfg, nF) != 0) goto out;
-  if (!ctx->forward_only) {  /* inference: nothing the backward would read is written */
-    const char *mode = getenv("WUBU_B200_INFERENCE");  /* "fast": single fp16 GEMM operands */
-    if (wubu_b200_gen_set_forward_only(ctx->gen, (mode && strcmp(mode, "fast") == 0) ? 2 : 1) != 0) {
-      fail("generator: forward-only mode failed");
-      goto out;
+  {  /* inference: nothing the backward would read is written; WUBU_B200_INFERENCE=fast selects
+      * single fp16 GEMM operands */
+    const char *env = getenv("WUBU_B200_INFERENCE");
+    const int mode = (env && strcmp(env, "fast") == 0) ? 2 : 1;
+    if (ctx->forward_only != mode) {
+      if (wubu_b200_gen_set_forward_only(ctx->gen, mode) != 0) {
+        fail("generator: forward-only mode failed");
+        goto out;
+      }
+      ctx->forward_only = mode;
     }
-    ctx->forward_only = 1;
   }
   if (ctx->n_out > max_samples) {
     fail("generator: max_samples is smaller than the output");
