@@ -441,10 +441,10 @@ void noise_wgrad_reduce(const float* wpart, int nparts, int C, int k, float* dW,
 constexpr int kPostK = 7;
 constexpr int kPostC = 32;
 
-// Warp = 16 consecutive output rows of one item, lane = channel: the 22-row input window is read
-// once (coalesced), each lane forms its channel's 16 partial sums, and one transpose-reduction per
-// half gives lane r the output of row r.
-constexpr int kPostWarpRows = 16;
+// Warp = 32 consecutive output rows of one item, lane = channel: the 38-row input window is read
+// once (coalesced), each lane forms its channel's 32 partial sums, and one transpose-reduction
+// gives lane r the output of row r.
+constexpr int kPostWarpRows = 32;
 
 
 __global__ void __launch_bounds__(256) post_forward_kernel(const f16* __restrict__ hi, const f16* __restrict__ lo,
