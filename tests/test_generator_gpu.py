@@ -303,3 +303,30 @@ def test_fast_inference_forward_matches_oracle(tag, B, F):
     assert e_fast <= FWD_TOL
     assert e_exact <= 1e-5
     assert np.array_equal(again, exact)
+
+
+def test_fast_inference_range_error_returns_to_the_exact_pairs():
+    """A fast-inference forward (single fp16 operands) whose operand reaches 65504 is recomputed on the
+    range-safe bf16 pairs, and the context stays on them (asking for the fast mode again keeps them)."""
+    cfg = model.decoder_only("40k")
+    B, F = 1, 4
+    P = flatten(cfg, G.init_params_ref(cfg, 1))
+    z = G.counter_normal(2, 1, B * 192 * F).reshape(B, 192, F).astype(np.float32)
+    bad = z.copy()
+    bad[0, 5, 2] = 1e5
+    ref = Generator(cfg, B, F)  # a context already on the bf16 pairs
+    ref.set_params(P)
+    ref.upload(bad)
+    ref.forward()
+    want = ref.forward()
+    ref.close()
+    gen = Generator(cfg, B, F)
+    gen.set_params(P)
+    gen.set_forward_only(True, fast=True)
+    gen.upload(bad)
+    got = gen.forward()  # overflows, falls back, recomputes
+    assert np.isfinite(got).all()
+    assert np.array_equal(got, want)
+    gen.set_forward_only(True, fast=True)
+    assert np.array_equal(gen.forward(), want)
+    gen.close()
