@@ -52,6 +52,10 @@ def parse():
     ap.add_argument("--infer", action="store_true",
                     help="forward-only long-clip inference (40 kHz, batch 1, 6000 frames = 2.4M samples, f0 "
                          "median-filtered over 5 frames) on one GPU: prints its own JSON line and exits")
+    ap.add_argument("--gan", action="store_true",
+                    help="the discriminator side of one RVC GAN iteration (MultiPeriodDiscriminator, periods "
+                         "2..17, batch --batch of --frames x hop samples): discriminator step with AdamW, then "
+                         "generator_loss + feature_loss and dL/dy_hat; prints its own JSON line and exits")
     ap.add_argument("--kernel", default=None, metavar="WHICH,STAGE",
                     help="time one convolution of the step alone (kernel_bench: which 0 f1, 1 d1, 2 g1, 3 f2, "
                          "4 d2, 5 ups forward, 6 ups input gradient, 7 ups weight gradient, 8 conv_pre, 9 g2) inside an NVTX range 'kb<which><stage>' and exit")
@@ -256,6 +260,129 @@ def run_infer(args):
     gen.close()
 
 
+def gan_flops(B, T, periods=(2, 3, 5, 7, 11, 17)):
+    """Algorithmic FLOPs of one discriminator iteration: forward over real + generated twice (the
+    discriminator step and the generator side), the weight gradients and the input gradients of
+    every layer but the first in the discriminator step, and the input gradients of every layer
+    over the generated half on the generator side."""
+    s_layers = [(1, 16, 15, 1, 1, 7), (16, 64, 41, 4, 4, 20), (64, 256, 41, 4, 16, 20), (256, 1024, 41, 4, 64, 20),
+                (1024, 1024, 41, 4, 256, 20), (1024, 1024, 5, 1, 1, 2), (1024, 1, 3, 1, 1, 1)]
+    p_layers = [(1, 32, 5, 3, 1, 2), (32, 128, 5, 3, 1, 2), (128, 512, 5, 3, 1, 2), (512, 1024, 5, 3, 1, 2),
+                (1024, 1024, 5, 1, 1, 2), (1024, 1, 3, 1, 1, 1)]
+    total = 0.0
+    for p in (0,) + tuple(periods):
+        q = p or 1
+        L, N = -(-T // q), 2 * B * q
+        for li, (ci, co, k, st, grp, pad) in enumerate(p_layers if p else s_layers):
+            L = (L + 2 * pad - k) // st + 1
+            f = 2.0 * N * L * co * (ci // grp) * k  # one pass over both halves
+            total += 2 * f + f + (f if li else 0) + f / 2
+    return total
+
+
+def run_gan(args):
+    """The discriminator side of one GAN training iteration, inputs resident (value) and through the
+    public API with host inputs and dL/dy_hat read back (e2e)."""
+    import ctypes
+
+    import torch
+    from wuburvc_b200 import gan, model
+
+    cfg = model.config(args.config)
+    B, T = args.batch, args.frames * model.hop(cfg)
+    rng = np.random.default_rng(77)
+    flat = np.zeros(gan.param_total(), np.float32)
+    for name, (off, shp) in gan.param_table().items():
+        n = int(np.prod(shp))
+        if name.endswith("weight_v"):
+            v = rng.standard_normal(shp).astype(np.float32) / np.sqrt(shp[1] * shp[2])
+            flat[off:off + n] = v.reshape(-1)
+            flat[off - shp[0]:off] = np.sqrt((v.reshape(shp[0], -1) ** 2).sum(1))  # weight_g = ||v||
+        elif name.endswith("bias"):
+            flat[off:off + n] = 0.01 * rng.standard_normal(n)
+    y = (0.3 * rng.standard_normal((B, T))).astype(np.float32)
+    y_hat = (0.5 * y + 0.2 * rng.standard_normal((B, T))).astype(np.float32)
+    d = gan.Discriminator(B, T)
+    d.set_params(flat)
+    Lh = gan.L()
+    yd, yhd = torch.from_numpy(y).cuda(), torch.from_numpy(y_hat).cuda()
+    dyd = torch.empty_like(yhd)
+    stream = torch.cuda.ExternalStream(Lh.wubu_b200_disc_stream(d.h), device=0)
+    torch.cuda.synchronize()
+
+    def device_iter():
+        check_rc(Lh.wubu_b200_disc_step(d.h, yd.data_ptr(), yhd.data_ptr(), gan.DEVICE, None))
+        n = Lh.wubu_b200_disc_launches(d.h)
+        check_rc(Lh.wubu_b200_disc_gen_loss(d.h, yd.data_ptr(), yhd.data_ptr(), dyd.data_ptr(), gan.DEVICE, None))
+        return n + Lh.wubu_b200_disc_launches(d.h)
+
+    for _ in range(max(3, args.warmup)):
+        launches = device_iter()
+    torch.cuda.synchronize()
+    with Clocks(0) as clk:
+        s, e = torch.cuda.Event(True), torch.cuda.Event(True)
+        s.record(stream)
+        for _ in range(args.steps):
+            device_iter()
+        e.record(stream)
+        torch.cuda.synchronize()
+        ms = s.elapsed_time(e) / args.steps
+        # e2e: host waveforms in, dL/dy_hat and the losses out, every iteration
+        dy = np.empty((B, T), np.float32)
+        losses = np.zeros(2, np.float32)
+        loss_d = np.zeros(1, np.float32)
+        vp = ctypes.c_void_p
+        s2, e2 = torch.cuda.Event(True), torch.cuda.Event(True)
+        s2.record(stream)
+        for _ in range(args.steps):
+            check_rc(Lh.wubu_b200_disc_step(d.h, y.ctypes.data_as(vp), y_hat.ctypes.data_as(vp), 0,
+                                            loss_d.ctypes.data_as(vp)))
+            check_rc(Lh.wubu_b200_disc_gen_loss(d.h, y.ctypes.data_as(vp), y_hat.ctypes.data_as(vp),
+                                                dy.ctypes.data_as(vp), 0, losses.ctypes.data_as(vp)))
+        e2.record(stream)
+        torch.cuda.synchronize()
+        ms_e2e = s2.elapsed_time(e2) / args.steps
+    assert np.isfinite(dy).all() and np.isfinite(losses).all() and np.isfinite(loss_d).all()
+    clocks = clk.summary()
+    secs = B * T / cfg["sr"]
+    fl = gan_flops(B, T)
+    mhz = (clocks or {}).get("sm_max_mhz") or 1965.0
+    peak = 148 * 128 * 2 * mhz * 1e6 / 1e12  # fp32 FMA lanes x 2 FLOP x clock
+    cpu = None
+    if not args.no_cpu_baseline:
+        import torch as th
+
+        from oracle import gan_ref
+
+        th.set_num_threads(os.cpu_count() or 1)
+        P = gan_ref.init_params()
+        t0 = time.time()
+        gan_ref.d_step(P, y[:1], y_hat[:1], dtype=th.float32)
+        gan_ref.g_step(P, y[:1], y_hat[:1], dtype=th.float32)
+        dt = time.time() - t0
+        cpu = {"value": (T / cfg["sr"]) / dt, "unit": "audio-s/s", "cores": th.get_num_threads(), "kind": "port",
+               "sample": f"one item ({T} samples): upstream's discriminator step + generator side in torch "
+                         f"float32 on the host cores (oracle/gan_ref.py), {dt:.2f} s"}
+    print(json.dumps({"metric": "GAN discriminator iteration audio-sec/sec", "value": secs / (ms / 1e3),
+                      "unit": "audio-s/s", "n_gpus": 1, "steps": args.steps, "warmup": max(3, args.warmup),
+                      "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                      "dtype": "fp32", "data": "synthetic",
+                      "config": {"workload": f"MultiPeriodDiscriminator (S + periods 2,3,5,7,11,17), batch {B} x "
+                                             f"{T} samples real + generated: discriminator step + AdamW, then "
+                                             "generator_loss + feature_loss and dL/dy_hat",
+                                 "l2": "activations ~1.4 GB per iteration, larger than L2"},
+                      "e2e": {"value": secs / (ms_e2e / 1e3), "unit": "audio-s/s",
+                              "h2d_bytes_per_step": int(4 * y.nbytes), "d2h_bytes_per_step": int(dy.nbytes + 12),
+                              "ms_per_step": ms_e2e},
+                      "gpu_launches": launches,
+                      "roofline": {"bound": "fp32 FMA (CUDA cores)", "achieved": fl / (ms / 1e3) / 1e12,
+                                   "peak": peak, "unit": "TFLOP/s", "frac": fl / (ms / 1e3) / 1e12 / peak,
+                                   "peak_source": "nominal: 148 SMs x 128 fp32 lanes x 2 x sampled max clock",
+                                   "traffic": None},
+                      "cpu_baseline": cpu, "clocks": clocks}))
+    d.close()
+
+
 def check_rc(rc):
     if rc != 0:
         raise RuntimeError(f"wuburvc_b200 call failed ({rc})")
@@ -265,6 +392,9 @@ def main():
     args = parse()
     if args.infer:
         run_infer(args)
+        return
+    if args.gan:
+        run_gan(args)
         return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

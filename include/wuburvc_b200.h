@@ -267,6 +267,48 @@ int wubu_b200_gen_attach_comm(WubuB200Gen* gen, int rank, int world, const void*
  * further step.  Needs an attached communicator. */
 int wubu_b200_gen_set_comm_timeout_ms(WubuB200Gen* gen, int ms);
 
+/* ---------------------------------------------------------------------------------------------
+ * 3. The GAN discriminators of RVC training (wubu_b200_disc_*): MultiPeriodDiscriminator =
+ *    DiscriminatorS + one DiscriminatorP per period (knowledge/rvc_original/infer/module/
+ *    models.py:928-1094), weight-normed, with discriminator_loss / generator_loss / feature_loss
+ *    (train/losses.py:4-40) and torch.optim.AdamW, in the step order of train/train.py:500-525:
+ *      wubu_b200_disc_step      forward on (real, generated detached), discriminator loss, every
+ *                               parameter gradient, AdamW
+ *      wubu_b200_disc_gen_loss  forward through the (updated) discriminators, generator_loss +
+ *                               feature_loss (real feature maps detached) and dL/dy_hat, which the
+ *                               generator takes as its dldy
+ *    fp32 throughout.  periods = NULL or n_periods = 0: [2, 3, 5, 7, 11, 17] (V2 passes
+ *    {2, 3, 5, 7, 11, 17, 23, 37}).  Parameters: one flat fp32 buffer in upstream's state_dict
+ *    order, per convolution bias [C_out], weight_g [C_out], weight_v [C_out][C_in/groups][k].
+ * ------------------------------------------------------------------------------------------- */
+typedef struct WubuB200Disc WubuB200Disc;
+#define WUBU_B200_DISC_DEVICE 1    /* y, y_hat (and dldy_hat) are device pointers; no host sync */
+#define WUBU_B200_DISC_NO_UPDATE 2 /* wubu_b200_disc_step: gradients only, no AdamW step */
+int wubu_b200_disc_param_count(const int* periods, int n_periods);       /* tensors */
+long long wubu_b200_disc_param_total(const int* periods, int n_periods); /* floats */
+int wubu_b200_disc_param_info(const int* periods, int n_periods, int index, char* name, int name_cap, int* shape3,
+                              long long* offset);
+/* B items of T samples per call; stream = NULL: the context makes its own. */
+WubuB200Disc* wubu_b200_disc_create(int B, int T, const int* periods, int n_periods, void* stream);
+void wubu_b200_disc_destroy(WubuB200Disc* d);
+long long wubu_b200_disc_n_params(const WubuB200Disc* d);
+int wubu_b200_disc_set_params(WubuB200Disc* d, const float* host_flat);
+int wubu_b200_disc_get_params(WubuB200Disc* d, float* host_flat);
+int wubu_b200_disc_get_grads(WubuB200Disc* d, float* host_flat);
+/* torch.optim.AdamW hyper-parameters; default lr 1e-4, betas (0.8, 0.99), eps 1e-9 (the RVC
+ * training configs), weight decay 0.01 (torch's default). */
+int wubu_b200_disc_set_adamw(WubuB200Disc* d, float lr, float b1, float b2, float eps, float wd);
+/* y, y_hat: [B][T] fp32.  loss_d (host, may be NULL with WUBU_B200_DISC_DEVICE: then the call
+ * returns without synchronising) receives discriminator_loss. */
+int wubu_b200_disc_step(WubuB200Disc* d, const float* y, const float* y_hat, int flags, float* loss_d);
+/* dldy_hat [B][T] receives d(generator_loss + feature_loss)/d y_hat; losses2 (host, may be NULL
+ * as above) receives {generator_loss, feature_loss}. */
+int wubu_b200_disc_gen_loss(WubuB200Disc* d, const float* y, const float* y_hat, float* dldy_hat, int flags,
+                            float* losses2);
+void* wubu_b200_disc_stream(WubuB200Disc* d);
+int wubu_b200_disc_sync(WubuB200Disc* d);
+int wubu_b200_disc_launches(const WubuB200Disc* d); /* kernels the last step / gen_loss call launched */
+
 #ifdef __cplusplus
 }
 #endif

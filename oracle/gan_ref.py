@@ -143,42 +143,46 @@ def feature_loss(fr, fg):
     return 2 * sum((a.detach() - b).abs().mean() for A, Bm in zip(fr, fg) for a, b in zip(A, Bm))
 
 
-def _tensors(P, requires_grad=False):
+def _tensors(P, requires_grad=False, dtype=None):
     torch = _torch()
-    return OrderedDict((n, torch.tensor(np.asarray(v, np.float64), requires_grad=requires_grad))
+    dtype = dtype or torch.float64
+    return OrderedDict((n, torch.tensor(np.asarray(v), dtype=dtype, requires_grad=requires_grad))
                        for n, v in P.items())
 
 
-def d_step(P, y, y_hat, periods=PERIODS_V1):
+def d_step(P, y, y_hat, periods=PERIODS_V1, dtype=None):
     """The discriminator's loss on (real y, generated y_hat detached) and its gradient per
-    parameter (flat float64 arrays)."""
+    parameter (flat float64 arrays).  dtype torch.float32 runs upstream's own fp32 arithmetic
+    (the floor a fp32 implementation is measured against); the default is float64."""
     torch = _torch()
-    Pt = _tensors(P, True)
-    yr = torch.tensor(np.asarray(y, np.float64))
-    yg = torch.tensor(np.asarray(y_hat, np.float64))
+    dtype = dtype or torch.float64
+    Pt = _tensors(P, True, dtype)
+    yr = torch.tensor(np.asarray(y), dtype=dtype)
+    yg = torch.tensor(np.asarray(y_hat), dtype=dtype)
     r = mpd_forward(Pt, yr, periods)
     g = mpd_forward(Pt, yg, periods)
     loss = discriminator_loss([a for a, _ in r], [a for a, _ in g])
     loss.backward()
-    grads = OrderedDict((n, t.grad.numpy().reshape(-1).copy()) for n, t in Pt.items())
-    logits = np.concatenate([a.detach().numpy().reshape(-1) for a, _ in r]
-                            + [a.detach().numpy().reshape(-1) for a, _ in g])
+    grads = OrderedDict((n, t.grad.double().numpy().reshape(-1).copy()) for n, t in Pt.items())
+    logits = np.concatenate([a.detach().double().numpy().reshape(-1) for a, _ in r]
+                            + [a.detach().double().numpy().reshape(-1) for a, _ in g])
     return float(loss.detach()), grads, logits
 
 
-def g_step(P, y, y_hat, periods=PERIODS_V1):
+def g_step(P, y, y_hat, periods=PERIODS_V1, dtype=None):
     """generator_loss + feature_loss through the discriminator (real feature maps detached):
     (loss_gen, loss_fm, dL/dy_hat [B, T])."""
     torch = _torch()
-    Pt = _tensors(P, False)
-    yr = torch.tensor(np.asarray(y, np.float64))
-    yg = torch.tensor(np.asarray(y_hat, np.float64), requires_grad=True)
+    dtype = dtype or torch.float64
+    Pt = _tensors(P, False, dtype)
+    yr = torch.tensor(np.asarray(y), dtype=dtype)
+    yg = torch.tensor(np.asarray(y_hat), dtype=dtype, requires_grad=True)
     r = mpd_forward(Pt, yr, periods)
     g = mpd_forward(Pt, yg, periods)
     lg = generator_loss([a for a, _ in g])
     lf = feature_loss([f for _, f in r], [f for _, f in g])
     (lg + lf).backward()
-    return float(lg), float(lf), yg.grad.numpy().copy()
+    return float(lg.detach()), float(lf.detach()), yg.grad.double().numpy().copy()
 
 
 def adamw(P, grads, m, v, t, lr, betas, eps, wd):

@@ -53,3 +53,19 @@ def test_generator_side_gradient(gold, step):
     want = gold["dldy_hat"]
     got = step["dldy_hat"]
     assert np.linalg.norm(got - want) / np.linalg.norm(want) < 1e-6
+
+
+def test_generator_side_gradient_moves_at_fp32_resolution(gold):
+    """dL/dy_hat is discontinuous where a generated feature ties with the real one (the sign of
+    feature_loss) or a LeakyReLU input sits at 0: a relative change of 1e-7 in y_hat (fp32 rounding
+    size) moves the fp64 result by ~5e-4 at this shape.  This is why the GPU check of dL/dy_hat
+    (fp32) is gated at a few times that rather than at the continuous gradients' 1e-4."""
+    from oracle import generator_ref as G
+
+    P = D.init_params(D.PERIODS_V1, int(gold["seed"]))
+    y, y_hat = gold["y"], gold["y_hat"]
+    _, _, d0 = D.g_step(P, y, y_hat)
+    eps = 1e-7 * G.counter_normal(99, 0, y_hat.size).reshape(y_hat.shape)
+    _, _, d1 = D.g_step(P, y, y_hat * (1 + eps))
+    moved = np.linalg.norm(d1 - d0) / np.linalg.norm(d0)
+    assert 1e-5 < moved < 1e-3

@@ -143,3 +143,31 @@ def test_precision_option_is_checked_before_any_device_call():
     o = TrainOptions()
     o.batch, o.frames, o.precision = 1, 4, 7
     assert not L().wubu_b200_gen_create(ctypes.byref(c), ctypes.byref(o))
+
+
+def test_discriminator_table_and_argument_checks_without_a_gpu():
+    """The discriminators' parameter table is upstream's state_dict (MultiPeriodDiscriminator and
+    V2, models.py:928-978) and every entry point checks its arguments before a device call."""
+    import ctypes
+
+    from oracle import gan_ref
+    from wuburvc_b200 import gan
+
+    for per in (gan.PERIODS_V1, gan.PERIODS_V2):
+        t = gan.param_table(per)
+        assert list(t) == list(gan_ref.param_shapes(per))
+        assert all(tuple(s) == tuple(gan_ref.param_shapes(per)[n]) for n, (_, s) in t.items())
+    assert gan.param_total() == 54968286
+    h = gan.L()
+    bad = (ctypes.c_int * 1)(1)
+    assert h.wubu_b200_disc_param_count(bad, 1) == -1
+    assert h.wubu_b200_disc_param_total(bad, 1) == -1
+    assert h.wubu_b200_disc_param_info(None, 0, 129, None, 0, None, None) == -1
+    assert not h.wubu_b200_disc_create(0, 12800, None, 0, None)
+    assert not h.wubu_b200_disc_create(1, 64, None, 0, None)
+    assert h.wubu_b200_disc_step(None, None, None, 0, None) == -1
+    assert h.wubu_b200_disc_gen_loss(None, None, None, None, 0, None) == -1
+    assert h.wubu_b200_disc_set_adamw(None, 1e-4, 0.8, 0.99, 1e-9, 0.01) == -1
+    assert h.wubu_b200_disc_sync(None) == -1
+    assert h.wubu_b200_disc_launches(None) == -1
+    assert h.wubu_b200_disc_n_params(None) == -1
