@@ -132,95 +132,109 @@ __global__ void __launch_bounds__(kPos) disc_conv_dgrad_kernel(const float* __re
   for (int i = 0; i < TCI; ++i) dx[((size_t)n * L.C_in + ci0 + i) * L.L_in + u] = acc[i];
 }
 
-// Register-tiled implicit GEMMs for the dense layers (64 | channels per group), which carry nearly
-// all the FLOPs: a 256-thread block computes 64 channels x 128 positions, 4 x 8 per thread, over
-// K chunks of 16 staged in shared memory; each position's sequence offset is decoded once per block.
+// Register-tiled implicit GEMMs for the dense layers, which carry nearly all the FLOPs: a 256-thread
+// block computes 64 rows x 128 columns, 4 x 8 per thread, over K chunks of 16 rows double-buffered in
+// shared memory; the next chunk's global loads are issued into registers before the current chunk's
+// FMAs.  The forward and input-gradient kernels read a tap-major copy of the weights ([co][kk][ci],
+// written by the weight-norm kernel) and order K tap-major too, so one chunk lies inside one tap: the
+// tap, the channel base and each position's range check are uniform over the chunk.
 constexpr int kGM = 64, kGN = 128, kGK = 16;
 
-// forward: out[co][p] = sum_j w[co][j] X[j][p], j = (ci, kk), X = x[n][g cig + ci][t s + kk - pad]
-__global__ void __launch_bounds__(256) disc_gemm_fwd_kernel(const float* __restrict__ x, const float* __restrict__ w,
+struct GemmSmem {
+  float A[2][kGK][kGM + 4];
+  float B[2][kGK][kGN + 4];
+};
+
+__device__ __forceinline__ void gemm_chunk(const float (*A)[kGM + 4], const float (*B)[kGN + 4], int ty, int tx,
+                                           float (&acc)[4][8]) {
+#pragma unroll
+  for (int kq = 0; kq < kGK; ++kq) {
+    const float4 a = *reinterpret_cast<const float4*>(&A[kq][ty * 4]);
+    const float4 b0 = *reinterpret_cast<const float4*>(&B[kq][tx * 4]);
+    const float4 b1 = *reinterpret_cast<const float4*>(&B[kq][64 + tx * 4]);
+    const float av[4] = {a.x, a.y, a.z, a.w};
+    const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+      for (int c = 0; c < 8; ++c) acc[r][c] = fmaf(av[r], bv[c], acc[r][c]);
+  }
+}
+
+// column c (0..7) of a thread's tile -> column inside the block's 128
+__device__ __forceinline__ int gemm_col(int tx, int c) { return c < 4 ? tx * 4 + c : 64 + tx * 4 + c - 4; }
+
+// forward: out[co][p] = sum_{kk, ci} wt[co][kk][ci] x[n][g cig + ci][t s + kk - pad]  (cig % 16 == 0)
+__global__ void __launch_bounds__(256) disc_gemm_fwd_kernel(const float* __restrict__ x, const float* __restrict__ wt,
                                                            const float* __restrict__ bias, float* __restrict__ y,
                                                            DLayer L, int N) {
-  __shared__ __align__(16) float As[kGK][kGM + 4];
-  __shared__ __align__(16) float Bs[kGK][kGN];
-  __shared__ int pbase[kGN], pq0[kGN];
+  __shared__ __align__(16) GemmSmem sm;
   const int cig = L.C_in / L.groups, cog = L.C_out / L.groups, K = cig * L.k;
   const int co0 = blockIdx.y * kGM, g = co0 / cog;
   const int p0 = blockIdx.x * kGN, P = N * L.L_out;
   const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
-  if (tid < kGN) {
-    const int p = p0 + tid;
-    if (p < P) {
-      const int n = p / L.L_out, t = p - n * L.L_out;
-      pbase[tid] = (n * L.C_in + g * cig) * L.L_in;
-      pq0[tid] = t * L.s - L.pad;
-    } else {
-      pbase[tid] = 0;
-      pq0[tid] = -(1 << 30);  // every tap out of range: the position reads zeros
-    }
-  }
+  // loader roles: A rows akq, columns am + 16 i; B column (position) pl, rows bkq + 2 i
+  const int akq = tid & 15, am = tid >> 4, pl = tid & (kGN - 1), bkq = tid >> 7;
+  const int p = p0 + pl;
+  const bool live = p < P;
+  const int n = live ? p / L.L_out : 0, t = live ? p - n * L.L_out : 0;
+  const float* xb = x + ((size_t)n * L.C_in + (size_t)g * cig) * L.L_in;
+  const int q0 = t * L.s - L.pad;
+  const float* wrow = wt + (size_t)(co0 + am) * K;
+  float ra[4], rb[8];
+  auto load = [&](int k0) {
+    const int kk = k0 / cig, ci0 = k0 - kk * cig;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) ra[i] = __ldg(wrow + (size_t)16 * i * K + k0 + akq);
+    const int q = q0 + kk;
+    const bool ok = live && q >= 0 && q < L.L_in;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) rb[i] = ok ? __ldg(xb + (size_t)(ci0 + bkq + 2 * i) * L.L_in + q) : 0.f;
+  };
+  auto store = [&](int b) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) sm.A[b][akq][am + 16 * i] = ra[i];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) sm.B[b][bkq + 2 * i][pl] = rb[i];
+  };
   float acc[4][8];
 #pragma unroll
   for (int r = 0; r < 4; ++r)
 #pragma unroll
     for (int c = 0; c < 8; ++c) acc[r][c] = 0.f;
-  const float* wb = w + (size_t)co0 * K;
+  load(0);
+  store(0);
+  __syncthreads();
+  int b = 0;
   for (int k0 = 0; k0 < K; k0 += kGK) {
+    const bool more = k0 + kGK < K;
+    if (more) load(k0 + kGK);
+    gemm_chunk(sm.A[b], sm.B[b], ty, tx, acc);
+    if (more) store(b ^ 1);
     __syncthreads();
-    for (int e = tid; e < kGK * kGM; e += 256) {
-      const int m = e / kGK, kq = e - m * kGK, j = k0 + kq;
-      As[kq][m] = j < K ? wb[(size_t)m * K + j] : 0.f;
-    }
-    {
-      const int pl = tid & (kGN - 1), base = pbase[pl], q0 = pq0[pl];
-#pragma unroll
-      for (int i = 0; i < kGK / 2; ++i) {
-        const int kq = (tid >> 7) + 2 * i, j = k0 + kq;
-        float v = 0.f;
-        if (j < K) {
-          const int ci = j / L.k, q = q0 + j - ci * L.k;
-          if (q >= 0 && q < L.L_in) v = __ldg(x + base + ci * L.L_in + q);
-        }
-        Bs[kq][pl] = v;
-      }
-    }
-    __syncthreads();
-#pragma unroll
-    for (int kq = 0; kq < kGK; ++kq) {
-      const float4 a = *reinterpret_cast<const float4*>(&As[kq][ty * 4]);
-      const float4 b0 = *reinterpret_cast<const float4*>(&Bs[kq][tx * 4]);
-      const float4 b1 = *reinterpret_cast<const float4*>(&Bs[kq][64 + tx * 4]);
-      const float av[4] = {a.x, a.y, a.z, a.w};
-      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-#pragma unroll
-      for (int r = 0; r < 4; ++r)
-#pragma unroll
-        for (int c = 0; c < 8; ++c) acc[r][c] = fmaf(av[r], bv[c], acc[r][c]);
-    }
+    b ^= 1;
   }
 #pragma unroll
   for (int c = 0; c < 8; ++c) {
-    const int p = p0 + (c < 4 ? tx * 4 + c : 64 + tx * 4 + c - 4);
-    if (p >= P) continue;
-    const int n = p / L.L_out, t = p - n * L.L_out;
+    const int pc = p0 + gemm_col(tx, c);
+    if (pc >= P) continue;
+    const int nc = pc / L.L_out, tc = pc - nc * L.L_out;
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
       const int co = co0 + ty * 4 + r;
       float v = acc[r][c] + bias[co];
       if (L.act) v = v > 0.f ? v : v * kSlope;
-      y[((size_t)n * L.C_out + co) * L.L_out + t] = v;
+      y[((size_t)nc * L.C_out + co) * L.L_out + tc] = v;
     }
   }
 }
 
 // input gradient, one stride phase r per blockIdx.z: u = r + s v.  Only the taps kk = kk0 + i s
 // (kk0 = (r + pad) mod s) reach a whole output position t = v + c_r - i (c_r = (r + pad - kk0) / s), so
-// dx[ci][(n, v)] = sum_{j = (o, i)} w[o][ci][kk0 + i s] dz[n][o][v + c_r - i].
-__global__ void __launch_bounds__(256) disc_gemm_dgrad_kernel(const float* __restrict__ dz, const float* __restrict__ w,
+// dx[ci][(n, v)] = sum_{i, o} wt[o][kk0 + i s][ci] dz[n][o][v + c_r - i];  K ordered (i, o), cog % 16 == 0.
+__global__ void __launch_bounds__(256) disc_gemm_dgrad_kernel(const float* __restrict__ dz, const float* __restrict__ wt,
                                                              float* __restrict__ dx, DLayer L, int N) {
-  __shared__ __align__(16) float As[kGK][kGM + 4];
-  __shared__ __align__(16) float Bs[kGK][kGN];
-  __shared__ int pbase[kGN], pv0[kGN];
+  __shared__ __align__(16) GemmSmem sm;
   const int cig = L.C_in / L.groups, cog = L.C_out / L.groups;
   const int r = blockIdx.z;
   const int kk0 = (r + L.pad) % L.s, KT = (L.k - kk0 + L.s - 1) / L.s, c_r = (r + L.pad - kk0) / L.s;
@@ -229,78 +243,63 @@ __global__ void __launch_bounds__(256) disc_gemm_dgrad_kernel(const float* __res
   if (p0 >= P || KT <= 0) return;  // uniform over the block
   const int ci0 = blockIdx.y * kGM, g = ci0 / cig, cl0 = ci0 - g * cig;
   const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
-  if (tid < kGN) {
-    const int p = p0 + tid;
-    if (p < P) {
-      const int n = p / V, v = p - n * V;
-      pbase[tid] = (n * L.C_out + g * cog) * L.L_out;
-      pv0[tid] = v + c_r;
-    } else {
-      pbase[tid] = 0;
-      pv0[tid] = -(1 << 30);
-    }
-  }
+  // loader roles: A columns am (ci), rows akq + 4 i (o); B column (position) pl, rows bkq + 2 i
+  const int am = tid & 63, akq = tid >> 6, pl = tid & (kGN - 1), bkq = tid >> 7;
+  const int p = p0 + pl;
+  const bool live = p < P;
+  const int n = live ? p / V : 0, v = live ? p - n * V : 0;
+  const float* dzb = dz + ((size_t)n * L.C_out + (size_t)g * cog) * L.L_out;
+  const int v0 = v + c_r;
+  const float* wcol = wt + (size_t)g * cog * L.k * cig + cl0 + am;
+  float ra[4], rb[8];
+  auto load = [&](int k0) {
+    const int i = k0 / cog, o0 = k0 - i * cog, kk = kk0 + i * L.s;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) ra[j] = __ldg(wcol + ((size_t)(o0 + akq + 4 * j) * L.k + kk) * cig);
+    const int tt = v0 - i;
+    const bool ok = live && tt >= 0 && tt < L.L_out;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) rb[j] = ok ? __ldg(dzb + (size_t)(o0 + bkq + 2 * j) * L.L_out + tt) : 0.f;
+  };
+  auto store = [&](int b) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) sm.A[b][akq + 4 * j][am] = ra[j];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) sm.B[b][bkq + 2 * j][pl] = rb[j];
+  };
   float acc[4][8];
 #pragma unroll
   for (int a = 0; a < 4; ++a)
 #pragma unroll
     for (int c = 0; c < 8; ++c) acc[a][c] = 0.f;
+  load(0);
+  store(0);
+  __syncthreads();
+  int b = 0;
   for (int k0 = 0; k0 < K; k0 += kGK) {
+    const bool more = k0 + kGK < K;
+    if (more) load(k0 + kGK);
+    gemm_chunk(sm.A[b], sm.B[b], ty, tx, acc);
+    if (more) store(b ^ 1);
     __syncthreads();
-    for (int e = tid; e < kGK * kGM; e += 256) {
-      const int kq = e / kGM, m = e - kq * kGM, j = k0 + kq;
-      float v = 0.f;
-      if (j < K) {
-        const int o = j / KT, i = j - o * KT;
-        v = __ldg(w + ((size_t)(g * cog + o) * cig + cl0 + m) * L.k + kk0 + i * L.s);
-      }
-      As[kq][m] = v;
-    }
-    {
-      const int pl = tid & (kGN - 1), base = pbase[pl], v0 = pv0[pl];
-#pragma unroll
-      for (int i2 = 0; i2 < kGK / 2; ++i2) {
-        const int kq = (tid >> 7) + 2 * i2, j = k0 + kq;
-        float v = 0.f;
-        if (j < K) {
-          const int o = j / KT, t = v0 - (j - o * KT);
-          if (t >= 0 && t < L.L_out) v = __ldg(dz + base + o * L.L_out + t);
-        }
-        Bs[kq][pl] = v;
-      }
-    }
-    __syncthreads();
-#pragma unroll
-    for (int kq = 0; kq < kGK; ++kq) {
-      const float4 a = *reinterpret_cast<const float4*>(&As[kq][ty * 4]);
-      const float4 b0 = *reinterpret_cast<const float4*>(&Bs[kq][tx * 4]);
-      const float4 b1 = *reinterpret_cast<const float4*>(&Bs[kq][64 + tx * 4]);
-      const float av[4] = {a.x, a.y, a.z, a.w};
-      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-#pragma unroll
-      for (int a2 = 0; a2 < 4; ++a2)
-#pragma unroll
-        for (int c = 0; c < 8; ++c) acc[a2][c] = fmaf(av[a2], bv[c], acc[a2][c]);
-    }
+    b ^= 1;
   }
 #pragma unroll
   for (int c = 0; c < 8; ++c) {
-    const int p = p0 + (c < 4 ? tx * 4 + c : 64 + tx * 4 + c - 4);
-    if (p >= P) continue;
-    const int n = p / V, u = r + L.s * (p - n * V);
+    const int pc = p0 + gemm_col(tx, c);
+    if (pc >= P) continue;
+    const int nc = pc / V, u = r + L.s * (pc - nc * V);
 #pragma unroll
-    for (int a2 = 0; a2 < 4; ++a2) dx[((size_t)n * L.C_in + ci0 + ty * 4 + a2) * L.L_in + u] = acc[a2][c];
+    for (int a = 0; a < 4; ++a) dx[((size_t)nc * L.C_in + ci0 + ty * 4 + a) * L.L_in + u] = acc[a][c];
   }
 }
 
 // weight gradient of a dense layer: part[z][co][j] = sum_{p in split z} dz[n][co][t] X[p][j],
-// j = (ci, kk) or the bias column (X = 1); columns decoded once per block, positions once per chunk
+// j = (ci, kk) or the bias column (X = 1); K = positions, each thread decodes one per chunk
 __global__ void __launch_bounds__(256) disc_gemm_wgrad_kernel(const float* __restrict__ dz, const float* __restrict__ x,
                                                              float* __restrict__ part, DLayer L, int N, int chunk) {
-  __shared__ __align__(16) float As[kGK][kGM + 4];
-  __shared__ __align__(16) float Bs[kGK][kGN];
+  __shared__ __align__(16) GemmSmem sm;
   __shared__ int coff[kGN], ckk[kGN];
-  __shared__ int pdz[kGK], px[kGK], pq[kGK];
   const int cig = L.C_in / L.groups, cog = L.C_out / L.groups, cols = cig * L.k + 1;
   const int o0 = blockIdx.y * kGM, g = o0 / cog;
   const int c_base = blockIdx.x * kGN;
@@ -317,65 +316,65 @@ __global__ void __launch_bounds__(256) disc_gemm_wgrad_kernel(const float* __res
       ckk[tid] = col == cols - 1 ? -1 : -2;  // -1: the bias column (ones), -2: past the end (zeros)
     }
   }
+  __syncthreads();
+  // loader roles: position kq (both operands), A rows m0 + 16 i, B columns m0 + 16 i
+  const int kq = tid & 15, m0 = tid >> 4;
+  int boff[8], bkk[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    boff[i] = coff[m0 + 16 * i];
+    bkk[i] = ckk[m0 + 16 * i];
+  }
+  float ra[4], rb[8];
+  auto load = [&](int pq0) {
+    const int pp = pq0 + kq;
+    const bool live = pp < p_end;
+    const int n = live ? pp / L.L_out : 0, t = live ? pp - n * L.L_out : 0;
+    const float* dzp = dz + (size_t)n * L.C_out * L.L_out + t + (size_t)(o0 + m0) * L.L_out;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) ra[i] = live ? __ldg(dzp + (size_t)16 * i * L.L_out) : 0.f;
+    const float* xp = x + (size_t)n * L.C_in * L.L_in;
+    const int q0 = t * L.s - L.pad;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float v = 0.f;
+      if (live) {
+        if (bkk[i] == -1) {
+          v = 1.f;
+        } else if (bkk[i] >= 0) {
+          const int q = q0 + bkk[i];
+          if (q >= 0 && q < L.L_in) v = __ldg(xp + boff[i] + q);
+        }
+      }
+      rb[i] = v;
+    }
+  };
+  auto store = [&](int b) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) sm.A[b][kq][m0 + 16 * i] = ra[i];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) sm.B[b][kq][m0 + 16 * i] = rb[i];
+  };
   float acc[4][8];
 #pragma unroll
   for (int r = 0; r < 4; ++r)
 #pragma unroll
     for (int c = 0; c < 8; ++c) acc[r][c] = 0.f;
-  for (int p0 = p_beg; p0 < p_end; p0 += kGK) {
+  load(p_beg);
+  store(0);
+  __syncthreads();
+  int b = 0;
+  for (int pq0 = p_beg; pq0 < p_end; pq0 += kGK) {
+    const bool more = pq0 + kGK < p_end;
+    if (more) load(pq0 + kGK);
+    gemm_chunk(sm.A[b], sm.B[b], ty, tx, acc);
+    if (more) store(b ^ 1);
     __syncthreads();
-    if (tid < kGK) {
-      const int p = p0 + tid;
-      if (p < p_end) {
-        const int n = p / L.L_out, t = p - n * L.L_out;
-        pdz[tid] = n * L.C_out * L.L_out + t;
-        px[tid] = n * L.C_in * L.L_in;
-        pq[tid] = t * L.s - L.pad;
-      } else {
-        pdz[tid] = -1;
-        px[tid] = 0;
-        pq[tid] = -(1 << 30);
-      }
-    }
-    __syncthreads();
-    for (int e = tid; e < kGK * kGM; e += 256) {
-      const int m = e / kGK, kq = e - m * kGK, b = pdz[kq];
-      As[kq][m] = b >= 0 ? __ldg(dz + b + (o0 + m) * L.L_out) : 0.f;
-    }
-    {
-      const int cl = tid & (kGN - 1), off = coff[cl], kk = ckk[cl];
-#pragma unroll
-      for (int i = 0; i < kGK / 2; ++i) {
-        const int kq = (tid >> 7) + 2 * i;
-        float v = 0.f;
-        if (pdz[kq] >= 0) {
-          if (kk == -1) {
-            v = 1.f;
-          } else if (kk >= 0) {
-            const int q = pq[kq] + kk;
-            if (q >= 0 && q < L.L_in) v = __ldg(x + px[kq] + off + q);
-          }
-        }
-        Bs[kq][cl] = v;
-      }
-    }
-    __syncthreads();
-#pragma unroll
-    for (int kq = 0; kq < kGK; ++kq) {
-      const float4 a = *reinterpret_cast<const float4*>(&As[kq][ty * 4]);
-      const float4 b0 = *reinterpret_cast<const float4*>(&Bs[kq][tx * 4]);
-      const float4 b1 = *reinterpret_cast<const float4*>(&Bs[kq][64 + tx * 4]);
-      const float av[4] = {a.x, a.y, a.z, a.w};
-      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-#pragma unroll
-      for (int r = 0; r < 4; ++r)
-#pragma unroll
-        for (int c = 0; c < 8; ++c) acc[r][c] = fmaf(av[r], bv[c], acc[r][c]);
-    }
+    b ^= 1;
   }
 #pragma unroll
   for (int c = 0; c < 8; ++c) {
-    const int col = c_base + (c < 4 ? tx * 4 + c : 64 + tx * 4 + c - 4);
+    const int col = c_base + gemm_col(tx, c);
     if (col >= cols) continue;
 #pragma unroll
     for (int r = 0; r < 4; ++r) part[((size_t)blockIdx.z * L.C_out + o0 + ty * 4 + r) * cols + col] = acc[r][c];
@@ -524,15 +523,24 @@ __device__ __forceinline__ float2 block_sum2(float2 v) {
   return s;
 }
 
+// also writes the tap-major copy wt[o][kk][ci] of the dense layers' GEMM kernels when wt is given
 __global__ void __launch_bounds__(128) disc_wn_fwd_kernel(const float* __restrict__ v, const float* __restrict__ g,
-                                                          float* __restrict__ w, int len) {
+                                                          float* __restrict__ w, float* __restrict__ wt, int len,
+                                                          int k, int cig) {
   const int o = blockIdx.x;
   const float* vr = v + (size_t)o * len;
   float ss = 0.f;
   for (int i = threadIdx.x; i < len; i += 128) ss = fmaf(vr[i], vr[i], ss);
   ss = block_sum2<128>(make_float2(ss, 0.f)).x;
   const float scale = g[o] / sqrtf(ss);
-  for (int i = threadIdx.x; i < len; i += 128) w[(size_t)o * len + i] = vr[i] * scale;
+  for (int i = threadIdx.x; i < len; i += 128) {
+    const float val = vr[i] * scale;
+    w[(size_t)o * len + i] = val;
+    if (wt) {
+      const int ci = i / k, kk = i - ci * k;
+      wt[(size_t)o * len + kk * cig + ci] = val;
+    }
+  }
 }
 
 // dg = <dW, v> / ||v||;  dv = (g / ||v||) (dW - v <dW, v> / ||v||^2)
@@ -743,6 +751,8 @@ struct LayerRt {
   int tco = 1, tci = 1, tm = 1, tn = 64;
   int splits = 1, chunk = 0;
   bool gemm_wgrad = false;  // dense layer: disc_gemm_wgrad_kernel (tm = 64 rows x tn = 128 columns)
+  bool gemm_fwd = false, gemm_dgrad = false;  // disc_gemm_fwd_kernel / disc_gemm_dgrad_kernel
+  long long wt_off = -1;                       // tap-major weight copy of the GEMM kernels
   long long p_bias = 0, p_g = 0, p_v = 0, w_off = 0;
   int len = 0;
   float* a = nullptr;   // output [N][C_out][L_out]
@@ -771,8 +781,8 @@ struct WubuB200Disc {
   int B = 0, T = 0;
   std::vector<int> periods;
   std::vector<Net> nets;
-  long long n_params = 0, n_weff = 0;
-  float *params = nullptr, *grads = nullptr, *m = nullptr, *v = nullptr, *weff = nullptr;
+  long long n_params = 0, n_weff = 0, n_weft = 0;
+  float *params = nullptr, *grads = nullptr, *m = nullptr, *v = nullptr, *weff = nullptr, *weft = nullptr;
   float *part = nullptr, *dw = nullptr;
   float *y_dev = nullptr, *yh_dev = nullptr, *dldy_dev = nullptr;
   double* loss_part = nullptr;
@@ -809,9 +819,9 @@ int launch_fwd(WubuB200Disc* d, const LayerRt& l, const float* in) {
                                                                               d->params + l.p_bias, l.a, l.L, l.N);
     return check_launch(d);
   }
-  if ((l.L.C_out / l.L.groups) % kGM == 0) {
+  if (l.gemm_fwd) {
     const dim3 g2((l.N * l.L.L_out + kGN - 1) / kGN, l.L.C_out / kGM);
-    disc_gemm_fwd_kernel<<<g2, 256, 0, d->st>>>(in, d->weff + l.w_off, d->params + l.p_bias, l.a, l.L, l.N);
+    disc_gemm_fwd_kernel<<<g2, 256, 0, d->st>>>(in, d->weft + l.wt_off, d->params + l.p_bias, l.a, l.L, l.N);
     return check_launch(d);
   }
   const dim3 grid((l.N * l.L.L_out + kPos - 1) / kPos, l.L.C_out / l.tco);
@@ -829,10 +839,10 @@ int launch_fwd(WubuB200Disc* d, const LayerRt& l, const float* in) {
 
 // input gradient over n_seq sequences starting at the given (already offset) pointers
 int launch_dgrad(WubuB200Disc* d, const LayerRt& l, const float* dz, float* dx, int n_seq) {
-  if ((l.L.C_in / l.L.groups) % kGM == 0) {
+  if (l.gemm_dgrad) {
     const int V = (l.L.L_in + l.L.s - 1) / l.L.s;  // positions of the longest phase
     const dim3 g2((n_seq * V + kGN - 1) / kGN, l.L.C_in / kGM, l.L.s);
-    disc_gemm_dgrad_kernel<<<g2, 256, 0, d->st>>>(dz, d->weff + l.w_off, dx, l.L, n_seq);
+    disc_gemm_dgrad_kernel<<<g2, 256, 0, d->st>>>(dz, d->weft + l.wt_off, dx, l.L, n_seq);
     return check_launch(d);
   }
   const dim3 grid((n_seq * l.L.L_in + kPos - 1) / kPos, l.L.C_in / l.tci);
@@ -873,7 +883,9 @@ int refresh_weights(WubuB200Disc* d) {
   if (!d->weff_stale) return 0;
   for (auto& net : d->nets)
     for (auto& l : net.layers) {
-      disc_wn_fwd_kernel<<<l.L.C_out, 128, 0, d->st>>>(d->params + l.p_v, d->params + l.p_g, d->weff + l.w_off, l.len);
+      disc_wn_fwd_kernel<<<l.L.C_out, 128, 0, d->st>>>(d->params + l.p_v, d->params + l.p_g, d->weff + l.w_off,
+                                                       l.wt_off >= 0 ? d->weft + l.wt_off : nullptr, l.len, l.L.k,
+                                                       l.L.C_in / l.L.groups);
       DISC_TRY(check_launch(d));
     }
   d->weff_stale = false;
@@ -1084,7 +1096,13 @@ extern "C" WubuB200Disc* wubu_b200_disc_create(int B, int T, const int* periods,
         l.tm = kGM;
         l.tn = kGN;
       }
+      l.gemm_fwd = cog % kGM == 0 && cig % kGK == 0;
+      l.gemm_dgrad = cig % kGM == 0 && cog % kGK == 0;
       l.len = cig * sp[li].k;
+      if (l.gemm_fwd || l.gemm_dgrad) {
+        l.wt_off = d->n_weft;
+        d->n_weft += (long long)sp[li].co * l.len;
+      }
       l.p_bias = tab[ti].offset;
       l.p_g = tab[ti + 1].offset;
       l.p_v = tab[ti + 2].offset;
@@ -1117,6 +1135,7 @@ extern "C" WubuB200Disc* wubu_b200_disc_create(int B, int T, const int* periods,
   const size_t np = (size_t)d->n_params * sizeof(float);
   const size_t o_params = take(np), o_grads = take(np), o_m = take(np), o_v = take(np);
   const size_t o_weff = take((size_t)d->n_weff * sizeof(float));
+  const size_t o_weft = take((size_t)std::max(d->n_weft, 1LL) * sizeof(float));
   const size_t o_part = take(part_cap * sizeof(float)), o_dw = take(dw_cap * sizeof(float));
   const size_t bt = (size_t)B * T * sizeof(float);
   const size_t o_y = take(bt), o_yh = take(bt), o_dldy = take(bt);
@@ -1137,6 +1156,7 @@ extern "C" WubuB200Disc* wubu_b200_disc_create(int B, int T, const int* periods,
   d->m = reinterpret_cast<float*>(A + o_m);
   d->v = reinterpret_cast<float*>(A + o_v);
   d->weff = reinterpret_cast<float*>(A + o_weff);
+  d->weft = reinterpret_cast<float*>(A + o_weft);
   d->part = reinterpret_cast<float*>(A + o_part);
   d->dw = reinterpret_cast<float*>(A + o_dw);
   d->y_dev = reinterpret_cast<float*>(A + o_y);
