@@ -308,6 +308,14 @@ int wubu_b200_disc_gen_loss(WubuB200Disc* d, const float* y, const float* y_hat,
 void* wubu_b200_disc_stream(WubuB200Disc* d);
 int wubu_b200_disc_sync(WubuB200Disc* d);
 int wubu_b200_disc_launches(const WubuB200Disc* d); /* kernels the last step / gen_loss call launched */
+/* Data parallelism (torch DDP's semantics): after attaching, wubu_b200_disc_step all-reduces the
+ * gradient over NCCL on the context's stream and divides it by world before AdamW, so every rank
+ * holds the mean gradient over all ranks' items and takes the same step.  id128 from
+ * wubu_b200_nccl_unique_id on one rank, shipped to the others.  Host waits of an attached context
+ * are bounded by the comm timeout (default 60 s): past it, or on an NCCL error, the communicator is
+ * aborted and the call returns WUBU_B200_ERR_COMM (the context takes no further step). */
+int wubu_b200_disc_attach_comm(WubuB200Disc* d, int rank, int world, const void* id128);
+int wubu_b200_disc_set_comm_timeout_ms(WubuB200Disc* d, int ms);
 
 #ifdef __cplusplus
 }

@@ -139,3 +139,80 @@ def test_rank_leaving_between_steps_is_detected_before_the_next_launch(tmp_path)
     r0, r1 = _run(tmp_path, "leave")
     assert r1 == ["step0", "left"]
     assert r0[0] == "step0" and r0[1].startswith("lost")
+
+
+def _disc_inputs():
+    T = 2400
+    y = (0.3 * G.counter_normal(43, 1, 4 * T).reshape(4, T)).astype(np.float32)
+    y_hat = (0.5 * y + 0.2 * G.counter_normal(43, 2, 4 * T).reshape(4, T)).astype(np.float32)
+    return y, y_hat
+
+
+def _disc_worker(rank, world, port, out_dir):
+    """One rank of the discriminators' data parallelism: 2 of the 4 items, gradient all-reduced and
+    averaged before AdamW."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import datetime
+
+    import torch.distributed as dist
+
+    from oracle import gan_ref as D
+    from wuburvc_b200 import Generator, gan
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    log = []
+    d = None
+    try:
+        y, y_hat = _disc_inputs()
+        sl = slice(2 * rank, 2 * rank + 2)
+        d = gan.Discriminator(2, y.shape[1])
+        d.set_params(gan.flatten(D.init_params(gan.PERIODS_V1, 3)))
+        uid = [Generator.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        d.attach_comm(rank, world, uid[0], timeout_s=30)
+        d.step(y[sl], y_hat[sl], update=False)
+        np.save(os.path.join(out_dir, f"dgrads{rank}.npy"), d.get_grads())
+        d.step(y[sl], y_hat[sl], update=True)
+        np.save(os.path.join(out_dir, f"dparams{rank}.npy"), d.get_params())
+        log.append("stepped")
+    finally:
+        if d is not None:
+            d.close()
+        with open(os.path.join(out_dir, f"dlog{rank}"), "w") as f:
+            f.write("\n".join(log))
+
+
+@needs_two
+def test_discriminator_two_ranks_equal_one_gpu_over_the_union_batch(tmp_path):
+    """The discriminators' averaged gradient over 2 ranks x 2 items equals one GPU's over the 4 items
+    (each item's forward is computed identically, only the weight gradients' summation order
+    differs: median rel-L2 <= 1e-6; per tensor <= 1e-4, as the weight-norm backward keeps only the
+    part of dW orthogonal to v, which on the 5-entry rows of the first layers amplifies that
+    rounding), and both ranks take the same AdamW step."""
+    import torch.multiprocessing as mp
+
+    from oracle import gan_ref as D
+    from wuburvc_b200 import gan
+
+    ctx = mp.start_processes(_disc_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2,
+                             start_method="spawn", join=False)
+    deadline = time.monotonic() + 300
+    while not ctx.join(timeout=2):
+        assert time.monotonic() < deadline, "ranks did not finish"
+    logs = [(tmp_path / f"dlog{r}").read_text().splitlines() for r in range(2)]
+    assert logs == [["stepped"], ["stepped"]]
+    g0, g1 = np.load(tmp_path / "dgrads0.npy"), np.load(tmp_path / "dgrads1.npy")
+    assert np.array_equal(g0, g1)
+    assert np.array_equal(np.load(tmp_path / "dparams0.npy"), np.load(tmp_path / "dparams1.npy"))
+    y, y_hat = _disc_inputs()
+    one = gan.Discriminator(4, y.shape[1])
+    one.set_params(gan.flatten(D.init_params(gan.PERIODS_V1, 3)))
+    one.step(y, y_hat, update=False)
+    want = gan.unflatten(one.get_grads())
+    one.close()
+    got = gan.unflatten(g0)
+    errs = [float(np.linalg.norm(got[n].astype(np.float64) - w) / np.linalg.norm(w)) for n, w in want.items()]
+    print(f"\n[dp2] discriminator gradients vs one GPU over the union batch: worst rel-L2 {max(errs):.2e}, "
+          f"median {np.median(errs):.2e}")
+    assert np.median(errs) <= 1e-6 and max(errs) <= 1e-4

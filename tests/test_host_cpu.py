@@ -171,3 +171,5 @@ def test_discriminator_table_and_argument_checks_without_a_gpu():
     assert h.wubu_b200_disc_sync(None) == -1
     assert h.wubu_b200_disc_launches(None) == -1
     assert h.wubu_b200_disc_n_params(None) == -1
+    assert h.wubu_b200_disc_attach_comm(None, 0, 2, None) == -1
+    assert h.wubu_b200_disc_set_comm_timeout_ms(None, 1000) == -1

@@ -263,4 +263,51 @@ int comm_unique_id(void* out128) {
   return 0;
 }
 
+// A plain communicator on the same NCCL (the discriminators' gradient all-reduce).
+int nccl_plain_init(void** out, int rank, int world, const void* id128) {
+  NcclApi& api = nccl();
+  if (!out || !id128 || world < 2 || rank < 0 || rank >= world) return WUBU_B200_ERR_ARG;
+  if (!api.ok) return WUBU_B200_ERR_COMM;
+  ncclUniqueId id;
+  memcpy(&id, id128, sizeof(id));
+  ncclComm_t c = nullptr;
+  const int rc = api.CommInitRank(&c, world, id, rank);
+  if (rc != ncclSuccess) {
+    fprintf(stderr, "wuburvc_b200: ncclCommInitRank failed: %s\n", api.GetErrorString ? api.GetErrorString(rc) : "?");
+    return WUBU_B200_ERR_COMM;
+  }
+  *out = c;
+  return 0;
+}
+
+int nccl_plain_allreduce_sum(void* comm, float* buf, size_t n, cudaStream_t st) {
+  NcclApi& api = nccl();
+  const int rc = api.AllReduce(buf, buf, n, ncclFloat32, ncclSum, static_cast<ncclComm_t>(comm), st);
+  if (rc != ncclSuccess) {
+    fprintf(stderr, "wuburvc_b200: ncclAllReduce failed: %s\n", api.GetErrorString ? api.GetErrorString(rc) : "?");
+    return WUBU_B200_ERR_COMM;
+  }
+  return 0;
+}
+
+// 0, or WUBU_B200_ERR_COMM when the communicator reports an asynchronous error
+int nccl_plain_async_error(void* comm) {
+  NcclApi& api = nccl();
+  int ae = ncclSuccess;
+  if (api.CommGetAsyncError && api.CommGetAsyncError(static_cast<ncclComm_t>(comm), &ae) == ncclSuccess &&
+      ae != ncclSuccess && ae != ncclInProgress)
+    return WUBU_B200_ERR_COMM;
+  return 0;
+}
+
+void nccl_plain_abort(void* comm) {
+  NcclApi& api = nccl();
+  if (comm && api.CommAbort) api.CommAbort(static_cast<ncclComm_t>(comm));
+}
+
+void nccl_plain_destroy(void* comm) {
+  NcclApi& api = nccl();
+  if (comm && api.CommDestroy) api.CommDestroy(static_cast<ncclComm_t>(comm));
+}
+
 }  // namespace wb

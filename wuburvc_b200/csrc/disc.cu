@@ -29,7 +29,13 @@
 #include <string>
 #include <vector>
 
+#include <sched.h>
+#include <unistd.h>
+
+#include <chrono>
+
 #include "../../include/wuburvc_b200.h"
+#include "nccl_plain.h"
 
 namespace wb {
 namespace disc {
@@ -147,17 +153,27 @@ struct GemmSmem {
 
 __device__ __forceinline__ void gemm_chunk(const float (*A)[kGM + 4], const float (*B)[kGN + 4], int ty, int tx,
                                            float (&acc)[4][8]) {
+  // fragments of step kq + 1 are read while step kq's FMAs run
+  float4 a = *reinterpret_cast<const float4*>(&A[0][ty * 4]);
+  float4 b0 = *reinterpret_cast<const float4*>(&B[0][tx * 4]);
+  float4 b1 = *reinterpret_cast<const float4*>(&B[0][64 + tx * 4]);
 #pragma unroll
   for (int kq = 0; kq < kGK; ++kq) {
-    const float4 a = *reinterpret_cast<const float4*>(&A[kq][ty * 4]);
-    const float4 b0 = *reinterpret_cast<const float4*>(&B[kq][tx * 4]);
-    const float4 b1 = *reinterpret_cast<const float4*>(&B[kq][64 + tx * 4]);
+    float4 an = a, b0n = b0, b1n = b1;
+    if (kq + 1 < kGK) {
+      an = *reinterpret_cast<const float4*>(&A[kq + 1][ty * 4]);
+      b0n = *reinterpret_cast<const float4*>(&B[kq + 1][tx * 4]);
+      b1n = *reinterpret_cast<const float4*>(&B[kq + 1][64 + tx * 4]);
+    }
     const float av[4] = {a.x, a.y, a.z, a.w};
     const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
     for (int r = 0; r < 4; ++r)
 #pragma unroll
       for (int c = 0; c < 8; ++c) acc[r][c] = fmaf(av[r], bv[c], acc[r][c]);
+    a = an;
+    b0 = b0n;
+    b1 = b1n;
   }
 }
 
@@ -684,6 +700,12 @@ __global__ void disc_adamw_kernel(float* __restrict__ p, const float* __restrict
   p[i] = p[i] * decay - step_size * (mi / denom);
 }
 
+// the all-reduced gradient sum -> the mean over the ranks (torch DDP's averaging)
+__global__ void disc_scale_kernel(float* __restrict__ g, long long n, float s) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) g[i] *= s;
+}
+
 // ------------------------------------------------------------------------------------------------
 // host runtime
 // ------------------------------------------------------------------------------------------------
@@ -797,6 +819,11 @@ struct WubuB200Disc {
   bool weff_stale = true;
   int launches = 0;
   void* arena = nullptr;
+  // data parallelism: the gradient is all-reduced (then averaged) before AdamW
+  void* comm = nullptr;
+  int rank = 0, world = 1;
+  int comm_timeout_ms = 60000;
+  bool comm_dead = false;  // aborted after a deadline or an NCCL error: no further step
 };
 
 namespace {
@@ -995,11 +1022,37 @@ int inputs(WubuB200Disc* d, const float* y, const float* yh, int flags, const fl
   return 0;
 }
 
+// Waits for the context's stream.  With a communicator the wait is bounded: past the deadline (a peer
+// that hangs or left mid-step) or on an NCCL error the communicator is aborted, which ends the
+// collective waiting on the peer, and the call returns WUBU_B200_ERR_COMM; the context takes no
+// further step.
+int bounded_sync(WubuB200Disc* d) {
+  if (!d->comm) return cudaStreamSynchronize(d->st) == cudaSuccess ? 0 : WUBU_B200_ERR_CUDA;
+  const auto t0 = std::chrono::steady_clock::now();
+  for (long long spins = 0;; ++spins) {
+    const cudaError_t q = cudaStreamQuery(d->st);
+    if (q == cudaSuccess) return 0;
+    if (q != cudaErrorNotReady) return WUBU_B200_ERR_CUDA;
+    const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0);
+    if (wb::nccl_plain_async_error(d->comm) || ms.count() > d->comm_timeout_ms) {
+      fprintf(stderr, "wuburvc_b200: discriminator all-reduce failed or timed out: aborting the communicator\n");
+      wb::nccl_plain_abort(d->comm);
+      d->comm = nullptr;
+      d->comm_dead = true;
+      cudaStreamSynchronize(d->st);
+      cudaGetLastError();
+      return WUBU_B200_ERR_COMM;
+    }
+    if (spins < 20000) sched_yield();
+    else usleep(50);
+  }
+}
+
 int read_losses(WubuB200Disc* d, float* out, int first, int n) {
-  if (!out) return cudaStreamSynchronize(d->st) == cudaSuccess ? 0 : WUBU_B200_ERR_CUDA;
-  if (cudaMemcpyAsync(d->losses_host, d->losses_dev, 4 * sizeof(float), cudaMemcpyDeviceToHost, d->st) != cudaSuccess ||
-      cudaStreamSynchronize(d->st) != cudaSuccess)
+  if (!out) return bounded_sync(d);
+  if (cudaMemcpyAsync(d->losses_host, d->losses_dev, 4 * sizeof(float), cudaMemcpyDeviceToHost, d->st) != cudaSuccess)
     return WUBU_B200_ERR_CUDA;
+  DISC_TRY(bounded_sync(d));
   memcpy(out, d->losses_host + first, n * sizeof(float));
   return 0;
 }
@@ -1041,6 +1094,7 @@ extern "C" int wubu_b200_disc_param_info(const int* periods, int n_periods, int 
 extern "C" void wubu_b200_disc_destroy(WubuB200Disc* d) {
   if (!d) return;
   if (d->st) cudaStreamSynchronize(d->st);
+  if (d->comm) wb::nccl_plain_destroy(d->comm);
   if (d->arena) cudaFree(d->arena);
   if (d->losses_host) cudaFreeHost(d->losses_host);
   if (d->own_stream && d->st) cudaStreamDestroy(d->st);
@@ -1247,11 +1301,18 @@ extern "C" int wubu_b200_disc_set_adamw(WubuB200Disc* d, float lr, float b1, flo
 
 extern "C" int wubu_b200_disc_step(WubuB200Disc* d, const float* y, const float* y_hat, int flags, float* loss_d) {
   if (!d || !y || !y_hat || (flags & ~(WUBU_B200_DISC_DEVICE | WUBU_B200_DISC_NO_UPDATE))) return WUBU_B200_ERR_ARG;
+  if (d->comm_dead) return WUBU_B200_ERR_COMM;
   d->launches = 0;
   const float *yd, *yhd;
   DISC_TRY(inputs(d, y, y_hat, flags, &yd, &yhd));
   DISC_TRY(forward(d, yd, yhd));
   DISC_TRY(backward_d(d));
+  if (d->comm) {
+    DISC_TRY(wb::nccl_plain_allreduce_sum(d->comm, d->grads, (size_t)d->n_params, d->st));
+    disc_scale_kernel<<<(unsigned)((d->n_params + 255) / 256), 256, 0, d->st>>>(d->grads, d->n_params,
+                                                                                1.f / (float)d->world);
+    DISC_TRY(check_launch(d));
+  }
   if (!(flags & WUBU_B200_DISC_NO_UPDATE)) DISC_TRY(adamw(d));
   if (loss_d || !(flags & WUBU_B200_DISC_DEVICE)) return read_losses(d, loss_d, 0, 1);
   return 0;
@@ -1260,6 +1321,7 @@ extern "C" int wubu_b200_disc_step(WubuB200Disc* d, const float* y, const float*
 extern "C" int wubu_b200_disc_gen_loss(WubuB200Disc* d, const float* y, const float* y_hat, float* dldy_hat,
                                        int flags, float* losses2) {
   if (!d || !y || !y_hat || !dldy_hat || (flags & ~WUBU_B200_DISC_DEVICE)) return WUBU_B200_ERR_ARG;
+  if (d->comm_dead) return WUBU_B200_ERR_COMM;
   d->launches = 0;
   const float *yd, *yhd;
   DISC_TRY(inputs(d, y, y_hat, flags, &yd, &yhd));
@@ -1277,7 +1339,23 @@ extern "C" void* wubu_b200_disc_stream(WubuB200Disc* d) { return d ? (void*)d->s
 
 extern "C" int wubu_b200_disc_sync(WubuB200Disc* d) {
   if (!d) return WUBU_B200_ERR_ARG;
-  return cudaStreamSynchronize(d->st) == cudaSuccess ? 0 : WUBU_B200_ERR_CUDA;
+  return bounded_sync(d);
+}
+
+extern "C" int wubu_b200_disc_attach_comm(WubuB200Disc* d, int rank, int world, const void* id128) {
+  if (!d || world < 1 || rank < 0 || rank >= world || (world > 1 && !id128) || d->comm) return WUBU_B200_ERR_ARG;
+  d->rank = rank;
+  d->world = world;
+  if (world == 1) return 0;
+  DISC_TRY(wb::nccl_plain_init(&d->comm, rank, world, id128));
+  d->comm_dead = false;
+  return 0;
+}
+
+extern "C" int wubu_b200_disc_set_comm_timeout_ms(WubuB200Disc* d, int ms) {
+  if (!d || ms <= 0) return WUBU_B200_ERR_ARG;
+  d->comm_timeout_ms = ms;
+  return 0;
 }
 
 extern "C" int wubu_b200_disc_launches(const WubuB200Disc* d) { return d ? d->launches : WUBU_B200_ERR_ARG; }

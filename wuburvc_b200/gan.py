@@ -38,6 +38,8 @@ _SIGS = {
     "wubu_b200_disc_stream": (_vp, [_vp]),
     "wubu_b200_disc_sync": (_ip, [_vp]),
     "wubu_b200_disc_launches": (_ip, [_vp]),
+    "wubu_b200_disc_attach_comm": (_ip, [_vp, _ip, _ip, _vp]),
+    "wubu_b200_disc_set_comm_timeout_ms": (_ip, [_vp, _ip]),
 }
 _bound = None
 
@@ -168,3 +170,10 @@ class Discriminator:
 
     def launches(self):
         return int(L().wubu_b200_disc_launches(self.h))
+
+    def attach_comm(self, rank, world, id128, timeout_s=60):
+        """Data parallelism: the gradient is all-reduced and averaged over the ranks before AdamW.
+        id128: 128 bytes from ``wuburvc_b200.Generator.nccl_unique_id()`` on one rank."""
+        buf = ctypes.create_string_buffer(bytes(id128), 128)
+        _check(L().wubu_b200_disc_attach_comm(self.h, int(rank), int(world), buf), "disc_attach_comm")
+        _check(L().wubu_b200_disc_set_comm_timeout_ms(self.h, int(timeout_s * 1000)), "disc_set_comm_timeout")
