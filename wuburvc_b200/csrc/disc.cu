@@ -145,33 +145,38 @@ __global__ void __launch_bounds__(kPos) disc_conv_dgrad_kernel(const float* __re
 // written by the weight-norm kernel) and order K tap-major too, so one chunk lies inside one tap: the
 // tap, the channel base and each position's range check are uniform over the chunk.
 constexpr int kGM = 64, kGN = 128, kGK = 16;
+constexpr int kGT = 128;  // threads of a GEMM block: 8 x 8 outputs each
 
 struct GemmSmem {
   float A[2][kGK][kGM + 4];
   float B[2][kGK][kGN + 4];
 };
 
+// one K chunk: thread (ty, tx) owns rows ty*8..ty*8+7 and columns tx*4..+3, 64+tx*4..+3; the
+// fragments of step kq + 1 are read while step kq's FMAs run
 __device__ __forceinline__ void gemm_chunk(const float (*A)[kGM + 4], const float (*B)[kGN + 4], int ty, int tx,
-                                           float (&acc)[4][8]) {
-  // fragments of step kq + 1 are read while step kq's FMAs run
-  float4 a = *reinterpret_cast<const float4*>(&A[0][ty * 4]);
+                                           float (&acc)[8][8]) {
+  float4 a0 = *reinterpret_cast<const float4*>(&A[0][ty * 8]);
+  float4 a1 = *reinterpret_cast<const float4*>(&A[0][ty * 8 + 4]);
   float4 b0 = *reinterpret_cast<const float4*>(&B[0][tx * 4]);
   float4 b1 = *reinterpret_cast<const float4*>(&B[0][64 + tx * 4]);
 #pragma unroll
   for (int kq = 0; kq < kGK; ++kq) {
-    float4 an = a, b0n = b0, b1n = b1;
+    float4 a0n = a0, a1n = a1, b0n = b0, b1n = b1;
     if (kq + 1 < kGK) {
-      an = *reinterpret_cast<const float4*>(&A[kq + 1][ty * 4]);
+      a0n = *reinterpret_cast<const float4*>(&A[kq + 1][ty * 8]);
+      a1n = *reinterpret_cast<const float4*>(&A[kq + 1][ty * 8 + 4]);
       b0n = *reinterpret_cast<const float4*>(&B[kq + 1][tx * 4]);
       b1n = *reinterpret_cast<const float4*>(&B[kq + 1][64 + tx * 4]);
     }
-    const float av[4] = {a.x, a.y, a.z, a.w};
+    const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
     const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
-    for (int r = 0; r < 4; ++r)
+    for (int r = 0; r < 8; ++r)
 #pragma unroll
       for (int c = 0; c < 8; ++c) acc[r][c] = fmaf(av[r], bv[c], acc[r][c]);
-    a = an;
+    a0 = a0n;
+    a1 = a1n;
     b0 = b0n;
     b1 = b1n;
   }
@@ -180,44 +185,49 @@ __device__ __forceinline__ void gemm_chunk(const float (*A)[kGM + 4], const floa
 // column c (0..7) of a thread's tile -> column inside the block's 128
 __device__ __forceinline__ int gemm_col(int tx, int c) { return c < 4 ? tx * 4 + c : 64 + tx * 4 + c - 4; }
 
+__device__ __forceinline__ void gemm_zero(float (&acc)[8][8]) {
+#pragma unroll
+  for (int r = 0; r < 8; ++r)
+#pragma unroll
+    for (int c = 0; c < 8; ++c) acc[r][c] = 0.f;
+}
+
 // forward: out[co][p] = sum_{kk, ci} wt[co][kk][ci] x[n][g cig + ci][t s + kk - pad]  (cig % 16 == 0)
-__global__ void __launch_bounds__(256) disc_gemm_fwd_kernel(const float* __restrict__ x, const float* __restrict__ wt,
-                                                           const float* __restrict__ bias, float* __restrict__ y,
-                                                           DLayer L, int N) {
+__global__ void __launch_bounds__(kGT, 3) disc_gemm_fwd_kernel(const float* __restrict__ x, const float* __restrict__ wt,
+                                                              const float* __restrict__ bias, float* __restrict__ y,
+                                                              DLayer L, int N) {
   __shared__ __align__(16) GemmSmem sm;
   const int cig = L.C_in / L.groups, cog = L.C_out / L.groups, K = cig * L.k;
   const int co0 = blockIdx.y * kGM, g = co0 / cog;
   const int p0 = blockIdx.x * kGN, P = N * L.L_out;
   const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
-  // loader roles: A rows akq, columns am + 16 i; B column (position) pl, rows bkq + 2 i
-  const int akq = tid & 15, am = tid >> 4, pl = tid & (kGN - 1), bkq = tid >> 7;
-  const int p = p0 + pl;
+  // loader roles: A row akq, columns am + 8 i; B: this thread's position, all 16 rows
+  const int akq = tid & 15, am = tid >> 4;
+  const int p = p0 + tid;
   const bool live = p < P;
   const int n = live ? p / L.L_out : 0, t = live ? p - n * L.L_out : 0;
   const float* xb = x + ((size_t)n * L.C_in + (size_t)g * cig) * L.L_in;
   const int q0 = t * L.s - L.pad;
   const float* wrow = wt + (size_t)(co0 + am) * K;
-  float ra[4], rb[8];
+  float ra[8], rb[kGK];
   auto load = [&](int k0) {
     const int kk = k0 / cig, ci0 = k0 - kk * cig;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) ra[i] = __ldg(wrow + (size_t)16 * i * K + k0 + akq);
+    for (int i = 0; i < 8; ++i) ra[i] = __ldg(wrow + (size_t)8 * i * K + k0 + akq);
     const int q = q0 + kk;
     const bool ok = live && q >= 0 && q < L.L_in;
+    const float* xq = xb + (size_t)ci0 * L.L_in + q;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) rb[i] = ok ? __ldg(xb + (size_t)(ci0 + bkq + 2 * i) * L.L_in + q) : 0.f;
+    for (int i = 0; i < kGK; ++i) rb[i] = ok ? __ldg(xq + (size_t)i * L.L_in) : 0.f;
   };
   auto store = [&](int b) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) sm.A[b][akq][am + 16 * i] = ra[i];
+    for (int i = 0; i < 8; ++i) sm.A[b][akq][am + 8 * i] = ra[i];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) sm.B[b][bkq + 2 * i][pl] = rb[i];
+    for (int i = 0; i < kGK; ++i) sm.B[b][i][tid] = rb[i];
   };
-  float acc[4][8];
-#pragma unroll
-  for (int r = 0; r < 4; ++r)
-#pragma unroll
-    for (int c = 0; c < 8; ++c) acc[r][c] = 0.f;
+  float acc[8][8];
+  gemm_zero(acc);
   load(0);
   store(0);
   __syncthreads();
@@ -236,8 +246,8 @@ __global__ void __launch_bounds__(256) disc_gemm_fwd_kernel(const float* __restr
     if (pc >= P) continue;
     const int nc = pc / L.L_out, tc = pc - nc * L.L_out;
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const int co = co0 + ty * 4 + r;
+    for (int r = 0; r < 8; ++r) {
+      const int co = co0 + ty * 8 + r;
       float v = acc[r][c] + bias[co];
       if (L.act) v = v > 0.f ? v : v * kSlope;
       y[((size_t)nc * L.C_out + co) * L.L_out + tc] = v;
@@ -248,8 +258,9 @@ __global__ void __launch_bounds__(256) disc_gemm_fwd_kernel(const float* __restr
 // input gradient, one stride phase r per blockIdx.z: u = r + s v.  Only the taps kk = kk0 + i s
 // (kk0 = (r + pad) mod s) reach a whole output position t = v + c_r - i (c_r = (r + pad - kk0) / s), so
 // dx[ci][(n, v)] = sum_{i, o} wt[o][kk0 + i s][ci] dz[n][o][v + c_r - i];  K ordered (i, o), cog % 16 == 0.
-__global__ void __launch_bounds__(256) disc_gemm_dgrad_kernel(const float* __restrict__ dz, const float* __restrict__ wt,
-                                                             float* __restrict__ dx, DLayer L, int N) {
+__global__ void __launch_bounds__(kGT, 3) disc_gemm_dgrad_kernel(const float* __restrict__ dz,
+                                                                const float* __restrict__ wt, float* __restrict__ dx,
+                                                                DLayer L, int N) {
   __shared__ __align__(16) GemmSmem sm;
   const int cig = L.C_in / L.groups, cog = L.C_out / L.groups;
   const int r = blockIdx.z;
@@ -259,35 +270,33 @@ __global__ void __launch_bounds__(256) disc_gemm_dgrad_kernel(const float* __res
   if (p0 >= P || KT <= 0) return;  // uniform over the block
   const int ci0 = blockIdx.y * kGM, g = ci0 / cig, cl0 = ci0 - g * cig;
   const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
-  // loader roles: A columns am (ci), rows akq + 4 i (o); B column (position) pl, rows bkq + 2 i
-  const int am = tid & 63, akq = tid >> 6, pl = tid & (kGN - 1), bkq = tid >> 7;
-  const int p = p0 + pl;
+  // loader roles: A column am (ci), rows akq + 2 j (o); B: this thread's position, all 16 rows
+  const int am = tid & 63, akq = tid >> 6;
+  const int p = p0 + tid;
   const bool live = p < P;
   const int n = live ? p / V : 0, v = live ? p - n * V : 0;
   const float* dzb = dz + ((size_t)n * L.C_out + (size_t)g * cog) * L.L_out;
   const int v0 = v + c_r;
   const float* wcol = wt + (size_t)g * cog * L.k * cig + cl0 + am;
-  float ra[4], rb[8];
+  float ra[8], rb[kGK];
   auto load = [&](int k0) {
     const int i = k0 / cog, o0 = k0 - i * cog, kk = kk0 + i * L.s;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) ra[j] = __ldg(wcol + ((size_t)(o0 + akq + 4 * j) * L.k + kk) * cig);
+    for (int j = 0; j < 8; ++j) ra[j] = __ldg(wcol + ((size_t)(o0 + akq + 2 * j) * L.k + kk) * cig);
     const int tt = v0 - i;
     const bool ok = live && tt >= 0 && tt < L.L_out;
+    const float* dq = dzb + (size_t)o0 * L.L_out + tt;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) rb[j] = ok ? __ldg(dzb + (size_t)(o0 + bkq + 2 * j) * L.L_out + tt) : 0.f;
+    for (int j = 0; j < kGK; ++j) rb[j] = ok ? __ldg(dq + (size_t)j * L.L_out) : 0.f;
   };
   auto store = [&](int b) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) sm.A[b][akq + 4 * j][am] = ra[j];
+    for (int j = 0; j < 8; ++j) sm.A[b][akq + 2 * j][am] = ra[j];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) sm.B[b][bkq + 2 * j][pl] = rb[j];
+    for (int j = 0; j < kGK; ++j) sm.B[b][j][tid] = rb[j];
   };
-  float acc[4][8];
-#pragma unroll
-  for (int a = 0; a < 4; ++a)
-#pragma unroll
-    for (int c = 0; c < 8; ++c) acc[a][c] = 0.f;
+  float acc[8][8];
+  gemm_zero(acc);
   load(0);
   store(0);
   __syncthreads();
@@ -306,14 +315,15 @@ __global__ void __launch_bounds__(256) disc_gemm_dgrad_kernel(const float* __res
     if (pc >= P) continue;
     const int nc = pc / V, u = r + L.s * (pc - nc * V);
 #pragma unroll
-    for (int a = 0; a < 4; ++a) dx[((size_t)nc * L.C_in + ci0 + ty * 4 + a) * L.L_in + u] = acc[a][c];
+    for (int a = 0; a < 8; ++a) dx[((size_t)nc * L.C_in + ci0 + ty * 8 + a) * L.L_in + u] = acc[a][c];
   }
 }
 
 // weight gradient of a dense layer: part[z][co][j] = sum_{p in split z} dz[n][co][t] X[p][j],
 // j = (ci, kk) or the bias column (X = 1); K = positions, each thread decodes one per chunk
-__global__ void __launch_bounds__(256) disc_gemm_wgrad_kernel(const float* __restrict__ dz, const float* __restrict__ x,
-                                                             float* __restrict__ part, DLayer L, int N, int chunk) {
+__global__ void __launch_bounds__(kGT, 3) disc_gemm_wgrad_kernel(const float* __restrict__ dz,
+                                                                const float* __restrict__ x, float* __restrict__ part,
+                                                                DLayer L, int N, int chunk) {
   __shared__ __align__(16) GemmSmem sm;
   __shared__ int coff[kGN], ckk[kGN];
   const int cig = L.C_in / L.groups, cog = L.C_out / L.groups, cols = cig * L.k + 1;
@@ -321,7 +331,7 @@ __global__ void __launch_bounds__(256) disc_gemm_wgrad_kernel(const float* __res
   const int c_base = blockIdx.x * kGN;
   const int P = N * L.L_out, p_beg = blockIdx.z * chunk, p_end = min(P, p_beg + chunk);
   const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
-  if (tid < kGN) {
+  {
     const int col = c_base + tid;
     if (col < cols - 1) {
       const int ci = col / L.k;
@@ -333,33 +343,28 @@ __global__ void __launch_bounds__(256) disc_gemm_wgrad_kernel(const float* __res
     }
   }
   __syncthreads();
-  // loader roles: position kq (both operands), A rows m0 + 16 i, B columns m0 + 16 i
+  // loader roles: position kq (both operands); A rows m0 + 8 i (i < 8), B columns m0 + 8 i (i < 16)
   const int kq = tid & 15, m0 = tid >> 4;
-  int boff[8], bkk[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    boff[i] = coff[m0 + 16 * i];
-    bkk[i] = ckk[m0 + 16 * i];
-  }
-  float ra[4], rb[8];
+  float ra[8], rb[16];
   auto load = [&](int pq0) {
     const int pp = pq0 + kq;
     const bool live = pp < p_end;
     const int n = live ? pp / L.L_out : 0, t = live ? pp - n * L.L_out : 0;
     const float* dzp = dz + (size_t)n * L.C_out * L.L_out + t + (size_t)(o0 + m0) * L.L_out;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) ra[i] = live ? __ldg(dzp + (size_t)16 * i * L.L_out) : 0.f;
+    for (int i = 0; i < 8; ++i) ra[i] = live ? __ldg(dzp + (size_t)8 * i * L.L_out) : 0.f;
     const float* xp = x + (size_t)n * L.C_in * L.L_in;
     const int q0 = t * L.s - L.pad;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
+    for (int i = 0; i < 16; ++i) {
+      const int kk = ckk[m0 + 8 * i];
       float v = 0.f;
       if (live) {
-        if (bkk[i] == -1) {
+        if (kk == -1) {
           v = 1.f;
-        } else if (bkk[i] >= 0) {
-          const int q = q0 + bkk[i];
-          if (q >= 0 && q < L.L_in) v = __ldg(xp + boff[i] + q);
+        } else if (kk >= 0) {
+          const int q = q0 + kk;
+          if (q >= 0 && q < L.L_in) v = __ldg(xp + coff[m0 + 8 * i] + q);
         }
       }
       rb[i] = v;
@@ -367,15 +372,12 @@ __global__ void __launch_bounds__(256) disc_gemm_wgrad_kernel(const float* __res
   };
   auto store = [&](int b) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) sm.A[b][kq][m0 + 16 * i] = ra[i];
+    for (int i = 0; i < 8; ++i) sm.A[b][kq][m0 + 8 * i] = ra[i];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) sm.B[b][kq][m0 + 16 * i] = rb[i];
+    for (int i = 0; i < 16; ++i) sm.B[b][kq][m0 + 8 * i] = rb[i];
   };
-  float acc[4][8];
-#pragma unroll
-  for (int r = 0; r < 4; ++r)
-#pragma unroll
-    for (int c = 0; c < 8; ++c) acc[r][c] = 0.f;
+  float acc[8][8];
+  gemm_zero(acc);
   load(p_beg);
   store(0);
   __syncthreads();
@@ -393,7 +395,7 @@ __global__ void __launch_bounds__(256) disc_gemm_wgrad_kernel(const float* __res
     const int col = c_base + gemm_col(tx, c);
     if (col >= cols) continue;
 #pragma unroll
-    for (int r = 0; r < 4; ++r) part[((size_t)blockIdx.z * L.C_out + o0 + ty * 4 + r) * cols + col] = acc[r][c];
+    for (int r = 0; r < 8; ++r) part[((size_t)blockIdx.z * L.C_out + o0 + ty * 8 + r) * cols + col] = acc[r][c];
   }
 }
 
@@ -848,7 +850,7 @@ int launch_fwd(WubuB200Disc* d, const LayerRt& l, const float* in) {
   }
   if (l.gemm_fwd) {
     const dim3 g2((l.N * l.L.L_out + kGN - 1) / kGN, l.L.C_out / kGM);
-    disc_gemm_fwd_kernel<<<g2, 256, 0, d->st>>>(in, d->weft + l.wt_off, d->params + l.p_bias, l.a, l.L, l.N);
+    disc_gemm_fwd_kernel<<<g2, kGT, 0, d->st>>>(in, d->weft + l.wt_off, d->params + l.p_bias, l.a, l.L, l.N);
     return check_launch(d);
   }
   const dim3 grid((l.N * l.L.L_out + kPos - 1) / kPos, l.L.C_out / l.tco);
@@ -869,7 +871,7 @@ int launch_dgrad(WubuB200Disc* d, const LayerRt& l, const float* dz, float* dx, 
   if (l.gemm_dgrad) {
     const int V = (l.L.L_in + l.L.s - 1) / l.L.s;  // positions of the longest phase
     const dim3 g2((n_seq * V + kGN - 1) / kGN, l.L.C_in / kGM, l.L.s);
-    disc_gemm_dgrad_kernel<<<g2, 256, 0, d->st>>>(dz, d->weft + l.wt_off, dx, l.L, n_seq);
+    disc_gemm_dgrad_kernel<<<g2, kGT, 0, d->st>>>(dz, d->weft + l.wt_off, dx, l.L, n_seq);
     return check_launch(d);
   }
   const dim3 grid((n_seq * l.L.L_in + kPos - 1) / kPos, l.L.C_in / l.tci);
@@ -888,7 +890,7 @@ int launch_wgrad(WubuB200Disc* d, const LayerRt& l, const float* in) {
   const int cols = l.len + 1;
   const dim3 grid((cols + l.tn - 1) / l.tn, l.L.C_out / l.tm, l.splits);
   if (l.gemm_wgrad) {
-    disc_gemm_wgrad_kernel<<<grid, 256, 0, d->st>>>(l.da, in, d->part, l.L, l.N, l.chunk);
+    disc_gemm_wgrad_kernel<<<grid, kGT, 0, d->st>>>(l.da, in, d->part, l.L, l.N, l.chunk);
   } else switch (l.tm) {
     case 64: disc_conv_wgrad_kernel<64, 64><<<grid, 256, 0, d->st>>>(l.da, in, d->part, l.L, l.N, l.chunk); break;
     case 32: disc_conv_wgrad_kernel<32, 64><<<grid, 256, 0, d->st>>>(l.da, in, d->part, l.L, l.N, l.chunk); break;
