@@ -14,13 +14,17 @@
 //
 // Kernels (fp32 FMA on the CUDA cores; the strided and grouped convolutions of the discriminators
 // have no stride-1 channels-last form for the tensor-core kernels of the generator):
-//   disc_conv_fwd     out[n][co][t] = act(b[co] + sum_{ci in group, k} w[co][ci][k] x[n][ci][t s + k - pad])
-//   disc_conv_dgrad   dx[n][ci][u]  = sum_{co in group, k : u + pad - k = t s} w[co][ci][k] dz[n][co][t]
-//   disc_conv_wgrad   dW[co][ci, k | bias] = sum_{n, t} dz[n][co][t] x[n][ci][t s + k - pad]  (tiled
-//                     GEMM over the (n, t) positions, split over position ranges; partials reduced
-//                     in a fixed order, so every result is deterministic)
-// plus the weight norm w = g v / ||v|| (per output row) and its backward, the loss terms, the
-// LeakyReLU / feature-matching gradient, the reflect-pad adjoint and torch's AdamW.
+//   forward         out[n][co][t] = act(b[co] + sum_{ci in group, k} w[co][ci][k] x[n][ci][t s + k - pad])
+//   input gradient  dx[n][ci][u]  = sum_{co in group, k : u + pad - k = t s} w[co][ci][k] dz[n][co][t]
+//   weight gradient dW[co][ci, k | bias] = sum_{n, t} dz[n][co][t] x[n][ci][t s + k - pad]  (split over
+//                   position ranges; partials reduced in a fixed order, so every result is deterministic)
+// The dense layers (64 | channels per group), which carry nearly all the FLOPs, run these as
+// register-tiled implicit GEMMs (disc_gemm_{fwd,dgrad,wgrad}_kernel); the grouped layers, the
+// one-channel first layers and conv_post run them as one output row per thread
+// (disc_conv_{fwd,dgrad,wgrad}_kernel, disc_post_fwd_kernel).  Plus the weight norm
+// w = g v / ||v|| (per output row) and its backward, the loss terms, the LeakyReLU /
+// feature-matching gradient, the reflect-pad adjoint, torch's AdamW, and the data-parallel gradient
+// all-reduce.
 #include <cuda_runtime.h>
 
 #include <cmath>
