@@ -84,7 +84,9 @@ def test_flatten_roundtrip():
     assert flat.size == param_total(cfg)
 
 
-def test_flops_match_survey():
+def test_training_flops_per_item():
+    """Algorithmic FLOPs of one training item (forward + input and weight gradients of every
+    convolution, 2 per multiply-add): 40 kHz at 32 frames, 32 kHz at 40, 48 kHz at 36."""
     assert abs(model.train_flops_per_item(model.config("40k"), 32) / 1e9 - 87.79) < 0.01
     assert abs(model.train_flops_per_item(model.config("32k"), 40) / 1e9 - 92.27) < 0.01
     assert abs(model.train_flops_per_item(model.config("48k"), 36) / 1e9 - 118.97) < 0.01

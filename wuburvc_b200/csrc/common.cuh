@@ -183,7 +183,7 @@ WB_DEV void tma_load_4d_warp(void* dst, const CUtensorMap* map, uint64_t* bar, i
       : "memory");
 }
 
-// Bounded wait by a converged warp; every lane gets the same verdict.  The spin loop lives inside one
+// Bounded wait by a converged warp; every lane gets the same result.  The spin loop lives inside one
 // asm block so the compiler sees no divergent control flow around the issuing code (a C++ loop here
 // makes it treat descriptors as per-lane values and every tcgen05.mma pays for uniformising them).
 WB_DEV bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* err, int code,
